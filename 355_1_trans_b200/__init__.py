@@ -1,0 +1,405 @@
+"""bsgemm_b200 -- B200 (sm_100a) block-scaled GEMM library, Python host side.
+
+The package directory name starts with a digit, so import it with
+``importlib.import_module("355_1_trans_b200")``.
+
+Everything here is a thin host mirror of the reference's Python adapter
+(trace_block_scale_latest_20260914_040021/source_snapshot/blockscale_bpreshuffle.py:15-97)
+and of aiter's ``gemm_a8w8_bpreshuffle_opus`` API
+(opus_a8w8_bpreshuffle_integration_and_benchmark.md:113-135): it validates
+tensors, fills the C-ABI argument struct and calls the CUDA library
+``_build/libbsgemm_b200.so`` through ctypes on the current torch stream.
+There is no CPU or library fallback: if the shared library is missing or the
+device is not an sm_100 GPU, calls raise.
+"""
+from __future__ import annotations
+
+import ctypes
+from functools import lru_cache
+from pathlib import Path
+
+import torch
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "_build" / "libbsgemm_b200.so"
+
+# ---- C enums (include/bsgemm_b200.h) -----------------------------------------
+OK, ERR_INVALID_VALUE, ERR_UNSUPPORTED, ERR_ARCH, ERR_WORKSPACE, ERR_CUDA, ERR_TIMEOUT, ERR_ALIGNMENT = range(8)
+LAYOUTS = {"nt": 0, "tt": 1, "nn": 2, "tn": 3}
+B_RAW, B_KPANEL128, B_SHUFFLE16 = 0, 1, 2
+SF_NATIVE, SF_ROWMAJOR, SF_KMAJOR_T, SF_E8M0_SHUFFLE = 0, 1, 2, 3
+OUT_BF16, OUT_FP32 = 0, 1
+FAMILY_MXFP8, FAMILY_MXFP4, FAMILY_FP8_BLOCK = 0, 1, 2
+
+
+class BsgemmError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what} failed: {status} ({strerror(status)})")
+
+
+class Args(ctypes.Structure):
+    """bsgemm_args: the reference's 96-byte kargs prefix + extensions."""
+    _fields_ = (
+        [(name, ctypes.c_void_p) for name in ("ptr_a", "ptr_b", "ptr_c")]
+        + [(name, ctypes.c_int) for name in (
+            "m", "n", "k", "batch", "stride_a", "stride_b", "stride_c",
+            "stride_a_batch", "stride_b_batch", "stride_c_batch")]
+        + [(name, ctypes.c_void_p) for name in ("ptr_sfa", "ptr_sfb")]
+        + [(name, ctypes.c_int) for name in (
+            "stride_sfa", "stride_sfb", "stride_sfa_batch", "stride_sfb_batch",
+            "layout", "b_format", "sfa_format", "sfb_format", "out_dtype", "split_k")]
+        + [("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+           ("grid_blocks", ctypes.c_int), ("reserved", ctypes.c_int)]
+    )
+
+
+assert Args.ptr_sfa.offset == 64 and Args.stride_sfa.offset == 80
+assert Args.layout.offset == 96
+
+
+@lru_cache(None)
+def lib() -> ctypes.CDLL:
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f"{LIB_PATH} is missing: build it with `python 355_1_trans_b200/build.py` "
+            "(there is no fallback implementation)")
+    so = ctypes.CDLL(str(LIB_PATH))
+    P, I, S = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t
+    sigs = {
+        "bsgemm_args_init": (None, [ctypes.POINTER(Args)]),
+        "bsgemm_a8w8_mxfp8": (I, [ctypes.POINTER(Args), P]),
+        "bsgemm_a4w4_mxfp4": (I, [ctypes.POINTER(Args), P]),
+        "bsgemm_a8w8_blockscale_bpreshuffle": (I, [ctypes.POINTER(Args), P]),
+        "bsgemm_workspace_size": (S, [I, ctypes.POINTER(Args)]),
+        "bsgemm_pack_b": (I, [P, P, I, I, I, I, P]),
+        "bsgemm_pack_scales": (I, [P, I, P, I, I, I, I, P]),
+        "bsgemm_native_scales_size": (S, [I, I]),
+        "launch_blockscale_bpreshuffle": (I, [P, I, I, P]),
+        "bsgemm_strerror": (ctypes.c_char_p, [I]),
+        "bsgemm_check_device_error": (I, []),
+        "bsgemm_selftest_timeout": (I, [I]),
+        "bsgemm_version": (ctypes.c_char_p, []),
+    }
+    for name, (res, argt) in sigs.items():
+        fn = getattr(so, name)
+        fn.restype = res
+        fn.argtypes = argt
+    return so
+
+
+def strerror(status: int) -> str:
+    return lib().bsgemm_strerror(int(status)).decode()
+
+
+def version() -> str:
+    return lib().bsgemm_version().decode()
+
+
+def check_device_error() -> int:
+    """Synchronise and read/clear the device error word (0 or ERR_TIMEOUT)."""
+    return int(lib().bsgemm_check_device_error())
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _check(status: int, what: str):
+    if status != OK:
+        raise BsgemmError(status, what)
+
+
+_FP8 = (torch.float8_e4m3fn, torch.uint8)
+_SCALE_U8 = (torch.uint8, getattr(torch, "float8_e8m0fnu", torch.uint8))
+_FP4 = (torch.uint8, getattr(torch, "float4_e2m1fn_x2", torch.uint8))
+
+
+def _out(out, m, n, dtype, device, batch):
+    shape = (m, n) if batch == 1 else (batch, m, n)
+    if out is None:
+        return torch.empty(shape, device=device, dtype=dtype)
+    if tuple(out.shape) != shape or out.dtype != dtype or out.device != device or not out.is_contiguous():
+        raise ValueError("out must be a contiguous tensor of shape %s and dtype %s" % (shape, dtype))
+    return out
+
+
+def _workspace(family: int, args: Args, workspace, device):
+    need = int(lib().bsgemm_workspace_size(family, ctypes.byref(args)))
+    if need == 0:
+        return None
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=device)
+    elif workspace.numel() * workspace.element_size() < need:
+        raise ValueError(f"workspace needs {need} bytes")
+    args.workspace = workspace.data_ptr()
+    args.workspace_bytes = workspace.numel() * workspace.element_size()
+    return workspace
+
+
+def _record(tensors, device):
+    stream = torch.cuda.current_stream(device)
+    for t in tensors:
+        if t is not None and t.is_cuda:
+            t.record_stream(stream)
+
+
+# ---------------------------------------------------------------------------
+# MXFP8 / MXFP4
+# ---------------------------------------------------------------------------
+
+def gemm_a8w8_mxfp8(A, B, A_scale, B_scale, *, layout: str = "tn", out_dtype=torch.bfloat16,
+                    out=None, scale_format: str = "rowmajor", split_k: int = 0,
+                    workspace=None, grid_blocks: int = 0):
+    """MXFP8 GEMM (mxfp8_gemm/gemm_a8w8_mxfp8_host.cc:98-122 semantics).
+
+    A: E4M3 [M,K] (layout t*) or [K,M] (n*); B: E4M3 [N,K] (*n) or [K,N] (*t);
+    optional leading batch dim.  A_scale/B_scale: E8M0 bytes, [rows, K/32]
+    row-major (scale_format="rowmajor") or native atoms from pack_scales
+    (scale_format="native").  Returns C [M,N] (or [batch,M,N]) of out_dtype.
+    """
+    return _mx(A, B, A_scale, B_scale, fp4=False, layout=layout, out_dtype=out_dtype, out=out,
+               scale_format=scale_format, split_k=split_k, workspace=workspace,
+               grid_blocks=grid_blocks)
+
+
+def gemm_a4w4_mxfp4(A, B, A_scale, B_scale, *, out_dtype=torch.bfloat16, out=None,
+                    scale_format: str = "rowmajor", split_k: int = 0, workspace=None,
+                    grid_blocks: int = 0):
+    """MXFP4 GEMM (mxfp4_gemm_4wave_20261112/gemm_a4w4_mxfp4_4wave_host.cc:97-115
+    semantics): A [M,K/2], B [N,K/2] packed E2M1 bytes (even k low nibble),
+    K-major; scales E8M0 [rows, K/32] or native."""
+    return _mx(A, B, A_scale, B_scale, fp4=True, layout="tn", out_dtype=out_dtype, out=out,
+               scale_format=scale_format, split_k=split_k, workspace=workspace,
+               grid_blocks=grid_blocks)
+
+
+def _mx(A, B, A_scale, B_scale, *, fp4, layout, out_dtype, out, scale_format, split_k,
+        workspace, grid_blocks):
+    if layout not in LAYOUTS:
+        raise ValueError(f"layout must be one of {sorted(LAYOUTS)}")
+    if A.dim() != B.dim() or A.dim() not in (2, 3):
+        raise ValueError("A and B must both be 2-D or both 3-D (batched)")
+    tensors = (A, B, A_scale, B_scale)
+    if not A.is_cuda or any(t.device != A.device for t in tensors):
+        raise ValueError("all inputs must be on the same GPU")
+    ok_types = _FP4 if fp4 else _FP8
+    if A.dtype not in ok_types or B.dtype not in ok_types:
+        raise ValueError("A/B must hold %s bytes" % ("packed E2M1" if fp4 else "E4M3FN"))
+    if A_scale.dtype not in _SCALE_U8 or B_scale.dtype not in _SCALE_U8:
+        raise ValueError("scales must be E8M0 bytes")
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("out_dtype must be bfloat16 or float32")
+    batch = A.shape[0] if A.dim() == 3 else 1
+    code = LAYOUTS[layout]
+    a_km, b_km = bool(code & 1), bool(code & 2)
+    a2 = A.shape[-2:]
+    b2 = B.shape[-2:]
+    if fp4:
+        m, kh = a2
+        n = b2[0]
+        k = 2 * kh
+        if b2[1] != kh:
+            raise ValueError("A and B disagree on K")
+    else:
+        m, k = (a2[0], a2[1]) if a_km else (a2[1], a2[0])
+        n, kb = (b2[0], b2[1]) if b_km else (b2[1], b2[0])
+        if kb != k:
+            raise ValueError("A and B disagree on K")
+    for t in (A, B):
+        if t.stride(-1) != 1:
+            raise ValueError("A and B must have unit stride in the last dimension")
+    out = _out(out, m, n, out_dtype, A.device, batch)
+    args = Args()
+    lib().bsgemm_args_init(ctypes.byref(args))
+    args.ptr_a, args.ptr_b, args.ptr_c = A.data_ptr(), B.data_ptr(), out.data_ptr()
+    args.m, args.n, args.k, args.batch = m, n, k, batch
+    args.stride_a, args.stride_b, args.stride_c = A.stride(-2), B.stride(-2), n
+    if batch > 1:
+        args.stride_a_batch, args.stride_b_batch, args.stride_c_batch = A.stride(0), B.stride(0), m * n
+    args.ptr_sfa, args.ptr_sfb = A_scale.data_ptr(), B_scale.data_ptr()
+    if scale_format == "rowmajor":
+        kg = k // 32
+        for sc, rows in ((A_scale, m), (B_scale, n)):
+            if tuple(sc.shape[-2:]) != (rows, kg) or sc.stride(-1) != 1:
+                raise ValueError(f"scale must be [{rows}, {kg}] with unit inner stride")
+        args.sfa_format = args.sfb_format = SF_ROWMAJOR
+        args.stride_sfa, args.stride_sfb = A_scale.stride(-2), B_scale.stride(-2)
+        if batch > 1:
+            args.stride_sfa_batch, args.stride_sfb_batch = A_scale.stride(0), B_scale.stride(0)
+    elif scale_format == "native":
+        args.sfa_format = args.sfb_format = SF_NATIVE
+        if batch > 1:
+            args.stride_sfa_batch = A_scale.stride(0) if A_scale.dim() > 1 else 0
+            args.stride_sfb_batch = B_scale.stride(0) if B_scale.dim() > 1 else 0
+    else:
+        raise ValueError("scale_format must be 'rowmajor' or 'native'")
+    args.layout = code
+    args.out_dtype = OUT_BF16 if out_dtype == torch.bfloat16 else OUT_FP32
+    args.split_k = split_k
+    args.grid_blocks = grid_blocks
+    ws = _workspace(FAMILY_MXFP4 if fp4 else FAMILY_MXFP8, args, workspace, A.device)
+    fn = lib().bsgemm_a4w4_mxfp4 if fp4 else lib().bsgemm_a8w8_mxfp8
+    with torch.cuda.device(A.device):
+        status = fn(ctypes.byref(args), _stream(A.device))
+        _record((*tensors, out, ws), A.device)
+    _check(status, "bsgemm_a4w4_mxfp4" if fp4 else "bsgemm_a8w8_mxfp8")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# FP8 block-scale with fp32 scales (aiter gemm_a8w8_bpreshuffle_opus API)
+# ---------------------------------------------------------------------------
+
+def gemm_a8w8_bpreshuffle(A, B, x_scale, w_scale, out_dtype=torch.bfloat16, *,
+                          preshuffled: bool = True, x_scale_transposed: bool = False,
+                          out=None, split_k: int = 0, workspace=None, grid_blocks: int = 0):
+    """a8w8 GEMM with fp32 1x128 (x_scale [M,K/128]) and 128x128
+    (w_scale [N/128,K/128]) block scales, bf16/fp32 out.
+
+    preshuffled=True: B is the K-panel layout B'[K/128][N][128] (given as a
+    [K/128, N, 128] or flat [N, K] tensor), as aiter's wrapper produces
+    (opus_a8w8_bpreshuffle_integration_and_benchmark.md:76-81);
+    preshuffled=False: B is plain [N, K].  x_scale_transposed=True takes the
+    reference kernel's [K/128, M] SFA layout.
+    """
+    if A.dim() != 2:
+        raise ValueError("A must be [M, K]")
+    tensors = (A, B, x_scale, w_scale)
+    if not A.is_cuda or any(t.device != A.device for t in tensors):
+        raise ValueError("all inputs must be on the same GPU")
+    if A.dtype not in _FP8 or B.dtype not in _FP8:
+        raise ValueError("A/B must hold E4M3FN bytes")
+    if x_scale.dtype != torch.float32 or w_scale.dtype != torch.float32:
+        raise ValueError("scales must be fp32")
+    m, k = A.shape
+    if preshuffled:
+        if B.dim() == 3:
+            kt, n, inner = B.shape
+            if inner != 128 or kt * 128 != k:
+                raise ValueError("K-panel B must be [K/128, N, 128]")
+        else:
+            n = B.numel() // k
+        if not B.is_contiguous():
+            raise ValueError("K-panel B must be contiguous")
+    else:
+        n, kb = B.shape
+        if kb != k:
+            raise ValueError("A and B disagree on K")
+    kblk = k // 128
+    if x_scale_transposed:
+        if tuple(x_scale.shape) != (kblk, m) or x_scale.stride(1) != 1:
+            raise ValueError("transposed x_scale must be [K/128, M]")
+    elif tuple(x_scale.shape) != (m, kblk) or x_scale.stride(1) != 1:
+        raise ValueError("x_scale must be [M, K/128]")
+    if tuple(w_scale.shape) != ((n + 127) // 128, kblk) or w_scale.stride(1) != 1:
+        raise ValueError("w_scale must be [N/128, K/128]")
+    out = _out(out, m, n, out_dtype, A.device, 1)
+    args = Args()
+    lib().bsgemm_args_init(ctypes.byref(args))
+    args.ptr_a, args.ptr_b, args.ptr_c = A.data_ptr(), B.data_ptr(), out.data_ptr()
+    args.m, args.n, args.k, args.batch = m, n, k, 1
+    args.stride_a, args.stride_c = A.stride(0), n
+    args.stride_b = 128 if preshuffled else B.stride(0)
+    args.b_format = B_KPANEL128 if preshuffled else B_RAW
+    args.ptr_sfa, args.ptr_sfb = x_scale.data_ptr(), w_scale.data_ptr()
+    args.sfa_format = SF_KMAJOR_T if x_scale_transposed else SF_ROWMAJOR
+    args.stride_sfa = x_scale.stride(0)
+    args.sfb_format = SF_ROWMAJOR
+    args.stride_sfb = w_scale.stride(0)
+    args.layout = LAYOUTS["tn"]
+    args.out_dtype = OUT_BF16 if out_dtype == torch.bfloat16 else OUT_FP32
+    args.split_k = split_k
+    args.grid_blocks = grid_blocks
+    ws = _workspace(FAMILY_FP8_BLOCK, args, workspace, A.device)
+    with torch.cuda.device(A.device):
+        status = lib().bsgemm_a8w8_blockscale_bpreshuffle(ctypes.byref(args), _stream(A.device))
+        _record((*tensors, out, ws), A.device)
+    _check(status, "bsgemm_a8w8_blockscale_bpreshuffle")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# layout converters (device)
+# ---------------------------------------------------------------------------
+
+def pack_b(B, src_format: str, *, unpack: bool = False, out=None):
+    """Byte permutation of a [rows, kbytes] operand between a reference
+    preshuffle ('shuffle16' = aiter shuffle_weight(16,16), 'kpanel' =
+    B'[K/128][N][128]) and the raw K-major layout (unpack=True: raw -> format).
+    Returns a uint8 tensor of the same shape as the input's [rows, kbytes]."""
+    fmt = {"shuffle16": B_SHUFFLE16, "kpanel": B_KPANEL128}[src_format]
+    src = B.contiguous().view(torch.uint8)
+    if src.dim() == 3:           # K-panel given as [K/128, N, 128]
+        kt, rows, inner = src.shape
+        kbytes = kt * inner
+    else:
+        rows, kbytes = src.shape
+    if out is None:
+        out = torch.empty((rows, kbytes), dtype=torch.uint8, device=B.device)
+    with torch.cuda.device(B.device):
+        status = lib().bsgemm_pack_b(src.data_ptr(), out.data_ptr(), rows, kbytes, fmt,
+                                     int(unpack), _stream(B.device))
+        _record((src, out), B.device)
+    _check(status, "bsgemm_pack_b")
+    return out
+
+
+def native_scales_size(rows: int, kg: int) -> int:
+    return int(lib().bsgemm_native_scales_size(rows, kg))
+
+
+def pack_scales(sf, rows: int | None = None, kg: int | None = None, *, src_format: str = "rowmajor",
+                out=None):
+    """E8M0 [rows, kg] (row-major, or aiter e8m0_shuffle bytes with rows/kg given)
+    -> native tcgen05 scale atoms (uint8, native_scales_size(rows, kg) bytes)."""
+    src = sf.contiguous().view(torch.uint8)
+    if src_format == "rowmajor":
+        rows, kg = src.shape
+        fmt, stride = SF_ROWMAJOR, kg
+    elif src_format == "e8m0_shuffle":
+        if rows is None or kg is None:
+            raise ValueError("rows and kg are required for e8m0_shuffle input")
+        fmt, stride = SF_E8M0_SHUFFLE, 0
+    else:
+        raise ValueError("src_format must be 'rowmajor' or 'e8m0_shuffle'")
+    size = native_scales_size(rows, kg)
+    if out is None:
+        out = torch.empty(size, dtype=torch.uint8, device=sf.device)
+    with torch.cuda.device(sf.device):
+        status = lib().bsgemm_pack_scales(src.data_ptr(), stride, out.data_ptr(), rows, kg, fmt, 0,
+                                          _stream(sf.device))
+        _record((src, out), sf.device)
+    _check(status, "bsgemm_pack_scales")
+    return out
+
+
+def unpack_scales(native, rows: int, kg: int, *, dst_format: str = "rowmajor"):
+    """Inverse of pack_scales."""
+    if dst_format == "rowmajor":
+        out = torch.empty((rows, kg), dtype=torch.uint8, device=native.device)
+        fmt, stride = SF_ROWMAJOR, kg
+    elif dst_format == "e8m0_shuffle":
+        size = ((rows + 31) // 32 * 32) * ((kg + 7) // 8 * 8)
+        out = torch.empty(size, dtype=torch.uint8, device=native.device)
+        fmt, stride = SF_E8M0_SHUFFLE, 0
+    else:
+        raise ValueError("dst_format must be 'rowmajor' or 'e8m0_shuffle'")
+    with torch.cuda.device(native.device):
+        status = lib().bsgemm_pack_scales(native.data_ptr(), stride, out.data_ptr(), rows, kg, fmt, 1,
+                                          _stream(native.device))
+        _record((native, out), native.device)
+    _check(status, "bsgemm_pack_scales(unpack)")
+    return out
+
+
+def selftest_timeout(timeout_us: int = 2000) -> int:
+    """Run the bounded-wait self test; returns the status (ERR_TIMEOUT expected)."""
+    return int(lib().bsgemm_selftest_timeout(int(timeout_us)))
+
+
+__all__ = [
+    "Args", "BsgemmError", "lib", "strerror", "version", "check_device_error",
+    "gemm_a8w8_mxfp8", "gemm_a4w4_mxfp4", "gemm_a8w8_bpreshuffle",
+    "pack_b", "pack_scales", "unpack_scales", "native_scales_size", "selftest_timeout",
+]

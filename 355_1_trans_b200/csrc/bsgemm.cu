@@ -1,0 +1,679 @@
+// bsgemm.cu -- host side of the C ABI declared in include/bsgemm_b200.h:
+// argument validation, TMA tensor-map encoding, tile / split-K planning and
+// kernel dispatch.  The whole library is this one translation unit, so the
+// per-device error word (sm100.cuh) is shared by every kernel.
+//
+// Validation mirrors the reference launcher
+// (source_snapshot/gemm_a8w8_blockscale_bpreshuffle_launch.cc:31-65): null
+// pointers, flags, shapes, strides, 16-byte rules of TMA, and C overlapping an
+// input are rejected before anything is enqueued.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/bsgemm_b200.h"
+#include "fp8_block_gemm.cuh"
+#include "mx_gemm.cuh"
+#include "pack.cuh"
+
+namespace {
+
+using bsg::Fp8BlockCfg;
+using bsg::Fp8BlockParams;
+using bsg::MxCfg;
+using bsg::MxParams;
+
+constexpr unsigned long long kTimeoutNs = 10ull * 1000ull * 1000ull * 1000ull;  // 10 s per wait
+
+// ---------------------------------------------------------------------------
+// driver entry point for tensor-map encoding (no link-time libcuda dependency)
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Byte tensor map (uint8 elements) of rank 3 or 4 with 128B swizzle.
+// dims/strides innermost first; strides[i] is the byte stride of dim i+1.
+bool make_tmap_u8(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
+                  const uint64_t* strides, const uint32_t* box, bool swizzle128) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i < rank - 1) s[i] = strides[i];
+  }
+  const CUresult r =
+      fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, static_cast<cuuint32_t>(rank), const_cast<void*>(base),
+         d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+         swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// ---------------------------------------------------------------------------
+// device facts (cached per device)
+// ---------------------------------------------------------------------------
+struct DevInfo {
+  int sms = 0;
+  bool sm100 = false;
+  bool valid = false;
+};
+
+int device_info(DevInfo* out) {
+  static DevInfo cache[64];
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return BSG_ERR_CUDA;
+  if (dev < 0 || dev >= 64) return BSG_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev].valid) {
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return BSG_ERR_CUDA;
+    cache[dev].sms = prop.multiProcessorCount;
+    cache[dev].sm100 = prop.major == 10 && prop.minor == 0;
+    cache[dev].valid = true;
+  }
+  *out = cache[dev];
+  return BSG_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool overlaps(const void* a, uint64_t a_bytes, const void* b, uint64_t b_bytes) {
+  const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+  return x < y + b_bytes && y < x + a_bytes;
+}
+
+template <typename K>
+int set_smem(K kernel, uint32_t bytes) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(bytes)) == cudaSuccess
+             ? BSG_OK
+             : BSG_ERR_CUDA;
+}
+
+int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? BSG_OK : BSG_ERR_CUDA;
+}
+
+int grid_for(int units, const DevInfo& dev, int grid_blocks) {
+  int g = std::min(units, dev.sms);
+  if (grid_blocks > 0) g = std::min(g, grid_blocks);
+  return std::max(g, 1);
+}
+
+// ---------------------------------------------------------------------------
+// split-K planning
+// ---------------------------------------------------------------------------
+struct Plan {
+  int bn = 256;
+  int tiles_m = 1, tiles_n = 1;
+  int split = 1, kb_per = 1;
+  int num_kb = 1;
+  size_t ws_partials = 0;       // bytes of fp32 partials
+};
+
+void plan_split(Plan& pl, const bsgemm_args& a, int sms, bool allow_auto) {
+  const long long tiles = static_cast<long long>(pl.tiles_m) * pl.tiles_n * a.batch;
+  int split = 1;
+  if (a.split_k > 1) {
+    split = a.split_k;
+  } else if (a.split_k == 0 && allow_auto && tiles * 2 <= sms && pl.num_kb >= 8) {
+    // fill the machine, keep >= 4 K stages per slice
+    split = static_cast<int>(std::min<long long>(sms / tiles, pl.num_kb / 4));
+    split = std::max(1, std::min(split, 32));
+  }
+  split = std::min(split, pl.num_kb);
+  pl.kb_per = (pl.num_kb + split - 1) / split;
+  pl.split = (pl.num_kb + pl.kb_per - 1) / pl.kb_per;   // no empty slice
+  pl.ws_partials = pl.split > 1 ? static_cast<size_t>(pl.split) * a.batch * a.m * a.n * 4 : 0;
+}
+
+// ---------------------------------------------------------------------------
+// MXFP8 / MXFP4
+// ---------------------------------------------------------------------------
+size_t native_sf_bytes(int rows, int kg) {
+  return static_cast<size_t>((rows + 127) / 128) * static_cast<size_t>((kg + 3) / 4) * 512u;
+}
+
+size_t align256(size_t x) { return (x + 255u) & ~static_cast<size_t>(255u); }
+
+struct MxPlan : Plan {
+  size_t ws_sfa = 0, ws_sfb = 0;  // bytes of packed scales in the workspace
+};
+
+int mx_plan(const bsgemm_args& a, bool fp4, const DevInfo& dev, MxPlan& pl, bool allow_auto) {
+  const int kg = a.k / 32;
+  pl.tiles_m = (a.m + 127) / 128;
+  pl.num_kb = fp4 ? a.k / 256 : a.k / 128;
+  pl.bn = 256;
+  if (static_cast<long long>(pl.tiles_m) * ((a.n + 255) / 256) * a.batch < dev.sms / 2 || a.n <= 128)
+    pl.bn = 128;
+  pl.tiles_n = (a.n + pl.bn - 1) / pl.bn;
+  plan_split(pl, a, dev.sms, allow_auto);
+  pl.ws_sfa = a.sfa_format == BSG_SF_ROWMAJOR ? align256(native_sf_bytes(a.m, kg) * a.batch) : 0;
+  pl.ws_sfb = a.sfb_format == BSG_SF_ROWMAJOR ? align256(native_sf_bytes(a.n, kg) * a.batch) : 0;
+  return BSG_OK;
+}
+
+int validate_common(const bsgemm_args* a) {
+  if (!a || !a->ptr_a || !a->ptr_b || !a->ptr_c || !a->ptr_sfa || !a->ptr_sfb)
+    return BSG_ERR_INVALID_VALUE;
+  if (a->m <= 0 || a->n <= 0 || a->k <= 0 || a->batch <= 0) return BSG_ERR_INVALID_VALUE;
+  if (a->out_dtype != BSG_OUT_BF16 && a->out_dtype != BSG_OUT_FP32) return BSG_ERR_INVALID_VALUE;
+  if (a->split_k < 0 || a->grid_blocks < 0) return BSG_ERR_INVALID_VALUE;
+  if (a->layout < 0 || a->layout > 3) return BSG_ERR_INVALID_VALUE;
+  const int vec = a->out_dtype == BSG_OUT_BF16 ? 8 : 4;
+  if (a->n % vec || a->stride_c < a->n || a->stride_c % vec) return BSG_ERR_ALIGNMENT;
+  if (!aligned16(a->ptr_c)) return BSG_ERR_ALIGNMENT;
+  if (a->batch > 1 && (a->stride_c_batch < static_cast<long long>(a->m) * a->stride_c ||
+                       a->stride_c_batch % vec))
+    return BSG_ERR_INVALID_VALUE;
+  return BSG_OK;
+}
+
+// Operand extents in bytes, for the overlap test and tensor maps.
+uint64_t operand_bytes(long long rows_of_storage, long long ld, long long batch_stride, int batch) {
+  return static_cast<uint64_t>(batch > 1 ? batch_stride * (batch - 1) : 0) +
+         static_cast<uint64_t>(rows_of_storage) * ld;
+}
+
+template <int BN, int kFp4, bool kAMN, bool kBMN, bool kOutF32>
+int mx_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p, int grid,
+                cudaStream_t st) {
+  using Cfg = MxCfg<BN, kFp4>;
+  auto* kern = bsg::mx_gemm_kernel<BN, kFp4, kAMN, kBMN, kOutF32>;
+  if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
+  kern<<<grid, 256, Cfg::kSmemBytes, st>>>(ta, tb, p);
+  return launch_status();
+}
+
+template <int BN, int kFp4>
+int mx_launch_bn(bool amn, bool bmn, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
+                 const MxParams& p, int grid, cudaStream_t st) {
+  if constexpr (kFp4) {
+    return f32 ? mx_launch_t<BN, 1, false, false, true>(ta, tb, p, grid, st)
+               : mx_launch_t<BN, 1, false, false, false>(ta, tb, p, grid, st);
+  } else {
+    const int sel = (amn ? 4 : 0) | (bmn ? 2 : 0) | (f32 ? 1 : 0);
+    switch (sel) {
+      case 0: return mx_launch_t<BN, 0, false, false, false>(ta, tb, p, grid, st);
+      case 1: return mx_launch_t<BN, 0, false, false, true>(ta, tb, p, grid, st);
+      case 2: return mx_launch_t<BN, 0, false, true, false>(ta, tb, p, grid, st);
+      case 3: return mx_launch_t<BN, 0, false, true, true>(ta, tb, p, grid, st);
+      case 4: return mx_launch_t<BN, 0, true, false, false>(ta, tb, p, grid, st);
+      case 5: return mx_launch_t<BN, 0, true, false, true>(ta, tb, p, grid, st);
+      case 6: return mx_launch_t<BN, 0, true, true, false>(ta, tb, p, grid, st);
+      default: return mx_launch_t<BN, 0, true, true, true>(ta, tb, p, grid, st);
+    }
+  }
+}
+
+int splitk_reduce(const float* ws, const bsgemm_args& a, int split, int sms, cudaStream_t st) {
+  const long long total4 = static_cast<long long>(a.m) * a.n * a.batch / 4;
+  const int grid = static_cast<int>(std::min<long long>((total4 + 255) / 256, 8LL * sms));
+  if (a.out_dtype == BSG_OUT_FP32)
+    bsg::splitk_reduce_kernel<true><<<grid, 256, 0, st>>>(ws, a.ptr_c, a.m, a.n, a.batch, split,
+                                                         a.stride_c, a.stride_c_batch);
+  else
+    bsg::splitk_reduce_kernel<false><<<grid, 256, 0, st>>>(ws, a.ptr_c, a.m, a.n, a.batch, split,
+                                                          a.stride_c, a.stride_c_batch);
+  return launch_status();
+}
+
+int pack_sf_launch(const void* src, int src_stride, void* dst, int rows, int kg, int fmt,
+                   int unpack, cudaStream_t st) {
+  const long long words = static_cast<long long>((rows + 127) / 128) * ((kg + 3) / 4) * 128;
+  const int grid = static_cast<int>(std::min<long long>((words + 255) / 256, 4096));
+  bsg::pack_sf_native_kernel<<<grid, 256, 0, st>>>(static_cast<const uint8_t*>(src), src_stride,
+                                                  static_cast<uint8_t*>(dst), rows, kg, fmt,
+                                                  unpack);
+  return launch_status();
+}
+
+int mx_run(const bsgemm_args* args, bool fp4, cudaStream_t st) {
+  int rc = validate_common(args);
+  if (rc != BSG_OK) return rc;
+  const bsgemm_args& a = *args;
+  DevInfo dev;
+  if ((rc = device_info(&dev)) != BSG_OK) return rc;
+  if (!dev.sm100) return BSG_ERR_ARCH;
+  if (a.k % (fp4 ? 256 : 128)) return BSG_ERR_INVALID_VALUE;
+  const bool a_km = (a.layout & 1) != 0, b_km = (a.layout & 2) != 0;
+  if (fp4 && (!a_km || !b_km)) return BSG_ERR_UNSUPPORTED;   // .kind::mxf4 is K-major only
+  if (a.b_format != BSG_B_RAW) return BSG_ERR_UNSUPPORTED;   // repack with bsgemm_pack_b
+  for (int f : {a.sfa_format, a.sfb_format})
+    if (f != BSG_SF_NATIVE && f != BSG_SF_ROWMAJOR) return BSG_ERR_UNSUPPORTED;
+
+  const long long kbytes = fp4 ? a.k / 2 : a.k;
+  // A: K-major [M, kbytes] with ld stride_a, or M-major [K, M] with ld stride_a
+  const long long a_rows = a_km ? a.m : a.k, a_cols = a_km ? kbytes : a.m;
+  const long long b_rows = b_km ? a.n : a.k, b_cols = b_km ? kbytes : a.n;
+  if (a.stride_a < a_cols || a.stride_a % 16 || a.stride_b < b_cols || a.stride_b % 16)
+    return BSG_ERR_ALIGNMENT;
+  if (!aligned16(a.ptr_a) || !aligned16(a.ptr_b)) return BSG_ERR_ALIGNMENT;
+  if (a.batch > 1 && (a.stride_a_batch < a_rows * a.stride_a || a.stride_a_batch % 16 ||
+                      a.stride_b_batch < b_rows * a.stride_b || a.stride_b_batch % 16))
+    return BSG_ERR_INVALID_VALUE;
+  const int kg = a.k / 32;
+  // scale operands
+  const size_t sfa_nat = native_sf_bytes(a.m, kg), sfb_nat = native_sf_bytes(a.n, kg);
+  long long sfa_bs = 0, sfb_bs = 0;
+  if (a.sfa_format == BSG_SF_NATIVE) {
+    if (!aligned16(a.ptr_sfa)) return BSG_ERR_ALIGNMENT;
+    sfa_bs = a.batch > 1 ? (a.stride_sfa_batch ? a.stride_sfa_batch : static_cast<long long>(sfa_nat)) : 0;
+    if (sfa_bs % 16 || (a.batch > 1 && sfa_bs < static_cast<long long>(sfa_nat))) return BSG_ERR_INVALID_VALUE;
+  } else if (a.stride_sfa < kg ||
+             (a.batch > 1 && a.stride_sfa_batch < static_cast<long long>(a.m) * a.stride_sfa)) {
+    return BSG_ERR_INVALID_VALUE;
+  }
+  if (a.sfb_format == BSG_SF_NATIVE) {
+    if (!aligned16(a.ptr_sfb)) return BSG_ERR_ALIGNMENT;
+    sfb_bs = a.batch > 1 ? (a.stride_sfb_batch ? a.stride_sfb_batch : static_cast<long long>(sfb_nat)) : 0;
+    if (sfb_bs % 16 || (a.batch > 1 && sfb_bs < static_cast<long long>(sfb_nat))) return BSG_ERR_INVALID_VALUE;
+  } else if (a.stride_sfb < kg ||
+             (a.batch > 1 && a.stride_sfb_batch < static_cast<long long>(a.n) * a.stride_sfb)) {
+    return BSG_ERR_INVALID_VALUE;
+  }
+  // C must not overlap an input
+  const uint64_t c_bytes =
+      operand_bytes(a.m, a.stride_c, a.stride_c_batch, a.batch) * (a.out_dtype == BSG_OUT_BF16 ? 2 : 4);
+  if (overlaps(a.ptr_c, c_bytes, a.ptr_a, operand_bytes(a_rows, a.stride_a, a.stride_a_batch, a.batch)) ||
+      overlaps(a.ptr_c, c_bytes, a.ptr_b, operand_bytes(b_rows, a.stride_b, a.stride_b_batch, a.batch)))
+    return BSG_ERR_INVALID_VALUE;
+
+  MxPlan pl;
+  mx_plan(a, fp4, dev, pl, true);
+  size_t need = pl.ws_sfa + pl.ws_sfb + pl.ws_partials;
+  if (need > a.workspace_bytes || (need && !a.workspace)) {
+    if (a.split_k == 0 && pl.split > 1) {   // auto split-K: drop it rather than fail
+      bsgemm_args b2 = a;
+      b2.split_k = 1;
+      mx_plan(b2, fp4, dev, pl, false);
+      need = pl.ws_sfa + pl.ws_sfb + pl.ws_partials;
+    }
+    if (need > a.workspace_bytes || (need && !a.workspace)) return BSG_ERR_WORKSPACE;
+  }
+  if (need && !aligned16(a.workspace)) return BSG_ERR_ALIGNMENT;
+  uint8_t* ws = static_cast<uint8_t*>(a.workspace);
+  if (need && overlaps(a.ptr_c, c_bytes, ws, need)) return BSG_ERR_INVALID_VALUE;
+
+  // scales in row-major form are packed into the workspace first
+  const uint8_t* sfa = static_cast<const uint8_t*>(a.ptr_sfa);
+  const uint8_t* sfb = static_cast<const uint8_t*>(a.ptr_sfb);
+  if (a.sfa_format == BSG_SF_ROWMAJOR) {
+    for (int bb = 0; bb < a.batch; ++bb)
+      if ((rc = pack_sf_launch(sfa + static_cast<long long>(bb) * a.stride_sfa_batch, a.stride_sfa,
+                               ws + bb * sfa_nat, a.m, kg, BSG_SF_ROWMAJOR, 0, st)) != BSG_OK)
+        return rc;
+    sfa = ws;
+    sfa_bs = static_cast<long long>(sfa_nat);
+  }
+  if (a.sfb_format == BSG_SF_ROWMAJOR) {
+    for (int bb = 0; bb < a.batch; ++bb)
+      if ((rc = pack_sf_launch(sfb + static_cast<long long>(bb) * a.stride_sfb_batch, a.stride_sfb,
+                               ws + pl.ws_sfa + bb * sfb_nat, a.n, kg, BSG_SF_ROWMAJOR, 0, st)) != BSG_OK)
+        return rc;
+    sfb = ws + pl.ws_sfa;
+    sfb_bs = static_cast<long long>(sfb_nat);
+  }
+
+  // tensor maps (rank 3: inner, rows, batch)
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(a_cols), static_cast<uint64_t>(a_rows),
+                              static_cast<uint64_t>(a.batch)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_a),
+                                 static_cast<uint64_t>(a.batch > 1 ? a.stride_a_batch
+                                                                   : a_rows * a.stride_a)};
+    const uint32_t box[3] = {128u, 128u, 1u};
+    if (!make_tmap_u8(&ta, a.ptr_a, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(b_cols), static_cast<uint64_t>(b_rows),
+                              static_cast<uint64_t>(a.batch)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_b),
+                                 static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch
+                                                                   : b_rows * a.stride_b)};
+    const uint32_t box[3] = {128u, b_km ? static_cast<uint32_t>(pl.bn) : 128u, 1u};
+    if (!make_tmap_u8(&tb, a.ptr_b, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
+  }
+  MxParams p{};
+  p.m = a.m;
+  p.n = a.n;
+  p.k = a.k;
+  p.batch = a.batch;
+  p.num_kb = pl.num_kb;
+  p.tiles_m = pl.tiles_m;
+  p.tiles_n = pl.tiles_n;
+  p.split_k = pl.split;
+  p.kb_per_split = pl.kb_per;
+  p.total_units = pl.tiles_m * pl.tiles_n * a.batch * pl.split;
+  p.sfa = sfa;
+  p.sfb = sfb;
+  p.sfa_batch_stride = sfa_bs;
+  p.sfb_batch_stride = sfb_bs;
+  p.sf_kb_total = (kg + 3) / 4;
+  p.sfb_row_blocks = (a.n + 127) / 128;
+  p.c = a.ptr_c;
+  p.ldc = a.stride_c;
+  p.c_batch_stride = a.stride_c_batch;
+  p.ws = pl.split > 1 ? reinterpret_cast<float*>(ws + pl.ws_sfa + pl.ws_sfb) : nullptr;
+  p.timeout_ns = kTimeoutNs;
+  const int grid = grid_for(p.total_units, dev, a.grid_blocks);
+  const bool f32 = a.out_dtype == BSG_OUT_FP32;
+  rc = pl.bn == 256 ? (fp4 ? mx_launch_bn<256, 1>(!a_km, !b_km, f32, ta, tb, p, grid, st)
+                           : mx_launch_bn<256, 0>(!a_km, !b_km, f32, ta, tb, p, grid, st))
+                    : (fp4 ? mx_launch_bn<128, 1>(!a_km, !b_km, f32, ta, tb, p, grid, st)
+                           : mx_launch_bn<128, 0>(!a_km, !b_km, f32, ta, tb, p, grid, st));
+  if (rc != BSG_OK) return rc;
+  if (pl.split > 1) return splitk_reduce(p.ws, a, pl.split, dev.sms, st);
+  return BSG_OK;
+}
+
+// ---------------------------------------------------------------------------
+// FP8 block-scale (fp32 scales)
+// ---------------------------------------------------------------------------
+template <bool kKPanel, bool kOutF32>
+int fp8b_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockParams& p, int grid,
+                  cudaStream_t st) {
+  using Cfg = Fp8BlockCfg<128>;
+  auto* kern = bsg::fp8_block_gemm_kernel<128, kKPanel, kOutF32>;
+  if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
+  kern<<<grid, 256, Cfg::kSmemBytes, st>>>(ta, tb, p);
+  return launch_status();
+}
+
+void fp8b_plan(const bsgemm_args& a, const DevInfo& dev, Plan& pl, bool allow_auto) {
+  pl.bn = 128;
+  pl.tiles_m = (a.m + 127) / 128;
+  pl.tiles_n = (a.n + 127) / 128;
+  pl.num_kb = a.k / 128;
+  plan_split(pl, a, dev.sms, allow_auto);
+}
+
+int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
+  int rc = validate_common(args);
+  if (rc != BSG_OK) return rc;
+  const bsgemm_args& a = *args;
+  DevInfo dev;
+  if ((rc = device_info(&dev)) != BSG_OK) return rc;
+  if (!dev.sm100) return BSG_ERR_ARCH;
+  if (a.k % 128) return BSG_ERR_INVALID_VALUE;
+  if (a.layout != BSG_LAYOUT_TN) return BSG_ERR_UNSUPPORTED;
+  if (a.b_format != BSG_B_RAW && a.b_format != BSG_B_KPANEL128) return BSG_ERR_UNSUPPORTED;
+  if (a.sfa_format != BSG_SF_ROWMAJOR && a.sfa_format != BSG_SF_KMAJOR_T) return BSG_ERR_UNSUPPORTED;
+  if (a.sfb_format != BSG_SF_ROWMAJOR) return BSG_ERR_UNSUPPORTED;
+  const bool kpanel = a.b_format == BSG_B_KPANEL128;
+  const int kb = a.k / 128, nb = (a.n + 127) / 128;
+  if (a.stride_a < a.k || a.stride_a % 16 || !aligned16(a.ptr_a) || !aligned16(a.ptr_b))
+    return BSG_ERR_ALIGNMENT;
+  if (kpanel ? a.stride_b != 128 : (a.stride_b < a.k || a.stride_b % 16)) return BSG_ERR_ALIGNMENT;
+  const long long b_elems = kpanel ? static_cast<long long>(a.n) * a.k : static_cast<long long>(a.n) * a.stride_b;
+  if (a.batch > 1 && (a.stride_a_batch < static_cast<long long>(a.m) * a.stride_a ||
+                      a.stride_a_batch % 16 || a.stride_b_batch < b_elems || a.stride_b_batch % 16))
+    return BSG_ERR_INVALID_VALUE;
+  // fp32 scale strides (floats)
+  long long sfa_m, sfa_k;
+  if (a.sfa_format == BSG_SF_ROWMAJOR) {
+    if (a.stride_sfa < kb) return BSG_ERR_INVALID_VALUE;
+    sfa_m = a.stride_sfa;
+    sfa_k = 1;
+  } else {
+    if (a.stride_sfa < a.m) return BSG_ERR_INVALID_VALUE;
+    sfa_m = 1;
+    sfa_k = a.stride_sfa;
+  }
+  if (a.stride_sfb < kb) return BSG_ERR_INVALID_VALUE;
+  if (a.batch > 1 && (a.stride_sfa_batch < static_cast<long long>(a.m) * kb ||
+                      a.stride_sfb_batch < static_cast<long long>(nb) * kb))
+    return BSG_ERR_INVALID_VALUE;
+  const uint64_t c_bytes =
+      operand_bytes(a.m, a.stride_c, a.stride_c_batch, a.batch) * (a.out_dtype == BSG_OUT_BF16 ? 2 : 4);
+  if (overlaps(a.ptr_c, c_bytes, a.ptr_a, operand_bytes(a.m, a.stride_a, a.stride_a_batch, a.batch)) ||
+      overlaps(a.ptr_c, c_bytes, a.ptr_b,
+               static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch * (a.batch - 1) : 0) + b_elems) ||
+      overlaps(a.ptr_c, c_bytes, a.ptr_sfa,
+               4ull * (a.batch > 1 ? a.stride_sfa_batch * a.batch : static_cast<long long>(a.m) * kb)) ||
+      overlaps(a.ptr_c, c_bytes, a.ptr_sfb,
+               4ull * (a.batch > 1 ? a.stride_sfb_batch * a.batch : static_cast<long long>(nb) * kb)))
+    return BSG_ERR_INVALID_VALUE;
+
+  Plan pl;
+  fp8b_plan(a, dev, pl, true);
+  if (pl.ws_partials > a.workspace_bytes || (pl.ws_partials && !a.workspace)) {
+    if (a.split_k == 0) {
+      bsgemm_args b2 = a;
+      b2.split_k = 1;
+      fp8b_plan(b2, dev, pl, false);
+    } else {
+      return BSG_ERR_WORKSPACE;
+    }
+  }
+  if (pl.ws_partials && !aligned16(a.workspace)) return BSG_ERR_ALIGNMENT;
+  if (pl.ws_partials && overlaps(a.ptr_c, c_bytes, a.workspace, pl.ws_partials))
+    return BSG_ERR_INVALID_VALUE;
+
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(a.k), static_cast<uint64_t>(a.m),
+                              static_cast<uint64_t>(a.batch)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_a),
+                                 static_cast<uint64_t>(a.batch > 1 ? a.stride_a_batch
+                                                                   : static_cast<long long>(a.m) * a.stride_a)};
+    const uint32_t box[3] = {128u, 128u, 1u};
+    if (!make_tmap_u8(&ta, a.ptr_a, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
+  }
+  if (kpanel) {
+    const uint64_t dims[4] = {128u, static_cast<uint64_t>(a.n), static_cast<uint64_t>(kb),
+                              static_cast<uint64_t>(a.batch)};
+    const uint64_t strides[3] = {128u, static_cast<uint64_t>(a.n) * 128u,
+                                 static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch : b_elems)};
+    const uint32_t box[4] = {128u, 128u, 1u, 1u};
+    if (!make_tmap_u8(&tb, a.ptr_b, 4, dims, strides, box, true)) return BSG_ERR_CUDA;
+  } else {
+    const uint64_t dims[3] = {static_cast<uint64_t>(a.k), static_cast<uint64_t>(a.n),
+                              static_cast<uint64_t>(a.batch)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_b),
+                                 static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch : b_elems)};
+    const uint32_t box[3] = {128u, 128u, 1u};
+    if (!make_tmap_u8(&tb, a.ptr_b, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
+  }
+  Fp8BlockParams p{};
+  p.m = a.m;
+  p.n = a.n;
+  p.k = a.k;
+  p.batch = a.batch;
+  p.num_kb = pl.num_kb;
+  p.tiles_m = pl.tiles_m;
+  p.tiles_n = pl.tiles_n;
+  p.split_k = pl.split;
+  p.kb_per_split = pl.kb_per;
+  p.total_units = pl.tiles_m * pl.tiles_n * a.batch * pl.split;
+  p.sfa = static_cast<const float*>(a.ptr_sfa);
+  p.sfa_m = sfa_m;
+  p.sfa_k = sfa_k;
+  p.sfa_batch = a.stride_sfa_batch;
+  p.sfb = static_cast<const float*>(a.ptr_sfb);
+  p.sfb_n = a.stride_sfb;
+  p.sfb_k = 1;
+  p.sfb_batch = a.stride_sfb_batch;
+  p.c = a.ptr_c;
+  p.ldc = a.stride_c;
+  p.c_batch_stride = a.stride_c_batch;
+  p.ws = pl.split > 1 ? static_cast<float*>(a.workspace) : nullptr;
+  p.timeout_ns = kTimeoutNs;
+  const int grid = grid_for(p.total_units, dev, a.grid_blocks);
+  const bool f32 = a.out_dtype == BSG_OUT_FP32;
+  rc = kpanel ? (f32 ? fp8b_launch_t<true, true>(ta, tb, p, grid, st)
+                     : fp8b_launch_t<true, false>(ta, tb, p, grid, st))
+              : (f32 ? fp8b_launch_t<false, true>(ta, tb, p, grid, st)
+                     : fp8b_launch_t<false, false>(ta, tb, p, grid, st));
+  if (rc != BSG_OK) return rc;
+  if (pl.split > 1) return splitk_reduce(p.ws, a, pl.split, dev.sms, st);
+  return BSG_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+void bsgemm_args_init(bsgemm_args* a) {
+  if (!a) return;
+  std::memset(a, 0, sizeof(*a));
+  a->batch = 1;
+  a->layout = BSG_LAYOUT_TN;
+  a->b_format = BSG_B_RAW;
+  a->sfa_format = BSG_SF_ROWMAJOR;
+  a->sfb_format = BSG_SF_ROWMAJOR;
+  a->out_dtype = BSG_OUT_BF16;
+}
+
+int bsgemm_a8w8_mxfp8(const bsgemm_args* args, bsg_stream_t stream) {
+  return mx_run(args, false, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int bsgemm_a4w4_mxfp4(const bsgemm_args* args, bsg_stream_t stream) {
+  return mx_run(args, true, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int bsgemm_a8w8_blockscale_bpreshuffle(const bsgemm_args* args, bsg_stream_t stream) {
+  return fp8b_run(args, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t bsgemm_workspace_size(int family, const bsgemm_args* args) {
+  if (!args || args->m <= 0 || args->n <= 0 || args->k <= 0 || args->batch <= 0) return 0;
+  DevInfo dev;
+  if (device_info(&dev) != BSG_OK) return 0;
+  if (family == BSG_FAMILY_MXFP8 || family == BSG_FAMILY_MXFP4) {
+    MxPlan pl;
+    mx_plan(*args, family == BSG_FAMILY_MXFP4, dev, pl, true);
+    return pl.ws_sfa + pl.ws_sfb + pl.ws_partials;
+  }
+  if (family == BSG_FAMILY_FP8_BLOCK) {
+    Plan pl;
+    fp8b_plan(*args, dev, pl, true);
+    return pl.ws_partials;
+  }
+  return 0;
+}
+
+int bsgemm_pack_b(const void* src, void* dst, int rows, int kbytes, int src_format, int unpack,
+                  bsg_stream_t stream) {
+  if (!src || !dst || rows <= 0 || kbytes <= 0 || (unpack != 0 && unpack != 1))
+    return BSG_ERR_INVALID_VALUE;
+  if (!aligned16(src) || !aligned16(dst) || kbytes % 16) return BSG_ERR_ALIGNMENT;
+  const uint64_t bytes = static_cast<uint64_t>(rows) * kbytes;
+  if (overlaps(src, bytes, dst, bytes)) return BSG_ERR_INVALID_VALUE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const long long chunks = static_cast<long long>(rows) * (kbytes / 16);
+  const int grid = static_cast<int>(std::min<long long>((chunks + 255) / 256, 8192));
+  if (src_format == BSG_B_SHUFFLE16) {
+    if (rows % 16) return BSG_ERR_INVALID_VALUE;
+    bsg::pack_b_shuffle16_kernel<<<grid, 256, 0, st>>>(static_cast<const uint4*>(src),
+                                                       static_cast<uint4*>(dst), rows, kbytes, unpack);
+  } else if (src_format == BSG_B_KPANEL128) {
+    if (kbytes % 128) return BSG_ERR_INVALID_VALUE;
+    bsg::pack_b_kpanel_kernel<<<grid, 256, 0, st>>>(static_cast<const uint4*>(src),
+                                                    static_cast<uint4*>(dst), rows, kbytes, unpack);
+  } else {
+    return BSG_ERR_INVALID_VALUE;
+  }
+  return launch_status();
+}
+
+size_t bsgemm_native_scales_size(int rows, int kg) {
+  if (rows <= 0 || kg <= 0) return 0;
+  return native_sf_bytes(rows, kg);
+}
+
+int bsgemm_pack_scales(const void* src, int src_stride, void* dst, int rows, int kg,
+                       int src_format, int unpack, bsg_stream_t stream) {
+  if (!src || !dst || rows <= 0 || kg <= 0 || (unpack != 0 && unpack != 1))
+    return BSG_ERR_INVALID_VALUE;
+  if (src_format != BSG_SF_ROWMAJOR && src_format != BSG_SF_E8M0_SHUFFLE) return BSG_ERR_INVALID_VALUE;
+  if (src_format == BSG_SF_ROWMAJOR && src_stride < kg) return BSG_ERR_INVALID_VALUE;
+  const void* native = unpack ? src : dst;
+  if (!aligned16(native)) return BSG_ERR_ALIGNMENT;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (unpack && src_format == BSG_SF_E8M0_SHUFFLE) {
+    const long long n = static_cast<long long>((rows + 31) / 32 * 32) * ((kg + 7) / 8 * 8);
+    bsg::fill_u8_kernel<<<static_cast<int>(std::min<long long>((n + 255) / 256, 4096)), 256, 0, st>>>(
+        static_cast<uint8_t*>(dst), n, 0x7F);
+  }
+  return pack_sf_launch(src, src_stride, dst, rows, kg, src_format, unpack, st);
+}
+
+int launch_blockscale_bpreshuffle(const void* kargs, int output_bf16, int tiles,
+                                  bsg_stream_t stream) {
+  (void)kargs;
+  (void)output_bf16;
+  (void)tiles;
+  (void)stream;
+  return static_cast<int>(cudaErrorNotSupported);
+}
+
+const char* bsgemm_strerror(int status) {
+  switch (status) {
+    case BSG_OK: return "success";
+    case BSG_ERR_INVALID_VALUE: return "invalid argument";
+    case BSG_ERR_UNSUPPORTED: return "unsupported combination of formats or layouts";
+    case BSG_ERR_ARCH: return "device is not sm_100 (B200)";
+    case BSG_ERR_WORKSPACE: return "workspace missing or too small";
+    case BSG_ERR_CUDA: return "CUDA call failed";
+    case BSG_ERR_TIMEOUT: return "device-side bounded wait expired";
+    case BSG_ERR_ALIGNMENT: return "pointer or stride violates the 16-byte rules";
+    default: return "unknown status";
+  }
+}
+
+int bsgemm_check_device_error(void) {
+  int v = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return BSG_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(&v, bsg::g_bsg_device_error, sizeof(int)) != cudaSuccess)
+    return BSG_ERR_CUDA;
+  const int zero = 0;
+  if (v != 0 && cudaMemcpyToSymbol(bsg::g_bsg_device_error, &zero, sizeof(int)) != cudaSuccess)
+    return BSG_ERR_CUDA;
+  return v == 0 ? BSG_OK : v;
+}
+
+int bsgemm_selftest_timeout(int timeout_us) {
+  if (timeout_us <= 0 || timeout_us > 10 * 1000 * 1000) return BSG_ERR_INVALID_VALUE;
+  int rc = bsgemm_check_device_error();   // start from a clean word
+  if (rc == BSG_ERR_CUDA) return rc;
+  bsg::selftest_timeout_kernel<<<1, 32>>>(static_cast<unsigned long long>(timeout_us) * 1000ull);
+  if (cudaGetLastError() != cudaSuccess) return BSG_ERR_CUDA;
+  return bsgemm_check_device_error();
+}
+
+const char* bsgemm_version(void) { return "bsgemm_b200 0.1 (sm_100a)"; }
+
+}  // extern "C"

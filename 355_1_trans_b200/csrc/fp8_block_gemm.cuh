@@ -1,0 +1,296 @@
+// fp8_block_gemm.cuh -- FP8 (E4M3) GEMM with fp32 block scales, DeepSeek
+// style: one scale per (row, 128-K block) of A and per (128-N block, 128-K
+// block) of B, for sm_100a.
+//
+// Semantics (reference, paths relative to its project root):
+//   block_scale_gemm_bpreshuffle/gemm_a8w8_blockscale_bpreshuffle_kernel_template.hpp:
+//   204-601 with scale_c_tile :24-39 and load_sfb :284-289: for each 128-K
+//   block kb, the unscaled partial product (A B^T)_kb is multiplied by
+//   sfa[m,kb] * sfb[n/128,kb] and added to an fp32 accumulator.
+//
+// Because the scales are arbitrary fp32 (not powers of two) they cannot be
+// folded into a block-scaled MMA.  Instead:
+//   - the single-thread issuer runs 4 x .kind::f8f6f4 MMAs (K = 32 each) per
+//     128-K block into one of two TMEM buffers (128 x BN fp32 each), so the
+//     tensor core fills buffer kb+1 while buffer kb is being promoted;
+//   - the epilogue warps (the "promotion" warps) tcgen05.ld each finished
+//     partial and FMA it into a register accumulator with the per-row A scale
+//     times the per-tile B scale, then release the buffer; after the last K
+//     block they round to bf16 (RNE) and store.
+// B is read either raw [N,K] or in the reference's K-panel preshuffle
+// B'[K/128][N][128] (a 3D/4D tensor map makes both land identically in smem).
+#pragma once
+
+#include "mx_gemm.cuh"
+
+namespace bsg {
+
+struct Fp8BlockParams {
+  int m, n, k;
+  int batch;
+  int num_kb;
+  int tiles_m, tiles_n;
+  int split_k, kb_per_split;
+  int total_units;
+  const float* sfa;
+  long long sfa_m, sfa_k, sfa_batch;   // float strides: row, k-block, batch
+  const float* sfb;
+  long long sfb_n, sfb_k, sfb_batch;   // float strides: 128-row block, k-block, batch
+  void* c;
+  long long ldc;
+  long long c_batch_stride;
+  float* ws;
+  unsigned long long timeout_ns;
+};
+
+template <int BN>
+struct Fp8BlockCfg {
+  static_assert(BN == 128, "promotion accumulator holds 128 columns per thread");
+  static constexpr uint32_t kABytes = 128u * 128u;
+  static constexpr uint32_t kBBytes = static_cast<uint32_t>(BN) * 128u;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = 6;
+  static constexpr uint32_t kOffB = kABytes * kStages;
+  static constexpr uint32_t kOffBar = kOffB + kBBytes * kStages;
+  static constexpr uint32_t kSmemBytes = kOffBar + 256u + 1024u;
+  static constexpr uint32_t kTmemCols = 2u * BN;  // two accumulator buffers
+};
+
+template <int BN, bool kKPanel, bool kOutF32>
+__global__ void __launch_bounds__(256, 1)
+    fp8_block_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                          const __grid_constant__ CUtensorMap tmB, const Fp8BlockParams p) {
+  using Cfg = Fp8BlockCfg<BN>;
+  constexpr int S = Cfg::kStages;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~static_cast<uintptr_t>(1023u));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + Cfg::kOffB;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* acc_full = empty_bar + S;    // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint64_t* drain_bar = acc_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31u;
+
+  if (threadIdx.x == 32) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_holder, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    int last_stage = -1;
+    uint32_t last_phase = 0;
+    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+      int b, mt, nt, s;
+      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, b, mt, nt, s);
+      const int kb0 = s * p.kb_per_split;
+      const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        uint64_t* fb = &full_bar[stage];
+        mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
+        tma_load_3d(sA + stage * Cfg::kABytes, &tmA, fb, kb * 128, mt * 128, b);
+        if constexpr (kKPanel)
+          tma_load_4d(sB + stage * Cfg::kBBytes, &tmB, fb, 0, nt * BN, kb, b);
+        else
+          tma_load_3d(sB + stage * Cfg::kBBytes, &tmB, fb, kb * 128, nt * BN, b);
+        last_stage = stage;
+        last_phase = phase;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (!ok && last_stage >= 0) {
+      int dummy = 0;
+      mbar_wait(&full_bar[last_stage], last_phase, &dummy, p.timeout_ns);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------------ MMA issuer
+    const uint32_t idesc = idesc_f8f6f4(false, false, 128, BN);
+    const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t kbi = 0;   // K blocks issued by this CTA, selects the TMEM buffer
+    bool ok = true;
+    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+      int b, mt, nt, s;
+      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, b, mt, nt, s);
+      const int kb0 = s * p.kb_per_split;
+      const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
+      for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
+        const uint32_t buf = kbi & 1u;
+        const uint32_t use = kbi >> 1;   // how many times this buffer was used before
+        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = sA0 + stage * Cfg::kABytes;
+        const uint32_t b_addr = sB0 + stage * Cfg::kBBytes;
+        const uint32_t d = tmem_base + buf * BN;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const uint64_t adesc = make_sdesc(a_addr + 32u * t, 16u, 1024u, kLayoutSW128);
+          const uint64_t bdesc = make_sdesc(b_addr + 32u * t, 16u, 1024u, kLayoutSW128);
+          umma_f8f6f4(d, adesc, bdesc, idesc, t > 0 ? 1u : 0u);
+        }
+        tc_commit(&empty_bar[stage]);
+        tc_commit(&acc_full[buf]);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    tc_commit(drain_bar);
+    int dummy = 0;
+    mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ promotion + store
+    const int q = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    uint32_t kbi = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+      int b, mt, nt, s;
+      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, b, mt, nt, s);
+      const int kb0 = s * p.kb_per_split;
+      const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
+      const int row = mt * 128 + q * 32 + static_cast<int>(lane);
+      const bool row_ok = row < p.m;
+      const int n0 = nt * BN;
+      const float* sfa_row = p.sfa + b * p.sfa_batch + static_cast<long long>(row_ok ? row : 0) * p.sfa_m;
+      const float* sfb_blk = p.sfb + b * p.sfb_batch + static_cast<long long>(n0 / 128) * p.sfb_n;
+      float acc[BN];
+#pragma unroll
+      for (int i = 0; i < BN; ++i) acc[i] = 0.0f;
+      float sa_next = row_ok ? __ldg(sfa_row + kb0 * p.sfa_k) : 0.0f;
+      float sb_next = __ldg(sfb_blk + kb0 * p.sfb_k);
+      for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
+        const float scale = sa_next * sb_next;
+        if (kb + 1 < kb1) {
+          sa_next = row_ok ? __ldg(sfa_row + (kb + 1) * p.sfa_k) : 0.0f;
+          sb_next = __ldg(sfb_blk + (kb + 1) * p.sfb_k);
+        }
+        const uint32_t buf = kbi & 1u;
+        const uint32_t use = kbi >> 1;
+        if (!mbar_wait(&acc_full[buf], use & 1u, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem_base + lane_base + buf * BN + static_cast<uint32_t>(c * 32), r);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[c * 32 + i] = fmaf(__uint_as_float(r[i]), scale, acc[c * 32 + i]);
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[buf]);
+      }
+      if (!ok) break;
+      if (!row_ok) continue;
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col0 = n0 + c * 32;
+        if (col0 >= p.n) continue;
+        const bool full = col0 + 32 <= p.n;
+        if (p.split_k > 1) {
+          float* dst = p.ws + ((static_cast<long long>(s) * p.batch + b) * p.m + row) *
+                                  static_cast<long long>(p.n) + col0;
+          if (full) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              st_global_v4(dst + 4 * v, __float_as_uint(acc[c * 32 + 4 * v]),
+                           __float_as_uint(acc[c * 32 + 4 * v + 1]),
+                           __float_as_uint(acc[c * 32 + 4 * v + 2]),
+                           __float_as_uint(acc[c * 32 + 4 * v + 3]));
+          } else {
+            #pragma unroll
+            for (int v = 0; v < 32; ++v)
+              if (col0 + v < p.n) dst[v] = acc[c * 32 + v];
+          }
+        } else if constexpr (kOutF32) {
+          float* dst = reinterpret_cast<float*>(p.c) + b * p.c_batch_stride +
+                       static_cast<long long>(row) * p.ldc + col0;
+          if (full) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              st_global_v4(dst + 4 * v, __float_as_uint(acc[c * 32 + 4 * v]),
+                           __float_as_uint(acc[c * 32 + 4 * v + 1]),
+                           __float_as_uint(acc[c * 32 + 4 * v + 2]),
+                           __float_as_uint(acc[c * 32 + 4 * v + 3]));
+          } else {
+            #pragma unroll
+            for (int v = 0; v < 32; ++v)
+              if (col0 + v < p.n) dst[v] = acc[c * 32 + v];
+          }
+        } else {
+          uint16_t* dst = reinterpret_cast<uint16_t*>(p.c) + b * p.c_batch_stride +
+                          static_cast<long long>(row) * p.ldc + col0;
+          if (full) {
+            uint32_t w[16];
+#pragma unroll
+            for (int v = 0; v < 16; ++v) w[v] = pack_bf16x2(acc[c * 32 + 2 * v], acc[c * 32 + 2 * v + 1]);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              st_global_v4(dst + 8 * v, w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+          } else {
+            #pragma unroll
+              for (int v = 0; v < 32; ++v)
+                if (col0 + v < p.n) dst[v] = static_cast<uint16_t>(pack_bf16x2(acc[c * 32 + v], 0.0f) & 0xFFFFu);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+}
+
+}  // namespace bsg

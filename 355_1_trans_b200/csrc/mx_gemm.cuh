@@ -1,0 +1,385 @@
+// mx_gemm.cuh -- MXFP8 (E4M3, .kind::mxf8f6f4) and MXFP4 (packed E2M1,
+// .kind::mxf4 block32) block-scaled GEMM for sm_100a.
+//
+// Semantics (reference, paths relative to its project root):
+//   mxfp8_gemm/gemm_a8w8_mxfp8_kernel_template.hpp:301-432 with
+//   scale_and_accumulate :37-57, and
+//   mxfp4_gemm_4wave_20261112/candidate_m10/gemm_a4w4_mxfp4_4wave_kernel_template.hpp:384-1169:
+//   C[b,m,n] = sum_g 2^(sfa[m,g]-127) * 2^(sfb[n,g]-127) * sum_{k in g} A[m,k] B[n,k],
+//   g = 32 consecutive K, fp32 accumulation, bf16 (RNE) or fp32 output.
+//
+// Design (one CTA per SM, persistent over output tiles of 128 x BN):
+//   warp 0      TMA producer: A/B tiles (128-byte K slabs, 128B swizzle) by
+//               tensor maps, scale atoms by plain bulk copies, one mbarrier
+//               per stage with transaction bytes;
+//   warp 1      single-thread tcgen05 issuer: scale atoms smem -> TMEM with
+//               tcgen05.cp, then 4 block-scaled MMAs per stage into a
+//               128 x BN fp32 TMEM accumulator; tcgen05.commit frees stages;
+//   warp 2      TMEM allocator;
+//   warps 4-7   epilogue: tcgen05.ld (warp w reads TMEM lanes 32*(w%4)..),
+//               fp32 -> bf16 RNE, 16-byte global stores; or fp32 partials
+//               to the split-K workspace.
+// The MMA instruction K is 32 (fp8) / 64 (fp4), i.e. 32 bytes of a 128-byte
+// swizzled row; one stage holds 128 bytes of K per row (128 fp8 / 256 fp4
+// elements) and 1 (fp8) or 2 (fp4) scale atoms per 128 rows.
+#pragma once
+
+#include "sm100.cuh"
+
+namespace bsg {
+
+struct MxParams {
+  int m, n, k;                   // k in elements
+  int batch;
+  int num_kb;                    // 128-byte K stages over the whole K
+  int tiles_m, tiles_n;
+  int split_k, kb_per_split;
+  int total_units;               // batch * tiles_m * tiles_n * split_k
+  const uint8_t* sfa;            // native scale atoms
+  const uint8_t* sfb;
+  long long sfa_batch_stride;    // bytes
+  long long sfb_batch_stride;
+  int sf_kb_total;               // scale atoms along K per 128-row block
+  int sfb_row_blocks;            // 128-row blocks of the B scales, ceil(n / 128)
+  void* c;                       // output
+  long long ldc;                 // elements
+  long long c_batch_stride;      // elements
+  float* ws;                     // split-K partials [split][batch][m][n]
+  unsigned long long timeout_ns;
+};
+
+template <int BN, int kFp4>
+struct MxCfg {
+  static constexpr int kBlockM = 128;
+  static constexpr int kSfAtomsK = kFp4 ? 2 : 1;           // scale atoms per stage along K
+  static constexpr int kSfbRowBlocks = BN / 128;
+  static constexpr uint32_t kABytes = 128u * 128u;
+  static constexpr uint32_t kBBytes = static_cast<uint32_t>(BN) * 128u;
+  static constexpr uint32_t kSfaBytes = 512u * kSfAtomsK;
+  static constexpr uint32_t kSfbBytes = 512u * kSfAtomsK * kSfbRowBlocks;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+  static constexpr uint32_t kSmemBudget = 225u * 1024u;
+  static constexpr int kStages = static_cast<int>((kSmemBudget - 2048u) / kStageBytes) > 8
+                                     ? 8
+                                     : static_cast<int>((kSmemBudget - 2048u) / kStageBytes);
+  // smem: [A x S][B x S][SFA x S][SFB x S][barriers]
+  static constexpr uint32_t kOffB = kABytes * kStages;
+  static constexpr uint32_t kOffSfa = kOffB + kBBytes * kStages;
+  static constexpr uint32_t kOffSfb = kOffSfa + kSfaBytes * kStages;
+  static constexpr uint32_t kOffBar = kOffSfb + kSfbBytes * kStages;
+  static constexpr uint32_t kSmemBytes = kOffBar + 256u + 1024u;  // + alignment slack
+  // TMEM columns: accumulator [0, BN), then SFA (4 per K atom), SFB.
+  static constexpr uint32_t kColSfa = BN;
+  static constexpr uint32_t kColSfb = BN + 4u * kSfAtomsK;
+  static constexpr uint32_t kColsUsed = kColSfb + 4u * kSfAtomsK * kSfbRowBlocks;
+  static constexpr uint32_t kTmemCols = kColsUsed <= 32 ? 32 : kColsUsed <= 64 ? 64
+                                        : kColsUsed <= 128 ? 128 : kColsUsed <= 256 ? 256 : 512;
+  static_assert(kStages >= 2, "shared memory too small for two stages");
+  static_assert(kColsUsed <= 512, "TMEM overflow");
+};
+
+__device__ __forceinline__ void decode_unit(int u, int tiles_m, int tiles_n, int split_k, int& b,
+                                            int& mt, int& nt, int& s) {
+  s = u % split_k;
+  int t = u / split_k;
+  mt = t % tiles_m;
+  t /= tiles_m;
+  nt = t % tiles_n;
+  b = t / tiles_n;
+}
+
+template <int BN, int kFp4, bool kAMN, bool kBMN, bool kOutF32>
+__global__ void __launch_bounds__(256, 1)
+    mx_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const MxParams p) {
+  using Cfg = MxCfg<BN, kFp4>;
+  constexpr int S = Cfg::kStages;
+
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the 128B-swizzled operand tiles
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~static_cast<uintptr_t>(1023u));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + Cfg::kOffB;
+  uint8_t* sSfa = smem + Cfg::kOffSfa;
+  uint8_t* sSfb = smem + Cfg::kOffSfb;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* tmem_full = empty_bar + S;
+  uint64_t* tmem_empty = tmem_full + 1;
+  uint64_t* drain_bar = tmem_empty + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31u;
+
+  if (threadIdx.x == 32) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    mbar_init(tmem_full, 1);
+    mbar_init(tmem_empty, 128);
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_holder, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    int last_stage = -1;
+    uint32_t last_phase = 0;
+    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+      int b, mt, nt, s;
+      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, b, mt, nt, s);
+      const int kb0 = s * p.kb_per_split;
+      const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
+      const uint8_t* sfa_tile = p.sfa + b * p.sfa_batch_stride +
+                                static_cast<long long>(mt) * p.sf_kb_total * 512;
+      const uint8_t* sfb_tile = p.sfb + b * p.sfb_batch_stride +
+                                static_cast<long long>(nt) * Cfg::kSfbRowBlocks * p.sf_kb_total * 512;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        uint64_t* fb = &full_bar[stage];
+        // the last N tile may cover fewer 128-row scale blocks than BN / 128;
+        // copy only the ones that exist (the columns beyond N are never stored)
+        const int sfb_rows = min(Cfg::kSfbRowBlocks, p.sfb_row_blocks - nt * Cfg::kSfbRowBlocks);
+        mbar_arrive_expect_tx(fb, Cfg::kStageBytes - static_cast<uint32_t>(Cfg::kSfbRowBlocks - sfb_rows) *
+                                                         512u * Cfg::kSfAtomsK);
+        uint8_t* a_dst = sA + stage * Cfg::kABytes;
+        uint8_t* b_dst = sB + stage * Cfg::kBBytes;
+        const int kbyte = kb * 128;
+        if constexpr (!kAMN) {
+          tma_load_3d(a_dst, &tmA, fb, kbyte, mt * 128, b);
+        } else {
+          tma_load_3d(a_dst, &tmA, fb, mt * 128, kbyte, b);
+        }
+        if constexpr (!kBMN) {
+          tma_load_3d(b_dst, &tmB, fb, kbyte, nt * BN, b);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 128; ++j)
+            tma_load_3d(b_dst + j * 16384, &tmB, fb, nt * BN + j * 128, kbyte, b);
+        }
+        const long long atom_k = static_cast<long long>(kb) * Cfg::kSfAtomsK;
+        bulk_load(sSfa + stage * Cfg::kSfaBytes, sfa_tile + atom_k * 512, Cfg::kSfaBytes, fb);
+#pragma unroll
+        for (int r = 0; r < Cfg::kSfbRowBlocks; ++r)
+          if (r < sfb_rows)
+            bulk_load(sSfb + stage * Cfg::kSfbBytes + r * 512 * Cfg::kSfAtomsK,
+                    sfb_tile + (static_cast<long long>(r) * p.sf_kb_total + atom_k) * 512,
+                    512u * Cfg::kSfAtomsK, fb);
+        last_stage = stage;
+        last_phase = phase;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (!ok && last_stage >= 0) {
+      // give the copies already in flight a bounded chance to land before exit
+      int dummy = 0;
+      mbar_wait(&full_bar[last_stage], last_phase, &dummy, p.timeout_ns);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------------ MMA issuer
+    constexpr uint32_t kFmt = kFp4 ? 1u : 0u;
+    const uint32_t idesc0 = idesc_block_scaled(kFmt, kFmt, kAMN, kBMN, 128, BN);
+    // K-major: SBO = 8 rows x 128 B; MN-major: LBO = next 128-element MN slab,
+    // SBO = next 8 K rows.
+    constexpr uint32_t kALbo = kAMN ? 128u * 128u : 16u;
+    constexpr uint32_t kBLbo = kBMN ? 128u * 128u : 16u;
+    constexpr uint32_t kSbo = 1024u;
+    constexpr uint32_t kKStep = kAMN ? 32u * 128u : 32u;   // bytes per MMA along K (A)
+    constexpr uint32_t kKStepB = kBMN ? 32u * 128u : 32u;
+    const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
+    const uint32_t sSfa0 = smem_u32(sSfa), sSfb0 = smem_u32(sSfb);
+    int stage = 0;
+    uint32_t phase = 0;
+    int iter = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x, ++iter) {
+      int b, mt, nt, s;
+      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, b, mt, nt, s);
+      const int kb0 = s * p.kb_per_split;
+      const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
+      if (!mbar_wait(tmem_empty, (static_cast<uint32_t>(iter) & 1u) ^ 1u, abort_flag,
+                     p.timeout_ns)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int j = 0; j < Cfg::kSfAtomsK; ++j) {
+          tmem_cp_sf_atom(tmem_base + Cfg::kColSfa + 4u * j,
+                          sSfa0 + stage * Cfg::kSfaBytes + 512u * j);
+#pragma unroll
+          for (int r = 0; r < Cfg::kSfbRowBlocks; ++r)
+            tmem_cp_sf_atom(tmem_base + Cfg::kColSfb + 4u * (j * Cfg::kSfbRowBlocks + r),
+                            sSfb0 + stage * Cfg::kSfbBytes + 512u * (r * Cfg::kSfAtomsK + j));
+        }
+        const uint32_t a_addr = sA0 + stage * Cfg::kABytes;
+        const uint32_t b_addr = sB0 + stage * Cfg::kBBytes;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const uint32_t j = kFp4 ? static_cast<uint32_t>(t >> 1) : 0u;
+          const uint32_t sf_id = kFp4 ? static_cast<uint32_t>((t & 1) * 2) : static_cast<uint32_t>(t);
+          const uint64_t adesc = make_sdesc(a_addr + t * kKStep, kALbo, kSbo, kLayoutSW128);
+          const uint64_t bdesc = make_sdesc(b_addr + t * kKStepB, kBLbo, kSbo, kLayoutSW128);
+          const uint32_t idesc = idesc_with_sf_id(idesc0, sf_id, sf_id);
+          const uint32_t tsfa = tmem_base + Cfg::kColSfa + 4u * j;
+          const uint32_t tsfb = tmem_base + Cfg::kColSfb + 4u * j * Cfg::kSfbRowBlocks;
+          const uint32_t acc = (kb > kb0 || t > 0) ? 1u : 0u;
+          if constexpr (kFp4)
+            umma_mxf4(tmem_base, adesc, bdesc, idesc, tsfa, tsfb, acc);
+          else
+            umma_mxf8f6f4(tmem_base, adesc, bdesc, idesc, tsfa, tsfb, acc);
+        }
+        tc_commit(&empty_bar[stage]);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      tc_commit(tmem_full);
+    }
+    // drain: wait until every tcgen05 op issued above has completed
+    tc_commit(drain_bar);
+    int dummy = 0;
+    mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    int iter = 0;
+    for (int u = blockIdx.x; u < p.total_units; u += gridDim.x, ++iter) {
+      int b, mt, nt, s;
+      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, b, mt, nt, s);
+      if (!mbar_wait(tmem_full, static_cast<uint32_t>(iter) & 1u, abort_flag, p.timeout_ns)) break;
+      tc_fence_after();
+      const int row = mt * 128 + q * 32 + static_cast<int>(lane);
+      const bool row_ok = row < p.m;
+      const int n0 = nt * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + lane_base + static_cast<uint32_t>(c * 32), r);
+        const int col0 = n0 + c * 32;
+        if (!row_ok || col0 >= p.n) continue;
+        const bool full = col0 + 32 <= p.n;
+        if (p.split_k > 1) {
+          float* dst = p.ws + ((static_cast<long long>(s) * p.batch + b) * p.m + row) *
+                                  static_cast<long long>(p.n) + col0;
+          if (full) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              st_global_v4(dst + 4 * v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+          } else {
+            #pragma unroll
+            for (int v = 0; v < 32; ++v)
+              if (col0 + v < p.n) dst[v] = __uint_as_float(r[v]);
+          }
+        } else if constexpr (kOutF32) {
+          float* dst = reinterpret_cast<float*>(p.c) + b * p.c_batch_stride +
+                       static_cast<long long>(row) * p.ldc + col0;
+          if (full) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              st_global_v4(dst + 4 * v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+          } else {
+            #pragma unroll
+            for (int v = 0; v < 32; ++v)
+              if (col0 + v < p.n) dst[v] = __uint_as_float(r[v]);
+          }
+        } else {
+          uint16_t* dst = reinterpret_cast<uint16_t*>(p.c) + b * p.c_batch_stride +
+                          static_cast<long long>(row) * p.ldc + col0;
+          if (full) {
+            uint32_t w[16];
+#pragma unroll
+            for (int v = 0; v < 16; ++v)
+              w[v] = pack_bf16x2(__uint_as_float(r[2 * v]), __uint_as_float(r[2 * v + 1]));
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              st_global_v4(dst + 8 * v, w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+          } else {
+            #pragma unroll
+              for (int v = 0; v < 32; ++v)
+                if (col0 + v < p.n) dst[v] = static_cast<uint16_t>(pack_bf16x2(__uint_as_float(r[v]), 0.0f) & 0xFFFFu);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(tmem_empty);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+}
+
+// Deterministic split-K reduction: C = sum_{s=0..S-1} ws[s] in fixed order.
+template <bool kOutF32>
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* __restrict__ c, int m,
+                                     int n, int batch, int split, long long ldc,
+                                     long long c_batch_stride) {
+  const long long per_batch = static_cast<long long>(m) * n;
+  const long long total4 = per_batch * batch / 4;   // n % 4 == 0
+  const long long slice = per_batch * batch;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long e = i * 4;
+    float4 acc = reinterpret_cast<const float4*>(ws)[i];
+    for (int s = 1; s < split; ++s) {
+      const float4 v = reinterpret_cast<const float4*>(ws + s * slice)[i];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    const long long bb = e / per_batch;
+    const long long rem = e - bb * per_batch;
+    const long long row = rem / n, col = rem - row * n;
+    if constexpr (kOutF32) {
+      float* dst = reinterpret_cast<float*>(c) + bb * c_batch_stride + row * ldc + col;
+      *reinterpret_cast<float4*>(dst) = acc;
+    } else {
+      uint16_t* dst = reinterpret_cast<uint16_t*>(c) + bb * c_batch_stride + row * ldc + col;
+      uint2 w;
+      w.x = pack_bf16x2(acc.x, acc.y);
+      w.y = pack_bf16x2(acc.z, acc.w);
+      *reinterpret_cast<uint2*>(dst) = w;
+    }
+  }
+}
+
+}  // namespace bsg

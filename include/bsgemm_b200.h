@@ -1,0 +1,232 @@
+/*
+ * bsgemm_b200.h -- C ABI of the B200 (sm_100a) block-scaled GEMM library.
+ *
+ * Drop-in boundary for the reference's host launchers of three GEMM families
+ * (paths relative to the reference project root):
+ *   MXFP8  a8w8  E4M3 x E4M3, one E8M0 scale per 32 K     mxfp8_gemm/
+ *   MXFP4  a4w4  packed E2M1, one E8M0 scale per 32 K      mxfp4_gemm_4wave_20261112/
+ *   FP8 block-scale, fp32 scales 1x128 (A) / 128x128 (B),
+ *        K-panel preshuffled B                             block_scale_gemm_bpreshuffle/
+ * plus the reference's one shipped extern "C" entry point,
+ * launch_blockscale_bpreshuffle (E8M0 1x128/128x128 scales).
+ *
+ * Conventions kept from the reference launcher
+ * (trace_block_scale_latest_20260914_040021/source_snapshot/
+ *  gemm_a8w8_blockscale_bpreshuffle_launch.cc:29-65):
+ *   - the caller owns every buffer; no entry point allocates device memory;
+ *   - a GEMM entry point enqueues its kernels on the caller's stream and
+ *     returns without synchronising;
+ *   - arguments are validated first; errors are returned, never aborted on;
+ *   - entry points keep no per-call state and may be called concurrently.
+ *
+ * Layout letters (BASELINE / CUTLASS convention; the reference's letters are
+ * swapped, e.g. its "nt" is this "tn"):
+ *   tn = A K-major [M,K], B K-major [N,K]      (BSG_LAYOUT_TN = 3)
+ *   nn = A M-major [K,M], B K-major [N,K]      (BSG_LAYOUT_NN = 2)
+ *   tt = A K-major [M,K], B N-major [K,N]      (BSG_LAYOUT_TT = 1)
+ *   nt = A M-major [K,M], B N-major [K,N]      (BSG_LAYOUT_NT = 0)
+ * i.e. bit0 = A is K-major, bit1 = B is K-major.
+ */
+#ifndef BSGEMM_B200_H
+#define BSGEMM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BSG_API __attribute__((visibility("default")))
+#else
+#define BSG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *bsg_stream_t; /* == cudaStream_t */
+
+/* ---- status codes ------------------------------------------------------- */
+enum {
+    BSG_OK = 0,
+    BSG_ERR_INVALID_VALUE = 1,   /* null pointer, bad flag, bad shape/stride, overlap */
+    BSG_ERR_UNSUPPORTED = 2,     /* valid but not implemented combination */
+    BSG_ERR_ARCH = 3,            /* device is not sm_100 (B200) */
+    BSG_ERR_WORKSPACE = 4,       /* split-K workspace missing or too small */
+    BSG_ERR_CUDA = 5,            /* a CUDA runtime/driver call failed */
+    BSG_ERR_TIMEOUT = 6,         /* a device-side bounded wait expired */
+    BSG_ERR_ALIGNMENT = 7        /* pointer/stride violates TMA 16-byte rules */
+};
+
+/* ---- enums of bsgemm_args ---------------------------------------------- */
+enum { BSG_LAYOUT_NT = 0, BSG_LAYOUT_TT = 1, BSG_LAYOUT_NN = 2, BSG_LAYOUT_TN = 3 };
+
+enum {
+    BSG_B_RAW = 0,          /* plain [N,K] (K-major) or [K,N] (N-major) */
+    BSG_B_KPANEL128 = 1,    /* B'[K/128][N][128] (reference shuffle_b) */
+    BSG_B_SHUFFLE16 = 2     /* aiter shuffle_weight(16,16): needs bsgemm_pack_b first */
+};
+
+enum {
+    BSG_SF_NATIVE = 0,      /* E8M0 tcgen05 atoms, see bsgemm_pack_scales */
+    BSG_SF_ROWMAJOR = 1,    /* E8M0 [rows, K/32] (reference raw) or fp32 [rows, K/128] */
+    BSG_SF_KMAJOR_T = 2,    /* fp32 SFA stored transposed [K/128, M] (reference kernel) */
+    BSG_SF_E8M0_SHUFFLE = 3 /* aiter e8m0_shuffle: needs bsgemm_pack_scales first */
+};
+
+enum { BSG_OUT_BF16 = 0, BSG_OUT_FP32 = 1 };
+
+enum { BSG_FAMILY_MXFP8 = 0, BSG_FAMILY_MXFP4 = 1, BSG_FAMILY_FP8_BLOCK = 2 };
+
+/*
+ * Kernel arguments.  The first 96 bytes are field-for-field the reference's
+ * opus_gemm_scale_kargs / opus_gemm_kargs / opus_gemm_mxfp4_scale_kargs
+ * (source_snapshot/gemm_a8w8_mxfp8_scale_common.h:12-38,
+ *  mxfp8_gemm/gemm_a8w8_mxfp8_common.h:4-25,
+ *  mxfp4_gemm_4wave_20261112/gemm_a4w4_mxfp4_4wave_traits.hpp:7-27).
+ * Units: strides of fp8 tensors and of C in ELEMENTS, of packed fp4 tensors in
+ * BYTES (as the reference), E8M0 scale strides in bytes, fp32 scale strides
+ * in floats.  For BSG_SF_NATIVE the scale strides are ignored except the batch
+ * strides (bytes between batches; 0 = densely packed).
+ */
+typedef struct bsgemm_args {
+    const void *ptr_a;
+    const void *ptr_b;
+    void *ptr_c;
+    int m;
+    int n;
+    int k;
+    int batch;
+    int stride_a;
+    int stride_b;
+    int stride_c;
+    int stride_a_batch;
+    int stride_b_batch;
+    int stride_c_batch;
+    const void *ptr_sfa;
+    const void *ptr_sfb;
+    int stride_sfa;
+    int stride_sfb;
+    int stride_sfa_batch;
+    int stride_sfb_batch;
+    /* ---- extensions (not in the reference's 96-byte struct) ---- */
+    int layout;             /* BSG_LAYOUT_* */
+    int b_format;           /* BSG_B_* */
+    int sfa_format;         /* BSG_SF_* */
+    int sfb_format;         /* BSG_SF_* */
+    int out_dtype;          /* BSG_OUT_* */
+    int split_k;            /* 0 = auto, 1 = none, >1 = forced number of K slices */
+    void *workspace;        /* caller-owned scratch for split-K partials (fp32) */
+    size_t workspace_bytes;
+    int grid_blocks;        /* 0 = one CTA per SM; >0 caps the persistent grid
+                               (the reference's PERSIST_GRID / m10 grid_blocks) */
+    int reserved;
+} bsgemm_args;
+
+/* Fill the 96-byte prefix's defaults and zero the extensions. */
+BSG_API void bsgemm_args_init(bsgemm_args *args);
+
+/*
+ * MXFP8: C[b,m,n] = sum_g 2^(sfa[m,g]-127) 2^(sfb[n,g]-127) sum_{k in g} A*B,
+ * g = 32 consecutive K.  A/B E4M3FN bytes in any of the four layouts
+ * (args->layout); SFA/SFB in BSG_SF_NATIVE or BSG_SF_ROWMAJOR ([rows,K/32]
+ * bytes, row stride stride_sf*).  Requires K % 128 == 0, N % 8 == 0 (bf16) or
+ * N % 4 == 0 (fp32); M arbitrary.
+ * Replaces the launch of gemm_a8w8_mxfp8_kernel in
+ * mxfp8_gemm/gemm_a8w8_mxfp8_host.cc:287-295 (its kargs at :265-285), without
+ * the reference's K == 256 and M/N % 256 limits.
+ */
+BSG_API int bsgemm_a8w8_mxfp8(const bsgemm_args *args, bsg_stream_t stream);
+
+/*
+ * MXFP4: same contraction with E2M1 elements packed two per byte, even k in
+ * the low nibble; A [M,K/2] and B [N,K/2] bytes, K-major only (layout TN).
+ * B may be BSG_B_RAW or, after bsgemm_pack_b, the raw form of an aiter
+ * shuffle_weight(16,16) buffer.  Requires K % 128 == 0.
+ * Replaces gemm_a4w4_mxfp4_4wave_kernel's launch in
+ * mxfp4_gemm_4wave_20261112/gemm_a4w4_mxfp4_4wave_host.cc:211-213 and the
+ * persistent launch of candidate_m10/gemm_a4w4_mxfp4_4wave_host.cc:242-250.
+ */
+BSG_API int bsgemm_a4w4_mxfp4(const bsgemm_args *args, bsg_stream_t stream);
+
+/*
+ * FP8 block-scale with fp32 scales: C = sum_kb sfa[m,kb] * sfb[n/128,kb] *
+ * (A B^T)_kb over 128-K blocks.  A E4M3 [M,K] (K-major); B K-major as
+ * BSG_B_RAW [N,K] or BSG_B_KPANEL128 B'[K/128][N][128] (stride_b = 128, as the
+ * reference kargs); SFA fp32 BSG_SF_ROWMAJOR [M,K/128] (aiter x_scale) or
+ * BSG_SF_KMAJOR_T [K/128,M] (reference kernel); SFB fp32 [N/128,K/128]
+ * row-major.  Requires K % 128 == 0, N % 8 == 0.
+ * Replaces gemm_a8w8_blockscale_bpreshuffle_kernel's launch in
+ * block_scale_gemm_bpreshuffle/gemm_a8w8_blockscale_bpreshuffle_host.cc:
+ * 275-281 and aiter's gemm_a8w8_bpreshuffle_opus.
+ */
+BSG_API int bsgemm_a8w8_blockscale_bpreshuffle(const bsgemm_args *args, bsg_stream_t stream);
+
+/*
+ * Bytes of split-K workspace the call would need (0 when it runs without
+ * split-K).  family = BSG_FAMILY_*.
+ */
+BSG_API size_t bsgemm_workspace_size(int family, const bsgemm_args *args);
+
+/*
+ * Device repack of B into the raw layout the kernels read (async on stream).
+ *   src_format BSG_B_KPANEL128 or BSG_B_SHUFFLE16; dst is [rows, kbytes] bytes
+ *   (kbytes = K for fp8, K/2 for fp4).  rows % 16 == 0 and kbytes % 16 == 0
+ *   for SHUFFLE16; kbytes % 128 == 0 for KPANEL128.  unpack = 1 runs the
+ *   inverse permutation (raw -> src_format).
+ * Replaces the host preshuffles of the reference (shuffle_b,
+ * block_scale_gemm_bpreshuffle/..._host.cc:96-111; pack_weight_16x16,
+ * source_snapshot/gemm_a8w8_mxfp8_scale_host.cc:161-179; candidate_m10 bs,
+ * mxfp4_gemm_4wave_20261112/candidate_m10/gemm_a4w4_mxfp4_4wave_host.cc:215-225).
+ */
+BSG_API int bsgemm_pack_b(const void *src, void *dst, int rows, int kbytes, int src_format,
+                  int unpack, bsg_stream_t stream);
+
+/*
+ * Device repack of an E8M0 scale matrix [rows, kg] (kg = K/32) into the
+ * native tcgen05 layout: 512-byte atoms of 128 rows x 4 groups, atom (rb,kb)
+ * at (rb*ceil(kg/4)+kb)*512, byte ((r%32)*4 + (r%128)/32)*4 + g%4; padding
+ * 0x7F.  src_format BSG_SF_ROWMAJOR (row stride src_stride bytes) or
+ * BSG_SF_E8M0_SHUFFLE (aiter layout, candidate_m10/..._host.cc:194-206).
+ * unpack = 1 writes native -> src_format instead.
+ */
+BSG_API int bsgemm_pack_scales(const void *src, int src_stride, void *dst, int rows, int kg,
+                       int src_format, int unpack, bsg_stream_t stream);
+/* Bytes of a native scale buffer for [rows, kg]. */
+BSG_API size_t bsgemm_native_scales_size(int rows, int kg);
+
+/*
+ * Exact drop-in for the reference's only extern "C" launcher
+ * (source_snapshot/gemm_a8w8_blockscale_bpreshuffle_launch.cc:31-65):
+ * E4M3 A [M,K], B in shuffle_weight(16,16) layout, E8M0 SFA [K/128,M],
+ * E8M0 SFB [N/128,K/128]; bf16 (output_bf16 = 1) or fp32 C.  Same
+ * validation rules (M,N % 256, K % 128, dense strides, no overlap).
+ * Returns 0 (cudaSuccess) or a cudaError_t value, as the reference.
+ * The kargs struct is the first 96 bytes of bsgemm_args.
+ */
+BSG_API int launch_blockscale_bpreshuffle(const void *opus_gemm_scale_kargs, int output_bf16,
+                                  int tiles, bsg_stream_t stream);
+
+/* Human-readable status. */
+BSG_API const char *bsgemm_strerror(int status);
+
+/*
+ * Device-side error word of the current device (set by a kernel whose
+ * bounded wait expired); reading it synchronises the device and clears it.
+ * Returns BSG_OK or BSG_ERR_TIMEOUT (or BSG_ERR_CUDA if the read failed).
+ */
+BSG_API int bsgemm_check_device_error(void);
+
+/*
+ * Self-test of the bounded-wait path: launches one tiny kernel whose
+ * mbarrier nothing ever arrives at, with a wait limit of timeout_us; returns
+ * the status the kernel reported (BSG_ERR_TIMEOUT expected).  Synchronous.
+ */
+BSG_API int bsgemm_selftest_timeout(int timeout_us);
+
+/* Library version string. */
+BSG_API const char *bsgemm_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

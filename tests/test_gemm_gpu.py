@@ -1,0 +1,274 @@
+"""Parity of the sm_100a kernels (through the C ABI) with the CPU oracle.
+
+Each case follows the reference's self-checking host drivers: inputs are
+seeded and quantised on the host, the raw operands go to the oracle and the
+(possibly repacked) operands to the GPU, C is NaN-poisoned before the launch,
+and the result must meet the BASELINE tolerance |err| <= 2^-7 |ref| + 1e-3
+(max relative error <= 1e-2) on bf16 outputs.  Fixture patterns of the
+reference (unit scales, K-pattern scales, persistent-grid overrides, ragged
+shapes) are all exercised.
+"""
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_close, dev_u8, mxfp4_problem, mxfp8_problem, scale_mode
+
+pytestmark = pytest.mark.gpu
+
+
+def poisoned(shape, dtype, device):
+    return torch.full(shape, float("nan"), dtype=dtype, device=device)
+
+
+def run_mxfp8(bs, orc, cuda, m, n, k, *, seed=1, layout="tn", sf_mode="data", out_dtype=torch.bfloat16,
+              split_k=0, grid_blocks=0, batch=1, native=False):
+    qa_l, qb_l, sa_l, sb_l = mxfp8_problem(orc, m, n, k, seed, sf_mode, batch)
+    refs = [orc.gemm_mxfp8(qa, qb, sa, sb, f64=True)[0] for qa, qb, sa, sb in zip(qa_l, qb_l, sa_l, sb_l)]
+    a_host = [qa if layout[0] == "t" else np.ascontiguousarray(qa.T) for qa in qa_l]
+    b_host = [qb if layout[1] == "n" else np.ascontiguousarray(qb.T) for qb in qb_l]
+    A = dev_u8(np.stack(a_host) if batch > 1 else a_host[0], cuda).view(torch.float8_e4m3fn)
+    B = dev_u8(np.stack(b_host) if batch > 1 else b_host[0], cuda).view(torch.float8_e4m3fn)
+    SA = dev_u8(np.stack(sa_l) if batch > 1 else sa_l[0], cuda)
+    SB = dev_u8(np.stack(sb_l) if batch > 1 else sb_l[0], cuda)
+    fmt = "rowmajor"
+    if native:
+        assert batch == 1
+        SA, SB = bs.pack_scales(SA), bs.pack_scales(SB)
+        fmt = "native"
+    out = poisoned((m, n) if batch == 1 else (batch, m, n), out_dtype, cuda)
+    bs.gemm_a8w8_mxfp8(A, B, SA, SB, layout=layout, out_dtype=out_dtype, out=out, scale_format=fmt,
+                       split_k=split_k, grid_blocks=grid_blocks)
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    got = out.float().cpu().numpy()
+    if batch == 1:
+        got = got[None]
+    for b in range(batch):
+        assert_close(orc, refs[b], got[b], f"mxfp8 {m}x{n}x{k} {layout} b{b}")
+    return refs, got
+
+
+# ---- MXFP8 ---------------------------------------------------------------------------
+
+def test_mxfp8_256_tn_bf16(bs, orc, cuda):
+    """M=N=K=256, tn, bf16 out, data-derived scales."""
+    refs, got = run_mxfp8(bs, orc, cuda, 256, 256, 256)
+    # also the reference's own acceptance rule (valid_vector with bf16 bounds)
+    mag = orc.gemm_mxfp8(*[x[0] for x in mxfp8_problem(orc, 256, 256, 256, 1)], f64=True)[1]
+    errors, _ = orc.check_e8m0_rule(refs[0], got[0], mag, bf16=True, rel_mag=1e-3)
+    assert errors == 0
+
+
+@pytest.mark.parametrize("sf_mode", ["unit", "kpattern", "rowpattern"])
+def test_mxfp8_scale_patterns(bs, orc, cuda, sf_mode):
+    run_mxfp8(bs, orc, cuda, 256, 256, 512, seed=2, sf_mode=sf_mode)
+
+
+def test_mxfp8_fp32_out(bs, orc, cuda):
+    refs, got = run_mxfp8(bs, orc, cuda, 128, 256, 256, seed=3, out_dtype=torch.float32)
+    # fp32 out: the reference's 1e-3-relative-to-magnitude rule holds tightly
+    np.testing.assert_allclose(got[0], refs[0], rtol=1e-5, atol=1e-3)
+
+
+@pytest.mark.parametrize("layout", ["tn", "nn", "tt", "nt"])
+def test_mxfp8_layouts(bs, orc, cuda, layout):
+    run_mxfp8(bs, orc, cuda, 256, 384, 512, seed=4, layout=layout, sf_mode="kpattern")
+
+
+def test_mxfp8_ragged(bs, orc, cuda):
+    run_mxfp8(bs, orc, cuda, 200, 264, 384, seed=5)
+
+
+def test_mxfp8_batched(bs, orc, cuda):
+    run_mxfp8(bs, orc, cuda, 128, 256, 256, seed=6, batch=2)
+
+
+@pytest.mark.parametrize("split_k", [2, 3])
+def test_mxfp8_split_k(bs, orc, cuda, split_k):
+    run_mxfp8(bs, orc, cuda, 128, 256, 1024, seed=7, split_k=split_k, sf_mode="kpattern")
+
+
+def test_mxfp8_auto_split_skinny(bs, orc, cuda):
+    run_mxfp8(bs, orc, cuda, 16, 512, 2048, seed=8)
+
+
+def test_mxfp8_native_scales(bs, orc, cuda):
+    run_mxfp8(bs, orc, cuda, 256, 256, 512, seed=9, native=True, sf_mode="rowpattern")
+
+
+@pytest.mark.parametrize("grid_blocks", [1, 37])
+def test_mxfp8_persistent_grid(bs, orc, cuda, grid_blocks):
+    """The reference's PERSIST_GRID override: many tiles per CTA."""
+    run_mxfp8(bs, orc, cuda, 512, 512, 256, seed=10, grid_blocks=grid_blocks)
+
+
+# ---- MXFP4 ---------------------------------------------------------------------------
+
+def run_mxfp4(bs, orc, cuda, m, n, k, *, seed=1, sf_mode="data", split_k=0, out_dtype=torch.bfloat16,
+              grid_blocks=0):
+    qa, qb, sa, sb = mxfp4_problem(orc, m, n, k, seed, sf_mode)
+    ref, mag = orc.gemm_mxfp4(qa, qb, sa, sb)
+    out = poisoned((m, n), out_dtype, cuda)
+    bs.gemm_a4w4_mxfp4(dev_u8(qa, cuda), dev_u8(qb, cuda), dev_u8(sa, cuda), dev_u8(sb, cuda),
+                       out=out, out_dtype=out_dtype, split_k=split_k, grid_blocks=grid_blocks)
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    got = out.float().cpu().numpy()
+    calc_diff = assert_close(orc, ref, got, f"mxfp4 {m}x{n}x{k}")
+    assert calc_diff < 0.02      # the reference's cosine-style gate
+    return ref, got, mag
+
+
+def test_mxfp4_256(bs, orc, cuda):
+    run_mxfp4(bs, orc, cuda, 256, 256, 512)
+
+
+@pytest.mark.parametrize("sf_mode", ["unit", "kpattern", "rowpattern"])
+def test_mxfp4_scale_patterns(bs, orc, cuda, sf_mode):
+    run_mxfp4(bs, orc, cuda, 256, 512, 1024, seed=2, sf_mode=sf_mode)
+
+
+def test_mxfp4_reference_rule(bs, orc, cuda):
+    """mxfp4 host compare(): tol = 1e-4 + 5e-5 * sum|term| + |ref|/256."""
+    ref, got, mag = run_mxfp4(bs, orc, cuda, 128, 256, 512, seed=3, out_dtype=torch.float32)
+    tol = 1e-4 + 5e-5 * mag + np.abs(ref) / 256
+    assert np.all(np.abs(got - ref) <= tol)
+
+
+def test_mxfp4_ragged_and_split(bs, orc, cuda):
+    run_mxfp4(bs, orc, cuda, 16, 384, 2048, seed=4, split_k=4)
+    run_mxfp4(bs, orc, cuda, 130, 256, 512, seed=5)
+
+
+def test_mxfp4_shuffled_b(bs, orc, cuda):
+    """B given in aiter shuffle_weight(16,16) bytes: bsgemm_pack_b restores the
+    raw layout bit-exactly on the device (candidate_m10 bs layout)."""
+    qa, qb, sa, sb = mxfp4_problem(orc, 128, 256, 512, 6, "kpattern")
+    sh = orc.shuffle_weight16(qb)
+    raw = bs.pack_b(dev_u8(sh, cuda), "shuffle16")
+    assert np.array_equal(raw.cpu().numpy(), qb)
+    ref, _ = orc.gemm_mxfp4(qa, qb, sa, sb)
+    out = bs.gemm_a4w4_mxfp4(dev_u8(qa, cuda), raw, dev_u8(sa, cuda), dev_u8(sb, cuda))
+    assert_close(orc, ref, out.float().cpu().numpy(), "mxfp4 shuffled B")
+
+
+# ---- FP8 block-scale (fp32 scales) --------------------------------------------------
+
+def run_fp8_block(bs, orc, cuda, m, n, k, *, seed=1, kpanel=True, transposed=False, split_k=0,
+                  out_dtype=torch.bfloat16):
+    x = orc.normal((m, k), seed=seed * 77)
+    w = orc.normal((n, k), seed=seed * 77 + 1)
+    qa, sa = orc.quant_fp8_block(x, 1)
+    qb, sb = orc.quant_fp8_block(w, 128)
+    ref, _ = orc.gemm_fp8_block(qa, qb, sa, sb)
+    A = dev_u8(qa, cuda).view(torch.float8_e4m3fn)
+    if kpanel:
+        B = dev_u8(orc.shuffle_kpanel(qb), cuda).view(torch.float8_e4m3fn)
+    else:
+        B = dev_u8(qb, cuda).view(torch.float8_e4m3fn)
+    SA = torch.from_numpy(np.ascontiguousarray(sa.T if transposed else sa)).to(cuda)
+    SB = torch.from_numpy(sb).to(cuda)
+    out = poisoned((m, n), out_dtype, cuda)
+    bs.gemm_a8w8_bpreshuffle(A, B, SA, SB, out_dtype, preshuffled=kpanel, x_scale_transposed=transposed,
+                             out=out, split_k=split_k)
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    got = out.float().cpu().numpy()
+    assert_close(orc, ref, got, f"fp8 block {m}x{n}x{k}")
+    return ref, got
+
+
+def test_fp8_block_kpanel(bs, orc, cuda):
+    run_fp8_block(bs, orc, cuda, 256, 256, 512)
+
+
+def test_fp8_block_raw_b_transposed_sfa(bs, orc, cuda):
+    run_fp8_block(bs, orc, cuda, 256, 384, 384, seed=2, kpanel=False, transposed=True)
+
+
+def test_fp8_block_fp32_out(bs, orc, cuda):
+    ref, got = run_fp8_block(bs, orc, cuda, 128, 256, 512, seed=3, out_dtype=torch.float32)
+    np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("m", [1, 16, 64, 200])
+def test_fp8_block_decode_shapes(bs, orc, cuda, m):
+    run_fp8_block(bs, orc, cuda, m, 1024, 2048, seed=4 + m)
+
+
+def test_fp8_block_split_k(bs, orc, cuda):
+    run_fp8_block(bs, orc, cuda, 64, 512, 2048, seed=9, split_k=5)
+
+
+# ---- packers -------------------------------------------------------------------------
+
+def test_pack_b_roundtrips(bs, orc, cuda):
+    rng = np.random.default_rng(3)
+    b = rng.integers(0, 256, size=(256, 512), dtype=np.uint8)
+    for fmt, shuffled in (("shuffle16", orc.shuffle_weight16(b)), ("kpanel", orc.shuffle_kpanel(b))):
+        raw = bs.pack_b(dev_u8(shuffled, cuda), fmt)
+        assert np.array_equal(raw.cpu().numpy(), b), fmt
+        back = bs.pack_b(raw, fmt, unpack=True)
+        assert np.array_equal(back.cpu().numpy().reshape(-1), shuffled.reshape(-1)), fmt
+
+
+def test_pack_scales_matches_oracle(bs, orc, cuda):
+    rng = np.random.default_rng(4)
+    for rows, kg in ((256, 16), (200, 12), (40, 8), (1, 4)):
+        sf = rng.integers(0, 256, size=(rows, kg), dtype=np.uint8)
+        nat = bs.pack_scales(dev_u8(sf, cuda))
+        assert np.array_equal(nat.cpu().numpy(), orc.sf_to_native(sf)), (rows, kg)
+        assert np.array_equal(bs.unpack_scales(nat, rows, kg).cpu().numpy(), sf)
+        esh = orc.e8m0_shuffle(sf)
+        nat2 = bs.pack_scales(dev_u8(esh, cuda), rows, kg, src_format="e8m0_shuffle")
+        assert np.array_equal(nat2.cpu().numpy(), orc.sf_to_native(sf))
+        assert np.array_equal(bs.unpack_scales(nat, rows, kg, dst_format="e8m0_shuffle").cpu().numpy(), esh)
+
+
+# ---- failure detection ---------------------------------------------------------------
+
+def test_bounded_wait_reports_timeout(bs, cuda):
+    """A wait on an mbarrier that nothing arrives at returns an error status
+    after its limit; the context stays usable."""
+    assert bs.selftest_timeout(2000) == bs.ERR_TIMEOUT
+    assert bs.check_device_error() == 0
+    x = torch.ones(4, device=cuda)
+    assert float(x.sum()) == 4.0
+
+
+# ---- full size (row sample) ----------------------------------------------------------
+
+@pytest.mark.parametrize("layout", ["tn", "nt"])
+def test_mxfp8_8192_row_sample(bs, orc, cuda, layout):
+    """BASELINE config 3 at full size: every output row is produced by the GPU;
+    64 sampled rows are checked against the oracle."""
+    m = n = k = 8192
+    x = orc.normal((m, k), seed=81)
+    w = orc.normal((n, k), seed=82)
+    qa, sa = orc.quant_mxfp8(x)
+    qb, sb = orc.quant_mxfp8(w)
+    A = dev_u8(qa if layout[0] == "t" else np.ascontiguousarray(qa.T), cuda).view(torch.float8_e4m3fn)
+    B = dev_u8(qb if layout[1] == "n" else np.ascontiguousarray(qb.T), cuda).view(torch.float8_e4m3fn)
+    out = bs.gemm_a8w8_mxfp8(A, B, dev_u8(sa, cuda), dev_u8(sb, cuda), layout=layout)
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    rows = np.random.default_rng(0).choice(m, 64, replace=False)
+    rows.sort()
+    ref, _ = orc.gemm_mxfp8(qa[rows], qb, sa[rows], sb, f64=True)
+    got = out[torch.from_numpy(rows).to(cuda)].float().cpu().numpy()
+    assert_close(orc, ref, got, f"mxfp8 8192^3 {layout} sample")
+    assert not torch.isnan(out).any()
+
+
+def test_mxfp4_8192_row_sample(bs, orc, cuda):
+    m = n = k = 8192
+    qa, qb, sa, sb = mxfp4_problem(orc, m, n, k, 11)
+    out = bs.gemm_a4w4_mxfp4(dev_u8(qa, cuda), dev_u8(qb, cuda), dev_u8(sa, cuda), dev_u8(sb, cuda))
+    torch.cuda.synchronize()
+    rows = np.random.default_rng(1).choice(m, 64, replace=False)
+    rows.sort()
+    ref, _ = orc.gemm_mxfp4(qa[rows], qb, sa[rows], sb)
+    got = out[torch.from_numpy(rows).to(cuda)].float().cpu().numpy()
+    assert_close(orc, ref, got, "mxfp4 8192^3 sample")
+    assert not torch.isnan(out).any()
