@@ -1,0 +1,487 @@
+#!/usr/bin/env python
+"""Benchmark of the block-scaled GEMM hot path (driver contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload mxfp8|mxfp4|fp8block] [--layout tn|nn|tt|nt]
+
+Default workload (BASELINE metric, configs[2]): MXFP8 GEMM M=N=K=8192, layout
+tn, E4M3 with E8M0 scales per 32 K, bf16 out, fp32 accumulation.  One step is
+one GEMM over the whole problem.  For N > 1 GPUs (torchrun, one process per
+GPU) the GEMM is partitioned along N with weights pre-sharded: every rank
+computes its own M x 8192 x K column shard (weak scaling, no collective in the
+timed region; configs[4]).
+
+Printed JSON line: value = TFLOPS of the whole job from device-side CUDA
+events (max over ranks), e2e = the same GEMM through the public C-ABI call
+with pinned host buffers (inputs H2D + output D2H inside the timed region),
+roofline of the GEMM kernel, cpu_baseline = the reference's CPU verification
+GEMM (restated in oracle/, "port") on a row sample, and sampled clocks.
+
+--impl reference times the reference's CPU GEMM (the oracle port; the
+reference itself is HIP-only and cannot be built here) on the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="mxfp8", choices=["mxfp8", "mxfp4", "fp8block"])
+    ap.add_argument("--layout", default="tn", choices=["tn", "nn", "tt", "nt"])
+    ap.add_argument("--m", type=int, default=8192)
+    ap.add_argument("--n", type=int, default=8192, help="per-rank N")
+    ap.add_argument("--k", type=int, default=8192)
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        out_dir = ROOT / "gpurun_out"
+        out_dir.mkdir(exist_ok=True)
+        self.path = out_dir / f"clocks_rank{self.gpu}.csv"
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
+
+
+# ---------------------------------------------------------------------------
+# synthetic inputs on the device (torch ops; not the measured path)
+# ---------------------------------------------------------------------------
+def quant_mx_torch(x, qmax, fp4):
+    """Per-32 power-of-two scales 2^ceil(log2(amax/qmax)) and RNE-quantised
+    elements, computed with torch on the device."""
+    import torch
+    rows, k = x.shape
+    g = x.view(rows, k // 32, 32).float()
+    amax = g.abs().amax(dim=2)
+    mant, ex = torch.frexp((amax / qmax).clamp_min(1e-30))
+    e = torch.where(mant == 0.5, ex - 1, ex).clamp(-127, 127)
+    e = torch.where(amax > 0, e, torch.zeros_like(e))
+    sf = (e + 127).to(torch.uint8)
+    scaled = torch.ldexp(g, (-e).unsqueeze(-1).float()).view(rows, k)
+    if not fp4:
+        return scaled.to(torch.float8_e4m3fn), sf
+    # E2M1 RNE by thresholds on |v|: codes 0..7 <-> {0,.5,1,1.5,2,3,4,6}
+    a = scaled.abs()
+    thr = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], device=x.device)
+    code = torch.bucketize(a, thr, right=False).to(torch.uint8)   # ties go low...
+    ties_up = torch.isin(a, torch.tensor([0.75, 1.75, 3.5], device=x.device))  # ...except to even codes
+    code = code + ties_up.to(torch.uint8)
+    code = code | ((scaled < 0).to(torch.uint8) << 3)
+    packed = code[:, 0::2] | (code[:, 1::2] << 4)
+    return packed.contiguous(), sf
+
+
+def make_mx_inputs(bs, m, n, k, fp4, layout, device, seed):
+    import torch
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    x = torch.randn(m, k, device=device, generator=gen)
+    w = torch.randn(n, k, device=device, generator=gen)
+    qmax = 6.0 if fp4 else 448.0
+    qa, sa = quant_mx_torch(x, qmax, fp4)
+    qb, sb = quant_mx_torch(w, qmax, fp4)
+    del x, w
+    if not fp4:
+        if layout[0] == "n":
+            qa = qa.view(torch.uint8).t().contiguous().view(torch.float8_e4m3fn)
+        if layout[1] == "t":
+            qb = qb.view(torch.uint8).t().contiguous().view(torch.float8_e4m3fn)
+    return qa, qb, sa, sb
+
+
+def make_fp8block_inputs(m, n, k, device, seed):
+    import torch
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    x = torch.randn(m, k, device=device, generator=gen)
+    w = torch.randn(n, k, device=device, generator=gen)
+    xa = x.view(m, k // 128, 128).abs().amax(dim=2).clamp_min(1e-30) / 448.0
+    qa = (x.view(m, k // 128, 128) / xa.unsqueeze(-1)).view(m, k).to(torch.float8_e4m3fn)
+    wb = w.view(n // 128, 128, k // 128, 128).abs().amax(dim=(1, 3)).clamp_min(1e-30) / 448.0
+    qb = (w.view(n // 128, 128, k // 128, 128) / wb[:, None, :, None]).view(n, k).to(torch.float8_e4m3fn)
+    # K-panel preshuffle B'[K/128][N][128]
+    qb_kp = qb.view(torch.uint8).view(n, k // 128, 128).permute(1, 0, 2).contiguous().view(torch.float8_e4m3fn)
+    return qa, qb_kp, xa.contiguous(), wb.contiguous()
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (the reference's CPU GEMM restated in oracle/, "port")
+# ---------------------------------------------------------------------------
+def cpu_baseline(workload, m, n, k, target_s=12.0, max_rows=None):
+    import numpy as np
+    from oracle import oracle as orc
+    orc.build()
+    cores = orc.num_threads()
+    rng = np.random.default_rng(0)
+
+    def sample(rows):
+        if workload == "mxfp8":
+            qa, sa = orc.quant_mxfp8(rng.standard_normal((rows, k)).astype(np.float32))
+            qb, sb = orc.quant_mxfp8(rng.standard_normal((n, k)).astype(np.float32)) if not hasattr(sample, "b") else sample.b
+            sample.b = (qb, sb)
+            t0 = time.perf_counter()
+            orc.gemm_mxfp8(qa, qb, sa, sb)
+            return time.perf_counter() - t0
+        if workload == "mxfp4":
+            qa, sa = orc.quant_mxfp4(rng.standard_normal((rows, k)).astype(np.float32))
+            if not hasattr(sample, "b"):
+                sample.b = orc.quant_mxfp4(rng.standard_normal((n, k)).astype(np.float32))
+            qb, sb = sample.b
+            t0 = time.perf_counter()
+            orc.gemm_mxfp4(qa, qb, sa, sb)
+            return time.perf_counter() - t0
+        qa, sa = orc.quant_fp8_block(rng.standard_normal((rows, k)).astype(np.float32), 1)
+        if not hasattr(sample, "b"):
+            sample.b = orc.quant_fp8_block(rng.standard_normal((n, k)).astype(np.float32), 128)
+        qb, sb = sample.b
+        t0 = time.perf_counter()
+        orc.gemm_fp8_block(qa, qb, sa, sb)
+        return time.perf_counter() - t0
+
+    t1 = sample(1)
+    rows = max(1, min(int(target_s / max(t1, 1e-6)), max_rows or m, m))
+    t = sample(rows) if rows > 1 else t1
+    tflops = 2.0 * rows * n * k / t / 1e12
+    return {"value": tflops, "unit": "TFLOPS", "cores": cores, "kind": "port",
+            "sample": f"{rows} of {m} rows x N={n} x K={k} ({t:.1f} s, extrapolated to TFLOPS)"}
+
+
+def metric_name(workload):
+    return {"mxfp8": "MXFP8 block-scaled GEMM TFLOPS (8192^3)",
+            "mxfp4": "MXFP4 block-scaled GEMM TFLOPS (8192^3)",
+            "fp8block": "FP8 fp32-block-scale GEMM TFLOPS"}[workload]
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return 0
+    import numpy as np
+    from oracle import oracle as orc
+    orc.build()
+    m, n, k = args.m, args.n * world, args.k
+    rng = np.random.default_rng(0)
+    rows = 1
+    if args.workload == "mxfp8":
+        qb, sb = orc.quant_mxfp8(rng.standard_normal((n, k)).astype(np.float32))
+        qa, sa = orc.quant_mxfp8(rng.standard_normal((rows, k)).astype(np.float32))
+        fn = lambda: orc.gemm_mxfp8(qa, qb, sa, sb)
+    elif args.workload == "mxfp4":
+        qb, sb = orc.quant_mxfp4(rng.standard_normal((n, k)).astype(np.float32))
+        qa, sa = orc.quant_mxfp4(rng.standard_normal((rows, k)).astype(np.float32))
+        fn = lambda: orc.gemm_mxfp4(qa, qb, sa, sb)
+    else:
+        qb, sb = orc.quant_fp8_block(rng.standard_normal((n, k)).astype(np.float32), 128)
+        qa, sa = orc.quant_fp8_block(rng.standard_normal((rows, k)).astype(np.float32), 1)
+        fn = lambda: orc.gemm_fp8_block(qa, qb, sa, sb)
+    # bound the whole run to a few minutes
+    t0 = time.perf_counter()
+    fn()
+    t_one = time.perf_counter() - t0
+    budget = 150.0
+    steps = max(1, min(args.steps, int(budget / max(t_one, 1e-6))))
+    for _ in range(min(args.warmup, 2)):
+        fn()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        fn()
+    dt = (time.perf_counter() - t0) / steps
+    value = 2.0 * rows * n * k / dt / 1e12
+    cores = orc.num_threads()
+    line = {
+        "impl": "reference", "metric": metric_name(args.workload), "value": value, "unit": "TFLOPS",
+        "n_gpus": world, "steps": steps, "warmup": min(args.warmup, 2), "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "mxfp8" if args.workload == "mxfp8" else ("mxfp4" if args.workload == "mxfp4" else "fp8-e4m3"),
+        "data": "synthetic",
+        "config": {"workload": f"{args.workload} M={m} N={n} K={k} layout={args.layout}",
+                   "sample_rows_per_step": rows},
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": cores, "kind": "port",
+                         "sample": f"{rows} row x N={n} x K={k} per step, {steps} steps"},
+        "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference CPU verification GEMM restated in oracle/ (the reference is HIP/gfx950-only "
+                "and cannot be built here)",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    bs = importlib.import_module("355_1_trans_b200")
+    peaks, peak_kind = load_peaks()
+
+    m, n, k = args.m, args.n, args.k
+    wl = args.workload
+    fp4 = wl == "mxfp4"
+    if wl in ("mxfp8", "mxfp4"):
+        qa, qb, sa, sb = make_mx_inputs(bs, m, n, k, fp4, args.layout if not fp4 else "tn", dev, 1234 + rank)
+        if world > 1:
+            # the replicated activation A (and its scales) is broadcast once from rank 0
+            dist.broadcast(qa.view(torch.uint8), 0)
+            dist.broadcast(sa, 0)
+        sa_n = bs.pack_scales(sa)   # weights' and activations' scales in the native atom layout
+        sb_n = bs.pack_scales(sb)
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        if fp4:
+            call = lambda: bs.gemm_a4w4_mxfp4(qa, qb, sa_n, sb_n, out=out, scale_format="native")
+            a_bytes, b_bytes = m * k // 2, n * k // 2
+        else:
+            call = lambda: bs.gemm_a8w8_mxfp8(qa, qb, sa_n, sb_n, layout=args.layout, out=out,
+                                              scale_format="native")
+            a_bytes, b_bytes = m * k, n * k
+        sf_bytes = (m + n) * k // 32
+    else:
+        qa, qb, sa, sb = make_fp8block_inputs(m, n, k, dev, 1234 + rank)
+        if world > 1:
+            dist.broadcast(qa.view(torch.uint8), 0)
+            dist.broadcast(sa, 0)
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        call = lambda: bs.gemm_a8w8_bpreshuffle(qa, qb, sa, sb, torch.bfloat16, preshuffled=True, out=out)
+        a_bytes, b_bytes = m * k, n * k
+        sf_bytes = 4 * m * (k // 128) + 4 * (n // 128) * (k // 128)
+    flops = 2.0 * m * n * k
+    alg_bytes = a_bytes + b_bytes + sf_bytes + 2 * m * n
+    torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+
+    stream = torch.cuda.current_stream(dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)   # let the sampler take its first readings
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        starts[i].record(stream)
+        call()
+        ends[i].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    total_ms = t_start.elapsed_time(t_end)
+    kern_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    tm = torch.tensor([total_ms, kern_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+    total_ms, kern_ms = float(tm[0]), float(tm[1])
+    ms_per_step = total_ms / args.steps
+    value = world * flops / (ms_per_step * 1e-3) / 1e12
+    assert bs.check_device_error() == 0
+
+    # optional all-gather of the bf16 column shards (reported, not in value)
+    allgather_ms = None
+    if world > 1:
+        gathered = torch.empty(world, m, n, dtype=torch.bfloat16, device=dev)
+        for _ in range(2):
+            dist.all_gather_into_tensor(gathered, out)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(5):
+            dist.all_gather_into_tensor(gathered, out)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ag = torch.tensor([e0.elapsed_time(e1) / 5], dtype=torch.float64, device=dev)
+        dist.all_reduce(ag, op=dist.ReduceOp.MAX)
+        allgather_ms = float(ag[0])
+        del gathered
+
+    # e2e through the public API with pinned host buffers (reference-facing
+    # row-major scales, packed inside the library call)
+    e2e = None
+    h_a = qa.view(torch.uint8).cpu().pin_memory()
+    h_b = qb.view(torch.uint8).cpu().pin_memory()
+    h_sa = sa.cpu().pin_memory()
+    h_sb = sb.cpu().pin_memory()
+    h_out = torch.empty(m, n, dtype=torch.bfloat16).pin_memory()
+    d_a, d_b = torch.empty_like(qa.view(torch.uint8)), torch.empty_like(qb.view(torch.uint8))
+    d_sa, d_sb = torch.empty_like(sa), torch.empty_like(sb)
+
+    def e2e_step():
+        d_a.copy_(h_a, non_blocking=True)
+        d_b.copy_(h_b, non_blocking=True)
+        d_sa.copy_(h_sa, non_blocking=True)
+        d_sb.copy_(h_sb, non_blocking=True)
+        if wl == "mxfp8":
+            r = bs.gemm_a8w8_mxfp8(d_a.view(torch.float8_e4m3fn), d_b.view(torch.float8_e4m3fn), d_sa, d_sb,
+                                   layout=args.layout, out=out)
+        elif wl == "mxfp4":
+            r = bs.gemm_a4w4_mxfp4(d_a, d_b, d_sa, d_sb, out=out)
+        else:
+            r = bs.gemm_a8w8_bpreshuffle(d_a.view(torch.float8_e4m3fn), d_b.view(torch.float8_e4m3fn),
+                                         d_sa, d_sb, torch.bfloat16, preshuffled=True, out=out)
+        h_out.copy_(r, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    et = torch.tensor([e0.elapsed_time(e1) / args.e2e_steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(et, op=dist.ReduceOp.MAX)
+    e2e_ms = float(et[0])
+    h2d = h_a.numel() + h_b.numel() + h_sa.numel() * h_sa.element_size() + h_sb.numel() * h_sb.element_size()
+    e2e = {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS", "ms_per_step": e2e_ms,
+           "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(m * n * 2),
+           "path": "C-ABI call with pinned host buffers, reference-facing row-major scales"}
+
+    # roofline of the GEMM kernel
+    if wl == "fp8block" and m <= 128:
+        bound, unit = "hbm", "GB/s"
+        achieved = alg_bytes / (kern_ms * 1e-3) / 1e9
+        peak = peaks.get("hbm_gbs")
+        basis = f"hbm_gbs ({peak_kind})"
+    else:
+        bound, unit = "tensor", "TFLOP/s"
+        achieved = flops / (kern_ms * 1e-3) / 1e12
+        bf16 = peaks.get("bf16_tflops")
+        mult = 4.0 if fp4 else 2.0
+        peak = bf16 * mult
+        basis = (f"{mult:.0f} x bf16_tflops burst ({peak_kind}, {bf16} TF/s): dense "
+                 f"{'MXFP4' if fp4 else 'FP8/MXFP8'} tensor rate is {mult:.0f}x bf16 on B200")
+    roofline = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                "frac": achieved / peak if peak else None, "traffic": None, "peak_basis": basis,
+                "algorithmic_bytes_per_launch": alg_bytes, "flops_per_launch": flops,
+                "kernel_ms": kern_ms}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(wl, m, n, k)
+
+    if rank == 0:
+        line = {
+            "metric": metric_name(wl), "value": value, "unit": "TFLOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": {"mxfp8": "mxfp8", "mxfp4": "mxfp4", "fp8block": "fp8-e4m3"}[wl],
+            "data": "synthetic (seeded torch.randn, quantised on device)",
+            "config": {"workload": f"{wl} M={m} N={n}/rank K={k} layout={args.layout if wl == 'mxfp8' else 'tn'}",
+                       "out": "bf16", "accum": "fp32",
+                       "scales": "native tcgen05 atoms (pre-packed)" if wl != "fp8block" else "fp32 1x128 / 128x128",
+                       "parallelism": f"N-sharded x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs + output exceed the 126 MB L2; no flush"},
+            "gpu_launches": args.steps,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+        }
+        if allgather_ms is not None:
+            line["allgather_ms"] = allgather_ms
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())
