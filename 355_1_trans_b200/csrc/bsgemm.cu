@@ -650,6 +650,8 @@ const char* bsgemm_strerror(int status) {
     case BSG_ERR_CUDA: return "CUDA call failed";
     case BSG_ERR_TIMEOUT: return "device-side bounded wait expired";
     case BSG_ERR_ALIGNMENT: return "pointer or stride violates the 16-byte rules";
+    case BSG_ERR_SCRATCH_LIMIT:
+      return "problem needs more than the fixed device scratch of the allocation-free entry point";
     default: return "unknown status";
   }
 }
@@ -675,5 +677,82 @@ int bsgemm_selftest_timeout(int timeout_us) {
 }
 
 const char* bsgemm_version(void) { return "bsgemm_b200 0.1 (sm_100a)"; }
+
+}  // extern "C"
+
+// ===========================================================================
+// Allocation-free MXFP8 entry point
+//
+// Some callers cannot allocate device memory at all: a serving runtime that
+// reserves the whole HBM budget up front and routes every byte through its
+// own allocator, or a host application that must never take the implicit
+// device synchronisation a cudaMalloc/cudaFree can cause in the middle of its
+// stream work.  bsgemm_a8w8_mxfp8 asks such callers for a workspace whenever
+// it repacks row-major scales or splits K; this variant instead uses a fixed
+// scratch array that lives in the library's own device image.
+//
+// Limits and behaviour:
+//   - the scratch is kNoAllocScratchBytes (8 MiB) on every GPU that loads the
+//     library, held until the process exits;
+//   - a problem whose repacked scales plus split-K partials exceed it is
+//     rejected with BSG_ERR_SCRATCH_LIMIT before anything is enqueued (with
+//     split_k == 0 the split is dropped first if that makes it fit);
+//   - every call on a device shares the one array, and it keeps whatever the
+//     last call left there.  The kernels overwrite every scratch byte they
+//     read (scale atoms are written whole, each K slice writes its complete
+//     partial tile), so nothing has to start at zero, but two calls whose
+//     work overlaps on the GPU (different streams, or different host threads
+//     without ordering) race on the scratch and corrupt each other;
+//   - the first call on a device looks up the array's device address with
+//     cudaGetSymbolAddress (once per device, with that device current); make
+//     that first call before any stream capture on the device.
+// ===========================================================================
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+
+// Device-side scratch.  In host code this name is only a host stand-in for
+// the symbol: never pass it to a kernel, always the address looked up below.
+static __device__ __align__(256) unsigned char g_bsg_noalloc_scratch[kNoAllocScratchBytes];
+
+int noalloc_scratch_ptr(void** out) {
+  static std::mutex mu;
+  static void* ptrs[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return BSG_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_bsg_noalloc_scratch) != cudaSuccess || !p) return BSG_ERR_CUDA;
+    ptrs[dev] = p;
+  }
+  *out = ptrs[dev];
+  return BSG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+BSG_API int bsgemm_a8w8_mxfp8_noalloc(const bsgemm_args* args, bsg_stream_t stream) {
+  int rc = validate_common(args);
+  if (rc != BSG_OK) return rc;
+  bsgemm_args a = *args;
+  a.workspace = nullptr;
+  a.workspace_bytes = 0;
+  size_t need = bsgemm_workspace_size(BSG_FAMILY_MXFP8, &a);
+  if (need > kNoAllocScratchBytes && a.split_k == 0) {
+    a.split_k = 1;                     // auto split-K does not fit: run unsplit
+    need = bsgemm_workspace_size(BSG_FAMILY_MXFP8, &a);
+  }
+  if (need > kNoAllocScratchBytes) return BSG_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  if ((rc = noalloc_scratch_ptr(&scratch)) != BSG_OK) return rc;
+  a.workspace = scratch;
+  a.workspace_bytes = kNoAllocScratchBytes;
+  return mx_run(&a, false, reinterpret_cast<cudaStream_t>(stream));
+}
+
+BSG_API size_t bsgemm_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
 
 }  // extern "C"

@@ -54,7 +54,8 @@ enum {
     BSG_ERR_WORKSPACE = 4,       /* split-K workspace missing or too small */
     BSG_ERR_CUDA = 5,            /* a CUDA runtime/driver call failed */
     BSG_ERR_TIMEOUT = 6,         /* a device-side bounded wait expired */
-    BSG_ERR_ALIGNMENT = 7        /* pointer/stride violates TMA 16-byte rules */
+    BSG_ERR_ALIGNMENT = 7,       /* pointer/stride violates TMA 16-byte rules */
+    BSG_ERR_SCRATCH_LIMIT = 8    /* bsgemm_a8w8_mxfp8_noalloc: problem exceeds its fixed scratch */
 };
 
 /* ---- enums of bsgemm_args ---------------------------------------------- */
@@ -222,6 +223,25 @@ BSG_API int bsgemm_check_device_error(void);
  * the status the kernel reported (BSG_ERR_TIMEOUT expected).  Synchronous.
  */
 BSG_API int bsgemm_selftest_timeout(int timeout_us);
+
+/*
+ * Allocation-free variant of bsgemm_a8w8_mxfp8 (same arguments, same
+ * results) for callers that cannot allocate device memory at all -- e.g. a
+ * serving runtime that owns the whole HBM budget through its own allocator,
+ * or code that must not take the device synchronisation an allocation can
+ * cause.  args->workspace is ignored: the scale repacking and split-K
+ * partials use a fixed 8 MiB scratch array in the library's device image
+ * (held on every GPU that loads the library until exit; see
+ * bsgemm_noalloc_scratch_bytes).  Problems that need more are rejected with
+ * BSG_ERR_SCRATCH_LIMIT.  All calls on a device share that one array: calls
+ * that overlap on the GPU race and corrupt each other.  The first call on a
+ * device looks the array's address up (once per device); make it before any
+ * stream capture.  No counterpart in the reference, whose launchers need no
+ * scratch.
+ */
+BSG_API int bsgemm_a8w8_mxfp8_noalloc(const bsgemm_args *args, bsg_stream_t stream);
+/* Size of that fixed scratch array in bytes. */
+BSG_API size_t bsgemm_noalloc_scratch_bytes(void);
 
 /* Library version string. */
 BSG_API const char *bsgemm_version(void);
