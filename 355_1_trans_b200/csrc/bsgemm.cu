@@ -28,6 +28,9 @@ using bsg::MxCfg;
 using bsg::MxParams;
 
 constexpr unsigned long long kTimeoutNs = 10ull * 1000ull * 1000ull * 1000ull;  // 10 s per wait
+// M tiles per rasterisation group: the CTAs in flight share a 16 x 128-row A
+// panel group and walk its N tiles together (L2 reuse of A and B).
+constexpr int kGroupM = 16;
 
 // ---------------------------------------------------------------------------
 // driver entry point for tensor-map encoding (no link-time libcuda dependency)
@@ -208,7 +211,7 @@ int mx_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p,
   using Cfg = MxCfg<BN, kFp4>;
   auto* kern = bsg::mx_gemm_kernel<BN, kFp4, kAMN, kBMN, kOutF32>;
   if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
-  kern<<<grid, 256, Cfg::kSmemBytes, st>>>(ta, tb, p);
+  kern<<<grid, bsg::kMxThreads, Cfg::kSmemBytes, st>>>(ta, tb, p);
   return launch_status();
 }
 
@@ -373,6 +376,7 @@ int mx_run(const bsgemm_args* args, bool fp4, cudaStream_t st) {
   p.split_k = pl.split;
   p.kb_per_split = pl.kb_per;
   p.total_units = pl.tiles_m * pl.tiles_n * a.batch * pl.split;
+  p.group_m = std::min(pl.tiles_m, kGroupM);
   p.sfa = sfa;
   p.sfb = sfb;
   p.sfa_batch_stride = sfa_bs;
@@ -514,6 +518,7 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
   p.split_k = pl.split;
   p.kb_per_split = pl.kb_per;
   p.total_units = pl.tiles_m * pl.tiles_n * a.batch * pl.split;
+  p.group_m = std::min(pl.tiles_m, kGroupM);
   p.sfa = static_cast<const float*>(a.ptr_sfa);
   p.sfa_m = sfa_m;
   p.sfa_k = sfa_k;

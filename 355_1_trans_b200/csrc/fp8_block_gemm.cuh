@@ -32,6 +32,7 @@ struct Fp8BlockParams {
   int tiles_m, tiles_n;
   int split_k, kb_per_split;
   int total_units;
+  int group_m;
   const float* sfa;
   long long sfa_m, sfa_k, sfa_batch;   // float strides: row, k-block, batch
   const float* sfb;
@@ -114,7 +115,7 @@ __global__ void __launch_bounds__(256, 1)
     uint32_t last_phase = 0;
     for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
       int b, mt, nt, s;
-      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, b, mt, nt, s);
+      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
       const int kb0 = s * p.kb_per_split;
       const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
       for (int kb = kb0; kb < kb1; ++kb) {
@@ -151,7 +152,7 @@ __global__ void __launch_bounds__(256, 1)
     bool ok = true;
     for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
       int b, mt, nt, s;
-      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, b, mt, nt, s);
+      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
       const int kb0 = s * p.kb_per_split;
       const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
       for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
@@ -194,7 +195,7 @@ __global__ void __launch_bounds__(256, 1)
     bool ok = true;
     for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
       int b, mt, nt, s;
-      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, b, mt, nt, s);
+      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
       const int kb0 = s * p.kb_per_split;
       const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
       const int row = mt * 128 + q * 32 + static_cast<int>(lane);

@@ -8,17 +8,21 @@
 //   C[b,m,n] = sum_g 2^(sfa[m,g]-127) * 2^(sfb[n,g]-127) * sum_{k in g} A[m,k] B[n,k],
 //   g = 32 consecutive K, fp32 accumulation, bf16 (RNE) or fp32 output.
 //
-// Design (one CTA per SM, persistent over output tiles of 128 x BN):
+// Design (one CTA per SM, persistent over output tiles of 128 x BN, grouped
+// rasterisation so concurrently running CTAs share A/B panels in L2):
 //   warp 0      TMA producer: A/B tiles (128-byte K slabs, 128B swizzle) by
-//               tensor maps, scale atoms by plain bulk copies, one mbarrier
-//               per stage with transaction bytes;
+//               tensor maps with L2 cache policies (A evict-last, B
+//               evict-first), scale atoms by plain bulk copies; one mbarrier
+//               per stage carries the transaction bytes;
 //   warp 1      single-thread tcgen05 issuer: scale atoms smem -> TMEM with
 //               tcgen05.cp, then 4 block-scaled MMAs per stage into a
 //               128 x BN fp32 TMEM accumulator; tcgen05.commit frees stages;
 //   warp 2      TMEM allocator;
-//   warps 4-7   epilogue: tcgen05.ld (warp w reads TMEM lanes 32*(w%4)..),
-//               fp32 -> bf16 RNE, 16-byte global stores; or fp32 partials
-//               to the split-K workspace.
+//   warps 4-11  epilogue, two warps per TMEM lane quarter (warp w reads lanes
+//               32*(w%4).., half of the columns each): the bf16 path drains
+//               the whole accumulator into packed registers, releases TMEM at
+//               once (the MMA warp starts the next tile) and then streams the
+//               stores; fp32 / split-K partial outputs store chunk by chunk.
 // The MMA instruction K is 32 (fp8) / 64 (fp4), i.e. 32 bytes of a 128-byte
 // swizzled row; one stage holds 128 bytes of K per row (128 fp8 / 256 fp4
 // elements) and 1 (fp8) or 2 (fp4) scale atoms per 128 rows.
@@ -35,6 +39,7 @@ struct MxParams {
   int tiles_m, tiles_n;
   int split_k, kb_per_split;
   int total_units;               // batch * tiles_m * tiles_n * split_k
+  int group_m;                   // rasterisation group (M tiles)
   const uint8_t* sfa;            // native scale atoms
   const uint8_t* sfb;
   long long sfa_batch_stride;    // bytes
@@ -47,6 +52,9 @@ struct MxParams {
   float* ws;                     // split-K partials [split][batch][m][n]
   unsigned long long timeout_ns;
 };
+
+constexpr int kMxThreads = 384;     // 4 control warps + 8 epilogue warps
+constexpr int kMxEpiThreads = 256;
 
 template <int BN, int kFp4>
 struct MxCfg {
@@ -74,22 +82,25 @@ struct MxCfg {
   static constexpr uint32_t kColsUsed = kColSfb + 4u * kSfAtomsK * kSfbRowBlocks;
   static constexpr uint32_t kTmemCols = kColsUsed <= 32 ? 32 : kColsUsed <= 64 ? 64
                                         : kColsUsed <= 128 ? 128 : kColsUsed <= 256 ? 256 : 512;
+  static constexpr int kHalfCols = BN / 2;   // columns per epilogue warp
   static_assert(kStages >= 2, "shared memory too small for two stages");
   static_assert(kColsUsed <= 512, "TMEM overflow");
 };
 
-__device__ __forceinline__ void decode_unit(int u, int tiles_m, int tiles_n, int split_k, int& b,
-                                            int& mt, int& nt, int& s) {
-  s = u % split_k;
-  int t = u / split_k;
-  mt = t % tiles_m;
-  t /= tiles_m;
-  nt = t % tiles_n;
-  b = t / tiles_n;
+// Store 32 fp32 accumulator columns of one row (fp32 output or split-K partial).
+__device__ __forceinline__ void store_row32_f32(float* dst, const uint32_t (&r)[32], int valid) {
+  if (valid >= 32) {
+#pragma unroll
+    for (int v = 0; v < 8; ++v) st_global_cs_v4(dst + 4 * v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+  } else {
+#pragma unroll
+    for (int v = 0; v < 32; ++v)
+      if (v < valid) dst[v] = __uint_as_float(r[v]);
+  }
 }
 
 template <int BN, int kFp4, bool kAMN, bool kBMN, bool kOutF32>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(kMxThreads, 1)
     mx_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const MxParams p) {
   using Cfg = MxCfg<BN, kFp4>;
@@ -120,7 +131,7 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(&empty_bar[i], 1);
     }
     mbar_init(tmem_full, 1);
-    mbar_init(tmem_empty, 128);
+    mbar_init(tmem_empty, kMxEpiThreads);
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -140,6 +151,8 @@ __global__ void __launch_bounds__(256, 1)
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------------ TMA producer
+    const uint64_t pol_a = l2_policy_evict_last();
+    const uint64_t pol_b = l2_policy_evict_first();
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -147,38 +160,39 @@ __global__ void __launch_bounds__(256, 1)
     uint32_t last_phase = 0;
     for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
       int b, mt, nt, s;
-      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, b, mt, nt, s);
+      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
       const int kb0 = s * p.kb_per_split;
       const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
       const uint8_t* sfa_tile = p.sfa + b * p.sfa_batch_stride +
                                 static_cast<long long>(mt) * p.sf_kb_total * 512;
       const uint8_t* sfb_tile = p.sfb + b * p.sfb_batch_stride +
                                 static_cast<long long>(nt) * Cfg::kSfbRowBlocks * p.sf_kb_total * 512;
+      // the last N tile may cover fewer 128-row scale blocks than BN / 128;
+      // copy only the ones that exist (the columns beyond N are never stored)
+      const int sfb_rows = min(Cfg::kSfbRowBlocks, p.sfb_row_blocks - nt * Cfg::kSfbRowBlocks);
+      const uint32_t tx_bytes =
+          Cfg::kStageBytes - static_cast<uint32_t>(Cfg::kSfbRowBlocks - sfb_rows) * 512u * Cfg::kSfAtomsK;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
           ok = false;
           break;
         }
         uint64_t* fb = &full_bar[stage];
-        // the last N tile may cover fewer 128-row scale blocks than BN / 128;
-        // copy only the ones that exist (the columns beyond N are never stored)
-        const int sfb_rows = min(Cfg::kSfbRowBlocks, p.sfb_row_blocks - nt * Cfg::kSfbRowBlocks);
-        mbar_arrive_expect_tx(fb, Cfg::kStageBytes - static_cast<uint32_t>(Cfg::kSfbRowBlocks - sfb_rows) *
-                                                         512u * Cfg::kSfAtomsK);
+        mbar_arrive_expect_tx(fb, tx_bytes);
         uint8_t* a_dst = sA + stage * Cfg::kABytes;
         uint8_t* b_dst = sB + stage * Cfg::kBBytes;
         const int kbyte = kb * 128;
         if constexpr (!kAMN) {
-          tma_load_3d(a_dst, &tmA, fb, kbyte, mt * 128, b);
+          tma_load_3d_hint(a_dst, &tmA, fb, kbyte, mt * 128, b, pol_a);
         } else {
-          tma_load_3d(a_dst, &tmA, fb, mt * 128, kbyte, b);
+          tma_load_3d_hint(a_dst, &tmA, fb, mt * 128, kbyte, b, pol_a);
         }
         if constexpr (!kBMN) {
-          tma_load_3d(b_dst, &tmB, fb, kbyte, nt * BN, b);
+          tma_load_3d_hint(b_dst, &tmB, fb, kbyte, nt * BN, b, pol_b);
         } else {
 #pragma unroll
           for (int j = 0; j < BN / 128; ++j)
-            tma_load_3d(b_dst + j * 16384, &tmB, fb, nt * BN + j * 128, kbyte, b);
+            tma_load_3d_hint(b_dst + j * 16384, &tmB, fb, nt * BN + j * 128, kbyte, b, pol_b);
         }
         const long long atom_k = static_cast<long long>(kb) * Cfg::kSfAtomsK;
         bulk_load(sSfa + stage * Cfg::kSfaBytes, sfa_tile + atom_k * 512, Cfg::kSfaBytes, fb);
@@ -186,8 +200,8 @@ __global__ void __launch_bounds__(256, 1)
         for (int r = 0; r < Cfg::kSfbRowBlocks; ++r)
           if (r < sfb_rows)
             bulk_load(sSfb + stage * Cfg::kSfbBytes + r * 512 * Cfg::kSfAtomsK,
-                    sfb_tile + (static_cast<long long>(r) * p.sf_kb_total + atom_k) * 512,
-                    512u * Cfg::kSfAtomsK, fb);
+                      sfb_tile + (static_cast<long long>(r) * p.sf_kb_total + atom_k) * 512,
+                      512u * Cfg::kSfAtomsK, fb);
         last_stage = stage;
         last_phase = phase;
         if (++stage == S) {
@@ -220,7 +234,7 @@ __global__ void __launch_bounds__(256, 1)
     bool ok = true;
     for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x, ++iter) {
       int b, mt, nt, s;
-      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, b, mt, nt, s);
+      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
       const int kb0 = s * p.kb_per_split;
       const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
       if (!mbar_wait(tmem_empty, (static_cast<uint32_t>(iter) & 1u) ^ 1u, abort_flag,
@@ -276,68 +290,65 @@ __global__ void __launch_bounds__(256, 1)
     mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue
+    constexpr int HC = Cfg::kHalfCols;
     const int q = warp & 3;
-    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const int half = (warp - 4) >> 2;
+    const uint32_t t_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                            static_cast<uint32_t>(half * HC);
     int iter = 0;
     for (int u = blockIdx.x; u < p.total_units; u += gridDim.x, ++iter) {
       int b, mt, nt, s;
-      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, b, mt, nt, s);
+      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
       if (!mbar_wait(tmem_full, static_cast<uint32_t>(iter) & 1u, abort_flag, p.timeout_ns)) break;
       tc_fence_after();
       const int row = mt * 128 + q * 32 + static_cast<int>(lane);
       const bool row_ok = row < p.m;
-      const int n0 = nt * BN;
+      const int col_base = nt * BN + half * HC;
+      const int valid_cols = p.n - col_base;   // may be <= 0 or > HC
+      if (p.split_k > 1 || kOutF32) {
+        float* dst = p.split_k > 1
+                         ? p.ws + ((static_cast<long long>(s) * p.batch + b) * p.m + row) *
+                                      static_cast<long long>(p.n) + col_base
+                         : reinterpret_cast<float*>(p.c) + b * p.c_batch_stride +
+                               static_cast<long long>(row) * p.ldc + col_base;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem_base + lane_base + static_cast<uint32_t>(c * 32), r);
-        const int col0 = n0 + c * 32;
-        if (!row_ok || col0 >= p.n) continue;
-        const bool full = col0 + 32 <= p.n;
-        if (p.split_k > 1) {
-          float* dst = p.ws + ((static_cast<long long>(s) * p.batch + b) * p.m + row) *
-                                  static_cast<long long>(p.n) + col0;
-          if (full) {
+        for (int c = 0; c < HC / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(t_base + static_cast<uint32_t>(c * 32), r);
+          if (row_ok && valid_cols > c * 32) store_row32_f32(dst + c * 32, r, valid_cols - c * 32);
+        }
+        tc_fence_before();
+        mbar_arrive(tmem_empty);
+      } else {
+        // drain the whole half-row into packed bf16 registers, release the
+        // accumulator, then store
+        uint32_t w[HC / 2];
 #pragma unroll
-            for (int v = 0; v < 8; ++v)
-              st_global_v4(dst + 4 * v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
-          } else {
-            #pragma unroll
-            for (int v = 0; v < 32; ++v)
-              if (col0 + v < p.n) dst[v] = __uint_as_float(r[v]);
-          }
-        } else if constexpr (kOutF32) {
-          float* dst = reinterpret_cast<float*>(p.c) + b * p.c_batch_stride +
-                       static_cast<long long>(row) * p.ldc + col0;
-          if (full) {
+        for (int c = 0; c < HC / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(t_base + static_cast<uint32_t>(c * 32), r);
 #pragma unroll
-            for (int v = 0; v < 8; ++v)
-              st_global_v4(dst + 4 * v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
-          } else {
-            #pragma unroll
-            for (int v = 0; v < 32; ++v)
-              if (col0 + v < p.n) dst[v] = __uint_as_float(r[v]);
-          }
-        } else {
+          for (int v = 0; v < 16; ++v)
+            w[c * 16 + v] = pack_bf16x2(__uint_as_float(r[2 * v]), __uint_as_float(r[2 * v + 1]));
+        }
+        tc_fence_before();
+        mbar_arrive(tmem_empty);
+        if (row_ok && valid_cols > 0) {
           uint16_t* dst = reinterpret_cast<uint16_t*>(p.c) + b * p.c_batch_stride +
-                          static_cast<long long>(row) * p.ldc + col0;
-          if (full) {
-            uint32_t w[16];
+                          static_cast<long long>(row) * p.ldc + col_base;
+          if (valid_cols >= HC) {
 #pragma unroll
-            for (int v = 0; v < 16; ++v)
-              w[v] = pack_bf16x2(__uint_as_float(r[2 * v]), __uint_as_float(r[2 * v + 1]));
-#pragma unroll
-            for (int v = 0; v < 4; ++v)
-              st_global_v4(dst + 8 * v, w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+            for (int v = 0; v < HC / 8; ++v)
+              st_global_cs_v4(dst + 8 * v, w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
           } else {
-            #pragma unroll
-              for (int v = 0; v < 32; ++v)
-                if (col0 + v < p.n) dst[v] = static_cast<uint16_t>(pack_bf16x2(__uint_as_float(r[v]), 0.0f) & 0xFFFFu);
+#pragma unroll
+            for (int v = 0; v < HC / 2; ++v) {
+              if (2 * v < valid_cols) dst[2 * v] = static_cast<uint16_t>(w[v] & 0xFFFFu);
+              if (2 * v + 1 < valid_cols) dst[2 * v + 1] = static_cast<uint16_t>(w[v] >> 16);
+            }
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(tmem_empty);
     }
   }
 

@@ -126,6 +126,38 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m, uin
       : "memory");
 }
 
+// L2 cache policies for TMA loads (createpolicy, fraction 1.0).
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* m, uint64_t* bar,
+                                                 int c0, int c1, int c2, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)),
+      "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d_hint(void* dst, const CUtensorMap* m, uint64_t* bar,
+                                                 int c0, int c1, int c2, int c3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+      "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // Plain (untiled) bulk copy global -> shared; both addresses 16-byte aligned,
 // bytes a multiple of 16.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
@@ -274,6 +306,34 @@ __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, ui
                                              uint32_t d) {
   asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d)
                : "memory");
+}
+
+// Streaming store (evict-first in L2): output tiles are written once.
+__device__ __forceinline__ void st_global_cs_v4(void* p, uint32_t a, uint32_t b, uint32_t c,
+                                                uint32_t d) {
+  asm volatile("st.global.cs.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
+// Grouped rasterisation of output tiles: consecutive work units walk the
+// N tiles of a group of `group_m` M tiles, so the CTAs running at the same
+// time share A panels (group_m x 128 rows) and B panels in L2.
+// Unit u = ((batch * tiles) + tile) * split_k + slice.
+__device__ __forceinline__ void decode_unit(int u, int tiles_m, int tiles_n, int split_k,
+                                            int group_m, int& b, int& mt, int& nt, int& s) {
+  s = u % split_k;
+  int t = u / split_k;
+  const int per_batch = tiles_m * tiles_n;
+  b = t / per_batch;
+  t -= b * per_batch;
+  const int group_size = group_m * tiles_n;
+  const int g = t / group_size;
+  const int first_m = g * group_m;
+  const int gm = min(tiles_m - first_m, group_m);
+  const int local = t - g * group_size;
+  mt = first_m + local % gm;
+  nt = local / gm;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
