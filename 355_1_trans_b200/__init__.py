@@ -29,6 +29,7 @@ LAYOUTS = {"nt": 0, "tt": 1, "nn": 2, "tn": 3}
 B_RAW, B_KPANEL128, B_SHUFFLE16 = 0, 1, 2
 SF_NATIVE, SF_ROWMAJOR, SF_KMAJOR_T, SF_E8M0_SHUFFLE = 0, 1, 2, 3
 OUT_BF16, OUT_FP32 = 0, 1
+KERNELS = {"auto": 0, "1cta": 1, "pair": 2}
 FAMILY_MXFP8, FAMILY_MXFP4, FAMILY_FP8_BLOCK = 0, 1, 2
 
 
@@ -50,7 +51,7 @@ class Args(ctypes.Structure):
             "stride_sfa", "stride_sfb", "stride_sfa_batch", "stride_sfb_batch",
             "layout", "b_format", "sfa_format", "sfb_format", "out_dtype", "split_k")]
         + [("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
-           ("grid_blocks", ctypes.c_int), ("reserved", ctypes.c_int)]
+           ("grid_blocks", ctypes.c_int), ("kernel", ctypes.c_int)]
     )
 
 
@@ -150,32 +151,34 @@ def _record(tensors, device):
 
 def gemm_a8w8_mxfp8(A, B, A_scale, B_scale, *, layout: str = "tn", out_dtype=torch.bfloat16,
                     out=None, scale_format: str = "rowmajor", split_k: int = 0,
-                    workspace=None, grid_blocks: int = 0):
+                    workspace=None, grid_blocks: int = 0, kernel: str = "auto"):
     """MXFP8 GEMM (mxfp8_gemm/gemm_a8w8_mxfp8_host.cc:98-122 semantics).
 
     A: E4M3 [M,K] (layout t*) or [K,M] (n*); B: E4M3 [N,K] (*n) or [K,N] (*t);
     optional leading batch dim.  A_scale/B_scale: E8M0 bytes, [rows, K/32]
     row-major (scale_format="rowmajor") or native atoms from pack_scales
     (scale_format="native").  Returns C [M,N] (or [batch,M,N]) of out_dtype.
+    kernel: "auto", "1cta" (128 x BN tiles, one CTA each) or "pair" (256 x 256
+    tiles on CTA pairs, cta_group::2).
     """
     return _mx(A, B, A_scale, B_scale, fp4=False, layout=layout, out_dtype=out_dtype, out=out,
                scale_format=scale_format, split_k=split_k, workspace=workspace,
-               grid_blocks=grid_blocks)
+               grid_blocks=grid_blocks, kernel=kernel)
 
 
 def gemm_a4w4_mxfp4(A, B, A_scale, B_scale, *, out_dtype=torch.bfloat16, out=None,
                     scale_format: str = "rowmajor", split_k: int = 0, workspace=None,
-                    grid_blocks: int = 0):
+                    grid_blocks: int = 0, kernel: str = "auto"):
     """MXFP4 GEMM (mxfp4_gemm_4wave_20261112/gemm_a4w4_mxfp4_4wave_host.cc:97-115
     semantics): A [M,K/2], B [N,K/2] packed E2M1 bytes (even k low nibble),
     K-major; scales E8M0 [rows, K/32] or native."""
     return _mx(A, B, A_scale, B_scale, fp4=True, layout="tn", out_dtype=out_dtype, out=out,
                scale_format=scale_format, split_k=split_k, workspace=workspace,
-               grid_blocks=grid_blocks)
+               grid_blocks=grid_blocks, kernel=kernel)
 
 
 def _mx(A, B, A_scale, B_scale, *, fp4, layout, out_dtype, out, scale_format, split_k,
-        workspace, grid_blocks):
+        workspace, grid_blocks, kernel="auto"):
     if layout not in LAYOUTS:
         raise ValueError(f"layout must be one of {sorted(LAYOUTS)}")
     if A.dim() != B.dim() or A.dim() not in (2, 3):
@@ -238,6 +241,7 @@ def _mx(A, B, A_scale, B_scale, *, fp4, layout, out_dtype, out, scale_format, sp
     args.out_dtype = OUT_BF16 if out_dtype == torch.bfloat16 else OUT_FP32
     args.split_k = split_k
     args.grid_blocks = grid_blocks
+    args.kernel = KERNELS[kernel]
     ws = _workspace(FAMILY_MXFP4 if fp4 else FAMILY_MXFP8, args, workspace, A.device)
     fn = lib().bsgemm_a4w4_mxfp4 if fp4 else lib().bsgemm_a8w8_mxfp8
     with torch.cuda.device(A.device):

@@ -18,6 +18,7 @@
 #include "../../include/bsgemm_b200.h"
 #include "fp8_block_gemm.cuh"
 #include "mx_gemm.cuh"
+#include "mx_gemm_2sm.cuh"
 #include "pack.cuh"
 
 namespace {
@@ -54,10 +55,10 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// Byte tensor map (uint8 elements) of rank 3 or 4 with 128B swizzle.
-// dims/strides innermost first; strides[i] is the byte stride of dim i+1.
-bool make_tmap_u8(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
-                  const uint64_t* strides, const uint32_t* box, bool swizzle128) {
+// Tensor map of rank 3 or 4; dims/strides innermost first; strides[i] is the
+// byte stride of dim i+1.
+bool make_tmap(CUtensorMap* m, CUtensorMapDataType dtype, const void* base, int rank,
+               const uint64_t* dims, const uint64_t* strides, const uint32_t* box, bool swizzle128) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t d[5], s[4];
@@ -69,11 +70,17 @@ bool make_tmap_u8(CUtensorMap* m, const void* base, int rank, const uint64_t* di
     if (i < rank - 1) s[i] = strides[i];
   }
   const CUresult r =
-      fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, static_cast<cuuint32_t>(rank), const_cast<void*>(base),
-         d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+      fn(m, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, s, b, e,
+         CU_TENSOR_MAP_INTERLEAVE_NONE,
          swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// Byte tensor map (uint8 elements), 128B swizzle for operand tiles.
+bool make_tmap_u8(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
+                  const uint64_t* strides, const uint32_t* box, bool swizzle128) {
+  return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, base, rank, dims, strides, box, swizzle128);
 }
 
 // ---------------------------------------------------------------------------
@@ -236,6 +243,39 @@ int mx_launch_bn(bool amn, bool bmn, bool f32, const CUtensorMap& ta, const CUte
   }
 }
 
+template <int kFp4, bool kAMN, bool kBMN>
+int mx2_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tsa,
+                 const CUtensorMap& tsb, const bsg::Mx2Params& p, int grid, cudaStream_t st) {
+  using Cfg = bsg::Mx2Cfg<kFp4>;
+  auto* kern = bsg::mx_gemm_2sm_kernel<kFp4, kAMN, kBMN>;
+  if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
+  kern<<<grid, bsg::kMxThreads, Cfg::kSmemBytes, st>>>(ta, tb, tsa, tsb, p);
+  return launch_status();
+}
+
+int mx2_launch(bool fp4, bool amn, bool bmn, const CUtensorMap& ta, const CUtensorMap& tb,
+               const CUtensorMap& tsa, const CUtensorMap& tsb, const bsg::Mx2Params& p, int grid,
+               cudaStream_t st) {
+  if (fp4) return mx2_launch_t<1, false, false>(ta, tb, tsa, tsb, p, grid, st);
+  const int sel = (amn ? 2 : 0) | (bmn ? 1 : 0);
+  switch (sel) {
+    case 0: return mx2_launch_t<0, false, false>(ta, tb, tsa, tsb, p, grid, st);
+    case 1: return mx2_launch_t<0, false, true>(ta, tb, tsa, tsb, p, grid, st);
+    case 2: return mx2_launch_t<0, true, false>(ta, tb, tsa, tsb, p, grid, st);
+    default: return mx2_launch_t<0, true, true>(ta, tb, tsa, tsb, p, grid, st);
+  }
+}
+
+// Scale-atom tensor map: a native scale buffer viewed as [batch][atoms][128 x u32].
+bool make_sf_tmap(CUtensorMap* m, const void* base, long long atoms_per_batch, int batch,
+                  long long batch_stride_bytes, int atoms_per_box) {
+  const uint64_t dims[3] = {128u, static_cast<uint64_t>(atoms_per_batch), static_cast<uint64_t>(batch)};
+  const uint64_t strides[2] = {512u, static_cast<uint64_t>(batch > 1 ? batch_stride_bytes
+                                                                     : atoms_per_batch * 512)};
+  const uint32_t box[3] = {128u, static_cast<uint32_t>(atoms_per_box), 1u};
+  return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, base, 3, dims, strides, box, false);
+}
+
 int splitk_reduce(const float* ws, const bsgemm_args& a, int split, int sms, cudaStream_t st) {
   const long long total4 = static_cast<long long>(a.m) * a.n * a.batch / 4;
   const int grid = static_cast<int>(std::min<long long>((total4 + 255) / 256, 8LL * sms));
@@ -343,6 +383,62 @@ int mx_run(const bsgemm_args* args, bool fp4, cudaStream_t st) {
         return rc;
     sfb = ws + pl.ws_sfa;
     sfb_bs = static_cast<long long>(sfb_nat);
+  }
+
+  // CTA-pair path: enough 256 x 256 tiles to fill the machine, no split-K
+  const long long pair_tiles = static_cast<long long>((a.m + 255) / 256) * ((a.n + 255) / 256) * a.batch;
+  const bool use_pair = a.kernel == BSG_KERNEL_PAIR ||
+                        (a.kernel == BSG_KERNEL_AUTO && pl.split == 1 && a.out_dtype == BSG_OUT_BF16 &&
+                         pair_tiles * 2 >= dev.sms);
+  if (a.kernel == BSG_KERNEL_PAIR && pl.split > 1) return BSG_ERR_UNSUPPORTED;
+  if (use_pair && (sfa_bs % 512 || sfb_bs % 512)) return BSG_ERR_UNSUPPORTED;
+  if (use_pair) {
+    CUtensorMap ta, tb, tsa, tsb;
+    const uint32_t box[3] = {128u, 128u, 1u};
+    {
+      const uint64_t dims[3] = {static_cast<uint64_t>(a_cols), static_cast<uint64_t>(a_rows),
+                                static_cast<uint64_t>(a.batch)};
+      const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_a),
+                                   static_cast<uint64_t>(a.batch > 1 ? a.stride_a_batch
+                                                                     : a_rows * a.stride_a)};
+      if (!make_tmap_u8(&ta, a.ptr_a, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
+    }
+    {
+      const uint64_t dims[3] = {static_cast<uint64_t>(b_cols), static_cast<uint64_t>(b_rows),
+                                static_cast<uint64_t>(a.batch)};
+      const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_b),
+                                   static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch
+                                                                     : b_rows * a.stride_b)};
+      if (!make_tmap_u8(&tb, a.ptr_b, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
+    }
+    const int sf_kb_total = (kg + 3) / 4;
+    const int atoms_k = fp4 ? 2 : 1;
+    if (!make_sf_tmap(&tsa, sfa, static_cast<long long>((a.m + 127) / 128) * sf_kb_total, a.batch, sfa_bs,
+                      atoms_k) ||
+        !make_sf_tmap(&tsb, sfb, static_cast<long long>((a.n + 127) / 128) * sf_kb_total, a.batch, sfb_bs,
+                      atoms_k))
+      return BSG_ERR_CUDA;
+    bsg::Mx2Params q{};
+    q.m = a.m;
+    q.n = a.n;
+    q.k = a.k;
+    q.batch = a.batch;
+    q.num_kb = pl.num_kb;
+    q.tiles_m = (a.m + 255) / 256;
+    q.tiles_n = (a.n + 255) / 256;
+    q.total_units = q.tiles_m * q.tiles_n * a.batch;
+    q.group_m = std::min(q.tiles_m, kGroupM / 2);
+    q.sf_kb_total = sf_kb_total;
+    q.sfa_row_blocks = (a.m + 127) / 128;
+    q.sfb_row_blocks = (a.n + 127) / 128;
+    q.c = a.ptr_c;
+    q.ldc = a.stride_c;
+    q.c_batch_stride = a.stride_c_batch;
+    q.timeout_ns = kTimeoutNs;
+    if (a.out_dtype != BSG_OUT_BF16) return BSG_ERR_UNSUPPORTED;
+    int clusters = std::min(q.total_units, dev.sms / 2);
+    if (a.grid_blocks > 0) clusters = std::min(clusters, std::max(1, a.grid_blocks / 2));
+    return mx2_launch(fp4, !a_km, !b_km, ta, tb, tsa, tsb, q, 2 * clusters, st);
   }
 
   // tensor maps (rank 3: inner, rows, batch)

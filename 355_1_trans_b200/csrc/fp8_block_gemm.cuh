@@ -142,7 +142,9 @@ __global__ void __launch_bounds__(256, 1)
       int dummy = 0;
       mbar_wait(&full_bar[last_stage], last_phase, &dummy, p.timeout_ns);
     }
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1) {
+    // MMA warp: all lanes run the loop, the elected lane issues
+    const bool issuer = elect_one();
     // ------------------------------------------------------------------ MMA issuer
     const uint32_t idesc = idesc_f8f6f4(false, false, 128, BN);
     const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
@@ -174,17 +176,20 @@ __global__ void __launch_bounds__(256, 1)
         for (int t = 0; t < 4; ++t) {
           const uint64_t adesc = make_sdesc(a_addr + 32u * t, 16u, 1024u, kLayoutSW128);
           const uint64_t bdesc = make_sdesc(b_addr + 32u * t, 16u, 1024u, kLayoutSW128);
-          umma_f8f6f4(d, adesc, bdesc, idesc, t > 0 ? 1u : 0u);
+          if (issuer) umma_f8f6f4(d, adesc, bdesc, idesc, t > 0 ? 1u : 0u);
         }
-        tc_commit(&empty_bar[stage]);
-        tc_commit(&acc_full[buf]);
+        if (issuer) {
+          tc_commit(&empty_bar[stage]);
+          tc_commit(&acc_full[buf]);
+        }
+        __syncwarp();
         if (++stage == S) {
           stage = 0;
           phase ^= 1u;
         }
       }
     }
-    tc_commit(drain_bar);
+    if (issuer) tc_commit(drain_bar);
     int dummy = 0;
     mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
   } else if (warp >= 4) {

@@ -14,9 +14,11 @@
 //               tensor maps with L2 cache policies (A evict-last, B
 //               evict-first), scale atoms by plain bulk copies; one mbarrier
 //               per stage carries the transaction bytes;
-//   warp 1      single-thread tcgen05 issuer: scale atoms smem -> TMEM with
-//               tcgen05.cp, then 4 block-scaled MMAs per stage into a
-//               128 x BN fp32 TMEM accumulator; tcgen05.commit frees stages;
+//   warp 1      tcgen05 issuer (whole warp runs the loop, one elected lane
+//               issues): scale atoms smem -> TMEM with tcgen05.cp into one of
+//               two alternating TMEM regions, then 4 block-scaled MMAs per
+//               stage into a 128 x BN fp32 TMEM accumulator; tcgen05.commit
+//               frees stages;
 //   warp 2      TMEM allocator;
 //   warps 4-11  epilogue, two warps per TMEM lane quarter (warp w reads lanes
 //               32*(w%4).., half of the columns each): the bf16 path drains
@@ -55,6 +57,7 @@ struct MxParams {
 
 constexpr int kMxThreads = 384;     // 4 control warps + 8 epilogue warps
 constexpr int kMxEpiThreads = 256;
+constexpr int kMxEpiWarps = 8;      // one tmem_empty arrival per epilogue warp
 
 template <int BN, int kFp4>
 struct MxCfg {
@@ -76,10 +79,14 @@ struct MxCfg {
   static constexpr uint32_t kOffSfb = kOffSfa + kSfaBytes * kStages;
   static constexpr uint32_t kOffBar = kOffSfb + kSfbBytes * kStages;
   static constexpr uint32_t kSmemBytes = kOffBar + 256u + 1024u;  // + alignment slack
-  // TMEM columns: accumulator [0, BN), then SFA (4 per K atom), SFB.
+  // TMEM columns: accumulator [0, BN), then two alternating scale-factor
+  // regions (SFA: 4 columns per K atom, SFB: 4 per K atom and 128 rows), so
+  // the scale copy of stage k+1 never overwrites columns the MMAs of stage k
+  // are still reading.
+  static constexpr uint32_t kSfRegionCols = 4u * kSfAtomsK * (1 + kSfbRowBlocks);
   static constexpr uint32_t kColSfa = BN;
   static constexpr uint32_t kColSfb = BN + 4u * kSfAtomsK;
-  static constexpr uint32_t kColsUsed = kColSfb + 4u * kSfAtomsK * kSfbRowBlocks;
+  static constexpr uint32_t kColsUsed = BN + 2u * kSfRegionCols;
   static constexpr uint32_t kTmemCols = kColsUsed <= 32 ? 32 : kColsUsed <= 64 ? 64
                                         : kColsUsed <= 128 ? 128 : kColsUsed <= 256 ? 256 : 512;
   static constexpr int kHalfCols = BN / 2;   // columns per epilogue warp
@@ -131,7 +138,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       mbar_init(&empty_bar[i], 1);
     }
     mbar_init(tmem_full, 1);
-    mbar_init(tmem_empty, kMxEpiThreads);
+    mbar_init(tmem_empty, kMxEpiWarps);
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -215,7 +222,9 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       int dummy = 0;
       mbar_wait(&full_bar[last_stage], last_phase, &dummy, p.timeout_ns);
     }
-  } else if (warp == 1 && lane == 0) {
+  } else if (warp == 1) {
+    // MMA warp: all lanes run the loop, the elected lane issues
+    const bool issuer = elect_one();
     // ------------------------------------------------------------------ MMA issuer
     constexpr uint32_t kFmt = kFp4 ? 1u : 0u;
     const uint32_t idesc0 = idesc_block_scaled(kFmt, kFmt, kAMN, kBMN, 128, BN);
@@ -231,6 +240,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     int stage = 0;
     uint32_t phase = 0;
     int iter = 0;
+    uint32_t sf_region = 0;   // alternates every stage
     bool ok = true;
     for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x, ++iter) {
       int b, mt, nt, s;
@@ -249,13 +259,15 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           break;
         }
         tc_fence_after();
+        const uint32_t sf_off = sf_region * Cfg::kSfRegionCols;
+        sf_region ^= 1u;
 #pragma unroll
         for (int j = 0; j < Cfg::kSfAtomsK; ++j) {
-          tmem_cp_sf_atom(tmem_base + Cfg::kColSfa + 4u * j,
+          if (issuer) tmem_cp_sf_atom(tmem_base + sf_off + Cfg::kColSfa + 4u * j,
                           sSfa0 + stage * Cfg::kSfaBytes + 512u * j);
 #pragma unroll
           for (int r = 0; r < Cfg::kSfbRowBlocks; ++r)
-            tmem_cp_sf_atom(tmem_base + Cfg::kColSfb + 4u * (j * Cfg::kSfbRowBlocks + r),
+            if (issuer) tmem_cp_sf_atom(tmem_base + sf_off + Cfg::kColSfb + 4u * (j * Cfg::kSfbRowBlocks + r),
                             sSfb0 + stage * Cfg::kSfbBytes + 512u * (r * Cfg::kSfAtomsK + j));
         }
         const uint32_t a_addr = sA0 + stage * Cfg::kABytes;
@@ -267,25 +279,27 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           const uint64_t adesc = make_sdesc(a_addr + t * kKStep, kALbo, kSbo, kLayoutSW128);
           const uint64_t bdesc = make_sdesc(b_addr + t * kKStepB, kBLbo, kSbo, kLayoutSW128);
           const uint32_t idesc = idesc_with_sf_id(idesc0, sf_id, sf_id);
-          const uint32_t tsfa = tmem_base + Cfg::kColSfa + 4u * j;
-          const uint32_t tsfb = tmem_base + Cfg::kColSfb + 4u * j * Cfg::kSfbRowBlocks;
+          const uint32_t tsfa = tmem_base + sf_off + Cfg::kColSfa + 4u * j;
+          const uint32_t tsfb = tmem_base + sf_off + Cfg::kColSfb + 4u * j * Cfg::kSfbRowBlocks;
           const uint32_t acc = (kb > kb0 || t > 0) ? 1u : 0u;
+          if (!issuer) continue;
           if constexpr (kFp4)
             umma_mxf4(tmem_base, adesc, bdesc, idesc, tsfa, tsfb, acc);
           else
             umma_mxf8f6f4(tmem_base, adesc, bdesc, idesc, tsfa, tsfb, acc);
         }
-        tc_commit(&empty_bar[stage]);
+        if (issuer) tc_commit(&empty_bar[stage]);
+        __syncwarp();
         if (++stage == S) {
           stage = 0;
           phase ^= 1u;
         }
       }
       if (!ok) break;
-      tc_commit(tmem_full);
+      if (issuer) tc_commit(tmem_full);
     }
     // drain: wait until every tcgen05 op issued above has completed
-    tc_commit(drain_bar);
+    if (issuer) tc_commit(drain_bar);
     int dummy = 0;
     mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
   } else if (warp >= 4) {
@@ -318,7 +332,8 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           if (row_ok && valid_cols > c * 32) store_row32_f32(dst + c * 32, r, valid_cols - c * 32);
         }
         tc_fence_before();
-        mbar_arrive(tmem_empty);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tmem_empty);
       } else {
         // drain the whole half-row into packed bf16 registers, release the
         // accumulator, then store
@@ -332,7 +347,8 @@ __global__ void __launch_bounds__(kMxThreads, 1)
             w[c * 16 + v] = pack_bf16x2(__uint_as_float(r[2 * v]), __uint_as_float(r[2 * v + 1]));
         }
         tc_fence_before();
-        mbar_arrive(tmem_empty);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tmem_empty);
         if (row_ok && valid_cols > 0) {
           uint16_t* dst = reinterpret_cast<uint16_t*>(p.c) + b * p.c_batch_stride +
                           static_cast<long long>(row) * p.ldc + col_base;

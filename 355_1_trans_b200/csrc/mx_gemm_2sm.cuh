@@ -1,0 +1,313 @@
+// mx_gemm_2sm.cuh -- CTA-pair (tcgen05 cta_group::2) variant of the MXFP8 /
+// MXFP4 block-scaled GEMM: a cluster of two CTAs on two SMs computes one
+// 256 x 256 output tile.
+//
+// Semantics are those of mx_gemm.cuh (reference: mxfp8_gemm/
+// gemm_a8w8_mxfp8_kernel_template.hpp:301-432, mxfp4_gemm_4wave_20261112/
+// candidate_m10/gemm_a4w4_mxfp4_4wave_kernel_template.hpp:384-1169).
+//
+// Why pairs: a 1-CTA 128 x 256 tile has to pull 48 KB of A+B into one SM per
+// 128-K stage.  In a pair each SM loads its own 128 rows of A and its own 128
+// rows (half) of B -- 32 KB per stage -- while the leader's pair-mode MMA
+// (M = 256, N = 256) reads A from each CTA's shared memory for that CTA's rows
+// and B from both, so per-SM load traffic per flop drops by a third and six
+// stages fit in shared memory.
+//
+// Protocol (rank 0 = leader, rank 1 = peer; identical shared-memory layout):
+//   producer (warp 0, both CTAs)  waits its own empty[s]; loads its A half, its
+//       B half, the A scale atoms of its own 128 rows and the B scale atoms of
+//       all 256 columns with the pair form of the TMA load, whose transaction
+//       bytes go to the LEADER's full[s]; the leader arms full[s] with the
+//       bytes of both CTAs;
+//   MMA (warp 1 of the leader)     waits full[s], copies the scale atoms to
+//       TMEM with the pair form of tcgen05.cp (each CTA's shared memory to its
+//       own TMEM, same columns), issues 4 pair MMAs, and commits to empty[s]
+//       of both CTAs (commit with a CTA mask); after the tile it commits to
+//       tmem_full of both CTAs;
+//   epilogue (warps 4-11, both)    wait their own tmem_full, drain their own
+//       TMEM rows (128 x 256 per CTA) into packed bf16 registers, arrive on the
+//       leader's tmem_empty (count 2 x 256), then store.
+// Every wait is bounded (sm100.cuh mbar_wait).
+#pragma once
+
+#include "mx_gemm.cuh"
+
+namespace bsg {
+
+struct Mx2Params {
+  int m, n, k;
+  int batch;
+  int num_kb;                    // 128-byte K stages
+  int tiles_m, tiles_n;          // 256-row / 256-column pair tiles
+  int total_units;               // batch * tiles_m * tiles_n
+  int group_m;
+  int sf_kb_total;               // scale atoms along K per 128-row block
+  int sfa_row_blocks, sfb_row_blocks;
+  void* c;
+  long long ldc;
+  long long c_batch_stride;
+  unsigned long long timeout_ns;
+};
+
+template <int kFp4>
+struct Mx2Cfg {
+  static constexpr int kSfAtomsK = kFp4 ? 2 : 1;
+  static constexpr uint32_t kABytes = 128u * 128u;       // this CTA's 128 rows
+  static constexpr uint32_t kBBytes = 128u * 128u;       // this CTA's half of B
+  static constexpr uint32_t kSfaBytes = 512u * kSfAtomsK;        // this CTA's 128 rows
+  static constexpr uint32_t kSfbBytes = 2u * 512u * kSfAtomsK;   // 256 columns
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+  static constexpr int kStages = static_cast<int>((225u * 1024u - 2048u) / kStageBytes) > 8
+                                     ? 8
+                                     : static_cast<int>((225u * 1024u - 2048u) / kStageBytes);
+  static constexpr uint32_t kOffB = kABytes * kStages;
+  static constexpr uint32_t kOffSfa = kOffB + kBBytes * kStages;
+  static constexpr uint32_t kOffSfb = kOffSfa + kSfaBytes * kStages;
+  static constexpr uint32_t kOffBar = kOffSfb + kSfbBytes * kStages;
+  static constexpr uint32_t kSmemBytes = kOffBar + 256u + 1024u;
+  // two alternating scale-factor regions after the 256 accumulator columns
+  static constexpr uint32_t kSfRegionCols = 12u * kSfAtomsK;
+  static constexpr uint32_t kColSfa = 256u;
+  static constexpr uint32_t kColSfb = 256u + 4u * kSfAtomsK;
+  static constexpr uint32_t kTmemCols = 512u;
+  static_assert(256u + 2u * kSfRegionCols <= 512u, "TMEM overflow");
+  static_assert(kStages >= 3, "pipeline too shallow");
+};
+
+template <int kFp4, bool kAMN, bool kBMN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
+    mx_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const __grid_constant__ CUtensorMap tmSfa,
+                       const __grid_constant__ CUtensorMap tmSfb, const Mx2Params p) {
+  using Cfg = Mx2Cfg<kFp4>;
+  constexpr int S = Cfg::kStages;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~static_cast<uintptr_t>(1023u));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + Cfg::kOffB;
+  uint8_t* sSfa = smem + Cfg::kOffSfa;
+  uint8_t* sSfb = smem + Cfg::kOffSfb;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* tmem_full = empty_bar + S;
+  uint64_t* tmem_empty = tmem_full + 1;
+  uint64_t* drain_bar = tmem_empty + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 32) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    mbar_init(tmem_full, 1);
+    mbar_init(tmem_empty, 2 * kMxEpiWarps);
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(tmem_holder, Cfg::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    prefetch_tmap(&tmSfa);
+    prefetch_tmap(&tmSfb);
+  }
+  tc_fence_before();
+  cluster_sync_all();   // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int cluster_id = static_cast<int>(blockIdx.x >> 1);
+  const int num_clusters = static_cast<int>(gridDim.x >> 1);
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------------ TMA producer (both CTAs)
+    const uint64_t pol_a = l2_policy_evict_last();
+    const uint64_t pol_b = l2_policy_evict_first();
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int u = cluster_id; u < p.total_units && ok; u += num_clusters) {
+      int b, mt, nt, s;
+      decode_unit(u, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
+      // scale atoms that exist at ragged edges: A rows of the leader always,
+      // of the peer only when its 128-row block is inside M; B columns of the
+      // whole 256-column tile, loaded by both CTAs
+      const bool peer_sfa = 2 * mt + 1 < p.sfa_row_blocks;
+      const bool my_sfa = rank == 0 || peer_sfa;
+      const int sfb_rows = min(2, p.sfb_row_blocks - 2 * nt);
+      const uint32_t sf_bytes =
+          (1u + (peer_sfa ? 1u : 0u) + 2u * static_cast<uint32_t>(sfb_rows)) * 512u * Cfg::kSfAtomsK;
+      const uint32_t tx_bytes = 2u * (Cfg::kABytes + Cfg::kBBytes) + sf_bytes;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        const uint32_t fb_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
+        if (leader) mbar_arrive_expect_tx(&full_bar[stage], tx_bytes);
+        uint8_t* a_dst = sA + stage * Cfg::kABytes;
+        uint8_t* b_dst = sB + stage * Cfg::kBBytes;
+        const int kbyte = kb * 128;
+        const int row_a = mt * 256 + static_cast<int>(rank) * 128;
+        const int row_b = nt * 256 + static_cast<int>(rank) * 128;
+        if constexpr (!kAMN)
+          tma_load_3d_pair(a_dst, &tmA, fb_leader, kbyte, row_a, b, pol_a);
+        else
+          tma_load_3d_pair(a_dst, &tmA, fb_leader, row_a, kbyte, b, pol_a);
+        if constexpr (!kBMN)
+          tma_load_3d_pair(b_dst, &tmB, fb_leader, kbyte, row_b, b, pol_b);
+        else
+          tma_load_3d_pair(b_dst, &tmB, fb_leader, row_b, kbyte, b, pol_b);
+        const int atom_k = kb * Cfg::kSfAtomsK;
+        if (my_sfa)
+          tma_load_3d_pair(sSfa + stage * Cfg::kSfaBytes, &tmSfa, fb_leader, 0,
+                           (2 * mt + static_cast<int>(rank)) * p.sf_kb_total + atom_k, b, pol_a);
+        for (int r = 0; r < sfb_rows; ++r)
+          tma_load_3d_pair(sSfb + stage * Cfg::kSfbBytes + r * 512 * Cfg::kSfAtomsK, &tmSfb, fb_leader,
+                           0, (2 * nt + r) * p.sf_kb_total + atom_k, b, pol_b);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1 && leader) {
+    // MMA warp: all lanes run the loop, the elected lane issues
+    const bool issuer = elect_one();
+    // ------------------------------------------------------------------ MMA issuer (leader)
+    constexpr uint32_t kFmt = kFp4 ? 1u : 0u;
+    const uint32_t idesc0 = idesc_block_scaled(kFmt, kFmt, kAMN, kBMN, 256, 256);
+    constexpr uint32_t kALbo = kAMN ? 128u * 128u : 16u;
+    constexpr uint32_t kBLbo = kBMN ? 128u * 128u : 16u;
+    constexpr uint32_t kSbo = 1024u;
+    constexpr uint32_t kKStep = kAMN ? 32u * 128u : 32u;
+    constexpr uint32_t kKStepB = kBMN ? 32u * 128u : 32u;
+    const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
+    const uint32_t sSfa0 = smem_u32(sSfa), sSfb0 = smem_u32(sSfb);
+    int stage = 0;
+    uint32_t phase = 0;
+    int iter = 0;
+    uint32_t sf_region = 0;   // alternates every stage
+    bool ok = true;
+    for (int u = cluster_id; u < p.total_units && ok; u += num_clusters, ++iter) {
+      if (!mbar_wait_cluster(tmem_empty, (static_cast<uint32_t>(iter) & 1u) ^ 1u, abort_flag,
+                             p.timeout_ns)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sf_off = sf_region * Cfg::kSfRegionCols;
+        sf_region ^= 1u;
+#pragma unroll
+        for (int j = 0; j < Cfg::kSfAtomsK; ++j) {
+          // A scales: 4 columns per K atom (each CTA's own rows)
+          if (issuer) tmem_cp_sf_atom_pair(tmem_base + sf_off + Cfg::kColSfa + 4u * j,
+                               sSfa0 + stage * Cfg::kSfaBytes + 512u * j);
+          // B scales: 8 columns per K atom (all 256 columns, in both CTAs)
+#pragma unroll
+          for (int r = 0; r < 2; ++r)
+            if (issuer) tmem_cp_sf_atom_pair(tmem_base + sf_off + Cfg::kColSfb + 4u * (j * 2 + r),
+                                 sSfb0 + stage * Cfg::kSfbBytes + 512u * (r * Cfg::kSfAtomsK + j));
+        }
+        const uint32_t a_addr = sA0 + stage * Cfg::kABytes;
+        const uint32_t b_addr = sB0 + stage * Cfg::kBBytes;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const uint32_t j = kFp4 ? static_cast<uint32_t>(t >> 1) : 0u;
+          const uint32_t sf_id = kFp4 ? static_cast<uint32_t>((t & 1) * 2) : static_cast<uint32_t>(t);
+          const uint64_t adesc = make_sdesc(a_addr + t * kKStep, kALbo, kSbo, kLayoutSW128);
+          const uint64_t bdesc = make_sdesc(b_addr + t * kKStepB, kBLbo, kSbo, kLayoutSW128);
+          const uint32_t idesc = idesc_with_sf_id(idesc0, sf_id, sf_id);
+          const uint32_t tsfa = tmem_base + sf_off + Cfg::kColSfa + 4u * j;
+          const uint32_t tsfb = tmem_base + sf_off + Cfg::kColSfb + 8u * j;
+          const uint32_t acc = (kb > 0 || t > 0) ? 1u : 0u;
+          if (!issuer) continue;
+          if constexpr (kFp4)
+            umma_mxf4_pair(tmem_base, adesc, bdesc, idesc, tsfa, tsfb, acc);
+          else
+            umma_mxf8f6f4_pair(tmem_base, adesc, bdesc, idesc, tsfa, tsfb, acc);
+        }
+        if (issuer) tc_commit_pair(&empty_bar[stage], 0x3);
+        __syncwarp();
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (issuer) tc_commit_pair(tmem_full, 0x3);
+    }
+    if (issuer) tc_commit_pair(drain_bar, 0x1);
+    int dummy = 0;
+    mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const int half = (warp - 4) >> 2;
+    const uint32_t t_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                            static_cast<uint32_t>(half * 128);
+    const uint32_t te_leader = mapa_shared(smem_u32(tmem_empty), 0);
+    int iter = 0;
+    for (int u = cluster_id; u < p.total_units; u += num_clusters, ++iter) {
+      int b, mt, nt, s;
+      decode_unit(u, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
+      if (!mbar_wait(tmem_full, static_cast<uint32_t>(iter) & 1u, abort_flag, p.timeout_ns)) break;
+      tc_fence_after();
+      const int row = mt * 256 + static_cast<int>(rank) * 128 + q * 32 + static_cast<int>(lane);
+      const int col_base = nt * 256 + half * 128;
+      const int valid_cols = p.n - col_base;
+      uint32_t w[64];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_base + static_cast<uint32_t>(c * 32), r);
+#pragma unroll
+        for (int v = 0; v < 16; ++v)
+          w[c * 16 + v] = pack_bf16x2(__uint_as_float(r[2 * v]), __uint_as_float(r[2 * v + 1]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(te_leader);
+      if (row < p.m && valid_cols > 0) {
+        uint16_t* dst = reinterpret_cast<uint16_t*>(p.c) + b * p.c_batch_stride +
+                        static_cast<long long>(row) * p.ldc + col_base;
+        if (valid_cols >= 128) {
+#pragma unroll
+          for (int v = 0; v < 16; ++v)
+            st_global_cs_v4(dst + 8 * v, w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+        } else {
+#pragma unroll
+          for (int v = 0; v < 64; ++v) {
+            if (2 * v < valid_cols) dst[2 * v] = static_cast<uint16_t>(w[v] & 0xFFFFu);
+            if (2 * v + 1 < valid_cols) dst[2 * v + 1] = static_cast<uint16_t>(w[v] >> 16);
+          }
+        }
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();   // both CTAs done with TMEM, barriers and remote arrives
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+}
+
+}  // namespace bsg

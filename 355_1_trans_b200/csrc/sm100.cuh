@@ -1,6 +1,7 @@
 // sm100.cuh -- thin inline-PTX layer for sm_100a: mbarriers with bounded
-// waits, TMA (tiled tensor and plain bulk copies, no cluster multicast),
-// tcgen05 TMEM allocation / copies / loads, and the block-scaled UMMA issue.
+// waits, TMA loads (tiled tensor and plain bulk copies, each CTA loading only
+// into its own shared memory), tcgen05 TMEM allocation / copies / loads, the
+// block-scaled UMMA issue, and the CTA-pair (cta_group::2) forms.
 //
 // Descriptor bit layouts follow the PTX ISA for tcgen05 (shared-memory matrix
 // descriptor, instruction descriptor for .kind::f8f6f4 / .kind::mxf8f6f4 /
@@ -29,6 +30,19 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+// One lane of a fully converged warp (the lowest active lane).  The MMA warps
+// run their loops on all 32 lanes -- so barrier waits and descriptor
+// arithmetic stay warp-uniform -- and only the elected lane issues tcgen05
+// instructions; issuing from a lane-divergent single-thread loop costs tens
+// of cycles per instruction more.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
 }
 
 __device__ __forceinline__ uint32_t lane_id() {
@@ -81,6 +95,59 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1; it < 0x7fffffffu; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0u) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > timeout_ns) break;
+    }
+  }
+  *abort_flag = 1;
+  atomicCAS(&g_bsg_device_error, 0, kDevErrTimeout);
+  return false;
+}
+
+// ---------------------------------------------------------------------------
+// clusters of two CTAs (CTA pairs for cta_group::2)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+// Whole-cluster barrier; every thread of both CTAs must execute it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+// Arrive on an mbarrier given by its cluster address (possibly the peer's).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// Bounded wait with cluster-scope acquire (for barriers that threads of the
+// peer CTA arrive at).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  volatile int* abort_flag, uint64_t timeout_ns) {
+  if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1; it < 0x7fffffffu; ++it) {
+    if (mbar_try_wait_acq_cluster(bar, parity)) return true;
     if ((it & 255u) == 0u) {
       if (*abort_flag) return false;
       if (globaltimer_ns() - t0 > timeout_ns) break;
@@ -158,6 +225,18 @@ __device__ __forceinline__ void tma_load_4d_hint(void* dst, const CUtensorMap* m
       : "memory");
 }
 
+// CTA-pair form: the data lands in the executing CTA's shared memory, the
+// transaction bytes are reported to the mbarrier at cluster address
+// `bar_cluster` (the pair leader's barrier).
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* m, uint32_t bar_cluster,
+                                                 int c0, int c1, int c2, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2), "r"(bar_cluster), "l"(policy)
+      : "memory");
+}
+
 // Plain (untiled) bulk copy global -> shared; both addresses 16-byte aligned,
 // bytes a multiple of 16.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
@@ -197,6 +276,30 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    smem_u32(bar))
                : "memory");
+}
+
+// CTA-pair TMEM allocation: issued by the same warp in both CTAs of the pair.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+// Arrive once, on the barrier at this shared-memory offset in every CTA of
+// cta_mask, when all pair-mode tcgen05 ops issued so far have completed.
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
 }
 
 // Shared-memory matrix descriptor (sm_100 version 1).
@@ -273,6 +376,36 @@ __device__ __forceinline__ void umma_f8f6f4(uint32_t tmem_d, uint64_t adesc, uin
       "}" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+__device__ __forceinline__ void umma_mxf8f6f4_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                                   uint32_t idesc, uint32_t tmem_sfa,
+                                                   uint32_t tmem_sfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t"
+      "}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tmem_sfa), "r"(tmem_sfb)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_mxf4_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                               uint32_t idesc, uint32_t tmem_sfa, uint32_t tmem_sfb,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t"
+      "}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tmem_sfa), "r"(tmem_sfb)
+      : "memory");
+}
+
+// Pair form of the scale-atom copy, issued by the pair leader.
+__device__ __forceinline__ void tmem_cp_sf_atom_pair(uint32_t taddr, uint32_t smem_addr) {
+  const uint64_t d = make_sdesc(smem_addr, 0, 128, kLayoutNone);
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(d) : "memory");
 }
 
 // Copy one 512-byte scale atom (32 rows of 128 bits, core matrices of 8x16B)

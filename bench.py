@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="mxfp8", choices=["mxfp8", "mxfp4", "fp8block"])
     ap.add_argument("--layout", default="tn", choices=["tn", "nn", "tt", "nt"])
+    ap.add_argument("--kernel", default="auto", choices=["auto", "1cta", "pair"],
+                    help="MX kernel: auto, single-CTA tiles or CTA pairs (cta_group::2)")
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=8192, help="per-rank N")
     ap.add_argument("--k", type=int, default=8192)
@@ -309,11 +311,12 @@ def run_ours(args):
         sb_n = bs.pack_scales(sb)
         out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
         if fp4:
-            call = lambda: bs.gemm_a4w4_mxfp4(qa, qb, sa_n, sb_n, out=out, scale_format="native")
+            call = lambda: bs.gemm_a4w4_mxfp4(qa, qb, sa_n, sb_n, out=out, scale_format="native",
+                                              kernel=args.kernel)
             a_bytes, b_bytes = m * k // 2, n * k // 2
         else:
             call = lambda: bs.gemm_a8w8_mxfp8(qa, qb, sa_n, sb_n, layout=args.layout, out=out,
-                                              scale_format="native")
+                                              scale_format="native", kernel=args.kernel)
             a_bytes, b_bytes = m * k, n * k
         sf_bytes = (m + n) * k // 32
     else:

@@ -26,7 +26,7 @@ def poisoned(shape, dtype, device):
 
 
 def run_mxfp8(bs, orc, cuda, m, n, k, *, seed=1, layout="tn", sf_mode="data", out_dtype=torch.bfloat16,
-              split_k=0, grid_blocks=0, batch=1, native=False):
+              split_k=0, grid_blocks=0, batch=1, native=False, kernel="auto"):
     qa_l, qb_l, sa_l, sb_l = mxfp8_problem(orc, m, n, k, seed, sf_mode, batch)
     res = [orc.gemm_mxfp8(qa, qb, sa, sb, f64=True) for qa, qb, sa, sb in zip(qa_l, qb_l, sa_l, sb_l)]
     refs, mags = [r[0] for r in res], [r[1] for r in res]
@@ -43,7 +43,7 @@ def run_mxfp8(bs, orc, cuda, m, n, k, *, seed=1, layout="tn", sf_mode="data", ou
         fmt = "native"
     out = poisoned((m, n) if batch == 1 else (batch, m, n), out_dtype, cuda)
     bs.gemm_a8w8_mxfp8(A, B, SA, SB, layout=layout, out_dtype=out_dtype, out=out, scale_format=fmt,
-                       split_k=split_k, grid_blocks=grid_blocks)
+                       split_k=split_k, grid_blocks=grid_blocks, kernel=kernel)
     torch.cuda.synchronize()
     assert bs.check_device_error() == 0
     got = out.float().cpu().numpy()
@@ -108,15 +108,37 @@ def test_mxfp8_persistent_grid(bs, orc, cuda, grid_blocks):
     run_mxfp8(bs, orc, cuda, 512, 512, 256, seed=10, grid_blocks=grid_blocks)
 
 
+# ---- CTA-pair (cta_group::2) kernel -----------------------------------------------------
+
+@pytest.mark.parametrize("layout", ["tn", "nn", "tt", "nt"])
+def test_mxfp8_pair_layouts(bs, orc, cuda, layout):
+    run_mxfp8(bs, orc, cuda, 512, 512, 512, seed=31, layout=layout, sf_mode="kpattern", kernel="pair")
+
+
+def test_mxfp8_pair_ragged_batched(bs, orc, cuda):
+    run_mxfp8(bs, orc, cuda, 300, 392, 384, seed=32, sf_mode="rowpattern", kernel="pair")
+    run_mxfp8(bs, orc, cuda, 256, 256, 256, seed=33, batch=2, kernel="pair")
+
+
+def test_mxfp8_pair_native_and_grid(bs, orc, cuda):
+    run_mxfp8(bs, orc, cuda, 768, 512, 256, seed=34, native=True, kernel="pair", grid_blocks=2)
+
+
+def test_mxfp4_pair(bs, orc, cuda):
+    run_mxfp4(bs, orc, cuda, 512, 512, 1024, seed=35, sf_mode="kpattern", kernel="pair")
+    run_mxfp4(bs, orc, cuda, 260, 264, 512, seed=36, sf_mode="rowpattern", kernel="pair")
+
+
 # ---- MXFP4 ---------------------------------------------------------------------------
 
 def run_mxfp4(bs, orc, cuda, m, n, k, *, seed=1, sf_mode="data", split_k=0, out_dtype=torch.bfloat16,
-              grid_blocks=0):
+              grid_blocks=0, kernel="auto"):
     qa, qb, sa, sb = mxfp4_problem(orc, m, n, k, seed, sf_mode)
     ref, mag = orc.gemm_mxfp4(qa, qb, sa, sb)
     out = poisoned((m, n), out_dtype, cuda)
     bs.gemm_a4w4_mxfp4(dev_u8(qa, cuda), dev_u8(qb, cuda), dev_u8(sa, cuda), dev_u8(sb, cuda),
-                       out=out, out_dtype=out_dtype, split_k=split_k, grid_blocks=grid_blocks)
+                       out=out, out_dtype=out_dtype, split_k=split_k, grid_blocks=grid_blocks,
+                       kernel=kernel)
     torch.cuda.synchronize()
     assert bs.check_device_error() == 0
     got = out.float().cpu().numpy()
@@ -244,8 +266,8 @@ def test_bounded_wait_reports_timeout(bs, cuda):
 
 # ---- full size (row sample) ----------------------------------------------------------
 
-@pytest.mark.parametrize("layout", ["tn", "nt"])
-def test_mxfp8_8192_row_sample(bs, orc, cuda, layout):
+@pytest.mark.parametrize("layout,kernel", [("tn", "auto"), ("nt", "auto"), ("tn", "1cta")])
+def test_mxfp8_8192_row_sample(bs, orc, cuda, layout, kernel):
     """BASELINE config 3 at full size: every output row is produced by the GPU;
     64 sampled rows are checked against the oracle."""
     m = n = k = 8192
@@ -255,7 +277,7 @@ def test_mxfp8_8192_row_sample(bs, orc, cuda, layout):
     qb, sb = orc.quant_mxfp8(w)
     A = dev_u8(qa if layout[0] == "t" else np.ascontiguousarray(qa.T), cuda).view(torch.float8_e4m3fn)
     B = dev_u8(qb if layout[1] == "n" else np.ascontiguousarray(qb.T), cuda).view(torch.float8_e4m3fn)
-    out = bs.gemm_a8w8_mxfp8(A, B, dev_u8(sa, cuda), dev_u8(sb, cuda), layout=layout)
+    out = bs.gemm_a8w8_mxfp8(A, B, dev_u8(sa, cuda), dev_u8(sb, cuda), layout=layout, kernel=kernel)
     torch.cuda.synchronize()
     assert bs.check_device_error() == 0
     rows = np.random.default_rng(0).choice(m, 64, replace=False)
