@@ -106,7 +106,9 @@ __global__ void __launch_bounds__(256, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
-  if (warp == 0 && lane == 0) {
+  if (warp == 0) {
+    // producer warp: all lanes run the loop, the elected lane issues the copies
+    const bool issuer = elect_one();
     // ------------------------------------------------------------------ TMA producer
     int stage = 0;
     uint32_t phase = 0;
@@ -124,12 +126,15 @@ __global__ void __launch_bounds__(256, 1)
           break;
         }
         uint64_t* fb = &full_bar[stage];
-        mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
-        tma_load_3d(sA + stage * Cfg::kABytes, &tmA, fb, kb * 128, mt * 128, b);
-        if constexpr (kKPanel)
-          tma_load_4d(sB + stage * Cfg::kBBytes, &tmB, fb, 0, nt * BN, kb, b);
-        else
-          tma_load_3d(sB + stage * Cfg::kBBytes, &tmB, fb, kb * 128, nt * BN, b);
+        if (issuer) {
+          mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
+          tma_load_3d(sA + stage * Cfg::kABytes, &tmA, fb, kb * 128, mt * 128, b);
+          if constexpr (kKPanel)
+            tma_load_4d(sB + stage * Cfg::kBBytes, &tmB, fb, 0, nt * BN, kb, b);
+          else
+            tma_load_3d(sB + stage * Cfg::kBBytes, &tmB, fb, kb * 128, nt * BN, b);
+        }
+        __syncwarp();
         last_stage = stage;
         last_phase = phase;
         if (++stage == S) {

@@ -156,7 +156,9 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
-  if (warp == 0 && lane == 0) {
+  if (warp == 0) {
+    // producer warp: all lanes run the loop, the elected lane issues the copies
+    const bool issuer = elect_one();
     // ------------------------------------------------------------------ TMA producer
     const uint64_t pol_a = l2_policy_evict_last();
     const uint64_t pol_b = l2_policy_evict_first();
@@ -185,30 +187,33 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           break;
         }
         uint64_t* fb = &full_bar[stage];
-        mbar_arrive_expect_tx(fb, tx_bytes);
+        if (issuer) mbar_arrive_expect_tx(fb, tx_bytes);
         uint8_t* a_dst = sA + stage * Cfg::kABytes;
         uint8_t* b_dst = sB + stage * Cfg::kBBytes;
         const int kbyte = kb * 128;
-        if constexpr (!kAMN) {
-          tma_load_3d_hint(a_dst, &tmA, fb, kbyte, mt * 128, b, pol_a);
-        } else {
-          tma_load_3d_hint(a_dst, &tmA, fb, mt * 128, kbyte, b, pol_a);
-        }
-        if constexpr (!kBMN) {
-          tma_load_3d_hint(b_dst, &tmB, fb, kbyte, nt * BN, b, pol_b);
-        } else {
+        if (issuer) {
+          if constexpr (!kAMN) {
+            tma_load_3d_hint(a_dst, &tmA, fb, kbyte, mt * 128, b, pol_a);
+          } else {
+            tma_load_3d_hint(a_dst, &tmA, fb, mt * 128, kbyte, b, pol_a);
+          }
+          if constexpr (!kBMN) {
+            tma_load_3d_hint(b_dst, &tmB, fb, kbyte, nt * BN, b, pol_b);
+          } else {
 #pragma unroll
-          for (int j = 0; j < BN / 128; ++j)
-            tma_load_3d_hint(b_dst + j * 16384, &tmB, fb, nt * BN + j * 128, kbyte, b, pol_b);
-        }
-        const long long atom_k = static_cast<long long>(kb) * Cfg::kSfAtomsK;
-        bulk_load(sSfa + stage * Cfg::kSfaBytes, sfa_tile + atom_k * 512, Cfg::kSfaBytes, fb);
+            for (int j = 0; j < BN / 128; ++j)
+              tma_load_3d_hint(b_dst + j * 16384, &tmB, fb, nt * BN + j * 128, kbyte, b, pol_b);
+          }
+          const long long atom_k = static_cast<long long>(kb) * Cfg::kSfAtomsK;
+          bulk_load(sSfa + stage * Cfg::kSfaBytes, sfa_tile + atom_k * 512, Cfg::kSfaBytes, fb);
 #pragma unroll
-        for (int r = 0; r < Cfg::kSfbRowBlocks; ++r)
-          if (r < sfb_rows)
-            bulk_load(sSfb + stage * Cfg::kSfbBytes + r * 512 * Cfg::kSfAtomsK,
-                      sfb_tile + (static_cast<long long>(r) * p.sf_kb_total + atom_k) * 512,
-                      512u * Cfg::kSfAtomsK, fb);
+          for (int r = 0; r < Cfg::kSfbRowBlocks; ++r)
+            if (r < sfb_rows)
+              bulk_load(sSfb + stage * Cfg::kSfbBytes + r * 512 * Cfg::kSfAtomsK,
+                        sfb_tile + (static_cast<long long>(r) * p.sf_kb_total + atom_k) * 512,
+                        512u * Cfg::kSfAtomsK, fb);
+        }
+        __syncwarp();
         last_stage = stage;
         last_phase = phase;
         if (++stage == S) {

@@ -130,7 +130,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
   const int cluster_id = static_cast<int>(blockIdx.x >> 1);
   const int num_clusters = static_cast<int>(gridDim.x >> 1);
 
-  if (warp == 0 && lane == 0) {
+  if (warp == 0) {
+    // producer warp: all lanes run the loop, the elected lane issues the copies
+    const bool issuer = elect_one();
     // ------------------------------------------------------------------ TMA producer (both CTAs)
     const uint64_t pol_a = l2_policy_evict_last();
     const uint64_t pol_b = l2_policy_evict_first();
@@ -155,27 +157,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
           break;
         }
         const uint32_t fb_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
-        if (leader) mbar_arrive_expect_tx(&full_bar[stage], tx_bytes);
+        if (leader && issuer) mbar_arrive_expect_tx(&full_bar[stage], tx_bytes);
         uint8_t* a_dst = sA + stage * Cfg::kABytes;
         uint8_t* b_dst = sB + stage * Cfg::kBBytes;
         const int kbyte = kb * 128;
         const int row_a = mt * 256 + static_cast<int>(rank) * 128;
         const int row_b = nt * 256 + static_cast<int>(rank) * 128;
-        if constexpr (!kAMN)
-          tma_load_3d_pair(a_dst, &tmA, fb_leader, kbyte, row_a, b, pol_a);
-        else
-          tma_load_3d_pair(a_dst, &tmA, fb_leader, row_a, kbyte, b, pol_a);
-        if constexpr (!kBMN)
-          tma_load_3d_pair(b_dst, &tmB, fb_leader, kbyte, row_b, b, pol_b);
-        else
-          tma_load_3d_pair(b_dst, &tmB, fb_leader, row_b, kbyte, b, pol_b);
-        const int atom_k = kb * Cfg::kSfAtomsK;
-        if (my_sfa)
-          tma_load_3d_pair(sSfa + stage * Cfg::kSfaBytes, &tmSfa, fb_leader, 0,
-                           (2 * mt + static_cast<int>(rank)) * p.sf_kb_total + atom_k, b, pol_a);
-        for (int r = 0; r < sfb_rows; ++r)
-          tma_load_3d_pair(sSfb + stage * Cfg::kSfbBytes + r * 512 * Cfg::kSfAtomsK, &tmSfb, fb_leader,
-                           0, (2 * nt + r) * p.sf_kb_total + atom_k, b, pol_b);
+        if (issuer) {
+          if constexpr (!kAMN)
+            tma_load_3d_pair(a_dst, &tmA, fb_leader, kbyte, row_a, b, pol_a);
+          else
+            tma_load_3d_pair(a_dst, &tmA, fb_leader, row_a, kbyte, b, pol_a);
+          if constexpr (!kBMN)
+            tma_load_3d_pair(b_dst, &tmB, fb_leader, kbyte, row_b, b, pol_b);
+          else
+            tma_load_3d_pair(b_dst, &tmB, fb_leader, row_b, kbyte, b, pol_b);
+          const int atom_k = kb * Cfg::kSfAtomsK;
+          if (my_sfa)
+            tma_load_3d_pair(sSfa + stage * Cfg::kSfaBytes, &tmSfa, fb_leader, 0,
+                             (2 * mt + static_cast<int>(rank)) * p.sf_kb_total + atom_k, b, pol_a);
+          for (int r = 0; r < sfb_rows; ++r)
+            tma_load_3d_pair(sSfb + stage * Cfg::kSfbBytes + r * 512 * Cfg::kSfAtomsK, &tmSfb, fb_leader,
+                             0, (2 * nt + r) * p.sf_kb_total + atom_k, b, pol_b);
+        }
+        __syncwarp();
         if (++stage == S) {
           stage = 0;
           phase ^= 1u;
