@@ -29,7 +29,7 @@ LAYOUTS = {"nt": 0, "tt": 1, "nn": 2, "tn": 3}
 B_RAW, B_KPANEL128, B_SHUFFLE16 = 0, 1, 2
 SF_NATIVE, SF_ROWMAJOR, SF_KMAJOR_T, SF_E8M0_SHUFFLE = 0, 1, 2, 3
 OUT_BF16, OUT_FP32 = 0, 1
-KERNELS = {"auto": 0, "1cta": 1, "pair": 2}
+KERNELS = {"auto": 0, "1cta": 1, "pair": 2, "swap": 3}
 FAMILY_MXFP8, FAMILY_MXFP4, FAMILY_FP8_BLOCK = 0, 1, 2
 
 
@@ -257,7 +257,8 @@ def _mx(A, B, A_scale, B_scale, *, fp4, layout, out_dtype, out, scale_format, sp
 
 def gemm_a8w8_bpreshuffle(A, B, x_scale, w_scale, out_dtype=torch.bfloat16, *,
                           preshuffled: bool = True, x_scale_transposed: bool = False,
-                          out=None, split_k: int = 0, workspace=None, grid_blocks: int = 0):
+                          out=None, split_k: int = 0, workspace=None, grid_blocks: int = 0,
+                          kernel: str = "auto"):
     """a8w8 GEMM with fp32 1x128 (x_scale [M,K/128]) and 128x128
     (w_scale [N/128,K/128]) block scales, bf16/fp32 out.
 
@@ -265,7 +266,8 @@ def gemm_a8w8_bpreshuffle(A, B, x_scale, w_scale, out_dtype=torch.bfloat16, *,
     [K/128, N, 128] or flat [N, K] tensor), as aiter's wrapper produces
     (opus_a8w8_bpreshuffle_integration_and_benchmark.md:76-81);
     preshuffled=False: B is plain [N, K].  x_scale_transposed=True takes the
-    reference kernel's [K/128, M] SFA layout.
+    reference kernel's [K/128, M] SFA layout.  kernel: "auto", "1cta" (128x128
+    output tiles) or "swap" (transposed decode kernel, M <= 64).
     """
     if A.dim() != 2:
         raise ValueError("A must be [M, K]")
@@ -315,6 +317,7 @@ def gemm_a8w8_bpreshuffle(A, B, x_scale, w_scale, out_dtype=torch.bfloat16, *,
     args.out_dtype = OUT_BF16 if out_dtype == torch.bfloat16 else OUT_FP32
     args.split_k = split_k
     args.grid_blocks = grid_blocks
+    args.kernel = KERNELS[kernel]
     ws = _workspace(FAMILY_FP8_BLOCK, args, workspace, A.device)
     with torch.cuda.device(A.device):
         status = lib().bsgemm_a8w8_blockscale_bpreshuffle(ctypes.byref(args), _stream(A.device))

@@ -17,6 +17,7 @@
 
 #include "../../include/bsgemm_b200.h"
 #include "fp8_block_gemm.cuh"
+#include "fp8_block_swap.cuh"
 #include "mx_gemm.cuh"
 #include "mx_gemm_2sm.cuh"
 #include "pack.cuh"
@@ -147,15 +148,37 @@ struct Plan {
   size_t ws_partials = 0;       // bytes of fp32 partials
 };
 
-void plan_split(Plan& pl, const bsgemm_args& a, int sms, bool allow_auto) {
+// Split-K choice for a persistent grid of `sms` CTAs: the wall time is set by
+// the busiest CTA, i.e. ceil(tiles * split / sms) rounds of ceil(num_kb /
+// split) K stages, plus the fp32 partials every split writes and the reduce
+// reads back (expressed in K-stage units: `partial_cost` per extra slice).
+// Take the smallest split within 3 % of the best cost, at least 4 K stages
+// per slice.
+int balanced_split(long long tiles, int num_kb, int sms, int max_split, double partial_cost) {
+  if (tiles >= sms || num_kb < 8) return 1;
+  double best = -1.0;
+  double cost[65];
+  const int smax = std::max(1, std::min(std::min(max_split, 64), num_kb / 4));
+  for (int s = 1; s <= smax; ++s) {
+    const long long rounds = (tiles * s + sms - 1) / sms;
+    cost[s] = static_cast<double>(rounds * ((num_kb + s - 1) / s)) + (s > 1 ? partial_cost * s : 0.0);
+    if (best < 0.0 || cost[s] < best) best = cost[s];
+  }
+  for (int s = 1; s <= smax; ++s)
+    if (cost[s] <= best * 1.03) return s;
+  return 1;
+}
+
+// bytes_per_kb: bytes one CTA streams per K stage (the cost unit).
+void plan_split(Plan& pl, const bsgemm_args& a, int sms, bool allow_auto, double bytes_per_kb) {
   const long long tiles = static_cast<long long>(pl.tiles_m) * pl.tiles_n * a.batch;
   int split = 1;
   if (a.split_k > 1) {
     split = a.split_k;
-  } else if (a.split_k == 0 && allow_auto && tiles * 2 <= sms && pl.num_kb >= 8) {
-    // fill the machine, keep >= 4 K stages per slice
-    split = static_cast<int>(std::min<long long>(sms / tiles, pl.num_kb / 4));
-    split = std::max(1, std::min(split, 32));
+  } else if (a.split_k == 0 && allow_auto) {
+    // each slice adds an fp32 M x N write and read, spread over all SMs
+    const double partial = 8.0 * a.m * a.n * a.batch / (static_cast<double>(sms) * bytes_per_kb);
+    split = balanced_split(tiles, pl.num_kb, sms, 64, partial);
   }
   split = std::min(split, pl.num_kb);
   pl.kb_per = (pl.num_kb + split - 1) / split;
@@ -184,7 +207,7 @@ int mx_plan(const bsgemm_args& a, bool fp4, const DevInfo& dev, MxPlan& pl, bool
   if (static_cast<long long>(pl.tiles_m) * ((a.n + 255) / 256) * a.batch < dev.sms / 2 || a.n <= 128)
     pl.bn = 128;
   pl.tiles_n = (a.n + pl.bn - 1) / pl.bn;
-  plan_split(pl, a, dev.sms, allow_auto);
+  plan_split(pl, a, dev.sms, allow_auto, 128.0 * (128 + pl.bn));
   pl.ws_sfa = a.sfa_format == BSG_SF_ROWMAJOR ? align256(native_sf_bytes(a.m, kg) * a.batch) : 0;
   pl.ws_sfb = a.sfb_format == BSG_SF_ROWMAJOR ? align256(native_sf_bytes(a.n, kg) * a.batch) : 0;
   return BSG_OK;
@@ -508,12 +531,45 @@ int fp8b_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockPa
   return launch_status();
 }
 
+// Rows of A per transposed-kernel tile (the MMA's N side): 16, 32 or 64.
+int swap_mn(int m) { return m <= 16 ? 16 : m <= 32 ? 32 : 64; }
+
+bool fp8b_use_swap(const bsgemm_args& a) {
+  return a.kernel == BSG_KERNEL_SWAP || (a.kernel == BSG_KERNEL_AUTO && a.m <= 64);
+}
+
 void fp8b_plan(const bsgemm_args& a, const DevInfo& dev, Plan& pl, bool allow_auto) {
-  pl.bn = 128;
-  pl.tiles_m = (a.m + 127) / 128;
-  pl.tiles_n = (a.n + 127) / 128;
   pl.num_kb = a.k / 128;
-  plan_split(pl, a, dev.sms, allow_auto);
+  pl.tiles_n = (a.n + 127) / 128;
+  if (fp8b_use_swap(a)) {
+    const int mn = swap_mn(a.m);
+    pl.bn = mn;
+    pl.tiles_m = (a.m + mn - 1) / mn;
+    plan_split(pl, a, dev.sms, allow_auto, 16384.0 + 128.0 * mn);
+  } else {
+    pl.bn = 128;
+    pl.tiles_m = (a.m + 127) / 128;
+    plan_split(pl, a, dev.sms, allow_auto, 32768.0);
+  }
+}
+
+template <int MN, bool kKPanel, bool kOutF32>
+int swap_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockParams& p, int grid,
+                  cudaStream_t st) {
+  using Cfg = bsg::SwapCfg<MN>;
+  auto* kern = bsg::fp8_block_swap_kernel<MN, kKPanel, kOutF32>;
+  if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
+  kern<<<grid, 256, Cfg::kSmemBytes, st>>>(ta, tb, p);
+  return launch_status();
+}
+
+template <int MN>
+int swap_launch_mn(bool kpanel, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
+                   const Fp8BlockParams& p, int grid, cudaStream_t st) {
+  return kpanel ? (f32 ? swap_launch_t<MN, true, true>(ta, tb, p, grid, st)
+                       : swap_launch_t<MN, true, false>(ta, tb, p, grid, st))
+                : (f32 ? swap_launch_t<MN, false, true>(ta, tb, p, grid, st)
+                       : swap_launch_t<MN, false, false>(ta, tb, p, grid, st));
 }
 
 int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
@@ -526,6 +582,8 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
   if (a.k % 128) return BSG_ERR_INVALID_VALUE;
   if (a.layout != BSG_LAYOUT_TN) return BSG_ERR_UNSUPPORTED;
   if (a.b_format != BSG_B_RAW && a.b_format != BSG_B_KPANEL128) return BSG_ERR_UNSUPPORTED;
+  if (a.kernel == BSG_KERNEL_SWAP && a.m > 64) return BSG_ERR_UNSUPPORTED;
+  if (a.kernel == BSG_KERNEL_PAIR) return BSG_ERR_UNSUPPORTED;
   if (a.sfa_format != BSG_SF_ROWMAJOR && a.sfa_format != BSG_SF_KMAJOR_T) return BSG_ERR_UNSUPPORTED;
   if (a.sfb_format != BSG_SF_ROWMAJOR) return BSG_ERR_UNSUPPORTED;
   const bool kpanel = a.b_format == BSG_B_KPANEL128;
@@ -585,7 +643,8 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
     const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_a),
                                  static_cast<uint64_t>(a.batch > 1 ? a.stride_a_batch
                                                                    : static_cast<long long>(a.m) * a.stride_a)};
-    const uint32_t box[3] = {128u, 128u, 1u};
+    const bool swap = fp8b_use_swap(a);
+    const uint32_t box[3] = {128u, swap ? static_cast<uint32_t>(swap_mn(a.m)) : 128u, 1u};
     if (!make_tmap_u8(&ta, a.ptr_a, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
   }
   if (kpanel) {
@@ -630,10 +689,18 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
   p.timeout_ns = kTimeoutNs;
   const int grid = grid_for(p.total_units, dev, a.grid_blocks);
   const bool f32 = a.out_dtype == BSG_OUT_FP32;
-  rc = kpanel ? (f32 ? fp8b_launch_t<true, true>(ta, tb, p, grid, st)
-                     : fp8b_launch_t<true, false>(ta, tb, p, grid, st))
-              : (f32 ? fp8b_launch_t<false, true>(ta, tb, p, grid, st)
-                     : fp8b_launch_t<false, false>(ta, tb, p, grid, st));
+  if (fp8b_use_swap(a)) {
+    switch (swap_mn(a.m)) {
+      case 16: rc = swap_launch_mn<16>(kpanel, f32, ta, tb, p, grid, st); break;
+      case 32: rc = swap_launch_mn<32>(kpanel, f32, ta, tb, p, grid, st); break;
+      default: rc = swap_launch_mn<64>(kpanel, f32, ta, tb, p, grid, st); break;
+    }
+  } else {
+    rc = kpanel ? (f32 ? fp8b_launch_t<true, true>(ta, tb, p, grid, st)
+                       : fp8b_launch_t<true, false>(ta, tb, p, grid, st))
+                : (f32 ? fp8b_launch_t<false, true>(ta, tb, p, grid, st)
+                       : fp8b_launch_t<false, false>(ta, tb, p, grid, st));
+  }
   if (rc != BSG_OK) return rc;
   if (pl.split > 1) return splitk_reduce(p.ws, a, pl.split, dev.sms, st);
   return BSG_OK;

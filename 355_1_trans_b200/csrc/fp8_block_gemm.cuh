@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(256, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 128);
+      mbar_init(&acc_empty[i], 4);   // one arrival per promotion warp
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -210,6 +210,9 @@ __global__ void __launch_bounds__(256, 1)
       const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
       const int row = mt * 128 + q * 32 + static_cast<int>(lane);
       const bool row_ok = row < p.m;
+      // a lane quarter whose 32 rows all lie beyond M (decode shapes) skips
+      // the promotion work but still releases the buffers
+      const bool quarter_live = mt * 128 + q * 32 < p.m;
       const int n0 = nt * BN;
       const float* sfa_row = p.sfa + b * p.sfa_batch + static_cast<long long>(row_ok ? row : 0) * p.sfa_m;
       const float* sfb_blk = p.sfb + b * p.sfb_batch + static_cast<long long>(n0 / 128) * p.sfb_n;
@@ -231,15 +234,18 @@ __global__ void __launch_bounds__(256, 1)
           break;
         }
         tc_fence_after();
+        if (quarter_live) {
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tmem_base + lane_base + buf * BN + static_cast<uint32_t>(c * 32), r);
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tmem_base + lane_base + buf * BN + static_cast<uint32_t>(c * 32), r);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c * 32 + i] = fmaf(__uint_as_float(r[i]), scale, acc[c * 32 + i]);
+            for (int i = 0; i < 32; ++i) acc[c * 32 + i] = fmaf(__uint_as_float(r[i]), scale, acc[c * 32 + i]);
+          }
         }
         tc_fence_before();
-        mbar_arrive(&acc_empty[buf]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
       }
       if (!ok) break;
       if (!row_ok) continue;

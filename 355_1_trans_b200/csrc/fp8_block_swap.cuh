@@ -1,0 +1,298 @@
+// fp8_block_swap.cuh -- decode-shaped (M <= 64) FP8 GEMM with fp32 block
+// scales, computed transposed ("swap-AB") so that it streams B from HBM.
+//
+// Semantics are those of fp8_block_gemm.cuh (reference:
+// block_scale_gemm_bpreshuffle/gemm_a8w8_blockscale_bpreshuffle_kernel_template.hpp:
+// 204-601): C[m,n] = sum_kb sfa[m,kb] * sfb[n/128,kb] * (A B^T)_kb[m,n].
+//
+// For a handful of activation rows the 128-row MMA side is wasted on A, so
+// the roles are swapped: the weight tile (128 rows of B = 128 output columns)
+// is the MMA's M side and the MN (16, 32 or 64) activation rows its N side.  The
+// per-128-K partial D^T[n, m] lands in TMEM lanes n, columns m; because all
+// 128 lanes of a tile share one 128x128 weight scale sfb[n/128, kb], the
+// promotion is acc[m] += D^T[n, m] * (sfb * sfa[m, kb]) per thread (lane n).
+// With MN columns per partial, up to 8 partials are in flight in TMEM, so the
+// MMA rarely waits for the promotion warps, and the small stages (16 KB of B
+// + MN x 128 B of A) allow a deep TMA pipeline: the kernel is bound by the B
+// stream from HBM.  The per-K-block scales (MN values of sfa and one sfb)
+// are staged into shared memory by the producer warp with asynchronous 4-byte
+// copies into a ring of kStages + kAccBufs slots -- as many K blocks as can be
+// between the producer and the promotion -- so neither the producer nor the
+// promotion ever waits on a global scale load.
+#pragma once
+
+#include "fp8_block_gemm.cuh"
+
+namespace bsg {
+
+// 32 lanes x 16 consecutive 32-bit TMEM columns -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32"
+      " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+template <int MN>
+struct SwapCfg {
+  static_assert(MN == 16 || MN == 32 || MN == 64, "MN must be 16, 32 or 64");
+  static constexpr uint32_t kWBytes = 128u * 128u;                 // weight tile
+  static constexpr uint32_t kXBytes = static_cast<uint32_t>(MN) * 128u;
+  static constexpr uint32_t kStageBytes = kWBytes + kXBytes;
+  static constexpr int kStages = static_cast<int>((210u * 1024u) / kStageBytes) > 12
+                                     ? 12
+                                     : static_cast<int>((210u * 1024u) / kStageBytes);
+  static constexpr int kAccBufs = (512 / MN) > 8 ? 8 : 512 / MN;
+  static constexpr uint32_t kTmemCols = static_cast<uint32_t>(kAccBufs * MN) < 32 ? 32u
+                                        : static_cast<uint32_t>(kAccBufs * MN);
+  static constexpr uint32_t kOffX = kWBytes * kStages;
+  static constexpr int kScaleSlots = kStages + kAccBufs;
+  static constexpr uint32_t kScaleSlot = static_cast<uint32_t>(MN + 4);   // floats: MN sfa, 1 sfb
+  static constexpr uint32_t kOffScale = kOffX + kXBytes * kStages;
+  static constexpr uint32_t kScaleBytes = static_cast<uint32_t>(kScaleSlots) * kScaleSlot * 4u;
+  static constexpr uint32_t kOffBar = kOffScale + ((kScaleBytes + 15u) & ~15u);
+  static constexpr uint32_t kSmemBytes = kOffBar + 1024u + 1024u;
+  static_assert(8u * (2u * kStages + 2u * kAccBufs + 2u * kScaleSlots + 1u) + 8u <= 1024u, "barrier area");
+  static_assert(kSmemBytes <= 227u * 1024u, "shared memory");
+};
+
+template <int MN, bool kKPanel, bool kOutF32>
+__global__ void __launch_bounds__(256, 1)
+    fp8_block_swap_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const Fp8BlockParams p) {
+  using Cfg = SwapCfg<MN>;
+  constexpr int S = Cfg::kStages;
+  constexpr int NB = Cfg::kAccBufs;
+  constexpr int R = Cfg::kScaleSlots;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~static_cast<uintptr_t>(1023u));
+  uint8_t* sW = smem;
+  uint8_t* sX = smem + Cfg::kOffX;
+  float* sScale = reinterpret_cast<float*>(smem + Cfg::kOffScale);   // slot: [MN] sfa, [MN] sfb
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* acc_full = empty_bar + S;   // [NB]
+  uint64_t* acc_empty = acc_full + NB;  // [NB]
+  uint64_t* scale_full = acc_empty + NB;  // [R]
+  uint64_t* scale_empty = scale_full + R;  // [R]
+  uint64_t* drain_bar = scale_empty + R;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31u;
+
+  if (threadIdx.x == 32) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < NB; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);   // one arrival per promotion warp
+    }
+    for (int i = 0; i < R; ++i) {
+      mbar_init(&scale_full[i], 32);  // one cp.async arrival per producer lane
+      mbar_init(&scale_empty[i], 4);  // one arrival per promotion warp
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_holder, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    const bool issuer = elect_one();
+    const uint64_t pol_w = l2_policy_evict_first();   // weights stream through once
+    const uint64_t pol_x = l2_policy_evict_last();    // activations are reread by every tile
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t kbi = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+      int b, mt, nt, s;
+      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+      const int kb0 = s * p.kb_per_split;
+      const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
+      const int m0 = mt * MN;
+      const int rows = min(MN, p.m - m0);
+      const float* sfa_t = p.sfa + b * p.sfa_batch + static_cast<long long>(m0) * p.sfa_m;
+      const float* sfb_blk = p.sfb + b * p.sfb_batch + static_cast<long long>(nt) * p.sfb_n;
+      for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        // this K block's scales into scale slot kbi % R (free once the
+        // promotion of K block kbi - R is done, which the stage and TMEM
+        // rings already imply, so this wait does not add a stall)
+        const uint32_t sl = kbi % R;
+        if (!mbar_wait(&scale_empty[sl], ((kbi / R) & 1u) ^ 1u, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        float* slot = sScale + sl * Cfg::kScaleSlot;
+#pragma unroll
+        for (int i = static_cast<int>(lane); i < MN; i += 32)
+          if (i < rows) cp_async_4(slot + i, sfa_t + i * p.sfa_m + kb * p.sfa_k);
+        if (lane == 0) cp_async_4(slot + MN, sfb_blk + kb * p.sfb_k);
+        cp_async_mbar_arrive(&scale_full[sl]);
+        if (issuer) {
+          uint64_t* fb = &full_bar[stage];
+          mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
+          if constexpr (kKPanel)
+            tma_load_4d_hint(sW + stage * Cfg::kWBytes, &tmB, fb, 0, nt * 128, kb, b, pol_w);
+          else
+            tma_load_3d_hint(sW + stage * Cfg::kWBytes, &tmB, fb, kb * 128, nt * 128, b, pol_w);
+          tma_load_3d_hint(sX + stage * Cfg::kXBytes, &tmA, fb, kb * 128, mt * MN, b, pol_x);
+        }
+        __syncwarp();
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    const bool issuer = elect_one();
+    const uint32_t idesc = idesc_f8f6f4(false, false, 128, MN);
+    const uint32_t sW0 = smem_u32(sW), sX0 = smem_u32(sX);
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t kbi = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+      int b, mt, nt, s;
+      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+      const int kb0 = s * p.kb_per_split;
+      const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
+      for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
+        const uint32_t buf = kbi % NB;
+        const uint32_t use = kbi / NB;
+        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t w_addr = sW0 + stage * Cfg::kWBytes;
+        const uint32_t x_addr = sX0 + stage * Cfg::kXBytes;
+        const uint32_t d = tmem_base + buf * MN;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const uint64_t adesc = make_sdesc(w_addr + 32u * t, 16u, 1024u, kLayoutSW128);
+          const uint64_t bdesc = make_sdesc(x_addr + 32u * t, 16u, 1024u, kLayoutSW128);
+          if (issuer) umma_f8f6f4(d, adesc, bdesc, idesc, t > 0 ? 1u : 0u);
+        }
+        if (issuer) {
+          tc_commit(&empty_bar[stage]);
+          tc_commit(&acc_full[buf]);
+        }
+        __syncwarp();
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (issuer) tc_commit(drain_bar);
+    int dummy = 0;
+    mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ promotion + store
+    const int q = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    uint32_t kbi = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+      int b, mt, nt, s;
+      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+      const int kb0 = s * p.kb_per_split;
+      const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
+      const int n = nt * 128 + q * 32 + static_cast<int>(lane);   // output column of this lane
+      const int m0 = mt * MN;
+      const int rows = min(MN, p.m - m0);
+      float acc[MN];
+#pragma unroll
+      for (int i = 0; i < MN; ++i) acc[i] = 0.0f;
+      for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
+        const uint32_t buf = kbi % NB;
+        const uint32_t use = kbi / NB;
+        const uint32_t sl = kbi % R;
+        if (!mbar_wait(&scale_full[sl], (kbi / R) & 1u, abort_flag, p.timeout_ns) ||
+            !mbar_wait(&acc_full[buf], use & 1u, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float* slot = sScale + sl * Cfg::kScaleSlot;
+        const float sb = slot[MN];
+        const uint32_t taddr = tmem_base + lane_base + buf * MN;
+        // 16 columns at a time: TMEM load, 16 combined scales, 16 FMAs
+#pragma unroll
+        for (int c = 0; c < MN / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld16(taddr + static_cast<uint32_t>(c * 16), r);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int row = c * 16 + i;
+            const float comb = row < rows ? sb * slot[row] : 0.0f;
+            acc[row] = fmaf(__uint_as_float(r[i]), comb, acc[row]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&acc_empty[buf]);
+          mbar_arrive(&scale_empty[sl]);
+        }
+      }
+      if (!ok) break;
+      if (n >= p.n) continue;
+      // store: lane n writes column n of every valid row (64 B per warp per row)
+#pragma unroll
+      for (int i = 0; i < MN; ++i) {
+        if (i >= rows) break;
+        const int m = m0 + i;
+        if (p.split_k > 1) {
+          p.ws[((static_cast<long long>(s) * p.batch + b) * p.m + m) * static_cast<long long>(p.n) + n] = acc[i];
+        } else if constexpr (kOutF32) {
+          reinterpret_cast<float*>(p.c)[b * p.c_batch_stride + static_cast<long long>(m) * p.ldc + n] = acc[i];
+        } else {
+          reinterpret_cast<uint16_t*>(p.c)[b * p.c_batch_stride + static_cast<long long>(m) * p.ldc + n] =
+              static_cast<uint16_t>(pack_bf16x2(acc[i], 0.0f) & 0xFFFFu);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+}
+
+}  // namespace bsg

@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--k", type=int, default=8192)
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="fp8 block-scale sweep of BASELINE configs[1] (M x (N,K), 24 shapes), one JSON line")
     return ap.parse_args()
 
 
@@ -479,10 +481,66 @@ def run_ours(args):
     return 0
 
 
+def run_sweep(args):
+    """M in {1,16,64,128,1024,8192} x (N,K) in {(7168,2048),
+    (4096,7168), (24576,1536), (7168,18432)}, fp32 block scales, K-panel B,
+    bf16 out.  Each timed GEMM is a CUDA-graph replay of the library call
+    (device time only), preceded by an L2 flush that READS a 256 MiB buffer (a
+    write-based flush would leave ~126 MB of dirty lines whose write-back would
+    be charged to the GEMM), timed with CUDA events; reports the median and,
+    separately, the host time of one eager call."""
+    import torch
+    dev = torch.device("cuda", 0)
+    bs = importlib.import_module("355_1_trans_b200")
+    peaks, peak_kind = load_peaks()
+    flush = torch.ones(64 << 20, dtype=torch.float32, device=dev)   # 256 MiB
+    sink = torch.empty((), dtype=torch.float32, device=dev)
+    rows = []
+    for (n, k) in ((7168, 2048), (4096, 7168), (24576, 1536), (7168, 18432)):
+        qa_full, qb, sa_full, sb = make_fp8block_inputs(8192, n, k, dev, 7)
+        for m in (1, 16, 64, 128, 1024, 8192):
+            qa, sa = qa_full[:m].contiguous(), sa_full[:m].contiguous()
+            out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+            call = lambda: bs.gemm_a8w8_bpreshuffle(qa, qb, sa, sb, torch.bfloat16, preshuffled=True, out=out)
+            for _ in range(3):
+                call()
+            # capture the call (its kernels and the split-K reduce) in a CUDA
+            # graph so that host-side argument handling is not timed
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                call()
+            times, host_us = [], []
+            for _ in range(max(5, args.steps)):
+                torch.sum(flush, dim=0, out=sink)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                g.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1))
+                t0 = time.perf_counter()
+                call()
+                host_us.append((time.perf_counter() - t0) * 1e6)
+                torch.cuda.synchronize()
+            del g
+            ms = statistics.median(times)
+            byts = m * k + n * k + 4 * m * (k // 128) + 4 * (n // 128) * (k // 128) + 2 * m * n
+            rows.append({"m": m, "n": n, "k": k, "us": ms * 1e3, "host_call_us": statistics.median(host_us),
+                         "tflops": 2.0 * m * n * k / ms / 1e9,
+                         "gbs": byts / ms / 1e6, "hbm_frac": byts / ms / 1e6 / peaks["hbm_gbs"]})
+    assert bs.check_device_error() == 0
+    print(json.dumps({"sweep": "fp8 block-scale (BASELINE configs[1])", "hbm_peak_gbs": peaks["hbm_gbs"],
+                      "peak_kind": peak_kind, "l2": "flushed (256 MiB read) before every timed launch", "rows": rows}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.sweep:
+        return run_sweep(args)
     return run_ours(args)
 
 

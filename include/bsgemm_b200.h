@@ -121,10 +121,11 @@ typedef struct bsgemm_args {
     int grid_blocks;        /* 0 = one CTA per SM; >0 caps the persistent grid
                                (the reference's PERSIST_GRID / m10 grid_blocks) */
     int kernel;             /* BSG_KERNEL_*: 0 = auto, 1 = single-CTA tiles,
-                               2 = CTA-pair (cta_group::2) 256x256 tiles */
+                               2 = CTA-pair (cta_group::2) 256x256 tiles (MX),
+                               3 = transposed decode kernel (fp32 block scale, M <= 64) */
 } bsgemm_args;
 
-enum { BSG_KERNEL_AUTO = 0, BSG_KERNEL_1CTA = 1, BSG_KERNEL_PAIR = 2 };
+enum { BSG_KERNEL_AUTO = 0, BSG_KERNEL_1CTA = 1, BSG_KERNEL_PAIR = 2, BSG_KERNEL_SWAP = 3 };
 
 /* Fill the 96-byte prefix's defaults and zero the extensions. */
 BSG_API void bsgemm_args_init(bsgemm_args *args);

@@ -183,7 +183,7 @@ def test_mxfp4_shuffled_b(bs, orc, cuda):
 # ---- FP8 block-scale (fp32 scales) --------------------------------------------------
 
 def run_fp8_block(bs, orc, cuda, m, n, k, *, seed=1, kpanel=True, transposed=False, split_k=0,
-                  out_dtype=torch.bfloat16):
+                  out_dtype=torch.bfloat16, kernel="auto"):
     x = orc.normal((m, k), seed=seed * 77)
     w = orc.normal((n, k), seed=seed * 77 + 1)
     qa, sa = orc.quant_fp8_block(x, 1)
@@ -198,7 +198,7 @@ def run_fp8_block(bs, orc, cuda, m, n, k, *, seed=1, kpanel=True, transposed=Fal
     SB = torch.from_numpy(sb).to(cuda)
     out = poisoned((m, n), out_dtype, cuda)
     bs.gemm_a8w8_bpreshuffle(A, B, SA, SB, out_dtype, preshuffled=kpanel, x_scale_transposed=transposed,
-                             out=out, split_k=split_k)
+                             out=out, split_k=split_k, kernel=kernel)
     torch.cuda.synchronize()
     assert bs.check_device_error() == 0
     got = out.float().cpu().numpy()
@@ -222,6 +222,19 @@ def test_fp8_block_fp32_out(bs, orc, cuda):
 @pytest.mark.parametrize("m", [1, 16, 64, 200])
 def test_fp8_block_decode_shapes(bs, orc, cuda, m):
     run_fp8_block(bs, orc, cuda, m, 1024, 2048, seed=4 + m)
+
+
+@pytest.mark.parametrize("m,kernel", [(1, "swap"), (7, "swap"), (16, "swap"), (30, "swap"), (64, "swap"),
+                                      (16, "1cta"), (64, "1cta")])
+def test_fp8_block_decode_kernels(bs, orc, cuda, m, kernel):
+    """Decode shapes through the transposed kernel and the standard one."""
+    run_fp8_block(bs, orc, cuda, m, 896, 2304, seed=40 + m, kernel=kernel, transposed=(m == 7))
+
+
+def test_fp8_block_swap_raw_b_fp32_split(bs, orc, cuda):
+    ref, got = run_fp8_block(bs, orc, cuda, 24, 640, 1536, seed=50, kpanel=False, kernel="swap",
+                             split_k=3, out_dtype=torch.float32)
+    np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-3)
 
 
 def test_fp8_block_split_k(bs, orc, cuda):
