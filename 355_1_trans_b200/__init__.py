@@ -151,7 +151,8 @@ def _record(tensors, device):
 
 def gemm_a8w8_mxfp8(A, B, A_scale, B_scale, *, layout: str = "tn", out_dtype=torch.bfloat16,
                     out=None, scale_format: str = "rowmajor", split_k: int = 0,
-                    workspace=None, grid_blocks: int = 0, kernel: str = "auto"):
+                    workspace=None, grid_blocks: int = 0, kernel: str = "auto",
+                    b_format: str = "raw"):
     """MXFP8 GEMM (mxfp8_gemm/gemm_a8w8_mxfp8_host.cc:98-122 semantics).
 
     A: E4M3 [M,K] (layout t*) or [K,M] (n*); B: E4M3 [N,K] (*n) or [K,N] (*t);
@@ -159,28 +160,36 @@ def gemm_a8w8_mxfp8(A, B, A_scale, B_scale, *, layout: str = "tn", out_dtype=tor
     row-major (scale_format="rowmajor") or native atoms from pack_scales
     (scale_format="native").  Returns C [M,N] (or [batch,M,N]) of out_dtype.
     kernel: "auto", "1cta" (128 x BN tiles, one CTA each) or "pair" (256 x 256
-    tiles on CTA pairs, cta_group::2).
+    tiles on CTA pairs, cta_group::2).  b_format "shuffle16": B holds aiter's
+    shuffle_weight(16,16) bytes of a K-major [N,K] B (read in place).
     """
     return _mx(A, B, A_scale, B_scale, fp4=False, layout=layout, out_dtype=out_dtype, out=out,
                scale_format=scale_format, split_k=split_k, workspace=workspace,
-               grid_blocks=grid_blocks, kernel=kernel)
+               grid_blocks=grid_blocks, kernel=kernel, b_format=b_format)
 
 
 def gemm_a4w4_mxfp4(A, B, A_scale, B_scale, *, out_dtype=torch.bfloat16, out=None,
                     scale_format: str = "rowmajor", split_k: int = 0, workspace=None,
-                    grid_blocks: int = 0, kernel: str = "auto"):
+                    grid_blocks: int = 0, kernel: str = "auto", b_format: str = "raw"):
     """MXFP4 GEMM (mxfp4_gemm_4wave_20261112/gemm_a4w4_mxfp4_4wave_host.cc:97-115
     semantics): A [M,K/2], B [N,K/2] packed E2M1 bytes (even k low nibble),
-    K-major; scales E8M0 [rows, K/32] or native."""
+    K-major; scales E8M0 [rows, K/32] or native.  b_format "shuffle16": B is
+    the shuffle_weight(16,16) form of the [N,K/2] bytes
+    (candidate_m10/gemm_a4w4_mxfp4_4wave_host.cc:215-225), read in place."""
     return _mx(A, B, A_scale, B_scale, fp4=True, layout="tn", out_dtype=out_dtype, out=out,
                scale_format=scale_format, split_k=split_k, workspace=workspace,
-               grid_blocks=grid_blocks, kernel=kernel)
+               grid_blocks=grid_blocks, kernel=kernel, b_format=b_format)
+
+
+_B_FORMATS = {"raw": B_RAW, "shuffle16": B_SHUFFLE16}
 
 
 def _mx(A, B, A_scale, B_scale, *, fp4, layout, out_dtype, out, scale_format, split_k,
-        workspace, grid_blocks, kernel="auto"):
+        workspace, grid_blocks, kernel="auto", b_format="raw"):
     if layout not in LAYOUTS:
         raise ValueError(f"layout must be one of {sorted(LAYOUTS)}")
+    if b_format not in _B_FORMATS:
+        raise ValueError(f"b_format must be one of {sorted(_B_FORMATS)}")
     if A.dim() != B.dim() or A.dim() not in (2, 3):
         raise ValueError("A and B must both be 2-D or both 3-D (batched)")
     tensors = (A, B, A_scale, B_scale)
@@ -238,6 +247,7 @@ def _mx(A, B, A_scale, B_scale, *, fp4, layout, out_dtype, out, scale_format, sp
     else:
         raise ValueError("scale_format must be 'rowmajor' or 'native'")
     args.layout = code
+    args.b_format = _B_FORMATS[b_format]
     args.out_dtype = OUT_BF16 if out_dtype == torch.bfloat16 else OUT_FP32
     args.split_k = split_k
     args.grid_blocks = grid_blocks
@@ -258,17 +268,23 @@ def _mx(A, B, A_scale, B_scale, *, fp4, layout, out_dtype, out, scale_format, sp
 def gemm_a8w8_bpreshuffle(A, B, x_scale, w_scale, out_dtype=torch.bfloat16, *,
                           preshuffled: bool = True, x_scale_transposed: bool = False,
                           out=None, split_k: int = 0, workspace=None, grid_blocks: int = 0,
-                          kernel: str = "auto"):
+                          kernel: str = "auto", b_layout: str | None = None):
     """a8w8 GEMM with fp32 1x128 (x_scale [M,K/128]) and 128x128
     (w_scale [N/128,K/128]) block scales, bf16/fp32 out.
 
     preshuffled=True: B is the K-panel layout B'[K/128][N][128] (given as a
     [K/128, N, 128] or flat [N, K] tensor), as aiter's wrapper produces
     (opus_a8w8_bpreshuffle_integration_and_benchmark.md:76-81);
-    preshuffled=False: B is plain [N, K].  x_scale_transposed=True takes the
-    reference kernel's [K/128, M] SFA layout.  kernel: "auto", "1cta" (128x128
-    output tiles) or "swap" (transposed decode kernel, M <= 64).
+    preshuffled=False: B is plain [N, K].  b_layout overrides both:
+    "kpanel", "shuffle16" (aiter shuffle_weight(16,16) bytes of [N, K], read in
+    place) or "raw".  x_scale_transposed=True takes the reference kernel's
+    [K/128, M] SFA layout.  kernel: "auto", "1cta" (128x128 output tiles) or
+    "swap" (transposed decode kernel, M <= 64).
     """
+    if b_layout is None:
+        b_layout = "kpanel" if preshuffled else "raw"
+    if b_layout not in ("kpanel", "shuffle16", "raw"):
+        raise ValueError("b_layout must be 'kpanel', 'shuffle16' or 'raw'")
     if A.dim() != 2:
         raise ValueError("A must be [M, K]")
     tensors = (A, B, x_scale, w_scale)
@@ -279,7 +295,7 @@ def gemm_a8w8_bpreshuffle(A, B, x_scale, w_scale, out_dtype=torch.bfloat16, *,
     if x_scale.dtype != torch.float32 or w_scale.dtype != torch.float32:
         raise ValueError("scales must be fp32")
     m, k = A.shape
-    if preshuffled:
+    if b_layout == "kpanel":
         if B.dim() == 3:
             kt, n, inner = B.shape
             if inner != 128 or kt * 128 != k:
@@ -292,6 +308,8 @@ def gemm_a8w8_bpreshuffle(A, B, x_scale, w_scale, out_dtype=torch.bfloat16, *,
         n, kb = B.shape
         if kb != k:
             raise ValueError("A and B disagree on K")
+        if b_layout == "shuffle16" and not B.is_contiguous():
+            raise ValueError("shuffled B must be contiguous")
     kblk = k // 128
     if x_scale_transposed:
         if tuple(x_scale.shape) != (kblk, m) or x_scale.stride(1) != 1:
@@ -306,8 +324,8 @@ def gemm_a8w8_bpreshuffle(A, B, x_scale, w_scale, out_dtype=torch.bfloat16, *,
     args.ptr_a, args.ptr_b, args.ptr_c = A.data_ptr(), B.data_ptr(), out.data_ptr()
     args.m, args.n, args.k, args.batch = m, n, k, 1
     args.stride_a, args.stride_c = A.stride(0), n
-    args.stride_b = 128 if preshuffled else B.stride(0)
-    args.b_format = B_KPANEL128 if preshuffled else B_RAW
+    args.stride_b = 128 if b_layout == "kpanel" else k if b_layout == "shuffle16" else B.stride(0)
+    args.b_format = {"kpanel": B_KPANEL128, "shuffle16": B_SHUFFLE16, "raw": B_RAW}[b_layout]
     args.ptr_sfa, args.ptr_sfb = x_scale.data_ptr(), w_scale.data_ptr()
     args.sfa_format = SF_KMAJOR_T if x_scale_transposed else SF_ROWMAJOR
     args.stride_sfa = x_scale.stride(0)
@@ -323,6 +341,77 @@ def gemm_a8w8_bpreshuffle(A, B, x_scale, w_scale, out_dtype=torch.bfloat16, *,
         status = lib().bsgemm_a8w8_blockscale_bpreshuffle(ctypes.byref(args), _stream(A.device))
         _record((*tensors, out, ws), A.device)
     _check(status, "bsgemm_a8w8_blockscale_bpreshuffle")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# E8M0 1x128 / 128x128 block scale: the reference's own ctypes adapter
+# ---------------------------------------------------------------------------
+
+class OpusGemmScaleKargs(ctypes.Structure):
+    """opus_gemm_scale_kargs, the reference's 96-byte launcher argument
+    (source_snapshot/gemm_a8w8_mxfp8_scale_common.h:12-38)."""
+    _fields_ = Args._fields_[:19]
+
+
+assert ctypes.sizeof(OpusGemmScaleKargs) == 96
+
+
+def gemm_a8w8_blockscale_bpreshuffle(A, B, A_scale, B_scale, dtype=torch.bfloat16, out=None, *,
+                                     tiles: int = 0):
+    """One GEMM launch through launch_blockscale_bpreshuffle, as the reference
+    adapter (source_snapshot/blockscale_bpreshuffle.py:37-97): A E4M3 [M,K];
+    B the shuffle_weight(16,16) bytes of E4M3 [N,K]; A_scale E8M0 [M,K/128]
+    stored column-major (strides (1, M)) or a contiguous tensor holding the
+    transposed [K/128, M] bytes; B_scale E8M0 [N/128,K/128] contiguous; bf16 or
+    fp32 out.  No input conversion and no workspace.  Differences from the
+    reference: any M >= 1 and N % 128 == 0 are accepted (it: M, N % 256).
+    Raises ValueError on bad inputs, RuntimeError on a nonzero CUDA status.
+    """
+    tensors = (A, B, A_scale, B_scale)
+    if any(t.ndim != 2 for t in tensors):
+        raise ValueError("A/B/A_scale/B_scale must be 2-D")
+    if not A.is_cuda or any(t.device != A.device for t in tensors):
+        raise ValueError("all inputs must be on the same GPU")
+    if A.dtype != torch.float8_e4m3fn or B.dtype not in (torch.float8_e4m3fn, torch.uint8):
+        raise ValueError("A/B must contain E4M3FN FP8 bytes")
+    if A_scale.dtype not in _SCALE_U8 or B_scale.dtype not in _SCALE_U8:
+        raise ValueError("scales must be E8M0 bytes, not FP32")
+    m, k = A.shape
+    n, bk = B.shape
+    if min(m, n, k) <= 0 or k != bk or n % 128 or k % 128:
+        raise ValueError("requires matching K, N % 128 == 0, K % 128 == 0")
+    if dtype not in (torch.bfloat16, torch.float32) or tiles not in (0, 1):
+        raise ValueError("dtype must be bf16/fp32; tiles must be 0 or 1")
+    if not A.is_contiguous() or not B.is_contiguous() or not B_scale.is_contiguous():
+        raise ValueError("A, packed B and B_scale must be contiguous")
+    if tuple(A_scale.shape) != (m, k // 128) or tuple(B_scale.shape) != (n // 128, k // 128):
+        raise ValueError("requires A_scale [M,K/128], B_scale [N/128,K/128]")
+    if not A_scale.is_contiguous() and A_scale.stride() != (1, m):
+        raise ValueError("A_scale must use dense column-major bytes")
+    output_bytes = 2 if dtype == torch.bfloat16 else 4
+    if max(m * k, n * k, m * n * output_bytes) > 2**31 - 1:
+        raise ValueError("every tensor must stay below 2 GiB")
+    if out is None:
+        out = torch.empty((m, n), device=A.device, dtype=dtype)
+    elif out.shape != (m, n) or out.dtype != dtype or out.device != A.device or not out.is_contiguous():
+        raise ValueError("out must be contiguous [M,N] with the requested dtype/device")
+    out_begin = out.data_ptr()
+    out_end = out_begin + out.numel() * out.element_size()
+    for tensor in tensors:
+        begin = tensor.data_ptr()
+        end = begin + tensor.numel() * tensor.element_size()
+        if out_begin < end and begin < out_end:
+            raise ValueError("out must not overlap any input tensor")
+    args = OpusGemmScaleKargs(A.data_ptr(), B.data_ptr(), out.data_ptr(), m, n, k, 1,
+                              k, k, n, m * k, n * k, m * n, A_scale.data_ptr(), B_scale.data_ptr(),
+                              m, k // 128, m * (k // 128), (n // 128) * (k // 128))
+    with torch.cuda.device(A.device):
+        status = lib().launch_blockscale_bpreshuffle(
+            ctypes.byref(args), int(dtype == torch.bfloat16), tiles, _stream(A.device))
+        _record((*tensors, out), A.device)
+    if status:
+        raise RuntimeError(f"blockscale bpreshuffle launch failed: CUDA error {status}")
     return out
 
 

@@ -11,6 +11,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <climits>
+#include <cstddef>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -118,17 +120,24 @@ bool overlaps(const void* a, uint64_t a_bytes, const void* b, uint64_t b_bytes) 
   return x < y + b_bytes && y < x + a_bytes;
 }
 
+// The CUDA error behind the calling thread's last BSG_ERR_CUDA (the
+// reference-compatible entry point returns CUDA error codes).
+thread_local cudaError_t t_last_cuda_error = cudaSuccess;
+
 template <typename K>
 int set_smem(K kernel, uint32_t bytes) {
-  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(bytes)) == cudaSuccess
-             ? BSG_OK
-             : BSG_ERR_CUDA;
+  const cudaError_t e =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e == cudaSuccess) return BSG_OK;
+  t_last_cuda_error = e;
+  return BSG_ERR_CUDA;
 }
 
 int launch_status() {
   const cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? BSG_OK : BSG_ERR_CUDA;
+  if (e == cudaSuccess) return BSG_OK;
+  t_last_cuda_error = e;
+  return BSG_ERR_CUDA;
 }
 
 int grid_for(int units, const DevInfo& dev, int grid_blocks) {
@@ -235,57 +244,90 @@ uint64_t operand_bytes(long long rows_of_storage, long long ld, long long batch_
          static_cast<uint64_t>(rows_of_storage) * ld;
 }
 
-template <int BN, int kFp4, bool kAMN, bool kBMN, bool kOutF32>
+template <int BN, int kFp4, bool kAMN, int kBMode, bool kOutF32, int kSfMode>
 int mx_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p, int grid,
                 cudaStream_t st) {
   using Cfg = MxCfg<BN, kFp4>;
-  auto* kern = bsg::mx_gemm_kernel<BN, kFp4, kAMN, kBMN, kOutF32>;
+  auto* kern = bsg::mx_gemm_kernel<BN, kFp4, kAMN, kBMode, kOutF32, kSfMode>;
   if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
   kern<<<grid, bsg::kMxThreads, Cfg::kSmemBytes, st>>>(ta, tb, p);
   return launch_status();
 }
 
+template <int BN, int kFp4, bool kAMN, int kBMode>
+int mx_launch_out(bool f32, const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p, int grid,
+                  cudaStream_t st) {
+  return f32 ? mx_launch_t<BN, kFp4, kAMN, kBMode, true, bsg::kSfNative>(ta, tb, p, grid, st)
+             : mx_launch_t<BN, kFp4, kAMN, kBMode, false, bsg::kSfNative>(ta, tb, p, grid, st);
+}
+
+// Native-scale instantiations: fp8 takes every A/B orientation and the
+// shuffled B; fp4 (.kind::mxf4) is K-major only.
 template <int BN, int kFp4>
-int mx_launch_bn(bool amn, bool bmn, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
+int mx_launch_bn(bool amn, int bmode, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
                  const MxParams& p, int grid, cudaStream_t st) {
   if constexpr (kFp4) {
-    return f32 ? mx_launch_t<BN, 1, false, false, true>(ta, tb, p, grid, st)
-               : mx_launch_t<BN, 1, false, false, false>(ta, tb, p, grid, st);
+    if (amn || bmode == bsg::kBMNMajor) return BSG_ERR_UNSUPPORTED;
+    return bmode == bsg::kBShuffle16 ? mx_launch_out<BN, 1, false, bsg::kBShuffle16>(f32, ta, tb, p, grid, st)
+                                     : mx_launch_out<BN, 1, false, bsg::kBKMajor>(f32, ta, tb, p, grid, st);
   } else {
-    const int sel = (amn ? 4 : 0) | (bmn ? 2 : 0) | (f32 ? 1 : 0);
-    switch (sel) {
-      case 0: return mx_launch_t<BN, 0, false, false, false>(ta, tb, p, grid, st);
-      case 1: return mx_launch_t<BN, 0, false, false, true>(ta, tb, p, grid, st);
-      case 2: return mx_launch_t<BN, 0, false, true, false>(ta, tb, p, grid, st);
-      case 3: return mx_launch_t<BN, 0, false, true, true>(ta, tb, p, grid, st);
-      case 4: return mx_launch_t<BN, 0, true, false, false>(ta, tb, p, grid, st);
-      case 5: return mx_launch_t<BN, 0, true, false, true>(ta, tb, p, grid, st);
-      case 6: return mx_launch_t<BN, 0, true, true, false>(ta, tb, p, grid, st);
-      default: return mx_launch_t<BN, 0, true, true, true>(ta, tb, p, grid, st);
+    if (amn) {
+      switch (bmode) {
+        case bsg::kBKMajor: return mx_launch_out<BN, 0, true, bsg::kBKMajor>(f32, ta, tb, p, grid, st);
+        case bsg::kBMNMajor: return mx_launch_out<BN, 0, true, bsg::kBMNMajor>(f32, ta, tb, p, grid, st);
+        default: return mx_launch_out<BN, 0, true, bsg::kBShuffle16>(f32, ta, tb, p, grid, st);
+      }
+    }
+    switch (bmode) {
+      case bsg::kBKMajor: return mx_launch_out<BN, 0, false, bsg::kBKMajor>(f32, ta, tb, p, grid, st);
+      case bsg::kBMNMajor: return mx_launch_out<BN, 0, false, bsg::kBMNMajor>(f32, ta, tb, p, grid, st);
+      default: return mx_launch_out<BN, 0, false, bsg::kBShuffle16>(f32, ta, tb, p, grid, st);
     }
   }
 }
 
-template <int kFp4, bool kAMN, bool kBMN>
+// Per-128 E8M0 scales (launch_blockscale_bpreshuffle): A K-major, B shuffled.
+template <int BN>
+int mx_launch_e8m0b(bool f32, const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p, int grid,
+                    cudaStream_t st) {
+  return f32 ? mx_launch_t<BN, 0, false, bsg::kBShuffle16, true, bsg::kSfE8m0Block128>(ta, tb, p, grid, st)
+             : mx_launch_t<BN, 0, false, bsg::kBShuffle16, false, bsg::kSfE8m0Block128>(ta, tb, p, grid, st);
+}
+
+template <int kFp4, bool kAMN, int kBMode, int kSfMode>
 int mx2_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tsa,
                  const CUtensorMap& tsb, const bsg::Mx2Params& p, int grid, cudaStream_t st) {
   using Cfg = bsg::Mx2Cfg<kFp4>;
-  auto* kern = bsg::mx_gemm_2sm_kernel<kFp4, kAMN, kBMN>;
+  auto* kern = bsg::mx_gemm_2sm_kernel<kFp4, kAMN, kBMode, kSfMode>;
   if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
   kern<<<grid, bsg::kMxThreads, Cfg::kSmemBytes, st>>>(ta, tb, tsa, tsb, p);
   return launch_status();
 }
 
-int mx2_launch(bool fp4, bool amn, bool bmn, const CUtensorMap& ta, const CUtensorMap& tb,
+int mx2_launch(bool fp4, bool amn, int bmode, int sfmode, const CUtensorMap& ta, const CUtensorMap& tb,
                const CUtensorMap& tsa, const CUtensorMap& tsb, const bsg::Mx2Params& p, int grid,
                cudaStream_t st) {
-  if (fp4) return mx2_launch_t<1, false, false>(ta, tb, tsa, tsb, p, grid, st);
-  const int sel = (amn ? 2 : 0) | (bmn ? 1 : 0);
-  switch (sel) {
-    case 0: return mx2_launch_t<0, false, false>(ta, tb, tsa, tsb, p, grid, st);
-    case 1: return mx2_launch_t<0, false, true>(ta, tb, tsa, tsb, p, grid, st);
-    case 2: return mx2_launch_t<0, true, false>(ta, tb, tsa, tsb, p, grid, st);
-    default: return mx2_launch_t<0, true, true>(ta, tb, tsa, tsb, p, grid, st);
+  using namespace bsg;
+  if (sfmode == kSfE8m0Block128) {
+    if (fp4 || amn || bmode != kBShuffle16) return BSG_ERR_UNSUPPORTED;
+    return mx2_launch_t<0, false, kBShuffle16, kSfE8m0Block128>(ta, tb, tsa, tsb, p, grid, st);
+  }
+  if (fp4) {
+    if (amn || bmode == kBMNMajor) return BSG_ERR_UNSUPPORTED;
+    return bmode == kBShuffle16 ? mx2_launch_t<1, false, kBShuffle16, kSfNative>(ta, tb, tsa, tsb, p, grid, st)
+                                : mx2_launch_t<1, false, kBKMajor, kSfNative>(ta, tb, tsa, tsb, p, grid, st);
+  }
+  if (amn) {
+    switch (bmode) {
+      case kBKMajor: return mx2_launch_t<0, true, kBKMajor, kSfNative>(ta, tb, tsa, tsb, p, grid, st);
+      case kBMNMajor: return mx2_launch_t<0, true, kBMNMajor, kSfNative>(ta, tb, tsa, tsb, p, grid, st);
+      default: return mx2_launch_t<0, true, kBShuffle16, kSfNative>(ta, tb, tsa, tsb, p, grid, st);
+    }
+  }
+  switch (bmode) {
+    case kBKMajor: return mx2_launch_t<0, false, kBKMajor, kSfNative>(ta, tb, tsa, tsb, p, grid, st);
+    case kBMNMajor: return mx2_launch_t<0, false, kBMNMajor, kSfNative>(ta, tb, tsa, tsb, p, grid, st);
+    default: return mx2_launch_t<0, false, kBShuffle16, kSfNative>(ta, tb, tsa, tsb, p, grid, st);
   }
 }
 
@@ -299,6 +341,33 @@ bool make_sf_tmap(CUtensorMap* m, const void* base, long long atoms_per_batch, i
   return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, base, 3, dims, strides, box, false);
 }
 
+// Operand tensor map over a plain [rows][ld] byte matrix (K-major or MN-major
+// tile of 128 bytes x box_rows, 128B swizzle).
+bool make_operand_tmap(CUtensorMap* m, const void* base, long long cols, long long rows, long long ld,
+                       long long batch_stride, int batch, uint32_t box_rows) {
+  const uint64_t dims[3] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(rows),
+                            static_cast<uint64_t>(batch)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(ld),
+                               static_cast<uint64_t>(batch > 1 ? batch_stride : rows * ld)};
+  const uint32_t box[3] = {128u, box_rows, 1u};
+  return make_tmap_u8(m, base, 3, dims, strides, box, true);
+}
+
+// Tensor map over B in the shuffle_weight(16,16) layout [N/16][Kb/16][16][16]
+// (Kb = K in bytes): dims (16-byte row x 8 rows = one 128-byte core matrix,
+// 16-byte K chunk, 8-row half of the 16-row group, 16-row group, batch).  A
+// box of (128, 8, 2, box_rows/16, 1) is one 128-byte K stage of box_rows rows
+// in the canonical no-swizzle K-major layout.
+bool make_shuffle16_tmap(CUtensorMap* m, const void* base, long long rows, long long kbytes,
+                         long long batch_stride, int batch, uint32_t box_rows) {
+  const uint64_t dims[5] = {128u, static_cast<uint64_t>(kbytes / 16), 2u, static_cast<uint64_t>(rows / 16),
+                            static_cast<uint64_t>(batch)};
+  const uint64_t strides[4] = {256u, 128u, static_cast<uint64_t>(kbytes) * 16u,
+                               static_cast<uint64_t>(batch > 1 ? batch_stride : rows * kbytes)};
+  const uint32_t box[5] = {128u, 8u, 2u, box_rows / 16u, 1u};
+  return make_tmap_u8(m, base, 5, dims, strides, box, false);
+}
+
 int splitk_reduce(const float* ws, const bsgemm_args& a, int split, int sms, cudaStream_t st) {
   const long long total4 = static_cast<long long>(a.m) * a.n * a.batch / 4;
   const int grid = static_cast<int>(std::min<long long>((total4 + 255) / 256, 8LL * sms));
@@ -310,6 +379,131 @@ int splitk_reduce(const float* ws, const bsgemm_args& a, int split, int sms, cud
                                                           a.stride_c, a.stride_c_batch);
   return launch_status();
 }
+
+// Resolved operands of one MX launch.
+struct MxOperands {
+  bool fp4 = false, a_mn = false;
+  int bmode = bsg::kBKMajor;
+  int sfmode = bsg::kSfNative;
+  long long a_rows = 0, a_cols = 0, b_rows = 0, b_cols = 0;   // storage extents (bytes)
+  long long kbytes = 0;
+  const uint8_t* sfa = nullptr;
+  const uint8_t* sfb = nullptr;
+  long long sfa_bs = 0, sfb_bs = 0;       // native: atom batch strides; e8m0: byte batch strides
+  long long sfa_ld = 0, sfb_ld = 0;       // e8m0 block-128 only
+  float* partials = nullptr;
+};
+
+bool make_b_tmap(CUtensorMap* m, const bsgemm_args& a, const MxOperands& o, uint32_t box_rows) {
+  if (o.bmode == bsg::kBShuffle16)
+    return make_shuffle16_tmap(m, a.ptr_b, a.n, o.kbytes, a.stride_b_batch, a.batch, box_rows);
+  return make_operand_tmap(m, a.ptr_b, o.b_cols, o.b_rows, a.stride_b, a.stride_b_batch, a.batch,
+                           o.bmode == bsg::kBMNMajor ? 128u : box_rows);
+}
+
+bool mx_use_pair(const bsgemm_args& a, const MxPlan& pl, const DevInfo& dev) {
+  const long long pair_tiles = static_cast<long long>((a.m + 255) / 256) * ((a.n + 255) / 256) * a.batch;
+  return a.kernel == BSG_KERNEL_PAIR ||
+         (a.kernel == BSG_KERNEL_AUTO && pl.split == 1 && a.out_dtype == BSG_OUT_BF16 &&
+          pair_tiles * 2 >= dev.sms);
+}
+
+// Tensor maps, parameters and launch of the planned MX GEMM (+ split-K reduce).
+int mx_launch_planned(const bsgemm_args& a, const MxOperands& o, const MxPlan& pl, const DevInfo& dev,
+                      cudaStream_t st) {
+  const bool e8m0b = o.sfmode == bsg::kSfE8m0Block128;
+  const int kg = a.k / 32;
+  if (mx_use_pair(a, pl, dev)) {
+    if (pl.split > 1 || a.out_dtype != BSG_OUT_BF16) return BSG_ERR_UNSUPPORTED;
+    if (!e8m0b && (o.sfa_bs % 512 || o.sfb_bs % 512)) return BSG_ERR_UNSUPPORTED;
+    CUtensorMap ta, tb, tsa, tsb;
+    if (!make_operand_tmap(&ta, a.ptr_a, o.a_cols, o.a_rows, a.stride_a, a.stride_a_batch, a.batch, 128u) ||
+        !make_b_tmap(&tb, a, o, 128u))
+      return BSG_ERR_CUDA;
+    const int sf_kb_total = (kg + 3) / 4;
+    const int atoms_k = o.fp4 ? 2 : 1;
+    if (e8m0b) {
+      std::memset(&tsa, 0, sizeof(tsa));   // unused: the kernel builds its scale atoms
+      std::memset(&tsb, 0, sizeof(tsb));
+    } else if (!make_sf_tmap(&tsa, o.sfa, static_cast<long long>((a.m + 127) / 128) * sf_kb_total, a.batch,
+                             o.sfa_bs, atoms_k) ||
+               !make_sf_tmap(&tsb, o.sfb, static_cast<long long>((a.n + 127) / 128) * sf_kb_total, a.batch,
+                             o.sfb_bs, atoms_k)) {
+      return BSG_ERR_CUDA;
+    }
+    bsg::Mx2Params q{};
+    q.m = a.m;
+    q.n = a.n;
+    q.k = a.k;
+    q.batch = a.batch;
+    q.num_kb = pl.num_kb;
+    q.tiles_m = (a.m + 255) / 256;
+    q.tiles_n = (a.n + 255) / 256;
+    q.total_units = q.tiles_m * q.tiles_n * a.batch;
+    q.group_m = std::min(q.tiles_m, kGroupM / 2);
+    q.sf_kb_total = sf_kb_total;
+    q.sfa_row_blocks = (a.m + 127) / 128;
+    q.sfb_row_blocks = (a.n + 127) / 128;
+    q.sfa = o.sfa;
+    q.sfb = o.sfb;
+    q.sfa_ld = o.sfa_ld;
+    q.sfb_ld = o.sfb_ld;
+    q.sfa_batch_stride = o.sfa_bs;
+    q.sfb_batch_stride = o.sfb_bs;
+    q.c = a.ptr_c;
+    q.ldc = a.stride_c;
+    q.c_batch_stride = a.stride_c_batch;
+    q.timeout_ns = kTimeoutNs;
+    int clusters = std::min(q.total_units, dev.sms / 2);
+    if (a.grid_blocks > 0) clusters = std::min(clusters, std::max(1, a.grid_blocks / 2));
+    return mx2_launch(o.fp4, o.a_mn, o.bmode, o.sfmode, ta, tb, tsa, tsb, q, 2 * clusters, st);
+  }
+
+  CUtensorMap ta, tb;
+  if (!make_operand_tmap(&ta, a.ptr_a, o.a_cols, o.a_rows, a.stride_a, a.stride_a_batch, a.batch, 128u) ||
+      !make_b_tmap(&tb, a, o, static_cast<uint32_t>(pl.bn)))
+    return BSG_ERR_CUDA;
+  MxParams p{};
+  p.m = a.m;
+  p.n = a.n;
+  p.k = a.k;
+  p.batch = a.batch;
+  p.num_kb = pl.num_kb;
+  p.tiles_m = pl.tiles_m;
+  p.tiles_n = pl.tiles_n;
+  p.split_k = pl.split;
+  p.kb_per_split = pl.kb_per;
+  p.total_units = pl.tiles_m * pl.tiles_n * a.batch * pl.split;
+  p.group_m = std::min(pl.tiles_m, kGroupM);
+  p.sfa = o.sfa;
+  p.sfb = o.sfb;
+  p.sfa_batch_stride = o.sfa_bs;
+  p.sfb_batch_stride = o.sfb_bs;
+  p.sf_kb_total = (kg + 3) / 4;
+  p.sfb_row_blocks = (a.n + 127) / 128;
+  p.sfa_ld = o.sfa_ld;
+  p.sfb_ld = o.sfb_ld;
+  p.c = a.ptr_c;
+  p.ldc = a.stride_c;
+  p.c_batch_stride = a.stride_c_batch;
+  p.ws = pl.split > 1 ? o.partials : nullptr;
+  p.timeout_ns = kTimeoutNs;
+  const int grid = grid_for(p.total_units, dev, a.grid_blocks);
+  const bool f32 = a.out_dtype == BSG_OUT_FP32;
+  int rc;
+  if (e8m0b)
+    rc = pl.bn == 256 ? mx_launch_e8m0b<256>(f32, ta, tb, p, grid, st) : mx_launch_e8m0b<128>(f32, ta, tb, p, grid, st);
+  else if (pl.bn == 256)
+    rc = o.fp4 ? mx_launch_bn<256, 1>(o.a_mn, o.bmode, f32, ta, tb, p, grid, st)
+               : mx_launch_bn<256, 0>(o.a_mn, o.bmode, f32, ta, tb, p, grid, st);
+  else
+    rc = o.fp4 ? mx_launch_bn<128, 1>(o.a_mn, o.bmode, f32, ta, tb, p, grid, st)
+               : mx_launch_bn<128, 0>(o.a_mn, o.bmode, f32, ta, tb, p, grid, st);
+  if (rc != BSG_OK) return rc;
+  if (pl.split > 1) return splitk_reduce(p.ws, a, pl.split, dev.sms, st);
+  return BSG_OK;
+}
+
 
 int pack_sf_launch(const void* src, int src_stride, void* dst, int rows, int kg, int fmt,
                    int unpack, cudaStream_t st) {
@@ -331,36 +525,44 @@ int mx_run(const bsgemm_args* args, bool fp4, cudaStream_t st) {
   if (a.k % (fp4 ? 256 : 128)) return BSG_ERR_INVALID_VALUE;
   const bool a_km = (a.layout & 1) != 0, b_km = (a.layout & 2) != 0;
   if (fp4 && (!a_km || !b_km)) return BSG_ERR_UNSUPPORTED;   // .kind::mxf4 is K-major only
-  if (a.b_format != BSG_B_RAW) return BSG_ERR_UNSUPPORTED;   // repack with bsgemm_pack_b
+  if (a.b_format != BSG_B_RAW && a.b_format != BSG_B_SHUFFLE16) return BSG_ERR_UNSUPPORTED;
+  const bool shuffled = a.b_format == BSG_B_SHUFFLE16;
+  if (shuffled && !b_km) return BSG_ERR_UNSUPPORTED;   // shuffle_weight is a K-major format
   for (int f : {a.sfa_format, a.sfb_format})
     if (f != BSG_SF_NATIVE && f != BSG_SF_ROWMAJOR) return BSG_ERR_UNSUPPORTED;
 
-  const long long kbytes = fp4 ? a.k / 2 : a.k;
+  MxOperands o;
+  o.fp4 = fp4;
+  o.a_mn = !a_km;
+  o.bmode = shuffled ? bsg::kBShuffle16 : (b_km ? bsg::kBKMajor : bsg::kBMNMajor);
+  o.kbytes = fp4 ? a.k / 2 : a.k;
   // A: K-major [M, kbytes] with ld stride_a, or M-major [K, M] with ld stride_a
-  const long long a_rows = a_km ? a.m : a.k, a_cols = a_km ? kbytes : a.m;
-  const long long b_rows = b_km ? a.n : a.k, b_cols = b_km ? kbytes : a.n;
-  if (a.stride_a < a_cols || a.stride_a % 16 || a.stride_b < b_cols || a.stride_b % 16)
+  o.a_rows = a_km ? a.m : a.k;
+  o.a_cols = a_km ? o.kbytes : a.m;
+  o.b_rows = b_km ? a.n : a.k;
+  o.b_cols = b_km ? o.kbytes : a.n;
+  if (a.stride_a < o.a_cols || a.stride_a % 16 || a.stride_b < o.b_cols || a.stride_b % 16)
     return BSG_ERR_ALIGNMENT;
+  if (shuffled && (a.n % 16 || a.stride_b != o.kbytes)) return BSG_ERR_INVALID_VALUE;   // dense 16x16 tiles
   if (!aligned16(a.ptr_a) || !aligned16(a.ptr_b)) return BSG_ERR_ALIGNMENT;
-  if (a.batch > 1 && (a.stride_a_batch < a_rows * a.stride_a || a.stride_a_batch % 16 ||
-                      a.stride_b_batch < b_rows * a.stride_b || a.stride_b_batch % 16))
+  if (a.batch > 1 && (a.stride_a_batch < o.a_rows * a.stride_a || a.stride_a_batch % 16 ||
+                      a.stride_b_batch < o.b_rows * a.stride_b || a.stride_b_batch % 16))
     return BSG_ERR_INVALID_VALUE;
   const int kg = a.k / 32;
   // scale operands
   const size_t sfa_nat = native_sf_bytes(a.m, kg), sfb_nat = native_sf_bytes(a.n, kg);
-  long long sfa_bs = 0, sfb_bs = 0;
   if (a.sfa_format == BSG_SF_NATIVE) {
     if (!aligned16(a.ptr_sfa)) return BSG_ERR_ALIGNMENT;
-    sfa_bs = a.batch > 1 ? (a.stride_sfa_batch ? a.stride_sfa_batch : static_cast<long long>(sfa_nat)) : 0;
-    if (sfa_bs % 16 || (a.batch > 1 && sfa_bs < static_cast<long long>(sfa_nat))) return BSG_ERR_INVALID_VALUE;
+    o.sfa_bs = a.batch > 1 ? (a.stride_sfa_batch ? a.stride_sfa_batch : static_cast<long long>(sfa_nat)) : 0;
+    if (o.sfa_bs % 16 || (a.batch > 1 && o.sfa_bs < static_cast<long long>(sfa_nat))) return BSG_ERR_INVALID_VALUE;
   } else if (a.stride_sfa < kg ||
              (a.batch > 1 && a.stride_sfa_batch < static_cast<long long>(a.m) * a.stride_sfa)) {
     return BSG_ERR_INVALID_VALUE;
   }
   if (a.sfb_format == BSG_SF_NATIVE) {
     if (!aligned16(a.ptr_sfb)) return BSG_ERR_ALIGNMENT;
-    sfb_bs = a.batch > 1 ? (a.stride_sfb_batch ? a.stride_sfb_batch : static_cast<long long>(sfb_nat)) : 0;
-    if (sfb_bs % 16 || (a.batch > 1 && sfb_bs < static_cast<long long>(sfb_nat))) return BSG_ERR_INVALID_VALUE;
+    o.sfb_bs = a.batch > 1 ? (a.stride_sfb_batch ? a.stride_sfb_batch : static_cast<long long>(sfb_nat)) : 0;
+    if (o.sfb_bs % 16 || (a.batch > 1 && o.sfb_bs < static_cast<long long>(sfb_nat))) return BSG_ERR_INVALID_VALUE;
   } else if (a.stride_sfb < kg ||
              (a.batch > 1 && a.stride_sfb_batch < static_cast<long long>(a.n) * a.stride_sfb)) {
     return BSG_ERR_INVALID_VALUE;
@@ -368,8 +570,8 @@ int mx_run(const bsgemm_args* args, bool fp4, cudaStream_t st) {
   // C must not overlap an input
   const uint64_t c_bytes =
       operand_bytes(a.m, a.stride_c, a.stride_c_batch, a.batch) * (a.out_dtype == BSG_OUT_BF16 ? 2 : 4);
-  if (overlaps(a.ptr_c, c_bytes, a.ptr_a, operand_bytes(a_rows, a.stride_a, a.stride_a_batch, a.batch)) ||
-      overlaps(a.ptr_c, c_bytes, a.ptr_b, operand_bytes(b_rows, a.stride_b, a.stride_b_batch, a.batch)))
+  if (overlaps(a.ptr_c, c_bytes, a.ptr_a, operand_bytes(o.a_rows, a.stride_a, a.stride_a_batch, a.batch)) ||
+      overlaps(a.ptr_c, c_bytes, a.ptr_b, operand_bytes(o.b_rows, a.stride_b, a.stride_b_batch, a.batch)))
     return BSG_ERR_INVALID_VALUE;
 
   MxPlan pl;
@@ -387,145 +589,118 @@ int mx_run(const bsgemm_args* args, bool fp4, cudaStream_t st) {
   if (need && !aligned16(a.workspace)) return BSG_ERR_ALIGNMENT;
   uint8_t* ws = static_cast<uint8_t*>(a.workspace);
   if (need && overlaps(a.ptr_c, c_bytes, ws, need)) return BSG_ERR_INVALID_VALUE;
+  if (a.kernel == BSG_KERNEL_PAIR && pl.split > 1) return BSG_ERR_UNSUPPORTED;
 
   // scales in row-major form are packed into the workspace first
-  const uint8_t* sfa = static_cast<const uint8_t*>(a.ptr_sfa);
-  const uint8_t* sfb = static_cast<const uint8_t*>(a.ptr_sfb);
+  o.sfa = static_cast<const uint8_t*>(a.ptr_sfa);
+  o.sfb = static_cast<const uint8_t*>(a.ptr_sfb);
   if (a.sfa_format == BSG_SF_ROWMAJOR) {
     for (int bb = 0; bb < a.batch; ++bb)
-      if ((rc = pack_sf_launch(sfa + static_cast<long long>(bb) * a.stride_sfa_batch, a.stride_sfa,
+      if ((rc = pack_sf_launch(o.sfa + static_cast<long long>(bb) * a.stride_sfa_batch, a.stride_sfa,
                                ws + bb * sfa_nat, a.m, kg, BSG_SF_ROWMAJOR, 0, st)) != BSG_OK)
         return rc;
-    sfa = ws;
-    sfa_bs = static_cast<long long>(sfa_nat);
+    o.sfa = ws;
+    o.sfa_bs = static_cast<long long>(sfa_nat);
   }
   if (a.sfb_format == BSG_SF_ROWMAJOR) {
     for (int bb = 0; bb < a.batch; ++bb)
-      if ((rc = pack_sf_launch(sfb + static_cast<long long>(bb) * a.stride_sfb_batch, a.stride_sfb,
+      if ((rc = pack_sf_launch(o.sfb + static_cast<long long>(bb) * a.stride_sfb_batch, a.stride_sfb,
                                ws + pl.ws_sfa + bb * sfb_nat, a.n, kg, BSG_SF_ROWMAJOR, 0, st)) != BSG_OK)
         return rc;
-    sfb = ws + pl.ws_sfa;
-    sfb_bs = static_cast<long long>(sfb_nat);
+    o.sfb = ws + pl.ws_sfa;
+    o.sfb_bs = static_cast<long long>(sfb_nat);
   }
+  o.partials = pl.split > 1 ? reinterpret_cast<float*>(ws + pl.ws_sfa + pl.ws_sfb) : nullptr;
+  return mx_launch_planned(a, o, pl, dev, st);
+}
 
-  // CTA-pair path: enough 256 x 256 tiles to fill the machine, no split-K
-  const long long pair_tiles = static_cast<long long>((a.m + 255) / 256) * ((a.n + 255) / 256) * a.batch;
-  const bool use_pair = a.kernel == BSG_KERNEL_PAIR ||
-                        (a.kernel == BSG_KERNEL_AUTO && pl.split == 1 && a.out_dtype == BSG_OUT_BF16 &&
-                         pair_tiles * 2 >= dev.sms);
-  if (a.kernel == BSG_KERNEL_PAIR && pl.split > 1) return BSG_ERR_UNSUPPORTED;
-  if (use_pair && (sfa_bs % 512 || sfb_bs % 512)) return BSG_ERR_UNSUPPORTED;
-  if (use_pair) {
-    CUtensorMap ta, tb, tsa, tsb;
-    const uint32_t box[3] = {128u, 128u, 1u};
-    {
-      const uint64_t dims[3] = {static_cast<uint64_t>(a_cols), static_cast<uint64_t>(a_rows),
-                                static_cast<uint64_t>(a.batch)};
-      const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_a),
-                                   static_cast<uint64_t>(a.batch > 1 ? a.stride_a_batch
-                                                                     : a_rows * a.stride_a)};
-      if (!make_tmap_u8(&ta, a.ptr_a, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
-    }
-    {
-      const uint64_t dims[3] = {static_cast<uint64_t>(b_cols), static_cast<uint64_t>(b_rows),
-                                static_cast<uint64_t>(a.batch)};
-      const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_b),
-                                   static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch
-                                                                     : b_rows * a.stride_b)};
-      if (!make_tmap_u8(&tb, a.ptr_b, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
-    }
-    const int sf_kb_total = (kg + 3) / 4;
-    const int atoms_k = fp4 ? 2 : 1;
-    if (!make_sf_tmap(&tsa, sfa, static_cast<long long>((a.m + 127) / 128) * sf_kb_total, a.batch, sfa_bs,
-                      atoms_k) ||
-        !make_sf_tmap(&tsb, sfb, static_cast<long long>((a.n + 127) / 128) * sf_kb_total, a.batch, sfb_bs,
-                      atoms_k))
-      return BSG_ERR_CUDA;
-    bsg::Mx2Params q{};
-    q.m = a.m;
-    q.n = a.n;
-    q.k = a.k;
-    q.batch = a.batch;
-    q.num_kb = pl.num_kb;
-    q.tiles_m = (a.m + 255) / 256;
-    q.tiles_n = (a.n + 255) / 256;
-    q.total_units = q.tiles_m * q.tiles_n * a.batch;
-    q.group_m = std::min(q.tiles_m, kGroupM / 2);
-    q.sf_kb_total = sf_kb_total;
-    q.sfa_row_blocks = (a.m + 127) / 128;
-    q.sfb_row_blocks = (a.n + 127) / 128;
-    q.c = a.ptr_c;
-    q.ldc = a.stride_c;
-    q.c_batch_stride = a.stride_c_batch;
-    q.timeout_ns = kTimeoutNs;
-    if (a.out_dtype != BSG_OUT_BF16) return BSG_ERR_UNSUPPORTED;
-    int clusters = std::min(q.total_units, dev.sms / 2);
-    if (a.grid_blocks > 0) clusters = std::min(clusters, std::max(1, a.grid_blocks / 2));
-    return mx2_launch(fp4, !a_km, !b_km, ta, tb, tsa, tsb, q, 2 * clusters, st);
-  }
+// ---------------------------------------------------------------------------
+// E8M0 1x128 / 128x128 block scale (the reference's launch_blockscale_bpreshuffle)
+// ---------------------------------------------------------------------------
+// Element count rows * cols * batch * bytes below 2^31, as the reference's
+// bounded_count (source_snapshot/gemm_a8w8_blockscale_bpreshuffle_launch.cc:10-15).
+bool bounded_count(int rows, int cols, int batch, int bytes) {
+  const uint64_t limit = static_cast<uint64_t>(INT32_MAX) / static_cast<uint64_t>(bytes);
+  if (rows <= 0 || cols <= 0 || batch <= 0 || static_cast<uint64_t>(rows) > limit / static_cast<uint64_t>(cols))
+    return false;
+  return static_cast<uint64_t>(batch) <= limit / (static_cast<uint64_t>(rows) * static_cast<uint64_t>(cols));
+}
 
-  // tensor maps (rank 3: inner, rows, batch)
-  CUtensorMap ta, tb;
-  {
-    const uint64_t dims[3] = {static_cast<uint64_t>(a_cols), static_cast<uint64_t>(a_rows),
-                              static_cast<uint64_t>(a.batch)};
-    const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_a),
-                                 static_cast<uint64_t>(a.batch > 1 ? a.stride_a_batch
-                                                                   : a_rows * a.stride_a)};
-    const uint32_t box[3] = {128u, 128u, 1u};
-    if (!make_tmap_u8(&ta, a.ptr_a, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
+// Returns a cudaError_t value.  Validation follows the reference launcher
+// (…_launch.cc:33-54) except that M may be any positive size and N a
+// multiple of 128 (the reference: M, N % 256); the tile shape is planned
+// here, so `tiles` is accepted (0 or 1) and otherwise unused.
+int e8m0b_run(const bsgemm_args& in, bool bf16, cudaStream_t st) {
+  const bsgemm_args& a = in;
+  if (!a.ptr_a || !a.ptr_b || !a.ptr_c || !a.ptr_sfa || !a.ptr_sfb) return cudaErrorInvalidValue;
+  if (a.m <= 0 || a.n <= 0 || a.k <= 0 || a.batch <= 0 || a.n % 128 || a.k % 128)
+    return cudaErrorInvalidValue;
+  const int kb = a.k / 128, nb = a.n / 128;
+  if (!bounded_count(a.m, a.k, a.batch, 1) || !bounded_count(a.n, a.k, a.batch, 1) ||
+      !bounded_count(a.m, a.n, a.batch, bf16 ? 2 : 4) || !bounded_count(a.m, kb, a.batch, 1) ||
+      !bounded_count(nb, kb, a.batch, 1))
+    return cudaErrorInvalidValue;
+  if (a.stride_a != a.k || a.stride_b != a.k || a.stride_c != a.n || a.stride_a_batch != a.m * a.k ||
+      a.stride_b_batch != a.n * a.k || a.stride_c_batch != a.m * a.n || a.stride_sfa != a.m ||
+      a.stride_sfb != kb || a.stride_sfa_batch != a.m * kb || a.stride_sfb_batch != nb * kb)
+    return cudaErrorInvalidValue;
+  const uint64_t c_bytes = static_cast<uint64_t>(a.m) * a.n * a.batch * (bf16 ? 2 : 4);
+  if (overlaps(a.ptr_c, c_bytes, a.ptr_a, static_cast<uint64_t>(a.stride_a_batch) * a.batch) ||
+      overlaps(a.ptr_c, c_bytes, a.ptr_b, static_cast<uint64_t>(a.stride_b_batch) * a.batch) ||
+      overlaps(a.ptr_c, c_bytes, a.ptr_sfa, static_cast<uint64_t>(a.stride_sfa_batch) * a.batch) ||
+      overlaps(a.ptr_c, c_bytes, a.ptr_sfb, static_cast<uint64_t>(a.stride_sfb_batch) * a.batch))
+    return cudaErrorInvalidValue;
+  // TMA and the vector stores need 16-byte aligned A, B and C
+  if (!aligned16(a.ptr_a) || !aligned16(a.ptr_b) || !aligned16(a.ptr_c)) return cudaErrorInvalidValue;
+  DevInfo dev;
+  if (device_info(&dev) != BSG_OK) {
+    const cudaError_t e = cudaGetLastError();
+    return e != cudaSuccess ? e : cudaErrorUnknown;
   }
-  {
-    const uint64_t dims[3] = {static_cast<uint64_t>(b_cols), static_cast<uint64_t>(b_rows),
-                              static_cast<uint64_t>(a.batch)};
-    const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_b),
-                                 static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch
-                                                                   : b_rows * a.stride_b)};
-    const uint32_t box[3] = {128u, b_km ? static_cast<uint32_t>(pl.bn) : 128u, 1u};
-    if (!make_tmap_u8(&tb, a.ptr_b, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
-  }
-  MxParams p{};
-  p.m = a.m;
-  p.n = a.n;
-  p.k = a.k;
-  p.batch = a.batch;
-  p.num_kb = pl.num_kb;
-  p.tiles_m = pl.tiles_m;
-  p.tiles_n = pl.tiles_n;
-  p.split_k = pl.split;
-  p.kb_per_split = pl.kb_per;
-  p.total_units = pl.tiles_m * pl.tiles_n * a.batch * pl.split;
-  p.group_m = std::min(pl.tiles_m, kGroupM);
-  p.sfa = sfa;
-  p.sfb = sfb;
-  p.sfa_batch_stride = sfa_bs;
-  p.sfb_batch_stride = sfb_bs;
-  p.sf_kb_total = (kg + 3) / 4;
-  p.sfb_row_blocks = (a.n + 127) / 128;
-  p.c = a.ptr_c;
-  p.ldc = a.stride_c;
-  p.c_batch_stride = a.stride_c_batch;
-  p.ws = pl.split > 1 ? reinterpret_cast<float*>(ws + pl.ws_sfa + pl.ws_sfb) : nullptr;
-  p.timeout_ns = kTimeoutNs;
-  const int grid = grid_for(p.total_units, dev, a.grid_blocks);
-  const bool f32 = a.out_dtype == BSG_OUT_FP32;
-  rc = pl.bn == 256 ? (fp4 ? mx_launch_bn<256, 1>(!a_km, !b_km, f32, ta, tb, p, grid, st)
-                           : mx_launch_bn<256, 0>(!a_km, !b_km, f32, ta, tb, p, grid, st))
-                    : (fp4 ? mx_launch_bn<128, 1>(!a_km, !b_km, f32, ta, tb, p, grid, st)
-                           : mx_launch_bn<128, 0>(!a_km, !b_km, f32, ta, tb, p, grid, st));
-  if (rc != BSG_OK) return rc;
-  if (pl.split > 1) return splitk_reduce(p.ws, a, pl.split, dev.sms, st);
-  return BSG_OK;
+  if (!dev.sm100) return cudaErrorInvalidDeviceFunction;
+
+  bsgemm_args g = a;
+  g.layout = BSG_LAYOUT_TN;
+  g.b_format = BSG_B_SHUFFLE16;
+  g.sfa_format = BSG_SF_NATIVE;   // no repack: the kernel builds its scale atoms
+  g.sfb_format = BSG_SF_NATIVE;
+  g.out_dtype = bf16 ? BSG_OUT_BF16 : BSG_OUT_FP32;
+  g.split_k = 1;                  // no workspace in this ABI
+  g.workspace = nullptr;
+  g.workspace_bytes = 0;
+  g.grid_blocks = 0;
+  g.kernel = BSG_KERNEL_AUTO;
+  MxOperands o;
+  o.bmode = bsg::kBShuffle16;
+  o.sfmode = bsg::kSfE8m0Block128;
+  o.kbytes = a.k;
+  o.a_rows = a.m;
+  o.a_cols = a.k;
+  o.b_rows = a.n;
+  o.b_cols = a.k;
+  o.sfa = static_cast<const uint8_t*>(a.ptr_sfa);
+  o.sfb = static_cast<const uint8_t*>(a.ptr_sfb);
+  o.sfa_bs = a.stride_sfa_batch;
+  o.sfb_bs = a.stride_sfb_batch;
+  o.sfa_ld = a.stride_sfa;
+  o.sfb_ld = a.stride_sfb;
+  MxPlan pl;
+  mx_plan(g, false, dev, pl, false);
+  t_last_cuda_error = cudaSuccess;
+  const int rc = mx_launch_planned(g, o, pl, dev, st);
+  if (rc == BSG_OK) return cudaSuccess;
+  if (rc == BSG_ERR_CUDA) return t_last_cuda_error != cudaSuccess ? t_last_cuda_error : cudaErrorUnknown;
+  return cudaErrorNotSupported;
 }
 
 // ---------------------------------------------------------------------------
 // FP8 block-scale (fp32 scales)
 // ---------------------------------------------------------------------------
-template <bool kKPanel, bool kOutF32>
+template <int kBFmt, bool kOutF32>
 int fp8b_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockParams& p, int grid,
                   cudaStream_t st) {
   using Cfg = Fp8BlockCfg<128>;
-  auto* kern = bsg::fp8_block_gemm_kernel<128, kKPanel, kOutF32>;
+  auto* kern = bsg::fp8_block_gemm_kernel<128, kBFmt, kOutF32>;
   if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
   kern<<<grid, 256, Cfg::kSmemBytes, st>>>(ta, tb, p);
   return launch_status();
@@ -553,23 +728,37 @@ void fp8b_plan(const bsgemm_args& a, const DevInfo& dev, Plan& pl, bool allow_au
   }
 }
 
-template <int MN, bool kKPanel, bool kOutF32>
+template <int MN, int kBFmt, bool kOutF32>
 int swap_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockParams& p, int grid,
                   cudaStream_t st) {
   using Cfg = bsg::SwapCfg<MN>;
-  auto* kern = bsg::fp8_block_swap_kernel<MN, kKPanel, kOutF32>;
+  auto* kern = bsg::fp8_block_swap_kernel<MN, kBFmt, kOutF32>;
   if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
   kern<<<grid, 256, Cfg::kSmemBytes, st>>>(ta, tb, p);
   return launch_status();
 }
 
+template <int kBFmt>
+int fp8b_launch_fmt(bool f32, const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockParams& p,
+                    int grid, cudaStream_t st) {
+  return f32 ? fp8b_launch_t<kBFmt, true>(ta, tb, p, grid, st) : fp8b_launch_t<kBFmt, false>(ta, tb, p, grid, st);
+}
+
+template <int MN, int kBFmt>
+int swap_launch_fmt(bool f32, const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockParams& p,
+                    int grid, cudaStream_t st) {
+  return f32 ? swap_launch_t<MN, kBFmt, true>(ta, tb, p, grid, st)
+             : swap_launch_t<MN, kBFmt, false>(ta, tb, p, grid, st);
+}
+
 template <int MN>
-int swap_launch_mn(bool kpanel, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
+int swap_launch_mn(int fmt, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
                    const Fp8BlockParams& p, int grid, cudaStream_t st) {
-  return kpanel ? (f32 ? swap_launch_t<MN, true, true>(ta, tb, p, grid, st)
-                       : swap_launch_t<MN, true, false>(ta, tb, p, grid, st))
-                : (f32 ? swap_launch_t<MN, false, true>(ta, tb, p, grid, st)
-                       : swap_launch_t<MN, false, false>(ta, tb, p, grid, st));
+  switch (fmt) {
+    case bsg::kFmtKPanel: return swap_launch_fmt<MN, bsg::kFmtKPanel>(f32, ta, tb, p, grid, st);
+    case bsg::kFmtShuffle16: return swap_launch_fmt<MN, bsg::kFmtShuffle16>(f32, ta, tb, p, grid, st);
+    default: return swap_launch_fmt<MN, bsg::kFmtRaw>(f32, ta, tb, p, grid, st);
+  }
 }
 
 int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
@@ -581,16 +770,20 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
   if (!dev.sm100) return BSG_ERR_ARCH;
   if (a.k % 128) return BSG_ERR_INVALID_VALUE;
   if (a.layout != BSG_LAYOUT_TN) return BSG_ERR_UNSUPPORTED;
-  if (a.b_format != BSG_B_RAW && a.b_format != BSG_B_KPANEL128) return BSG_ERR_UNSUPPORTED;
+  if (a.b_format != BSG_B_RAW && a.b_format != BSG_B_KPANEL128 && a.b_format != BSG_B_SHUFFLE16)
+    return BSG_ERR_UNSUPPORTED;
   if (a.kernel == BSG_KERNEL_SWAP && a.m > 64) return BSG_ERR_UNSUPPORTED;
   if (a.kernel == BSG_KERNEL_PAIR) return BSG_ERR_UNSUPPORTED;
   if (a.sfa_format != BSG_SF_ROWMAJOR && a.sfa_format != BSG_SF_KMAJOR_T) return BSG_ERR_UNSUPPORTED;
   if (a.sfb_format != BSG_SF_ROWMAJOR) return BSG_ERR_UNSUPPORTED;
   const bool kpanel = a.b_format == BSG_B_KPANEL128;
+  const bool shuf = a.b_format == BSG_B_SHUFFLE16;
+  const int bfmt = kpanel ? bsg::kFmtKPanel : shuf ? bsg::kFmtShuffle16 : bsg::kFmtRaw;
   const int kb = a.k / 128, nb = (a.n + 127) / 128;
   if (a.stride_a < a.k || a.stride_a % 16 || !aligned16(a.ptr_a) || !aligned16(a.ptr_b))
     return BSG_ERR_ALIGNMENT;
   if (kpanel ? a.stride_b != 128 : (a.stride_b < a.k || a.stride_b % 16)) return BSG_ERR_ALIGNMENT;
+  if (shuf && (a.stride_b != a.k || a.n % 16)) return BSG_ERR_INVALID_VALUE;   // dense 16x16 tiles
   const long long b_elems = kpanel ? static_cast<long long>(a.n) * a.k : static_cast<long long>(a.n) * a.stride_b;
   if (a.batch > 1 && (a.stride_a_batch < static_cast<long long>(a.m) * a.stride_a ||
                       a.stride_a_batch % 16 || a.stride_b_batch < b_elems || a.stride_b_batch % 16))
@@ -647,7 +840,9 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
     const uint32_t box[3] = {128u, swap ? static_cast<uint32_t>(swap_mn(a.m)) : 128u, 1u};
     if (!make_tmap_u8(&ta, a.ptr_a, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
   }
-  if (kpanel) {
+  if (shuf) {
+    if (!make_shuffle16_tmap(&tb, a.ptr_b, a.n, a.k, a.stride_b_batch, a.batch, 128u)) return BSG_ERR_CUDA;
+  } else if (kpanel) {
     const uint64_t dims[4] = {128u, static_cast<uint64_t>(a.n), static_cast<uint64_t>(kb),
                               static_cast<uint64_t>(a.batch)};
     const uint64_t strides[3] = {128u, static_cast<uint64_t>(a.n) * 128u,
@@ -691,15 +886,16 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
   const bool f32 = a.out_dtype == BSG_OUT_FP32;
   if (fp8b_use_swap(a)) {
     switch (swap_mn(a.m)) {
-      case 16: rc = swap_launch_mn<16>(kpanel, f32, ta, tb, p, grid, st); break;
-      case 32: rc = swap_launch_mn<32>(kpanel, f32, ta, tb, p, grid, st); break;
-      default: rc = swap_launch_mn<64>(kpanel, f32, ta, tb, p, grid, st); break;
+      case 16: rc = swap_launch_mn<16>(bfmt, f32, ta, tb, p, grid, st); break;
+      case 32: rc = swap_launch_mn<32>(bfmt, f32, ta, tb, p, grid, st); break;
+      default: rc = swap_launch_mn<64>(bfmt, f32, ta, tb, p, grid, st); break;
     }
   } else {
-    rc = kpanel ? (f32 ? fp8b_launch_t<true, true>(ta, tb, p, grid, st)
-                       : fp8b_launch_t<true, false>(ta, tb, p, grid, st))
-                : (f32 ? fp8b_launch_t<false, true>(ta, tb, p, grid, st)
-                       : fp8b_launch_t<false, false>(ta, tb, p, grid, st));
+    switch (bfmt) {
+      case bsg::kFmtKPanel: rc = fp8b_launch_fmt<bsg::kFmtKPanel>(f32, ta, tb, p, grid, st); break;
+      case bsg::kFmtShuffle16: rc = fp8b_launch_fmt<bsg::kFmtShuffle16>(f32, ta, tb, p, grid, st); break;
+      default: rc = fp8b_launch_fmt<bsg::kFmtRaw>(f32, ta, tb, p, grid, st); break;
+    }
   }
   if (rc != BSG_OK) return rc;
   if (pl.split > 1) return splitk_reduce(p.ws, a, pl.split, dev.sms, st);
@@ -801,11 +997,13 @@ int bsgemm_pack_scales(const void* src, int src_stride, void* dst, int rows, int
 
 int launch_blockscale_bpreshuffle(const void* kargs, int output_bf16, int tiles,
                                   bsg_stream_t stream) {
-  (void)kargs;
-  (void)output_bf16;
-  (void)tiles;
-  (void)stream;
-  return static_cast<int>(cudaErrorNotSupported);
+  if (!kargs || (output_bf16 != 0 && output_bf16 != 1) || (tiles != 0 && tiles != 1))
+    return static_cast<int>(cudaErrorInvalidValue);
+  static_assert(offsetof(bsgemm_args, layout) == 96, "96-byte reference prefix");
+  bsgemm_args a;
+  bsgemm_args_init(&a);
+  std::memcpy(&a, kargs, 96);
+  return e8m0b_run(a, output_bf16 == 1, reinterpret_cast<cudaStream_t>(stream));
 }
 
 const char* bsgemm_strerror(int status) {

@@ -44,6 +44,26 @@ struct Fp8BlockParams {
   unsigned long long timeout_ns;
 };
 
+// Weight (B) storage formats read in place:
+//   kFmtRaw        [N, K] K-major rows (128B-swizzled stage tiles);
+//   kFmtKPanel     the reference's shuffle_b K panels B'[K/128][N][128]
+//                  (block_scale_gemm_bpreshuffle/..._host.cc:96-111);
+//   kFmtShuffle16  aiter's shuffle_weight(16,16) [N/16][K/16][16][16]
+//                  (source_snapshot/gemm_a8w8_mxfp8_scale_host.cc:161-179),
+//                  landed by a 5-D tensor map in the canonical no-swizzle
+//                  K-major layout (see mx_gemm.cuh).
+constexpr int kFmtRaw = 0, kFmtKPanel = 1, kFmtShuffle16 = 2;
+
+// Shared-memory descriptor of K step t (32 bytes of K) of a 128-byte K stage
+// of a weight tile stored in format kBFmt.
+template <int kBFmt>
+__device__ __forceinline__ uint64_t weight_sdesc(uint32_t tile_addr, int t) {
+  if constexpr (kBFmt == kFmtShuffle16)
+    return make_sdesc(tile_addr + 256u * static_cast<uint32_t>(t), 128u, 1024u, kLayoutNone);
+  else
+    return make_sdesc(tile_addr + 32u * static_cast<uint32_t>(t), 16u, 1024u, kLayoutSW128);
+}
+
 template <int BN>
 struct Fp8BlockCfg {
   static_assert(BN == 128, "promotion accumulator holds 128 columns per thread");
@@ -57,7 +77,7 @@ struct Fp8BlockCfg {
   static constexpr uint32_t kTmemCols = 2u * BN;  // two accumulator buffers
 };
 
-template <int BN, bool kKPanel, bool kOutF32>
+template <int BN, int kBFmt, bool kOutF32>
 __global__ void __launch_bounds__(256, 1)
     fp8_block_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                           const __grid_constant__ CUtensorMap tmB, const Fp8BlockParams p) {
@@ -129,8 +149,11 @@ __global__ void __launch_bounds__(256, 1)
         if (issuer) {
           mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
           tma_load_3d(sA + stage * Cfg::kABytes, &tmA, fb, kb * 128, mt * 128, b);
-          if constexpr (kKPanel)
+          if constexpr (kBFmt == kFmtKPanel)
             tma_load_4d(sB + stage * Cfg::kBBytes, &tmB, fb, 0, nt * BN, kb, b);
+          else if constexpr (kBFmt == kFmtShuffle16)
+            tma_load_5d_hint(sB + stage * Cfg::kBBytes, &tmB, fb, 0, kb * 8, 0, nt * (BN / 16), b,
+                             l2_policy_evict_first());
           else
             tma_load_3d(sB + stage * Cfg::kBBytes, &tmB, fb, kb * 128, nt * BN, b);
         }
@@ -180,7 +203,7 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           const uint64_t adesc = make_sdesc(a_addr + 32u * t, 16u, 1024u, kLayoutSW128);
-          const uint64_t bdesc = make_sdesc(b_addr + 32u * t, 16u, 1024u, kLayoutSW128);
+          const uint64_t bdesc = weight_sdesc<kBFmt>(b_addr, t);
           if (issuer) umma_f8f6f4(d, adesc, bdesc, idesc, t > 0 ? 1u : 0u);
         }
         if (issuer) {

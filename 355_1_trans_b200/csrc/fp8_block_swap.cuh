@@ -61,7 +61,7 @@ struct SwapCfg {
   static_assert(kSmemBytes <= 227u * 1024u, "shared memory");
 };
 
-template <int MN, bool kKPanel, bool kOutF32>
+template <int MN, int kBFmt, bool kOutF32>
 __global__ void __launch_bounds__(256, 1)
     fp8_block_swap_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const Fp8BlockParams p) {
@@ -159,8 +159,10 @@ __global__ void __launch_bounds__(256, 1)
         if (issuer) {
           uint64_t* fb = &full_bar[stage];
           mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
-          if constexpr (kKPanel)
+          if constexpr (kBFmt == kFmtKPanel)
             tma_load_4d_hint(sW + stage * Cfg::kWBytes, &tmB, fb, 0, nt * 128, kb, b, pol_w);
+          else if constexpr (kBFmt == kFmtShuffle16)
+            tma_load_5d_hint(sW + stage * Cfg::kWBytes, &tmB, fb, 0, kb * 8, 0, nt * 8, b, pol_w);
           else
             tma_load_3d_hint(sW + stage * Cfg::kWBytes, &tmB, fb, kb * 128, nt * 128, b, pol_w);
           tma_load_3d_hint(sX + stage * Cfg::kXBytes, &tmA, fb, kb * 128, mt * MN, b, pol_x);
@@ -203,7 +205,7 @@ __global__ void __launch_bounds__(256, 1)
         const uint32_t d = tmem_base + buf * MN;
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-          const uint64_t adesc = make_sdesc(w_addr + 32u * t, 16u, 1024u, kLayoutSW128);
+          const uint64_t adesc = weight_sdesc<kBFmt>(w_addr, t);
           const uint64_t bdesc = make_sdesc(x_addr + 32u * t, 16u, 1024u, kLayoutSW128);
           if (issuer) umma_f8f6f4(d, adesc, bdesc, idesc, t > 0 ? 1u : 0u);
         }

@@ -28,6 +28,26 @@
 // The MMA instruction K is 32 (fp8) / 64 (fp4), i.e. 32 bytes of a 128-byte
 // swizzled row; one stage holds 128 bytes of K per row (128 fp8 / 256 fp4
 // elements) and 1 (fp8) or 2 (fp4) scale atoms per 128 rows.
+//
+// B operand modes (kBMode):
+//   kBKMajor     [N, K] rows, 128B-swizzled K slabs;
+//   kBMNMajor    [K, N] rows, 128B-swizzled N slabs (fp8 only);
+//   kBShuffle16  the reference's shuffle_weight(16,16) byte layout
+//                [N/16][Kbytes/16][16][16] read in place: every 16x16-byte
+//                tile is two 8-row x 16-byte core matrices, so a 5-D tensor
+//                map (core matrix, K chunk, half, N/16, batch) lands a stage
+//                in the canonical no-swizzle K-major layout (K-adjacent core
+//                matrices 128 B apart, 8-row groups 1024 B apart).
+// Scale modes (kSfMode):
+//   kSfNative        per-32-K E8M0 scales as native 512-byte atoms, copied
+//                    with bulk copies;
+//   kSfE8m0Block128  the reference's launch_blockscale_bpreshuffle scales:
+//                    one E8M0 byte per row per 128 K, A's transposed
+//                    [K/128][M], B's per 128 x 128 block [N/128][K/128]
+//                    (source_snapshot/gemm_a8w8_mxfp8_scale_host.cc:216-242).
+//                    Warp 3 rewrites each stage's bytes into atoms with the
+//                    byte replicated over the four 32-K groups, so the
+//                    block-scaled MMA applies one scale per 128 K.
 #pragma once
 
 #include "sm100.cuh"
@@ -48,6 +68,8 @@ struct MxParams {
   long long sfb_batch_stride;
   int sf_kb_total;               // scale atoms along K per 128-row block
   int sfb_row_blocks;            // 128-row blocks of the B scales, ceil(n / 128)
+  long long sfa_ld, sfb_ld;      // kSfE8m0Block128: bytes between K blocks of A's
+                                 // scales / between 128-column blocks of B's
   void* c;                       // output
   long long ldc;                 // elements
   long long c_batch_stride;      // elements
@@ -58,6 +80,9 @@ struct MxParams {
 constexpr int kMxThreads = 384;     // 4 control warps + 8 epilogue warps
 constexpr int kMxEpiThreads = 256;
 constexpr int kMxEpiWarps = 8;      // one tmem_empty arrival per epilogue warp
+
+constexpr int kBKMajor = 0, kBMNMajor = 1, kBShuffle16 = 2;
+constexpr int kSfNative = 0, kSfE8m0Block128 = 1;
 
 template <int BN, int kFp4>
 struct MxCfg {
@@ -106,12 +131,15 @@ __device__ __forceinline__ void store_row32_f32(float* dst, const uint32_t (&r)[
   }
 }
 
-template <int BN, int kFp4, bool kAMN, bool kBMN, bool kOutF32>
+template <int BN, int kFp4, bool kAMN, int kBMode, bool kOutF32, int kSfMode>
 __global__ void __launch_bounds__(kMxThreads, 1)
     mx_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const MxParams p) {
   using Cfg = MxCfg<BN, kFp4>;
   constexpr int S = Cfg::kStages;
+  constexpr bool kBMN = kBMode == kBMNMajor;
+  constexpr bool kBuildSf = kSfMode == kSfE8m0Block128;
+  static_assert(!kBuildSf || !kFp4, "per-128 E8M0 scales are an fp8 format");
 
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzled operand tiles
@@ -134,7 +162,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
 
   if (threadIdx.x == 32) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(&full_bar[i], 1);
+      mbar_init(&full_bar[i], kBuildSf ? 2 : 1);   // + the scale builder's arrival
       mbar_init(&empty_bar[i], 1);
     }
     mbar_init(tmem_full, 1);
@@ -180,7 +208,8 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       // copy only the ones that exist (the columns beyond N are never stored)
       const int sfb_rows = min(Cfg::kSfbRowBlocks, p.sfb_row_blocks - nt * Cfg::kSfbRowBlocks);
       const uint32_t tx_bytes =
-          Cfg::kStageBytes - static_cast<uint32_t>(Cfg::kSfbRowBlocks - sfb_rows) * 512u * Cfg::kSfAtomsK;
+          kBuildSf ? Cfg::kABytes + Cfg::kBBytes
+                   : Cfg::kStageBytes - static_cast<uint32_t>(Cfg::kSfbRowBlocks - sfb_rows) * 512u * Cfg::kSfAtomsK;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
           ok = false;
@@ -197,21 +226,26 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           } else {
             tma_load_3d_hint(a_dst, &tmA, fb, mt * 128, kbyte, b, pol_a);
           }
-          if constexpr (!kBMN) {
+          if constexpr (kBMode == kBKMajor) {
             tma_load_3d_hint(b_dst, &tmB, fb, kbyte, nt * BN, b, pol_b);
+          } else if constexpr (kBMode == kBShuffle16) {
+            // (core-matrix byte, 16-byte K chunk, half, 16-row group, batch)
+            tma_load_5d_hint(b_dst, &tmB, fb, 0, kb * 8, 0, nt * (BN / 16), b, pol_b);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 128; ++j)
               tma_load_3d_hint(b_dst + j * 16384, &tmB, fb, nt * BN + j * 128, kbyte, b, pol_b);
           }
-          const long long atom_k = static_cast<long long>(kb) * Cfg::kSfAtomsK;
-          bulk_load(sSfa + stage * Cfg::kSfaBytes, sfa_tile + atom_k * 512, Cfg::kSfaBytes, fb);
+          if constexpr (!kBuildSf) {
+            const long long atom_k = static_cast<long long>(kb) * Cfg::kSfAtomsK;
+            bulk_load(sSfa + stage * Cfg::kSfaBytes, sfa_tile + atom_k * 512, Cfg::kSfaBytes, fb);
 #pragma unroll
-          for (int r = 0; r < Cfg::kSfbRowBlocks; ++r)
-            if (r < sfb_rows)
-              bulk_load(sSfb + stage * Cfg::kSfbBytes + r * 512 * Cfg::kSfAtomsK,
-                        sfb_tile + (static_cast<long long>(r) * p.sf_kb_total + atom_k) * 512,
-                        512u * Cfg::kSfAtomsK, fb);
+            for (int r = 0; r < Cfg::kSfbRowBlocks; ++r)
+              if (r < sfb_rows)
+                bulk_load(sSfb + stage * Cfg::kSfbBytes + r * 512 * Cfg::kSfAtomsK,
+                          sfb_tile + (static_cast<long long>(r) * p.sf_kb_total + atom_k) * 512,
+                          512u * Cfg::kSfAtomsK, fb);
+          }
         }
         __syncwarp();
         last_stage = stage;
@@ -235,11 +269,15 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     const uint32_t idesc0 = idesc_block_scaled(kFmt, kFmt, kAMN, kBMN, 128, BN);
     // K-major: SBO = 8 rows x 128 B; MN-major: LBO = next 128-element MN slab,
     // SBO = next 8 K rows.
+    // Shuffled B (no swizzle): LBO = next 16-byte K chunk (128 B), SBO = next
+    // 8-row group (1024 B), one MMA step = two K chunks.
+    constexpr bool kBShuf = kBMode == kBShuffle16;
     constexpr uint32_t kALbo = kAMN ? 128u * 128u : 16u;
-    constexpr uint32_t kBLbo = kBMN ? 128u * 128u : 16u;
+    constexpr uint32_t kBLbo = kBMN ? 128u * 128u : kBShuf ? 128u : 16u;
     constexpr uint32_t kSbo = 1024u;
     constexpr uint32_t kKStep = kAMN ? 32u * 128u : 32u;   // bytes per MMA along K (A)
-    constexpr uint32_t kKStepB = kBMN ? 32u * 128u : 32u;
+    constexpr uint32_t kKStepB = kBMN ? 32u * 128u : kBShuf ? 256u : 32u;
+    constexpr uint32_t kBLayout = kBShuf ? kLayoutNone : kLayoutSW128;
     const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
     const uint32_t sSfa0 = smem_u32(sSfa), sSfb0 = smem_u32(sSfb);
     int stage = 0;
@@ -282,7 +320,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           const uint32_t j = kFp4 ? static_cast<uint32_t>(t >> 1) : 0u;
           const uint32_t sf_id = kFp4 ? static_cast<uint32_t>((t & 1) * 2) : static_cast<uint32_t>(t);
           const uint64_t adesc = make_sdesc(a_addr + t * kKStep, kALbo, kSbo, kLayoutSW128);
-          const uint64_t bdesc = make_sdesc(b_addr + t * kKStepB, kBLbo, kSbo, kLayoutSW128);
+          const uint64_t bdesc = make_sdesc(b_addr + t * kKStepB, kBLbo, kSbo, kBLayout);
           const uint32_t idesc = idesc_with_sf_id(idesc0, sf_id, sf_id);
           const uint32_t tsfa = tmem_base + sf_off + Cfg::kColSfa + 4u * j;
           const uint32_t tsfb = tmem_base + sf_off + Cfg::kColSfb + 4u * j * Cfg::kSfbRowBlocks;
@@ -307,6 +345,69 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     if (issuer) tc_commit(drain_bar);
     int dummy = 0;
     mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
+  } else if (warp == 3) {
+    if constexpr (kBuildSf) {
+      // -------------------------------------------------------------- scale builder
+      // Lane l owns 16 bytes of each atom: the words of rows l, l+32, l+64,
+      // l+96, each the row's scale byte repeated for the four 32-K groups.
+      // The next K block's bytes are loaded before waiting for the stage, so
+      // the global-load latency overlaps the pipeline wait.  Missing rows
+      // and column blocks get 0x7F (2^0); their outputs are never stored.
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+        int b, mt, nt, s;
+        decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+        const int kb0 = s * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
+        const int rows = p.m - mt * 128;
+        const int sfb_rows = min(Cfg::kSfbRowBlocks, p.sfb_row_blocks - nt * Cfg::kSfbRowBlocks);
+        const uint8_t* sa = p.sfa + b * p.sfa_batch_stride + mt * 128;
+        const uint8_t* sb = p.sfb + b * p.sfb_batch_stride +
+                            static_cast<long long>(nt) * Cfg::kSfbRowBlocks * p.sfb_ld;
+        uint32_t ca[4], cb[Cfg::kSfbRowBlocks];
+        auto load = [&](int kb, uint32_t (&va)[4], uint32_t (&vb)[Cfg::kSfbRowBlocks]) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int r = static_cast<int>(lane) + 32 * j;
+            const uint32_t v = r < rows ? __ldg(sa + kb * p.sfa_ld + r) : 0x7Fu;
+            va[j] = v * 0x01010101u;
+          }
+#pragma unroll
+          for (int r = 0; r < Cfg::kSfbRowBlocks; ++r) {
+            const uint32_t v = r < sfb_rows ? __ldg(sb + r * p.sfb_ld + kb) : 0x7Fu;
+            vb[r] = v * 0x01010101u;
+          }
+        };
+        if (kb0 < kb1) load(kb0, ca, cb);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          uint32_t na[4], nb[Cfg::kSfbRowBlocks];
+          if (kb + 1 < kb1) load(kb + 1, na, nb);
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          st_shared_v4(sSfa + stage * Cfg::kSfaBytes + lane * 16u, ca[0], ca[1], ca[2], ca[3]);
+#pragma unroll
+          for (int r = 0; r < Cfg::kSfbRowBlocks; ++r)
+            st_shared_v4(sSfb + stage * Cfg::kSfbBytes + r * 512 + lane * 16u, cb[r], cb[r], cb[r], cb[r]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full_bar[stage]);
+          if (kb + 1 < kb1) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ca[j] = na[j];
+#pragma unroll
+            for (int r = 0; r < Cfg::kSfbRowBlocks; ++r) cb[r] = nb[r];
+          }
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue
     constexpr int HC = Cfg::kHalfCols;

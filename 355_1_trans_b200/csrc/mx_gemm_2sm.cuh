@@ -27,7 +27,12 @@
 //   epilogue (warps 4-11, both)    wait their own tmem_full, drain their own
 //       TMEM rows (128 x 256 per CTA) into packed bf16 registers, arrive on the
 //       leader's tmem_empty (count 2 x 256), then store.
-// Every wait is bounded (sm100.cuh mbar_wait).
+//   scale builder (warp 3, both CTAs; kSfE8m0Block128 only)  writes its CTA's
+//       scale atoms for the stage from the per-128 E8M0 bytes (mx_gemm.cuh)
+//       and arrives on the leader's full[s] (release at cluster scope; the
+//       MMA warp then waits full[s] with a cluster-scope acquire).
+// B may be K-major, MN-major or the shuffle_weight(16,16) layout, as in
+// mx_gemm.cuh.  Every wait is bounded (sm100.cuh mbar_wait).
 #pragma once
 
 #include "mx_gemm.cuh"
@@ -43,6 +48,10 @@ struct Mx2Params {
   int group_m;
   int sf_kb_total;               // scale atoms along K per 128-row block
   int sfa_row_blocks, sfb_row_blocks;
+  // kSfE8m0Block128: raw scale bytes, A's [K/128][M], B's [N/128][K/128]
+  const uint8_t* sfa;
+  const uint8_t* sfb;
+  long long sfa_ld, sfb_ld, sfa_batch_stride, sfb_batch_stride;
   void* c;
   long long ldc;
   long long c_batch_stride;
@@ -74,13 +83,16 @@ struct Mx2Cfg {
   static_assert(kStages >= 3, "pipeline too shallow");
 };
 
-template <int kFp4, bool kAMN, bool kBMN>
+template <int kFp4, bool kAMN, int kBMode, int kSfMode>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
     mx_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmSfa,
                        const __grid_constant__ CUtensorMap tmSfb, const Mx2Params p) {
   using Cfg = Mx2Cfg<kFp4>;
   constexpr int S = Cfg::kStages;
+  constexpr bool kBMN = kBMode == kBMNMajor;
+  constexpr bool kBuildSf = kSfMode == kSfE8m0Block128;
+  static_assert(!kBuildSf || !kFp4, "per-128 E8M0 scales are an fp8 format");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -104,7 +116,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
 
   if (threadIdx.x == 32) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(&full_bar[i], 1);
+      mbar_init(&full_bar[i], kBuildSf ? 3 : 1);   // + both CTAs' scale builders
       mbar_init(&empty_bar[i], 1);
     }
     mbar_init(tmem_full, 1);
@@ -150,7 +162,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
       const int sfb_rows = min(2, p.sfb_row_blocks - 2 * nt);
       const uint32_t sf_bytes =
           (1u + (peer_sfa ? 1u : 0u) + 2u * static_cast<uint32_t>(sfb_rows)) * 512u * Cfg::kSfAtomsK;
-      const uint32_t tx_bytes = 2u * (Cfg::kABytes + Cfg::kBBytes) + sf_bytes;
+      const uint32_t tx_bytes = 2u * (Cfg::kABytes + Cfg::kBBytes) + (kBuildSf ? 0u : sf_bytes);
       for (int kb = 0; kb < p.num_kb; ++kb) {
         if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
           ok = false;
@@ -168,17 +180,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
             tma_load_3d_pair(a_dst, &tmA, fb_leader, kbyte, row_a, b, pol_a);
           else
             tma_load_3d_pair(a_dst, &tmA, fb_leader, row_a, kbyte, b, pol_a);
-          if constexpr (!kBMN)
+          if constexpr (kBMode == kBKMajor)
             tma_load_3d_pair(b_dst, &tmB, fb_leader, kbyte, row_b, b, pol_b);
+          else if constexpr (kBMode == kBShuffle16)
+            tma_load_5d_pair(b_dst, &tmB, fb_leader, 0, kb * 8, 0, row_b / 16, b, pol_b);
           else
             tma_load_3d_pair(b_dst, &tmB, fb_leader, row_b, kbyte, b, pol_b);
-          const int atom_k = kb * Cfg::kSfAtomsK;
-          if (my_sfa)
-            tma_load_3d_pair(sSfa + stage * Cfg::kSfaBytes, &tmSfa, fb_leader, 0,
-                             (2 * mt + static_cast<int>(rank)) * p.sf_kb_total + atom_k, b, pol_a);
-          for (int r = 0; r < sfb_rows; ++r)
-            tma_load_3d_pair(sSfb + stage * Cfg::kSfbBytes + r * 512 * Cfg::kSfAtomsK, &tmSfb, fb_leader,
-                             0, (2 * nt + r) * p.sf_kb_total + atom_k, b, pol_b);
+          if constexpr (!kBuildSf) {
+            const int atom_k = kb * Cfg::kSfAtomsK;
+            if (my_sfa)
+              tma_load_3d_pair(sSfa + stage * Cfg::kSfaBytes, &tmSfa, fb_leader, 0,
+                               (2 * mt + static_cast<int>(rank)) * p.sf_kb_total + atom_k, b, pol_a);
+            for (int r = 0; r < sfb_rows; ++r)
+              tma_load_3d_pair(sSfb + stage * Cfg::kSfbBytes + r * 512 * Cfg::kSfAtomsK, &tmSfb, fb_leader,
+                               0, (2 * nt + r) * p.sf_kb_total + atom_k, b, pol_b);
+          }
         }
         __syncwarp();
         if (++stage == S) {
@@ -193,11 +209,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
     // ------------------------------------------------------------------ MMA issuer (leader)
     constexpr uint32_t kFmt = kFp4 ? 1u : 0u;
     const uint32_t idesc0 = idesc_block_scaled(kFmt, kFmt, kAMN, kBMN, 256, 256);
+    constexpr bool kBShuf = kBMode == kBShuffle16;
     constexpr uint32_t kALbo = kAMN ? 128u * 128u : 16u;
-    constexpr uint32_t kBLbo = kBMN ? 128u * 128u : 16u;
+    constexpr uint32_t kBLbo = kBMN ? 128u * 128u : kBShuf ? 128u : 16u;
     constexpr uint32_t kSbo = 1024u;
     constexpr uint32_t kKStep = kAMN ? 32u * 128u : 32u;
-    constexpr uint32_t kKStepB = kBMN ? 32u * 128u : 32u;
+    constexpr uint32_t kKStepB = kBMN ? 32u * 128u : kBShuf ? 256u : 32u;
+    constexpr uint32_t kBLayout = kBShuf ? kLayoutNone : kLayoutSW128;
     const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
     const uint32_t sSfa0 = smem_u32(sSfa), sSfb0 = smem_u32(sSfb);
     int stage = 0;
@@ -213,7 +231,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
       }
       tc_fence_after();
       for (int kb = 0; kb < p.num_kb; ++kb) {
-        if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) {
+        const bool got = kBuildSf ? mbar_wait_cluster(&full_bar[stage], phase, abort_flag, p.timeout_ns)
+                                  : mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns);
+        if (!got) {
           ok = false;
           break;
         }
@@ -238,7 +258,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
           const uint32_t j = kFp4 ? static_cast<uint32_t>(t >> 1) : 0u;
           const uint32_t sf_id = kFp4 ? static_cast<uint32_t>((t & 1) * 2) : static_cast<uint32_t>(t);
           const uint64_t adesc = make_sdesc(a_addr + t * kKStep, kALbo, kSbo, kLayoutSW128);
-          const uint64_t bdesc = make_sdesc(b_addr + t * kKStepB, kBLbo, kSbo, kLayoutSW128);
+          const uint64_t bdesc = make_sdesc(b_addr + t * kKStepB, kBLbo, kSbo, kBLayout);
           const uint32_t idesc = idesc_with_sf_id(idesc0, sf_id, sf_id);
           const uint32_t tsfa = tmem_base + sf_off + Cfg::kColSfa + 4u * j;
           const uint32_t tsfb = tmem_base + sf_off + Cfg::kColSfb + 8u * j;
@@ -262,6 +282,63 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
     if (issuer) tc_commit_pair(drain_bar, 0x1);
     int dummy = 0;
     mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
+  } else if (warp == 3) {
+    if constexpr (kBuildSf) {
+      // -------------------------------------------------------------- scale builder (both CTAs)
+      // this CTA's 128 A rows and all 256 B columns, as in mx_gemm.cuh
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = cluster_id; u < p.total_units && ok; u += num_clusters) {
+        int b, mt, nt, s;
+        decode_unit(u, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
+        const int row_a = mt * 256 + static_cast<int>(rank) * 128;
+        const int rows = p.m - row_a;
+        const int sfb_rows = min(2, p.sfb_row_blocks - 2 * nt);
+        const uint8_t* sa = p.sfa + b * p.sfa_batch_stride + row_a;
+        const uint8_t* sb = p.sfb + b * p.sfb_batch_stride + static_cast<long long>(2 * nt) * p.sfb_ld;
+        uint32_t ca[4], cb[2];
+        auto load = [&](int kb, uint32_t (&va)[4], uint32_t (&vb)[2]) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int r = static_cast<int>(lane) + 32 * j;
+            const uint32_t v = r < rows ? __ldg(sa + kb * p.sfa_ld + r) : 0x7Fu;
+            va[j] = v * 0x01010101u;
+          }
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const uint32_t v = r < sfb_rows ? __ldg(sb + r * p.sfb_ld + kb) : 0x7Fu;
+            vb[r] = v * 0x01010101u;
+          }
+        };
+        load(0, ca, cb);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          uint32_t na[4], nb[2];
+          if (kb + 1 < p.num_kb) load(kb + 1, na, nb);
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          st_shared_v4(sSfa + stage * Cfg::kSfaBytes + lane * 16u, ca[0], ca[1], ca[2], ca[3]);
+#pragma unroll
+          for (int r = 0; r < 2; ++r)
+            st_shared_v4(sSfb + stage * Cfg::kSfbBytes + r * 512 + lane * 16u, cb[r], cb[r], cb[r], cb[r]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&full_bar[stage]), 0));
+          if (kb + 1 < p.num_kb) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ca[j] = na[j];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) cb[r] = nb[r];
+          }
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue (both CTAs)
     const int q = warp & 3;

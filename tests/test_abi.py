@@ -79,3 +79,37 @@ def test_product_does_not_import_oracle():
     for p in (ROOT / "355_1_trans_b200").rglob("*"):
         if p.suffix in (".py", ".cu", ".cuh", ".h", ".cpp"):
             assert "oracle" not in p.read_text(errors="ignore").replace("oracle-free", ""), p
+
+
+def _opus_kargs(bs, m=256, n=256, k=256, base=1 << 20):
+    """Dense kargs of the reference's launcher, fake (never dereferenced)
+    16-byte aligned addresses in disjoint ranges."""
+    kb = k // 128
+    return bs.OpusGemmScaleKargs(base, base + (1 << 24), base + (2 << 24), m, n, k, 1, k, k, n,
+                                 m * k, n * k, m * n, base + (3 << 24), base + (4 << 24),
+                                 m, kb, m * kb, (n // 128) * kb)
+
+
+def test_launch_blockscale_bpreshuffle_validation(bs):
+    """Error behaviour of the reference launcher
+    (source_snapshot/gemm_a8w8_blockscale_bpreshuffle_launch.cc:33-54): every
+    rejected case returns cudaErrorInvalidValue (1) before any CUDA call."""
+    lib = bs.lib()
+    fn = lib.launch_blockscale_bpreshuffle
+    INVALID = 1
+    assert fn(None, 1, 0, None) == INVALID
+    a = _opus_kargs(bs)
+    assert fn(ctypes.byref(a), 2, 0, None) == INVALID          # output_bf16 not 0/1
+    assert fn(ctypes.byref(a), 1, 2, None) == INVALID          # tiles not 0/1
+    for field, value in (("ptr_a", None), ("ptr_sfb", None), ("k", 200), ("n", 200),
+                         ("m", 0), ("batch", 0), ("stride_a", 512), ("stride_c", 512),
+                         ("stride_sfa", 2), ("stride_sfb", 1), ("stride_sfa_batch", 1),
+                         ("stride_b_batch", 1)):
+        b = _opus_kargs(bs)
+        setattr(b, field, value)
+        assert fn(ctypes.byref(b), 1, 0, None) == INVALID, field
+    c = _opus_kargs(bs)
+    c.ptr_c = c.ptr_a + 64                                     # C overlaps A
+    assert fn(ctypes.byref(c), 0, 0, None) == INVALID
+    d = _opus_kargs(bs, m=1 << 16, n=1 << 16, k=1 << 16)       # int32 element-count overflow
+    assert fn(ctypes.byref(d), 1, 0, None) == INVALID

@@ -180,24 +180,132 @@ def test_mxfp4_shuffled_b(bs, orc, cuda):
     assert_close(orc, ref, out.float().cpu().numpy(), mag, "mxfp4 shuffled B")
 
 
+@pytest.mark.parametrize("kernel", ["1cta", "pair"])
+def test_mxfp4_shuffled_b_in_place(bs, orc, cuda, kernel):
+    """shuffle_weight(16,16) B read in place (5-D tensor map into the
+    no-swizzle K-major layout): bit-identical to the raw-B launch."""
+    for m, n, k, seed in ((256, 512, 1024, 7), (200, 272, 512, 8)):
+        qa, qb, sa, sb = mxfp4_problem(orc, m, n, k, seed, "rowpattern")
+        ref, mag = orc.gemm_mxfp4(qa, qb, sa, sb)
+        A, SA, SB = dev_u8(qa, cuda), dev_u8(sa, cuda), dev_u8(sb, cuda)
+        raw = bs.gemm_a4w4_mxfp4(A, dev_u8(qb, cuda), SA, SB, kernel=kernel, split_k=1)
+        shuf = bs.gemm_a4w4_mxfp4(A, dev_u8(orc.shuffle_weight16(qb), cuda), SA, SB, kernel=kernel,
+                                  split_k=1, b_format="shuffle16")
+        torch.cuda.synchronize()
+        assert bs.check_device_error() == 0
+        assert torch.equal(raw, shuf)
+        assert_close(orc, ref, shuf.float().cpu().numpy(), mag, f"mxfp4 shuffled {kernel} {m}x{n}x{k}")
+
+
+@pytest.mark.parametrize("kernel,out_dtype", [("1cta", torch.bfloat16), ("1cta", torch.float32),
+                                              ("pair", torch.bfloat16)])
+def test_mxfp8_shuffled_b_in_place(bs, orc, cuda, kernel, out_dtype):
+    for m, n, k, seed in ((256, 512, 512, 9), (72, 400, 384, 10)):
+        qa_l, qb_l, sa_l, sb_l = mxfp8_problem(orc, m, n, k, seed, "rowpattern")
+        qa, qb, sa, sb = qa_l[0], qb_l[0], sa_l[0], sb_l[0]
+        ref, mag = orc.gemm_mxfp8(qa, qb, sa, sb, f64=True)
+        A = dev_u8(qa, cuda).view(torch.float8_e4m3fn)
+        SA, SB = dev_u8(sa, cuda), dev_u8(sb, cuda)
+        raw = bs.gemm_a8w8_mxfp8(A, dev_u8(qb, cuda).view(torch.float8_e4m3fn), SA, SB, kernel=kernel,
+                                 out_dtype=out_dtype, split_k=1)
+        shuf = bs.gemm_a8w8_mxfp8(A, dev_u8(orc.shuffle_weight16(qb), cuda).view(torch.float8_e4m3fn), SA, SB,
+                                  kernel=kernel, out_dtype=out_dtype, split_k=1, b_format="shuffle16")
+        torch.cuda.synchronize()
+        assert bs.check_device_error() == 0
+        assert torch.equal(raw, shuf)
+        assert_close(orc, ref, shuf.float().cpu().numpy(), mag, f"mxfp8 shuffled {kernel} {m}x{n}x{k}")
+
+
+# ---- E8M0 1x128 / 128x128 block scale: the reference's launch_blockscale_bpreshuffle --
+
+def e8m0_block_problem(orc, m, n, k, seed):
+    """E4M3 values of N(0,1) data, E8M0 scale bytes 124 + r % 7 as the
+    reference's fill_scales (source_snapshot/gemm_a8w8_mxfp8_scale_host.cc:155-160)."""
+    qa, _ = orc.quant_mxfp8(orc.normal((m, k), seed=seed * 31))
+    qb, _ = orc.quant_mxfp8(orc.normal((n, k), seed=seed * 31 + 1))
+    rng = np.random.default_rng(seed)
+    sfa_t = (124 + rng.integers(0, 7, size=(k // 128, m))).astype(np.uint8)
+    sfb = (124 + rng.integers(0, 7, size=(n // 128, k // 128))).astype(np.uint8)
+    return qa, qb, sfa_t, sfb
+
+
+def run_e8m0_block(bs, orc, cuda, m, n, k, *, seed=1, dtype=torch.bfloat16, colmajor=True):
+    qa, qb, sfa_t, sfb = e8m0_block_problem(orc, m, n, k, seed)
+    ref, mag = orc.gemm_e8m0_block(qa, qb, sfa_t, sfb)
+    A = dev_u8(qa, cuda).view(torch.float8_e4m3fn)
+    B = dev_u8(orc.shuffle_weight16(qb), cuda).view(torch.float8_e4m3fn)
+    if colmajor:
+        SA = dev_u8(sfa_t, cuda).t()                       # [M, K/128], strides (1, M)
+    else:
+        SA = dev_u8(sfa_t, cuda).reshape(m, k // 128)      # contiguous, transposed bytes
+    SB = dev_u8(sfb, cuda)
+    out = poisoned((m, n), dtype, cuda)
+    bs.gemm_a8w8_blockscale_bpreshuffle(A, B, SA, SB, dtype, out)
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    got = out.float().cpu().numpy()
+    errors, ratio = orc.check_e8m0_rule(ref, got, mag, bf16=dtype == torch.bfloat16)
+    assert errors == 0, f"e8m0 block {m}x{n}x{k}: {errors} errors, max ratio {ratio}"
+    if dtype == torch.bfloat16:
+        assert_close(orc, ref, got, mag, f"e8m0 block {m}x{n}x{k}")
+    return ref, got
+
+
+def test_e8m0_block_256(bs, orc, cuda):
+    run_e8m0_block(bs, orc, cuda, 256, 256, 512)
+
+
+def test_e8m0_block_fp32_and_ragged(bs, orc, cuda):
+    run_e8m0_block(bs, orc, cuda, 256, 512, 1024, seed=2, dtype=torch.float32)
+    run_e8m0_block(bs, orc, cuda, 200, 384, 256, seed=3, colmajor=False)
+    run_e8m0_block(bs, orc, cuda, 16, 1024, 2048, seed=4)
+
+
+def test_e8m0_block_pair_path(bs, orc, cuda):
+    """Enough 256x256 tiles for the CTA-pair kernel (its scale builders arrive
+    on the leader's barrier across the cluster)."""
+    run_e8m0_block(bs, orc, cuda, 2048, 2560, 256, seed=5)
+
+
+def test_e8m0_block_rejects_like_reference(bs, cuda):
+    A = torch.zeros((256, 256), dtype=torch.float8_e4m3fn, device=cuda)
+    B = torch.zeros((256, 256), dtype=torch.uint8, device=cuda)
+    SA = torch.zeros((256, 2), dtype=torch.uint8, device=cuda)
+    SB = torch.zeros((2, 2), dtype=torch.uint8, device=cuda)
+    with pytest.raises(ValueError):
+        bs.gemm_a8w8_blockscale_bpreshuffle(A, B, SA.float(), SB)      # fp32 scales
+    with pytest.raises(ValueError):
+        bs.gemm_a8w8_blockscale_bpreshuffle(A, B, SA, SB, tiles=2)
+    with pytest.raises(ValueError):
+        bs.gemm_a8w8_blockscale_bpreshuffle(A, B[:, :128].contiguous(), SA, SB)
+    out = torch.empty((256, 256), dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(ValueError):
+        bs.gemm_a8w8_blockscale_bpreshuffle(A, B, SA, SB, out=out[:, :128])
+
+
 # ---- FP8 block-scale (fp32 scales) --------------------------------------------------
 
 def run_fp8_block(bs, orc, cuda, m, n, k, *, seed=1, kpanel=True, transposed=False, split_k=0,
-                  out_dtype=torch.bfloat16, kernel="auto"):
+                  out_dtype=torch.bfloat16, kernel="auto", shuffle16=False):
     x = orc.normal((m, k), seed=seed * 77)
     w = orc.normal((n, k), seed=seed * 77 + 1)
     qa, sa = orc.quant_fp8_block(x, 1)
     qb, sb = orc.quant_fp8_block(w, 128)
     ref, mag = orc.gemm_fp8_block(qa, qb, sa, sb)
     A = dev_u8(qa, cuda).view(torch.float8_e4m3fn)
-    if kpanel:
+    if shuffle16:
+        B = dev_u8(orc.shuffle_weight16(qb), cuda).view(torch.float8_e4m3fn)
+        b_layout = "shuffle16"
+    elif kpanel:
         B = dev_u8(orc.shuffle_kpanel(qb), cuda).view(torch.float8_e4m3fn)
+        b_layout = "kpanel"
     else:
         B = dev_u8(qb, cuda).view(torch.float8_e4m3fn)
+        b_layout = "raw"
     SA = torch.from_numpy(np.ascontiguousarray(sa.T if transposed else sa)).to(cuda)
     SB = torch.from_numpy(sb).to(cuda)
     out = poisoned((m, n), out_dtype, cuda)
-    bs.gemm_a8w8_bpreshuffle(A, B, SA, SB, out_dtype, preshuffled=kpanel, x_scale_transposed=transposed,
+    bs.gemm_a8w8_bpreshuffle(A, B, SA, SB, out_dtype, b_layout=b_layout, x_scale_transposed=transposed,
                              out=out, split_k=split_k, kernel=kernel)
     torch.cuda.synchronize()
     assert bs.check_device_error() == 0
@@ -235,6 +343,12 @@ def test_fp8_block_swap_raw_b_fp32_split(bs, orc, cuda):
     ref, got = run_fp8_block(bs, orc, cuda, 24, 640, 1536, seed=50, kpanel=False, kernel="swap",
                              split_k=3, out_dtype=torch.float32)
     np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("m,kernel", [(16, "swap"), (48, "swap"), (200, "1cta")])
+def test_fp8_block_shuffle16_b(bs, orc, cuda, m, kernel):
+    """aiter shuffle_weight(16,16) weights read in place by both kernels."""
+    run_fp8_block(bs, orc, cuda, m, 768, 1024, seed=60 + m, kernel=kernel, shuffle16=True)
 
 
 def test_fp8_block_split_k(bs, orc, cuda):
