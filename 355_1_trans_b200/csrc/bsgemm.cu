@@ -628,9 +628,10 @@ bool bounded_count(int rows, int cols, int batch, int bytes) {
 
 // Returns a cudaError_t value.  Validation follows the reference launcher
 // (…_launch.cc:33-54) except that M may be any positive size and N a
-// multiple of 128 (the reference: M, N % 256); the tile shape is planned
-// here, so `tiles` is accepted (0 or 1) and otherwise unused.
-int e8m0b_run(const bsgemm_args& in, bool bf16, cudaStream_t st) {
+// multiple of 128 (the reference: M, N % 256).  `tiles` (0 or 1, the
+// reference's output-tiles-per-workgroup switch) selects the tile shape:
+// 0 = planned here (CTA pairs for large problems), 1 = single-CTA tiles.
+int e8m0b_run(const bsgemm_args& in, bool bf16, int tiles, cudaStream_t st) {
   const bsgemm_args& a = in;
   if (!a.ptr_a || !a.ptr_b || !a.ptr_c || !a.ptr_sfa || !a.ptr_sfb) return cudaErrorInvalidValue;
   if (a.m <= 0 || a.n <= 0 || a.k <= 0 || a.batch <= 0 || a.n % 128 || a.k % 128)
@@ -669,7 +670,7 @@ int e8m0b_run(const bsgemm_args& in, bool bf16, cudaStream_t st) {
   g.workspace = nullptr;
   g.workspace_bytes = 0;
   g.grid_blocks = 0;
-  g.kernel = BSG_KERNEL_AUTO;
+  g.kernel = tiles == 1 ? BSG_KERNEL_1CTA : BSG_KERNEL_AUTO;
   MxOperands o;
   o.bmode = bsg::kBShuffle16;
   o.sfmode = bsg::kSfE8m0Block128;
@@ -1003,7 +1004,7 @@ int launch_blockscale_bpreshuffle(const void* kargs, int output_bf16, int tiles,
   bsgemm_args a;
   bsgemm_args_init(&a);
   std::memcpy(&a, kargs, 96);
-  return e8m0b_run(a, output_bf16 == 1, reinterpret_cast<cudaStream_t>(stream));
+  return e8m0b_run(a, output_bf16 == 1, tiles, reinterpret_cast<cudaStream_t>(stream));
 }
 
 const char* bsgemm_strerror(int status) {

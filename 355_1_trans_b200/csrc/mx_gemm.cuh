@@ -84,6 +84,73 @@ constexpr int kMxEpiWarps = 8;      // one tmem_empty arrival per epilogue warp
 constexpr int kBKMajor = 0, kBMNMajor = 1, kBShuffle16 = 2;
 constexpr int kSfNative = 0, kSfE8m0Block128 = 1;
 
+// Walks the (unit, K block) sequence a persistent CTA (or CTA pair) visits,
+// across unit boundaries, so a warp can work several K blocks ahead.
+struct KbCursor {
+  int u, step, total;
+  int tiles_m, tiles_n, split, group_m, kb_per, num_kb;
+  int b, mt, nt, kb, kb1;
+  __device__ __forceinline__ void settle() {
+    while (u < total) {
+      int s;
+      decode_unit(u, tiles_m, tiles_n, split, group_m, b, mt, nt, s);
+      kb = s * kb_per;
+      kb1 = min(kb + kb_per, num_kb);
+      if (kb < kb1) return;
+      u += step;
+    }
+  }
+  __device__ __forceinline__ bool valid() const { return u < total; }
+  __device__ __forceinline__ void next() {
+    if (++kb >= kb1) {
+      u += step;
+      settle();
+    }
+  }
+};
+
+__device__ __forceinline__ KbCursor make_cursor(int u0, int step, int total, int tiles_m, int tiles_n,
+                                                int split, int group_m, int kb_per, int num_kb) {
+  KbCursor c;
+  c.u = u0;
+  c.step = step;
+  c.total = total;
+  c.tiles_m = tiles_m;
+  c.tiles_n = tiles_n;
+  c.split = split;
+  c.group_m = group_m;
+  c.kb_per = kb_per;
+  c.num_kb = num_kb;
+  c.b = c.mt = c.nt = c.kb = c.kb1 = 0;
+  c.settle();
+  return c;
+}
+
+// Per-128-K E8M0 scale bytes of one K block: va[j] for A row
+// lane + 32 j of the tile, vb[r] for B column block r of the tile.  Rows /
+// blocks that do not exist read as 0x7F (2^0); their outputs are never
+// stored.  The raw bytes are returned untouched: the first arithmetic use of
+// a loaded register waits for the load, so the replication into atom words
+// (e8m0_word) happens only when the stage is written, kSfPrefetch K blocks
+// later.
+template <int NBLK>
+__device__ __forceinline__ void e8m0_block_bytes(const uint8_t* sa, int rows, const uint8_t* sb, int nblocks,
+                                                 long long sfa_ld, long long sfb_ld, int kb, uint32_t lane,
+                                                 uint32_t (&va)[4], uint32_t (&vb)[NBLK]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int r = static_cast<int>(lane) + 32 * j;
+    va[j] = r < rows ? __ldg(sa + kb * sfa_ld + r) : 0x7Fu;
+  }
+#pragma unroll
+  for (int r = 0; r < NBLK; ++r) vb[r] = r < nblocks ? __ldg(sb + r * sfb_ld + kb) : 0x7Fu;
+}
+
+// The byte repeated over the four 32-K groups of an atom word.
+__device__ __forceinline__ uint32_t e8m0_word(uint32_t byte) { return byte * 0x01010101u; }
+
+constexpr int kSfPrefetch = 4;   // K blocks of scale bytes in flight per builder
+
 template <int BN, int kFp4>
 struct MxCfg {
   static constexpr int kBlockM = 128;
@@ -349,58 +416,53 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     if constexpr (kBuildSf) {
       // -------------------------------------------------------------- scale builder
       // Lane l owns 16 bytes of each atom: the words of rows l, l+32, l+64,
-      // l+96, each the row's scale byte repeated for the four 32-K groups.
-      // The next K block's bytes are loaded before waiting for the stage, so
-      // the global-load latency overlaps the pipeline wait.  Missing rows
-      // and column blocks get 0x7F (2^0); their outputs are never stored.
+      // l+96.  The bytes of the next kSfPrefetch K blocks are in flight in a
+      // register ring (statically indexed by unrolling), so global-load
+      // latency never stalls the pipeline.
+      constexpr int D = kSfPrefetch;
+      constexpr int NBLK = Cfg::kSfbRowBlocks;
+      KbCursor issue = make_cursor(blockIdx.x, gridDim.x, p.total_units, p.tiles_m, p.tiles_n, p.split_k,
+                                   p.group_m, p.kb_per_split, p.num_kb);
+      KbCursor cons = issue;
+      uint32_t ra[D][4], rb[D][NBLK];
+      auto load = [&](const KbCursor& c, uint32_t (&va)[4], uint32_t (&vb)[NBLK]) {
+        const uint8_t* sa = p.sfa + c.b * p.sfa_batch_stride + c.mt * 128;
+        const uint8_t* sb = p.sfb + c.b * p.sfb_batch_stride + static_cast<long long>(c.nt) * NBLK * p.sfb_ld;
+        e8m0_block_bytes<NBLK>(sa, p.m - c.mt * 128, sb, min(NBLK, p.sfb_row_blocks - c.nt * NBLK), p.sfa_ld,
+                               p.sfb_ld, c.kb, lane, va, vb);
+      };
+#pragma unroll
+      for (int i = 0; i < D; ++i)
+        if (issue.valid()) {
+          load(issue, ra[i], rb[i]);
+          issue.next();
+        }
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
-        int b, mt, nt, s;
-        decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
-        const int kb0 = s * p.kb_per_split;
-        const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
-        const int rows = p.m - mt * 128;
-        const int sfb_rows = min(Cfg::kSfbRowBlocks, p.sfb_row_blocks - nt * Cfg::kSfbRowBlocks);
-        const uint8_t* sa = p.sfa + b * p.sfa_batch_stride + mt * 128;
-        const uint8_t* sb = p.sfb + b * p.sfb_batch_stride +
-                            static_cast<long long>(nt) * Cfg::kSfbRowBlocks * p.sfb_ld;
-        uint32_t ca[4], cb[Cfg::kSfbRowBlocks];
-        auto load = [&](int kb, uint32_t (&va)[4], uint32_t (&vb)[Cfg::kSfbRowBlocks]) {
+      while (ok && cons.valid()) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int r = static_cast<int>(lane) + 32 * j;
-            const uint32_t v = r < rows ? __ldg(sa + kb * p.sfa_ld + r) : 0x7Fu;
-            va[j] = v * 0x01010101u;
-          }
-#pragma unroll
-          for (int r = 0; r < Cfg::kSfbRowBlocks; ++r) {
-            const uint32_t v = r < sfb_rows ? __ldg(sb + r * p.sfb_ld + kb) : 0x7Fu;
-            vb[r] = v * 0x01010101u;
-          }
-        };
-        if (kb0 < kb1) load(kb0, ca, cb);
-        for (int kb = kb0; kb < kb1; ++kb) {
-          uint32_t na[4], nb[Cfg::kSfbRowBlocks];
-          if (kb + 1 < kb1) load(kb + 1, na, nb);
+        for (int i = 0; i < D; ++i) {
+          if (!cons.valid()) break;
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
             ok = false;
             break;
           }
-          st_shared_v4(sSfa + stage * Cfg::kSfaBytes + lane * 16u, ca[0], ca[1], ca[2], ca[3]);
+          st_shared_v4(sSfa + stage * Cfg::kSfaBytes + lane * 16u, e8m0_word(ra[i][0]), e8m0_word(ra[i][1]),
+                       e8m0_word(ra[i][2]), e8m0_word(ra[i][3]));
 #pragma unroll
-          for (int r = 0; r < Cfg::kSfbRowBlocks; ++r)
-            st_shared_v4(sSfb + stage * Cfg::kSfbBytes + r * 512 + lane * 16u, cb[r], cb[r], cb[r], cb[r]);
+          for (int r = 0; r < NBLK; ++r) {
+            const uint32_t w = e8m0_word(rb[i][r]);
+            st_shared_v4(sSfb + stage * Cfg::kSfbBytes + r * 512 + lane * 16u, w, w, w, w);
+          }
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(&full_bar[stage]);
-          if (kb + 1 < kb1) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) ca[j] = na[j];
-#pragma unroll
-            for (int r = 0; r < Cfg::kSfbRowBlocks; ++r) cb[r] = nb[r];
+          if (issue.valid()) {
+            load(issue, ra[i], rb[i]);
+            issue.next();
           }
+          cons.next();
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;

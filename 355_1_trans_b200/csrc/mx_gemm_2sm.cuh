@@ -27,10 +27,17 @@
 //   epilogue (warps 4-11, both)    wait their own tmem_full, drain their own
 //       TMEM rows (128 x 256 per CTA) into packed bf16 registers, arrive on the
 //       leader's tmem_empty (count 2 x 256), then store.
-//   scale builder (warp 3, both CTAs; kSfE8m0Block128 only)  writes its CTA's
-//       scale atoms for the stage from the per-128 E8M0 bytes (mx_gemm.cuh)
-//       and arrives on the leader's full[s] (release at cluster scope; the
-//       MMA warp then waits full[s] with a cluster-scope acquire).
+//   scale builder (warp 3, both CTAs; kSfE8m0Block128 only)  writes its own
+//       CTA's scale atoms for the stage from the per-128 E8M0 bytes
+//       (mx_gemm.cuh), fences them for the async proxy (CTA scope) and
+//       arrives on its CTA's sf_ready[s]; that CTA's producer waits for
+//       sf_ready[s] before issuing the stage's pair loads, so the leader's
+//       full[s] -- which needs both CTAs' transaction bytes -- completes only
+//       after both CTAs' atoms are in place.  Every synchronisation stays at
+//       CTA scope: a cluster-scope proxy fence or release per stage (the
+//       builder writing the peer's atoms, or arriving on the leader's
+//       barrier) measured at about one memory latency each, a third to a
+//       half of the MMA rate.
 // B may be K-major, MN-major or the shuffle_weight(16,16) layout, as in
 // mx_gemm.cuh.  Every wait is bounded (sm100.cuh mbar_wait).
 #pragma once
@@ -74,6 +81,8 @@ struct Mx2Cfg {
   static constexpr uint32_t kOffSfb = kOffSfa + kSfaBytes * kStages;
   static constexpr uint32_t kOffBar = kOffSfb + kSfbBytes * kStages;
   static constexpr uint32_t kSmemBytes = kOffBar + 256u + 1024u;
+  // barriers: full, empty, sf_ready [S each], tmem_full, tmem_empty, drain; holder + abort flag
+  static_assert(8u * (3u * kStages + 3u) + 8u <= 256u, "barrier area");
   // two alternating scale-factor regions after the 256 accumulator columns
   static constexpr uint32_t kSfRegionCols = 12u * kSfAtomsK;
   static constexpr uint32_t kColSfa = 256u;
@@ -106,7 +115,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
   uint64_t* tmem_full = empty_bar + S;
   uint64_t* tmem_empty = tmem_full + 1;
   uint64_t* drain_bar = tmem_empty + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* sf_ready = drain_bar + 1;   // [S], kSfE8m0Block128 only
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(sf_ready + S);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -116,8 +126,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
 
   if (threadIdx.x == 32) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(&full_bar[i], kBuildSf ? 3 : 1);   // + both CTAs' scale builders
+      mbar_init(&full_bar[i], 1);
       mbar_init(&empty_bar[i], 1);
+      mbar_init(&sf_ready[i], 1);
     }
     mbar_init(tmem_full, 1);
     mbar_init(tmem_empty, 2 * kMxEpiWarps);
@@ -167,6 +178,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
         if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
           ok = false;
           break;
+        }
+        if constexpr (kBuildSf) {
+          // this CTA's scale atoms for the stage are written before its loads go out
+          if (!mbar_wait(&sf_ready[stage], phase, abort_flag, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
         }
         const uint32_t fb_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
         if (leader && issuer) mbar_arrive_expect_tx(&full_bar[stage], tx_bytes);
@@ -231,9 +249,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
       }
       tc_fence_after();
       for (int kb = 0; kb < p.num_kb; ++kb) {
-        const bool got = kBuildSf ? mbar_wait_cluster(&full_bar[stage], phase, abort_flag, p.timeout_ns)
-                                  : mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns);
-        if (!got) {
+        if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) {
           ok = false;
           break;
         }
@@ -285,53 +301,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
   } else if (warp == 3) {
     if constexpr (kBuildSf) {
       // -------------------------------------------------------------- scale builder (both CTAs)
-      // this CTA's 128 A rows and all 256 B columns, as in mx_gemm.cuh
+      // this CTA's 128 A rows and all 256 B columns, kSfPrefetch K blocks
+      // ahead, as in mx_gemm.cuh
+      constexpr int D = kSfPrefetch;
+      KbCursor issue = make_cursor(cluster_id, num_clusters, p.total_units, p.tiles_m, p.tiles_n, 1, p.group_m,
+                                   p.num_kb, p.num_kb);
+      KbCursor cons = issue;
+      uint32_t ra[D][4], rb[D][2];
+      auto load = [&](const KbCursor& c, uint32_t (&va)[4], uint32_t (&vb)[2]) {
+        const int row_a = c.mt * 256 + static_cast<int>(rank) * 128;
+        const uint8_t* sa = p.sfa + c.b * p.sfa_batch_stride + row_a;
+        const uint8_t* sb = p.sfb + c.b * p.sfb_batch_stride + static_cast<long long>(2 * c.nt) * p.sfb_ld;
+        e8m0_block_bytes<2>(sa, p.m - row_a, sb, min(2, p.sfb_row_blocks - 2 * c.nt), p.sfa_ld, p.sfb_ld, c.kb,
+                            lane, va, vb);
+      };
+#pragma unroll
+      for (int i = 0; i < D; ++i)
+        if (issue.valid()) {
+          load(issue, ra[i], rb[i]);
+          issue.next();
+        }
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int u = cluster_id; u < p.total_units && ok; u += num_clusters) {
-        int b, mt, nt, s;
-        decode_unit(u, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
-        const int row_a = mt * 256 + static_cast<int>(rank) * 128;
-        const int rows = p.m - row_a;
-        const int sfb_rows = min(2, p.sfb_row_blocks - 2 * nt);
-        const uint8_t* sa = p.sfa + b * p.sfa_batch_stride + row_a;
-        const uint8_t* sb = p.sfb + b * p.sfb_batch_stride + static_cast<long long>(2 * nt) * p.sfb_ld;
-        uint32_t ca[4], cb[2];
-        auto load = [&](int kb, uint32_t (&va)[4], uint32_t (&vb)[2]) {
+      while (ok && cons.valid()) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int r = static_cast<int>(lane) + 32 * j;
-            const uint32_t v = r < rows ? __ldg(sa + kb * p.sfa_ld + r) : 0x7Fu;
-            va[j] = v * 0x01010101u;
-          }
-#pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            const uint32_t v = r < sfb_rows ? __ldg(sb + r * p.sfb_ld + kb) : 0x7Fu;
-            vb[r] = v * 0x01010101u;
-          }
-        };
-        load(0, ca, cb);
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-          uint32_t na[4], nb[2];
-          if (kb + 1 < p.num_kb) load(kb + 1, na, nb);
+        for (int i = 0; i < D; ++i) {
+          if (!cons.valid()) break;
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
             ok = false;
             break;
           }
-          st_shared_v4(sSfa + stage * Cfg::kSfaBytes + lane * 16u, ca[0], ca[1], ca[2], ca[3]);
+          st_shared_v4(sSfa + stage * Cfg::kSfaBytes + lane * 16u, e8m0_word(ra[i][0]), e8m0_word(ra[i][1]),
+                       e8m0_word(ra[i][2]), e8m0_word(ra[i][3]));
 #pragma unroll
-          for (int r = 0; r < 2; ++r)
-            st_shared_v4(sSfb + stage * Cfg::kSfbBytes + r * 512 + lane * 16u, cb[r], cb[r], cb[r], cb[r]);
+          for (int r = 0; r < 2; ++r) {
+            const uint32_t w = e8m0_word(rb[i][r]);
+            st_shared_v4(sSfb + stage * Cfg::kSfbBytes + r * 512 + lane * 16u, w, w, w, w);
+          }
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&full_bar[stage]), 0));
-          if (kb + 1 < p.num_kb) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) ca[j] = na[j];
-#pragma unroll
-            for (int r = 0; r < 2; ++r) cb[r] = nb[r];
+          if (lane == 0) mbar_arrive(&sf_ready[stage]);
+          if (issue.valid()) {
+            load(issue, ra[i], rb[i]);
+            issue.next();
           }
+          cons.next();
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;

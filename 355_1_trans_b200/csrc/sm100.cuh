@@ -248,6 +248,20 @@ __device__ __forceinline__ void st_shared_v4(void* p, uint32_t a, uint32_t b, ui
                : "memory");
 }
 
+// 16-byte store to shared memory at a cluster address (e.g. the peer CTA's).
+__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, uint32_t a, uint32_t b, uint32_t c,
+                                              uint32_t d) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
+// Generic-proxy writes to shared memory of the cluster (this CTA's or a
+// peer's) visible to the async proxy.
+__device__ __forceinline__ void fence_proxy_async_cluster() {
+  asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
+}
+
 // CTA-pair form: the data lands in the executing CTA's shared memory, the
 // transaction bytes are reported to the mbarrier at cluster address
 // `bar_cluster` (the pair leader's barrier).

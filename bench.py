@@ -2,14 +2,18 @@
 """Benchmark of the block-scaled GEMM hot path (driver contract).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload mxfp8|mxfp4|fp8block] [--layout tn|nn|tt|nt]
+                    [--workload mxfp8|mxfp4|fp8block|e8m0block] [--layout tn|nn|tt|nt]
+                    [--b-format raw|shuffle16]
 
 Default workload (BASELINE metric, configs[2]): MXFP8 GEMM M=N=K=8192, layout
 tn, E4M3 with E8M0 scales per 32 K, bf16 out, fp32 accumulation.  One step is
 one GEMM over the whole problem.  For N > 1 GPUs (torchrun, one process per
 GPU) the GEMM is partitioned along N with weights pre-sharded: every rank
 computes its own M x 8192 x K column shard (weak scaling, no collective in the
-timed region; configs[4]).
+timed region; configs[4]).  --workload mxfp4 reads B in the preshuffled
+shuffle_weight(16,16) layout unless --b-format raw; e8m0block is
+the reference's own launcher, launch_blockscale_bpreshuffle (E8M0 1x128 /
+128x128 scales, shuffled B).
 
 Printed JSON line: value = TFLOPS of the whole job from device-side CUDA
 events (max over ranks), e2e = the same GEMM through the public C-ABI call
@@ -52,7 +56,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="mxfp8", choices=["mxfp8", "mxfp4", "fp8block"])
+    ap.add_argument("--workload", default="mxfp8", choices=["mxfp8", "mxfp4", "fp8block", "e8m0block"])
+    ap.add_argument("--b-format", default=None, choices=["raw", "shuffle16"],
+                    help="B layout for the MX workloads (default: shuffle16 for mxfp4, raw for mxfp8)")
     ap.add_argument("--layout", default="tn", choices=["tn", "nn", "tt", "nt"])
     ap.add_argument("--kernel", default="auto", choices=["auto", "1cta", "pair"],
                     help="MX kernel: auto, single-CTA tiles or CTA pairs (cta_group::2)")
@@ -161,6 +167,21 @@ def make_mx_inputs(bs, m, n, k, fp4, layout, device, seed):
     return qa, qb, sa, sb
 
 
+def make_e8m0block_inputs(bs, m, n, k, device, seed):
+    """E4M3 A [M,K] and shuffle_weight(16,16) B, E8M0 scale bytes 124..130
+    (the reference's fill_scales range): SFA column-major [M,K/128] (bytes
+    [K/128][M]), SFB [N/128,K/128]."""
+    import torch
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    qa = (torch.randn(m, k, device=device, generator=gen) * 64).to(torch.float8_e4m3fn)
+    qb = (torch.randn(n, k, device=device, generator=gen) * 64).to(torch.float8_e4m3fn)
+    qb_sh = bs.pack_b(qb.view(torch.uint8), "shuffle16", unpack=True).view(torch.float8_e4m3fn)
+    sfa_t = torch.randint(124, 131, (k // 128, m), device=device, generator=gen, dtype=torch.uint8)
+    sfb = torch.randint(124, 131, (n // 128, k // 128), device=device, generator=gen, dtype=torch.uint8)
+    return qa, qb_sh, sfa_t, sfb
+
+
 def make_fp8block_inputs(m, n, k, device, seed):
     import torch
     gen = torch.Generator(device=device)
@@ -202,6 +223,16 @@ def cpu_baseline(workload, m, n, k, target_s=12.0, max_rows=None):
             t0 = time.perf_counter()
             orc.gemm_mxfp4(qa, qb, sa, sb)
             return time.perf_counter() - t0
+        if workload == "e8m0block":
+            qa, _ = orc.quant_mxfp8(rng.standard_normal((rows, k)).astype(np.float32))
+            sfa_t = rng.integers(124, 131, size=(k // 128, rows)).astype(np.uint8)
+            if not hasattr(sample, "b"):
+                qb, _ = orc.quant_mxfp8(rng.standard_normal((n, k)).astype(np.float32))
+                sample.b = (qb, rng.integers(124, 131, size=(n // 128, k // 128)).astype(np.uint8))
+            qb, sfb = sample.b
+            t0 = time.perf_counter()
+            orc.gemm_e8m0_block(qa, qb, sfa_t, sfb)
+            return time.perf_counter() - t0
         qa, sa = orc.quant_fp8_block(rng.standard_normal((rows, k)).astype(np.float32), 1)
         if not hasattr(sample, "b"):
             sample.b = orc.quant_fp8_block(rng.standard_normal((n, k)).astype(np.float32), 128)
@@ -221,7 +252,8 @@ def cpu_baseline(workload, m, n, k, target_s=12.0, max_rows=None):
 def metric_name(workload):
     return {"mxfp8": "MXFP8 block-scaled GEMM TFLOPS (8192^3)",
             "mxfp4": "MXFP4 block-scaled GEMM TFLOPS (8192^3)",
-            "fp8block": "FP8 fp32-block-scale GEMM TFLOPS"}[workload]
+            "fp8block": "FP8 fp32-block-scale GEMM TFLOPS",
+            "e8m0block": "FP8 E8M0-block-scale GEMM TFLOPS (launch_blockscale_bpreshuffle)"}[workload]
 
 
 # ---------------------------------------------------------------------------
@@ -246,6 +278,12 @@ def run_reference(args):
         qb, sb = orc.quant_mxfp4(rng.standard_normal((n, k)).astype(np.float32))
         qa, sa = orc.quant_mxfp4(rng.standard_normal((rows, k)).astype(np.float32))
         fn = lambda: orc.gemm_mxfp4(qa, qb, sa, sb)
+    elif args.workload == "e8m0block":
+        qb, _ = orc.quant_mxfp8(rng.standard_normal((n, k)).astype(np.float32))
+        qa, _ = orc.quant_mxfp8(rng.standard_normal((rows, k)).astype(np.float32))
+        sfa_t = rng.integers(124, 131, size=(k // 128, rows)).astype(np.uint8)
+        sfb = rng.integers(124, 131, size=(n // 128, k // 128)).astype(np.uint8)
+        fn = lambda: orc.gemm_e8m0_block(qa, qb, sfa_t, sfb)
     else:
         qb, sb = orc.quant_fp8_block(rng.standard_normal((n, k)).astype(np.float32), 128)
         qa, sa = orc.quant_fp8_block(rng.standard_normal((rows, k)).astype(np.float32), 1)
@@ -268,7 +306,7 @@ def run_reference(args):
         "impl": "reference", "metric": metric_name(args.workload), "value": value, "unit": "TFLOPS",
         "n_gpus": world, "steps": steps, "warmup": min(args.warmup, 2), "ms_per_step": dt * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "mxfp8" if args.workload == "mxfp8" else ("mxfp4" if args.workload == "mxfp4" else "fp8-e4m3"),
+        "dtype": {"mxfp8": "mxfp8", "mxfp4": "mxfp4"}.get(args.workload, "fp8-e4m3"),
         "data": "synthetic",
         "config": {"workload": f"{args.workload} M={m} N={n} K={k} layout={args.layout}",
                    "sample_rows_per_step": rows},
@@ -303,8 +341,13 @@ def run_ours(args):
     m, n, k = args.m, args.n, args.k
     wl = args.workload
     fp4 = wl == "mxfp4"
+    b_format = args.b_format or ("shuffle16" if fp4 else "raw")
     if wl in ("mxfp8", "mxfp4"):
         qa, qb, sa, sb = make_mx_inputs(bs, m, n, k, fp4, args.layout if not fp4 else "tn", dev, 1234 + rank)
+        if b_format == "shuffle16":
+            if not fp4 and args.layout[1] != "n":
+                raise SystemExit("--b-format shuffle16 needs a K-major B (layout tn or nn)")
+            qb = bs.pack_b(qb.view(torch.uint8), "shuffle16", unpack=True).view(qb.dtype)
         if world > 1:
             # the replicated activation A (and its scales) is broadcast once from rank 0
             dist.broadcast(qa.view(torch.uint8), 0)
@@ -314,13 +357,22 @@ def run_ours(args):
         out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
         if fp4:
             call = lambda: bs.gemm_a4w4_mxfp4(qa, qb, sa_n, sb_n, out=out, scale_format="native",
-                                              kernel=args.kernel)
+                                              kernel=args.kernel, b_format=b_format)
             a_bytes, b_bytes = m * k // 2, n * k // 2
         else:
             call = lambda: bs.gemm_a8w8_mxfp8(qa, qb, sa_n, sb_n, layout=args.layout, out=out,
-                                              scale_format="native", kernel=args.kernel)
+                                              scale_format="native", kernel=args.kernel, b_format=b_format)
             a_bytes, b_bytes = m * k, n * k
         sf_bytes = (m + n) * k // 32
+    elif wl == "e8m0block":
+        qa, qb, sa, sb = make_e8m0block_inputs(bs, m, n, k, dev, 1234 + rank)
+        if world > 1:
+            dist.broadcast(qa.view(torch.uint8), 0)
+            dist.broadcast(sa, 0)
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        call = lambda: bs.gemm_a8w8_blockscale_bpreshuffle(qa, qb, sa.t(), sb, torch.bfloat16, out)
+        a_bytes, b_bytes = m * k, n * k
+        sf_bytes = m * (k // 128) + (n // 128) * (k // 128)
     else:
         qa, qb, sa, sb = make_fp8block_inputs(m, n, k, dev, 1234 + rank)
         if world > 1:
@@ -406,9 +458,12 @@ def run_ours(args):
         d_sb.copy_(h_sb, non_blocking=True)
         if wl == "mxfp8":
             r = bs.gemm_a8w8_mxfp8(d_a.view(torch.float8_e4m3fn), d_b.view(torch.float8_e4m3fn), d_sa, d_sb,
-                                   layout=args.layout, out=out)
+                                   layout=args.layout, out=out, b_format=b_format)
         elif wl == "mxfp4":
-            r = bs.gemm_a4w4_mxfp4(d_a, d_b, d_sa, d_sb, out=out)
+            r = bs.gemm_a4w4_mxfp4(d_a, d_b, d_sa, d_sb, out=out, b_format=b_format)
+        elif wl == "e8m0block":
+            r = bs.gemm_a8w8_blockscale_bpreshuffle(d_a.view(torch.float8_e4m3fn), d_b.view(torch.float8_e4m3fn),
+                                                    d_sa.t(), d_sb, torch.bfloat16, out)
         else:
             r = bs.gemm_a8w8_bpreshuffle(d_a.view(torch.float8_e4m3fn), d_b.view(torch.float8_e4m3fn),
                                          d_sa, d_sb, torch.bfloat16, preshuffled=True, out=out)
@@ -462,11 +517,15 @@ def run_ours(args):
             "metric": metric_name(wl), "value": value, "unit": "TFLOPS", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": {"mxfp8": "mxfp8", "mxfp4": "mxfp4", "fp8block": "fp8-e4m3"}[wl],
+            "dtype": {"mxfp8": "mxfp8", "mxfp4": "mxfp4", "fp8block": "fp8-e4m3", "e8m0block": "fp8-e4m3"}[wl],
             "data": "synthetic (seeded torch.randn, quantised on device)",
             "config": {"workload": f"{wl} M={m} N={n}/rank K={k} layout={args.layout if wl == 'mxfp8' else 'tn'}",
+                       "b_format": b_format if wl in ("mxfp8", "mxfp4") else
+                       ("shuffle16" if wl == "e8m0block" else "kpanel128"),
                        "out": "bf16", "accum": "fp32",
-                       "scales": "native tcgen05 atoms (pre-packed)" if wl != "fp8block" else "fp32 1x128 / 128x128",
+                       "scales": {"fp8block": "fp32 1x128 / 128x128",
+                                  "e8m0block": "E8M0 1x128 / 128x128 (reference launcher layout)"}.get(
+                                      wl, "native tcgen05 atoms (pre-packed)"),
                        "parallelism": f"N-sharded x{world}" if world > 1 else "single GPU",
                        "l2": "inputs + output exceed the 126 MB L2; no flush"},
             "gpu_launches": args.steps,
