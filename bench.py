@@ -50,6 +50,19 @@ def load_peaks():
     return PEAKS_FALLBACK, "fallback"
 
 
+def load_traffic(workload, m, n, k, b_format):
+    """DRAM bytes (read + write) of one launch of the workload's dominant
+    kernel from the committed ncu capture (profiles/dram_traffic.json), when
+    that capture was taken on this very shape; else None."""
+    p = ROOT / "profiles" / "dram_traffic.json"
+    if not p.exists():
+        return None, None
+    e = json.loads(p.read_text()).get(workload)
+    if not e or e["shape"] != [m, n, k] or (b_format is not None and e["b_format"] != b_format):
+        return None, None
+    return e["read_bytes"] + e["write_bytes"], f"ncu capture, profiles/{e['summary']}"
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -503,8 +516,10 @@ def run_ours(args):
         peak = bf16 * mult
         basis = (f"{mult:.0f} x bf16_tflops burst ({peak_kind}, {bf16} TF/s): dense "
                  f"{'MXFP4' if fp4 else 'FP8/MXFP8'} tensor rate is {mult:.0f}x bf16 on B200")
+    traffic, traffic_src = load_traffic(wl, m, n, k, b_format if wl in ("mxfp8", "mxfp4") else None)
     roofline = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
-                "frac": achieved / peak if peak else None, "traffic": None, "peak_basis": basis,
+                "frac": achieved / peak if peak else None, "traffic": traffic, "traffic_source": traffic_src,
+                "peak_basis": basis,
                 "algorithmic_bytes_per_launch": alg_bytes, "flops_per_launch": flops,
                 "kernel_ms": kern_ms}
 
