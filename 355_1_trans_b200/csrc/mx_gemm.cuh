@@ -44,7 +44,7 @@
 //   kSfE8m0Block128  the reference's launch_blockscale_bpreshuffle scales:
 //                    one E8M0 byte per row per 128 K, A's transposed
 //                    [K/128][M], B's per 128 x 128 block [N/128][K/128]
-//                    (source_snapshot/gemm_a8w8_mxfp8_scale_host.cc:216-242).
+//                    (source_snapshot/gemm_a8w8_mxfp8_scale_host.cc:219-248).
 //                    Warp 3 rewrites each stage's bytes into atoms with the
 //                    byte replicated over the four 32-K groups, so the
 //                    block-scaled MMA applies one scale per 128 K.

@@ -5,7 +5,7 @@
                     [--workload mxfp8|mxfp4|fp8block|e8m0block] [--layout tn|nn|tt|nt]
                     [--b-format raw|shuffle16]
 
-Default workload (BASELINE metric, configs[2]): MXFP8 GEMM M=N=K=8192, layout
+Default workload (the headline metric): MXFP8 GEMM M=N=K=8192, layout
 tn, E4M3 with E8M0 scales per 32 K, bf16 out, fp32 accumulation.  One step is
 one GEMM over the whole problem.  For N > 1 GPUs (torchrun, one process per
 GPU) the GEMM is partitioned along N with weights pre-sharded: every rank
@@ -33,6 +33,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -81,7 +82,7 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true",
-                    help="fp8 block-scale sweep of BASELINE configs[1] (M x (N,K), 24 shapes), one JSON line")
+                    help="fp8 block-scale sweep, M in {1,16,64,128,1024,8192} x 4 (N,K) shapes, one JSON line")
     return ap.parse_args()
 
 
@@ -99,8 +100,9 @@ class ClockSampler:
         self.path = None
 
     def start(self):
-        out_dir = ROOT / "gpurun_out"
-        out_dir.mkdir(exist_ok=True)
+        # raw samples go to $BENCH_CLOCKS_DIR (kept) or a temporary directory
+        out_dir = Path(os.environ.get("BENCH_CLOCKS_DIR") or tempfile.mkdtemp(prefix="bench_clocks_"))
+        out_dir.mkdir(parents=True, exist_ok=True)
         self.path = out_dir / f"clocks_rank{self.gpu}.csv"
         try:
             self.proc = subprocess.Popen(
@@ -556,7 +558,7 @@ def run_ours(args):
 
 
 def run_sweep(args):
-    """M in {1,16,64,128,1024,8192} x (N,K) in {(7168,2048),
+    """Decode/prefill sweep: M in {1,16,64,128,1024,8192} x (N,K) in {(7168,2048),
     (4096,7168), (24576,1536), (7168,18432)}, fp32 block scales, K-panel B,
     bf16 out.  Each timed GEMM is a CUDA-graph replay of the library call
     (device time only), preceded by an L2 flush that READS a 256 MiB buffer (a
@@ -604,7 +606,7 @@ def run_sweep(args):
                          "tflops": 2.0 * m * n * k / ms / 1e9,
                          "gbs": byts / ms / 1e6, "hbm_frac": byts / ms / 1e6 / peaks["hbm_gbs"]})
     assert bs.check_device_error() == 0
-    print(json.dumps({"sweep": "fp8 block-scale (BASELINE configs[1])", "hbm_peak_gbs": peaks["hbm_gbs"],
+    print(json.dumps({"sweep": "fp8 block-scale, M x (N,K) grid", "hbm_peak_gbs": peaks["hbm_gbs"],
                       "peak_kind": peak_kind, "l2": "flushed (256 MiB read) before every timed launch", "rows": rows}), flush=True)
     return 0
 

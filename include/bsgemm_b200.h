@@ -19,7 +19,7 @@
  *   - arguments are validated first; errors are returned, never aborted on;
  *   - entry points keep no per-call state and may be called concurrently.
  *
- * Layout letters (BASELINE / CUTLASS convention; the reference's letters are
+ * Layout letters (CUTLASS convention; the reference's letters are
  * swapped, e.g. its "nt" is this "tn"):
  *   tn = A K-major [M,K], B K-major [N,K]      (BSG_LAYOUT_TN = 3)
  *   nn = A M-major [K,M], B K-major [N,K]      (BSG_LAYOUT_NN = 2)

@@ -60,7 +60,7 @@ float or_bf16_to_f32(uint16_t b);
 uint64_t or_mix64(uint64_t x);
 void or_fill_normal(float *out, size_t n, uint64_t seed);
 
-/* ---- quantisers -------------------------------------
+/* ---- quantisers (benchmark input recipes) --------------------------------
  * MX (1x32): per row, per 32-K group: scale = 2^ceil(log2(amax / qmax)),
  * elements = RNE(x / scale).  qmax = 448 (E4M3) or 6 (E2M1).  Zero groups get
  * scale byte 127.  x is [rows, k] with row stride ldx; q is [rows, k] bytes

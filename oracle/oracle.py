@@ -290,7 +290,7 @@ def check_e8m0_rule(ref: np.ndarray, got: np.ndarray, mag: np.ndarray, bf16: boo
 
 def check_baseline_rule(ref: np.ndarray, got: np.ndarray, mag: np.ndarray | None = None,
                         mag_floor: float = 1e-6):
-    """BASELINE tolerance on bf16 outputs, per element
+    """Target tolerance on bf16 outputs, per element
         |err| <= 2^-7*|ref| + 1e-3 + mag_floor * sum|term|.
     The last term is the fp32-accumulation floor: where the terms cancel
     (|ref| << sum|term|) no fp32 computation can meet a bound relative to |ref|;

@@ -54,7 +54,7 @@ def assert_close(orc, ref, got, mag=None, what=""):
     """Tolerance of every parity test (bf16 outputs):
          |err| <= 2^-7 |ref| + 1e-3 + 1e-6 * sum|a*b*s|   per element,
          max relative error <= 1e-2 over non-cancelling elements.
-    The BASELINE rule plus an fp32-accumulation floor; see
+    The target rule plus an fp32-accumulation floor; see
     oracle.check_baseline_rule."""
     bad, max_rel, calc_diff = orc.check_baseline_rule(ref, got, mag)
     if bad:

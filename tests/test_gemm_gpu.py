@@ -3,7 +3,7 @@
 Each case follows the reference's self-checking host drivers: inputs are
 seeded and quantised on the host, the raw operands go to the oracle and the
 (possibly repacked) operands to the GPU, C is NaN-poisoned before the launch,
-and the result must meet the BASELINE tolerance on bf16 outputs,
+and the result must meet the target tolerance on bf16 outputs,
     |err| <= 2^-7 |ref| + 1e-3 + 1e-6 * sum|a*b*s|  per element,
     max relative error <= 1e-2 over non-cancelling elements,
 where the last term is an fp32-accumulation floor for elements whose terms
@@ -57,7 +57,7 @@ def run_mxfp8(bs, orc, cuda, m, n, k, *, seed=1, layout="tn", sf_mode="data", ou
 # ---- MXFP8 ---------------------------------------------------------------------------
 
 def test_mxfp8_256_tn_bf16(bs, orc, cuda):
-    """M=N=K=256, tn, bf16 out, data-derived scales."""
+    """The CPU-runnable case: M=N=K=256, tn, bf16 out, data-derived scales."""
     refs, got = run_mxfp8(bs, orc, cuda, 256, 256, 256)
     # also the reference's own acceptance rule (valid_vector with bf16 bounds)
     mag = orc.gemm_mxfp8(*[x[0] for x in mxfp8_problem(orc, 256, 256, 256, 1)], f64=True)[1]
@@ -220,7 +220,7 @@ def test_mxfp8_shuffled_b_in_place(bs, orc, cuda, kernel, out_dtype):
 
 def e8m0_block_problem(orc, m, n, k, seed):
     """E4M3 values of N(0,1) data, E8M0 scale bytes 124 + r % 7 as the
-    reference's fill_scales (source_snapshot/gemm_a8w8_mxfp8_scale_host.cc:155-160)."""
+    reference's fill_scales (source_snapshot/gemm_a8w8_mxfp8_scale_host.cc:154-159)."""
     qa, _ = orc.quant_mxfp8(orc.normal((m, k), seed=seed * 31))
     qb, _ = orc.quant_mxfp8(orc.normal((n, k), seed=seed * 31 + 1))
     rng = np.random.default_rng(seed)
@@ -395,7 +395,7 @@ def test_bounded_wait_reports_timeout(bs, cuda):
 
 @pytest.mark.parametrize("layout,kernel", [("tn", "auto"), ("nt", "auto"), ("tn", "1cta")])
 def test_mxfp8_8192_row_sample(bs, orc, cuda, layout, kernel):
-    """BASELINE config 3 at full size: every output row is produced by the GPU;
+    """MXFP4 8192^3 at full size: every output row is produced by the GPU;
     64 sampled rows are checked against the oracle."""
     m = n = k = 8192
     x = orc.normal((m, k), seed=81)
