@@ -67,7 +67,9 @@ def load_traffic(workload, m, n, k, b_format):
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=2000,
+                    help="timed GEMM launches (the default keeps the timed region near 1 s so the "
+                         "100 ms clock samples cover it)")
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="mxfp8", choices=["mxfp8", "mxfp4", "fp8block", "e8m0block"])
@@ -79,11 +81,17 @@ def parse():
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=8192, help="per-rank N")
     ap.add_argument("--k", type=int, default=8192)
+    ap.add_argument("--shape", default=None,
+                    help="M,N,K (N per rank); same as --m/--n/--k, which torchrun's own parser "
+                         "would take as abbreviations of its options")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true",
                     help="fp8 block-scale sweep, M in {1,16,64,128,1024,8192} x 4 (N,K) shapes, one JSON line")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.shape:
+        args.m, args.n, args.k = (int(v) for v in args.shape.split(","))
+    return args
 
 
 # ---------------------------------------------------------------------------
@@ -215,8 +223,21 @@ def make_fp8block_inputs(m, n, k, device, seed):
 # ---------------------------------------------------------------------------
 # CPU baseline (the reference's CPU GEMM restated in oracle/, "port")
 # ---------------------------------------------------------------------------
+def use_all_host_cores():
+    """The CPU legs run on every core this process may use (torchrun sets
+    OMP_NUM_THREADS=1 for its workers); must run before the OpenMP library
+    of the oracle is loaded."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    return n
+
+
 def cpu_baseline(workload, m, n, k, target_s=12.0, max_rows=None):
     import numpy as np
+    use_all_host_cores()
     from oracle import oracle as orc
     orc.build()
     cores = orc.num_threads()
@@ -280,6 +301,7 @@ def run_reference(args):
     if rank != 0:
         return 0
     import numpy as np
+    use_all_host_cores()
     from oracle import oracle as orc
     orc.build()
     m, n, k = args.m, args.n * world, args.k
