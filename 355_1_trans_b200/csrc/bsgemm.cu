@@ -368,15 +368,36 @@ bool make_shuffle16_tmap(CUtensorMap* m, const void* base, long long rows, long 
   return make_tmap_u8(m, base, 5, dims, strides, box, false);
 }
 
+// Deterministic split-K reduction, launched with programmatic stream
+// serialization: its launch overlaps the GEMM (which signals
+// launch_dependents at its start) and the kernel waits for the GEMM's
+// completion with griddepcontrol.wait before reading the partials.
 int splitk_reduce(const float* ws, const bsgemm_args& a, int split, int sms, cudaStream_t st) {
   const long long total4 = static_cast<long long>(a.m) * a.n * a.batch / 4;
   const int grid = static_cast<int>(std::min<long long>((total4 + 255) / 256, 8LL * sms));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const float* w = ws;
+  void* c = a.ptr_c;
+  int m = a.m, n = a.n, batch = a.batch;
+  long long ldc = a.stride_c, cbs = a.stride_c_batch;
+  cudaError_t e;
   if (a.out_dtype == BSG_OUT_FP32)
-    bsg::splitk_reduce_kernel<true><<<grid, 256, 0, st>>>(ws, a.ptr_c, a.m, a.n, a.batch, split,
-                                                         a.stride_c, a.stride_c_batch);
+    e = cudaLaunchKernelEx(&cfg, bsg::splitk_reduce_kernel<true>, w, c, m, n, batch, split, ldc, cbs);
   else
-    bsg::splitk_reduce_kernel<false><<<grid, 256, 0, st>>>(ws, a.ptr_c, a.m, a.n, a.batch, split,
-                                                          a.stride_c, a.stride_c_batch);
+    e = cudaLaunchKernelEx(&cfg, bsg::splitk_reduce_kernel<false>, w, c, m, n, batch, split, ldc, cbs);
+  if (e != cudaSuccess) {
+    t_last_cuda_error = e;
+    return BSG_ERR_CUDA;
+  }
   return launch_status();
 }
 
@@ -735,7 +756,7 @@ int swap_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockPa
   using Cfg = bsg::SwapCfg<MN>;
   auto* kern = bsg::fp8_block_swap_kernel<MN, kBFmt, kOutF32>;
   if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
-  kern<<<grid, 256, Cfg::kSmemBytes, st>>>(ta, tb, p);
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(ta, tb, p);
   return launch_status();
 }
 

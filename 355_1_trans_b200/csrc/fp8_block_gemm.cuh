@@ -125,6 +125,7 @@ __global__ void __launch_bounds__(256, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  if (threadIdx.x == 0) griddep_launch_dependents();   // a split-K reduce may launch now
 
   if (warp == 0) {
     // producer warp: all lanes run the loop, the elected lane issues the copies

@@ -41,6 +41,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 template <int MN>
 struct SwapCfg {
   static_assert(MN == 16 || MN == 32 || MN == 64, "MN must be 16, 32 or 64");
+  // promotion warps: one per TMEM lane quarter, two (each half of the MN
+  // columns) for MN = 64, so a warp's TMEM-load -> FMA chain per K block
+  // stays short
+  static constexpr int kPromoWarps = MN >= 64 ? 8 : 4;
+  static constexpr int kThreads = 128 + 32 * kPromoWarps;
+  static constexpr int kCols = MN * 4 / kPromoWarps;   // accumulator columns per thread
   static constexpr uint32_t kWBytes = 128u * 128u;                 // weight tile
   static constexpr uint32_t kXBytes = static_cast<uint32_t>(MN) * 128u;
   static constexpr uint32_t kStageBytes = kWBytes + kXBytes;
@@ -62,7 +68,7 @@ struct SwapCfg {
 };
 
 template <int MN, int kBFmt, bool kOutF32>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
     fp8_block_swap_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const Fp8BlockParams p) {
   using Cfg = SwapCfg<MN>;
@@ -96,11 +102,11 @@ __global__ void __launch_bounds__(256, 1)
     }
     for (int i = 0; i < NB; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4);   // one arrival per promotion warp
+      mbar_init(&acc_empty[i], Cfg::kPromoWarps);   // one arrival per promotion warp
     }
     for (int i = 0; i < R; ++i) {
       mbar_init(&scale_full[i], 32);  // one cp.async arrival per producer lane
-      mbar_init(&scale_empty[i], 4);  // one arrival per promotion warp
+      mbar_init(&scale_empty[i], Cfg::kPromoWarps);  // one arrival per promotion warp
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -118,6 +124,7 @@ __global__ void __launch_bounds__(256, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  if (threadIdx.x == 0) griddep_launch_dependents();   // a split-K reduce may launch now
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -225,7 +232,11 @@ __global__ void __launch_bounds__(256, 1)
     mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ promotion + store
+    // warp w: TMEM lane quarter w % 4 (= output columns), activation rows
+    // [c0, c0 + HC) of the tile
+    constexpr int HC = Cfg::kCols;
     const int q = warp & 3;
+    const int c0 = ((warp - 4) >> 2) * HC;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     uint32_t kbi = 0;
     bool ok = true;
@@ -237,9 +248,9 @@ __global__ void __launch_bounds__(256, 1)
       const int n = nt * 128 + q * 32 + static_cast<int>(lane);   // output column of this lane
       const int m0 = mt * MN;
       const int rows = min(MN, p.m - m0);
-      float acc[MN];
+      float acc[HC];
 #pragma unroll
-      for (int i = 0; i < MN; ++i) acc[i] = 0.0f;
+      for (int i = 0; i < HC; ++i) acc[i] = 0.0f;
       for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
         const uint32_t buf = kbi % NB;
         const uint32_t use = kbi / NB;
@@ -252,17 +263,31 @@ __global__ void __launch_bounds__(256, 1)
         tc_fence_after();
         const float* slot = sScale + sl * Cfg::kScaleSlot;
         const float sb = slot[MN];
-        const uint32_t taddr = tmem_base + lane_base + buf * MN;
-        // 16 columns at a time: TMEM load, 16 combined scales, 16 FMAs
+        const uint32_t taddr = tmem_base + lane_base + buf * MN + static_cast<uint32_t>(c0);
+        // 32 (or 16) columns per TMEM load: the load, the combined scales, the FMAs
+        if constexpr (HC % 32 == 0) {
 #pragma unroll
-        for (int c = 0; c < MN / 16; ++c) {
-          uint32_t r[16];
-          tmem_ld16(taddr + static_cast<uint32_t>(c * 16), r);
+          for (int c = 0; c < HC / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(taddr + static_cast<uint32_t>(c * 32), r);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int row = c * 16 + i;
-            const float comb = row < rows ? sb * slot[row] : 0.0f;
-            acc[row] = fmaf(__uint_as_float(r[i]), comb, acc[row]);
+            for (int i = 0; i < 32; ++i) {
+              const int row = c0 + c * 32 + i;
+              const float comb = row < rows ? sb * slot[row] : 0.0f;
+              acc[c * 32 + i] = fmaf(__uint_as_float(r[i]), comb, acc[c * 32 + i]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < HC / 16; ++c) {
+            uint32_t r[16];
+            tmem_ld16(taddr + static_cast<uint32_t>(c * 16), r);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int row = c0 + c * 16 + i;
+              const float comb = row < rows ? sb * slot[row] : 0.0f;
+              acc[c * 16 + i] = fmaf(__uint_as_float(r[i]), comb, acc[c * 16 + i]);
+            }
           }
         }
         tc_fence_before();
@@ -276,9 +301,9 @@ __global__ void __launch_bounds__(256, 1)
       if (n >= p.n) continue;
       // store: lane n writes column n of every valid row (64 B per warp per row)
 #pragma unroll
-      for (int i = 0; i < MN; ++i) {
-        if (i >= rows) break;
-        const int m = m0 + i;
+      for (int i = 0; i < HC; ++i) {
+        if (c0 + i >= rows) break;
+        const int m = m0 + c0 + i;
         if (p.split_k > 1) {
           p.ws[((static_cast<long long>(s) * p.batch + b) * p.m + m) * static_cast<long long>(p.n) + n] = acc[i];
         } else if constexpr (kOutF32) {

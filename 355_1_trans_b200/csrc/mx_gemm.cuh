@@ -250,6 +250,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  if (threadIdx.x == 0) griddep_launch_dependents();   // a split-K reduce may launch now
 
   if (warp == 0) {
     // producer warp: all lanes run the loop, the elected lane issues the copies
@@ -547,6 +548,7 @@ template <bool kOutF32>
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* __restrict__ c, int m,
                                      int n, int batch, int split, long long ldc,
                                      long long c_batch_stride) {
+  griddep_wait();   // launched programmatically behind the GEMM: wait for its partials
   const long long per_batch = static_cast<long long>(m) * n;
   const long long total4 = per_batch * batch / 4;   // n % 4 == 0
   const long long slice = per_batch * batch;

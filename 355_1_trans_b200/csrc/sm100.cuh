@@ -308,6 +308,17 @@ __device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Programmatic dependent launch: a grid launched with the programmatic
+// stream-serialization attribute may start while its predecessor runs;
+// griddep_wait blocks until the predecessor grid has completed and its
+// memory operations are visible.  griddep_launch_dependents lets the
+// dependent grid start launching (once every CTA of this grid issued it or
+// exited); it does not make this grid's results visible early.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------
 // tcgen05
 // ---------------------------------------------------------------------------

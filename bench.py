@@ -582,17 +582,48 @@ def run_ours(args):
 def run_sweep(args):
     """Decode/prefill sweep: M in {1,16,64,128,1024,8192} x (N,K) in {(7168,2048),
     (4096,7168), (24576,1536), (7168,18432)}, fp32 block scales, K-panel B,
-    bf16 out.  Each timed GEMM is a CUDA-graph replay of the library call
-    (device time only), preceded by an L2 flush that READS a 256 MiB buffer (a
-    write-based flush would leave ~126 MB of dirty lines whose write-back would
-    be charged to the GEMM), timed with CUDA events; reports the median and,
-    separately, the host time of one eager call."""
+    bf16 out.
+
+    Device time per GEMM call with cold L2: one CUDA graph replays R times
+    (L2 flush, GEMM call) and a second graph replays the R flushes alone; the
+    difference of the two CUDA-event times, divided by R, is the time of one
+    call including its launch gap behind the flush.  (Events on this GPU tick
+    in 2.048 us steps, too coarse to time one decode-sized call; over R calls
+    the step is R times smaller.)  The flush READS a 256 MiB buffer: a
+    write-based flush would leave ~126 MB of dirty lines whose write-back
+    would be charged to the GEMM.  The call's kernels (GEMM and, when K is
+    split, the reduce) are all captured.  Also reports the host time of one
+    eager call."""
     import torch
     dev = torch.device("cuda", 0)
     bs = importlib.import_module("355_1_trans_b200")
     peaks, peak_kind = load_peaks()
     flush = torch.ones(64 << 20, dtype=torch.float32, device=dev)   # 256 MiB
     sink = torch.empty((), dtype=torch.float32, device=dev)
+    reps = 20
+
+    def graph_time(fn, rounds):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(rounds):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        del g
+        return statistics.median(ts)
+
+    def flushes():
+        for _ in range(reps):
+            torch.sum(flush, dim=0, out=sink)
+
     rows = []
     for (n, k) in ((7168, 2048), (4096, 7168), (24576, 1536), (7168, 18432)):
         qa_full, qb, sa_full, sb = make_fp8block_inputs(8192, n, k, dev, 7)
@@ -600,36 +631,34 @@ def run_sweep(args):
             qa, sa = qa_full[:m].contiguous(), sa_full[:m].contiguous()
             out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
             call = lambda: bs.gemm_a8w8_bpreshuffle(qa, qb, sa, sb, torch.bfloat16, preshuffled=True, out=out)
+
+            def flush_and_gemm():
+                for _ in range(reps):
+                    torch.sum(flush, dim=0, out=sink)
+                    call()
+
             for _ in range(3):
                 call()
-            # capture the call (its kernels and the split-K reduce) in a CUDA
-            # graph so that host-side argument handling is not timed
             torch.cuda.synchronize()
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                call()
-            times, host_us = [], []
-            for _ in range(max(5, args.steps)):
-                torch.sum(flush, dim=0, out=sink)
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-                g.replay()
-                e1.record()
-                torch.cuda.synchronize()
-                times.append(e0.elapsed_time(e1))
+            rounds = max(3, args.steps)
+            t_both = graph_time(flush_and_gemm, rounds)
+            t_flush = graph_time(flushes, rounds)
+            ms = max(t_both - t_flush, 1e-6) / reps
+            host_us = []
+            for _ in range(rounds):
                 t0 = time.perf_counter()
                 call()
                 host_us.append((time.perf_counter() - t0) * 1e6)
                 torch.cuda.synchronize()
-            del g
-            ms = statistics.median(times)
             byts = m * k + n * k + 4 * m * (k // 128) + 4 * (n // 128) * (k // 128) + 2 * m * n
             rows.append({"m": m, "n": n, "k": k, "us": ms * 1e3, "host_call_us": statistics.median(host_us),
                          "tflops": 2.0 * m * n * k / ms / 1e9,
                          "gbs": byts / ms / 1e6, "hbm_frac": byts / ms / 1e6 / peaks["hbm_gbs"]})
     assert bs.check_device_error() == 0
     print(json.dumps({"sweep": "fp8 block-scale, M x (N,K) grid", "hbm_peak_gbs": peaks["hbm_gbs"],
-                      "peak_kind": peak_kind, "l2": "flushed (256 MiB read) before every timed launch", "rows": rows}), flush=True)
+                      "peak_kind": peak_kind, "l2": "flushed (256 MiB read) before every timed call",
+                      "timing": f"graph of {reps} x (flush, call) minus graph of {reps} flushes",
+                      "rows": rows}), flush=True)
     return 0
 
 

@@ -351,6 +351,32 @@ def test_fp8_block_shuffle16_b(bs, orc, cuda, m, kernel):
     run_fp8_block(bs, orc, cuda, m, 768, 1024, seed=60 + m, kernel=kernel, shuffle16=True)
 
 
+@pytest.mark.parametrize("grid_blocks", [3, 7, 0])
+def test_fp8_block_swap_grid_caps_deterministic(bs, orc, cuda, grid_blocks):
+    """Decode kernel under persistent-grid caps with auto split-K: correct,
+    bit-identical from launch to launch, and within tolerance unsplit."""
+    m, n, k = 24, 640, 2304
+    x = orc.normal((m, k), seed=70)
+    w = orc.normal((n, k), seed=71)
+    qa, sa = orc.quant_fp8_block(x, 1)
+    qb, sb = orc.quant_fp8_block(w, 128)
+    ref, mag = orc.gemm_fp8_block(qa, qb, sa, sb)
+    A = dev_u8(qa, cuda).view(torch.float8_e4m3fn)
+    B = dev_u8(orc.shuffle_kpanel(qb), cuda).view(torch.float8_e4m3fn)
+    SA, SB = torch.from_numpy(sa).to(cuda), torch.from_numpy(sb).to(cuda)
+    outs = []
+    for _ in range(2):
+        out = poisoned((m, n), torch.bfloat16, cuda)
+        bs.gemm_a8w8_bpreshuffle(A, B, SA, SB, torch.bfloat16, out=out, kernel="swap", grid_blocks=grid_blocks)
+        outs.append(out)
+    whole = bs.gemm_a8w8_bpreshuffle(A, B, SA, SB, torch.bfloat16, kernel="swap", split_k=1)
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    assert torch.equal(outs[0], outs[1])
+    assert_close(orc, ref, outs[0].float().cpu().numpy(), mag, f"grid cap {grid_blocks}")
+    assert_close(orc, ref, whole.float().cpu().numpy(), mag, "whole tiles")
+
+
 def test_fp8_block_split_k(bs, orc, cuda):
     run_fp8_block(bs, orc, cuda, 64, 512, 2048, seed=9, split_k=5)
 
