@@ -58,8 +58,27 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// Tensor map of rank 3 or 4; dims/strides innermost first; strides[i] is the
+// Tensor map of rank 2 to 5; dims/strides innermost first; strides[i] is the
 // byte stride of dim i+1.
+bool make_tmap_swz(CUtensorMap* m, CUtensorMapDataType dtype, const void* base, int rank,
+                   const uint64_t* dims, const uint64_t* strides, const uint32_t* box,
+                   CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i < rank - 1) s[i] = strides[i];
+  }
+  const CUresult r = fn(m, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, s, b, e,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool make_tmap(CUtensorMap* m, CUtensorMapDataType dtype, const void* base, int rank,
                const uint64_t* dims, const uint64_t* strides, const uint32_t* box, bool swizzle128) {
   EncodeTiledFn fn = encode_fn();
@@ -294,40 +313,43 @@ int mx_launch_e8m0b(bool f32, const CUtensorMap& ta, const CUtensorMap& tb, cons
              : mx_launch_t<BN, 0, false, bsg::kBShuffle16, false, bsg::kSfE8m0Block128>(ta, tb, p, grid, st);
 }
 
+// Operand list of a pair launch: A, B, the two scale maps, C.
+struct Mx2Maps {
+  CUtensorMap a, b, sfa, sfb, c;
+};
+
 template <int kFp4, bool kAMN, int kBMode, int kSfMode>
-int mx2_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tsa,
-                 const CUtensorMap& tsb, const bsg::Mx2Params& p, int grid, cudaStream_t st) {
+int mx2_launch_t(const Mx2Maps& t, const bsg::Mx2Params& p, int grid, cudaStream_t st) {
   using Cfg = bsg::Mx2Cfg<kFp4>;
   auto* kern = bsg::mx_gemm_2sm_kernel<kFp4, kAMN, kBMode, kSfMode>;
   if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
-  kern<<<grid, bsg::kMxThreads, Cfg::kSmemBytes, st>>>(ta, tb, tsa, tsb, p);
+  kern<<<grid, bsg::kMxThreads, Cfg::kSmemBytes, st>>>(t.a, t.b, t.sfa, t.sfb, t.c, p);
   return launch_status();
 }
 
-int mx2_launch(bool fp4, bool amn, int bmode, int sfmode, const CUtensorMap& ta, const CUtensorMap& tb,
-               const CUtensorMap& tsa, const CUtensorMap& tsb, const bsg::Mx2Params& p, int grid,
+int mx2_launch(bool fp4, bool amn, int bmode, int sfmode, const Mx2Maps& t, const bsg::Mx2Params& p, int grid,
                cudaStream_t st) {
   using namespace bsg;
   if (sfmode == kSfE8m0Block128) {
     if (fp4 || amn || bmode != kBShuffle16) return BSG_ERR_UNSUPPORTED;
-    return mx2_launch_t<0, false, kBShuffle16, kSfE8m0Block128>(ta, tb, tsa, tsb, p, grid, st);
+    return mx2_launch_t<0, false, kBShuffle16, kSfE8m0Block128>(t, p, grid, st);
   }
   if (fp4) {
     if (amn || bmode == kBMNMajor) return BSG_ERR_UNSUPPORTED;
-    return bmode == kBShuffle16 ? mx2_launch_t<1, false, kBShuffle16, kSfNative>(ta, tb, tsa, tsb, p, grid, st)
-                                : mx2_launch_t<1, false, kBKMajor, kSfNative>(ta, tb, tsa, tsb, p, grid, st);
+    return bmode == kBShuffle16 ? mx2_launch_t<1, false, kBShuffle16, kSfNative>(t, p, grid, st)
+                                : mx2_launch_t<1, false, kBKMajor, kSfNative>(t, p, grid, st);
   }
   if (amn) {
     switch (bmode) {
-      case kBKMajor: return mx2_launch_t<0, true, kBKMajor, kSfNative>(ta, tb, tsa, tsb, p, grid, st);
-      case kBMNMajor: return mx2_launch_t<0, true, kBMNMajor, kSfNative>(ta, tb, tsa, tsb, p, grid, st);
-      default: return mx2_launch_t<0, true, kBShuffle16, kSfNative>(ta, tb, tsa, tsb, p, grid, st);
+      case kBKMajor: return mx2_launch_t<0, true, kBKMajor, kSfNative>(t, p, grid, st);
+      case kBMNMajor: return mx2_launch_t<0, true, kBMNMajor, kSfNative>(t, p, grid, st);
+      default: return mx2_launch_t<0, true, kBShuffle16, kSfNative>(t, p, grid, st);
     }
   }
   switch (bmode) {
-    case kBKMajor: return mx2_launch_t<0, false, kBKMajor, kSfNative>(ta, tb, tsa, tsb, p, grid, st);
-    case kBMNMajor: return mx2_launch_t<0, false, kBMNMajor, kSfNative>(ta, tb, tsa, tsb, p, grid, st);
-    default: return mx2_launch_t<0, false, kBShuffle16, kSfNative>(ta, tb, tsa, tsb, p, grid, st);
+    case kBKMajor: return mx2_launch_t<0, false, kBKMajor, kSfNative>(t, p, grid, st);
+    case kBMNMajor: return mx2_launch_t<0, false, kBMNMajor, kSfNative>(t, p, grid, st);
+    default: return mx2_launch_t<0, false, kBShuffle16, kSfNative>(t, p, grid, st);
   }
 }
 
@@ -437,10 +459,24 @@ int mx_launch_planned(const bsgemm_args& a, const MxOperands& o, const MxPlan& p
   if (mx_use_pair(a, pl, dev)) {
     if (pl.split > 1 || a.out_dtype != BSG_OUT_BF16) return BSG_ERR_UNSUPPORTED;
     if (!e8m0b && (o.sfa_bs % 512 || o.sfb_bs % 512)) return BSG_ERR_UNSUPPORTED;
-    CUtensorMap ta, tb, tsa, tsb;
+    Mx2Maps t;
+    CUtensorMap &ta = t.a, &tb = t.b, &tsa = t.sfa, &tsb = t.sfb;
     if (!make_operand_tmap(&ta, a.ptr_a, o.a_cols, o.a_rows, a.stride_a, a.stride_a_batch, a.batch, 128u) ||
         !make_b_tmap(&tb, a, o, 128u))
       return BSG_ERR_CUDA;
+    {
+      // C (bf16) for the TMA-store epilogue: boxes of 32 columns x 32 rows, 64-byte swizzle
+      const uint64_t dims[3] = {static_cast<uint64_t>(a.n), static_cast<uint64_t>(a.m),
+                                static_cast<uint64_t>(a.batch)};
+      const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_c) * 2u,
+                                   static_cast<uint64_t>(a.batch > 1 ? a.stride_c_batch
+                                                                     : static_cast<long long>(a.m) * a.stride_c) *
+                                       2u};
+      const uint32_t box[3] = {32u, 32u, 1u};
+      if (!make_tmap_swz(&t.c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.ptr_c, 3, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_64B))
+        return BSG_ERR_CUDA;
+    }
     const int sf_kb_total = (kg + 3) / 4;
     const int atoms_k = o.fp4 ? 2 : 1;
     if (e8m0b) {
@@ -477,7 +513,7 @@ int mx_launch_planned(const bsgemm_args& a, const MxOperands& o, const MxPlan& p
     q.timeout_ns = kTimeoutNs;
     int clusters = std::min(q.total_units, dev.sms / 2);
     if (a.grid_blocks > 0) clusters = std::min(clusters, std::max(1, a.grid_blocks / 2));
-    return mx2_launch(o.fp4, o.a_mn, o.bmode, o.sfmode, ta, tb, tsa, tsb, q, 2 * clusters, st);
+    return mx2_launch(o.fp4, o.a_mn, o.bmode, o.sfmode, t, q, 2 * clusters, st);
   }
 
   CUtensorMap ta, tb;

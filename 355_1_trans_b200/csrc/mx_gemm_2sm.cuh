@@ -26,7 +26,10 @@
 //       tmem_full of both CTAs;
 //   epilogue (warps 4-11, both)    wait their own tmem_full, drain their own
 //       TMEM rows (128 x 256 per CTA) into packed bf16 registers, arrive on the
-//       leader's tmem_empty (count 2 x 256), then store.
+//       leader's tmem_empty (count 2 x 8 warps), then store through TMA: each
+//       warp stages 32 rows x 32 columns (2 KB, 64-byte swizzle, so the 32
+//       lanes' 16-byte writes spread over all banks) and issues a tensor store
+//       of that box; TMA clips the box at the M and N edges.
 //   scale builder (warp 3, both CTAs; kSfE8m0Block128 only)  writes its own
 //       CTA's scale atoms for the stage from the per-128 E8M0 bytes
 //       (mx_gemm.cuh), fences them for the async proxy (CTA scope) and
@@ -73,14 +76,20 @@ struct Mx2Cfg {
   static constexpr uint32_t kSfaBytes = 512u * kSfAtomsK;        // this CTA's 128 rows
   static constexpr uint32_t kSfbBytes = 2u * 512u * kSfAtomsK;   // 256 columns
   static constexpr uint32_t kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
-  static constexpr int kStages = static_cast<int>((225u * 1024u - 2048u) / kStageBytes) > 8
+  // shared memory left for stages after the epilogue staging (8 x 2 KB)
+  static constexpr uint32_t kStageBudget = 225u * 1024u - 2048u - 8u * 2048u;
+  static constexpr int kStages = static_cast<int>(kStageBudget / kStageBytes) > 8
                                      ? 8
-                                     : static_cast<int>((225u * 1024u - 2048u) / kStageBytes);
+                                     : static_cast<int>(kStageBudget / kStageBytes);
   static constexpr uint32_t kOffB = kABytes * kStages;
   static constexpr uint32_t kOffSfa = kOffB + kBBytes * kStages;
   static constexpr uint32_t kOffSfb = kOffSfa + kSfaBytes * kStages;
-  static constexpr uint32_t kOffBar = kOffSfb + kSfbBytes * kStages;
+  static constexpr uint32_t kOffOut = kOffSfb + kSfbBytes * kStages;   // 8 epilogue warps x 2 KB
+  static constexpr uint32_t kOutBytes = 32u * 64u;
+  static constexpr uint32_t kOffBar = kOffOut + 8u * kOutBytes;
   static constexpr uint32_t kSmemBytes = kOffBar + 256u + 1024u;
+  static_assert(kSmemBytes <= 227u * 1024u, "shared memory");
+  static_assert(kOffOut % 1024u == 0, "swizzled staging buffers need 1024-byte alignment");
   // barriers: full, empty, sf_ready [S each], tmem_full, tmem_empty, drain; holder + abort flag
   static_assert(8u * (3u * kStages + 3u) + 8u <= 256u, "barrier area");
   // two alternating scale-factor regions after the 256 accumulator columns
@@ -96,7 +105,8 @@ template <int kFp4, bool kAMN, int kBMode, int kSfMode>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
     mx_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmSfa,
-                       const __grid_constant__ CUtensorMap tmSfb, const Mx2Params p) {
+                       const __grid_constant__ CUtensorMap tmSfb, const __grid_constant__ CUtensorMap tmC,
+                       const Mx2Params p) {
   using Cfg = Mx2Cfg<kFp4>;
   constexpr int S = Cfg::kStages;
   constexpr bool kBMN = kBMode == kBMNMajor;
@@ -145,6 +155,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
     prefetch_tmap(&tmB);
     prefetch_tmap(&tmSfa);
     prefetch_tmap(&tmSfb);
+    prefetch_tmap(&tmC);
   }
   tc_fence_before();
   cluster_sync_all();   // barriers of both CTAs initialised, TMEM allocated
@@ -361,6 +372,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
     const uint32_t t_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                             static_cast<uint32_t>(half * 128);
     const uint32_t te_leader = mapa_shared(smem_u32(tmem_empty), 0);
+    uint8_t* out_buf = smem + Cfg::kOffOut + static_cast<uint32_t>(warp - 4) * Cfg::kOutBytes;
     int iter = 0;
     for (int u = cluster_id; u < p.total_units; u += num_clusters, ++iter) {
       int b, mt, nt, s;
@@ -382,22 +394,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(te_leader);
-      if (row < p.m && valid_cols > 0) {
-        uint16_t* dst = reinterpret_cast<uint16_t*>(p.c) + b * p.c_batch_stride +
-                        static_cast<long long>(row) * p.ldc + col_base;
-        if (valid_cols >= 128) {
+      // 4 boxes of 32 rows x 32 columns through this warp's staging buffer
+      const int row0 = mt * 256 + static_cast<int>(rank) * 128 + q * 32;
+      if (row0 < p.m && valid_cols > 0) {
+        const uint32_t swz = (lane >> 1) & 3u;   // 64-byte swizzle of row `lane`
 #pragma unroll
-          for (int v = 0; v < 16; ++v)
-            st_global_cs_v4(dst + 8 * v, w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
-        } else {
+        for (int c = 0; c < 4; ++c) {
+          if (c * 32 >= valid_cols) break;
+          if (lane == 0) bulk_wait_group_read0();   // the previous box has left the buffer
+          __syncwarp();
 #pragma unroll
-          for (int v = 0; v < 64; ++v) {
-            if (2 * v < valid_cols) dst[2 * v] = static_cast<uint16_t>(w[v] & 0xFFFFu);
-            if (2 * v + 1 < valid_cols) dst[2 * v + 1] = static_cast<uint16_t>(w[v] >> 16);
+          for (int j = 0; j < 4; ++j)
+            st_shared_v4(out_buf + lane * 64u + ((static_cast<uint32_t>(j) ^ swz) * 16u), w[c * 16 + 4 * j],
+                         w[c * 16 + 4 * j + 1], w[c * 16 + 4 * j + 2], w[c * 16 + 4 * j + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tmC, out_buf, col_base + c * 32, row0, b);
+            bulk_commit_group();
           }
         }
       }
     }
+    if (lane == 0) bulk_wait_group0();   // every store of this warp has completed
   }
 
   __syncwarp();
