@@ -81,6 +81,8 @@ def lib() -> ctypes.CDLL:
         "bsgemm_check_device_error": (I, []),
         "bsgemm_selftest_timeout": (I, [I]),
         "bsgemm_version": (ctypes.c_char_p, []),
+        "bsgemm_quantize": (I, [P, I, I, I, ctypes.c_longlong, I, P, ctypes.c_longlong, P, I,
+                                ctypes.c_longlong, P]),
     }
     for name, (res, argt) in sigs.items():
         fn = getattr(so, name)
@@ -413,6 +415,62 @@ def gemm_a8w8_blockscale_bpreshuffle(A, B, A_scale, B_scale, dtype=torch.bfloat1
     if status:
         raise RuntimeError(f"blockscale bpreshuffle launch failed: CUDA error {status}")
     return out
+
+
+# ---------------------------------------------------------------------------
+# activation quantise + pack (device)
+# ---------------------------------------------------------------------------
+QUANT_FORMATS = {"mxfp8": 0, "mxfp4": 1, "fp8_block": 2}
+
+
+def quantize(x, fmt: str = "mxfp8", *, scale_format: str | None = None):
+    """Quantise a bf16 or fp32 tensor [rows, cols] for the GEMMs in one device pass.
+
+    fmt "mxfp8": (E4M3 [rows, cols], E8M0 per 32 columns), "mxfp4": (packed
+    E2M1 [rows, cols/2] uint8, E8M0 per 32), "fp8_block": (E4M3, fp32 per 128).
+    scale_format: MX "native" (tcgen05 atoms, default) or "rowmajor"
+    [rows, cols/32]; fp8_block "rowmajor" [rows, cols/128] (default) or
+    "kmajor_t" [cols/128, rows].  Returns (q, scales)."""
+    if x.dim() != 2 or x.dtype not in (torch.bfloat16, torch.float32) or not x.is_cuda:
+        raise ValueError("x must be a 2-D bf16 or fp32 CUDA tensor")
+    if fmt not in QUANT_FORMATS:
+        raise ValueError(f"fmt must be one of {sorted(QUANT_FORMATS)}")
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    rows, cols = x.shape
+    dev = x.device
+    if fmt == "fp8_block":
+        scale_format = scale_format or "rowmajor"
+        q = torch.empty((rows, cols), dtype=torch.float8_e4m3fn, device=dev)
+        if scale_format == "rowmajor":
+            sf = torch.empty((rows, cols // 128), dtype=torch.float32, device=dev)
+            sff, ld = SF_ROWMAJOR, cols // 128
+        elif scale_format == "kmajor_t":
+            sf = torch.empty((cols // 128, rows), dtype=torch.float32, device=dev)
+            sff, ld = SF_KMAJOR_T, rows
+        else:
+            raise ValueError("fp8_block scale_format must be 'rowmajor' or 'kmajor_t'")
+        ldq = cols
+    else:
+        scale_format = scale_format or "native"
+        q = torch.empty((rows, cols // 2 if fmt == "mxfp4" else cols),
+                        dtype=torch.uint8 if fmt == "mxfp4" else torch.float8_e4m3fn, device=dev)
+        ldq = q.shape[1]
+        if scale_format == "native":
+            sf = torch.empty(native_scales_size(rows, cols // 32), dtype=torch.uint8, device=dev)
+            sff, ld = SF_NATIVE, 0
+        elif scale_format == "rowmajor":
+            sf = torch.empty((rows, cols // 32), dtype=torch.uint8, device=dev)
+            sff, ld = SF_ROWMAJOR, cols // 32
+        else:
+            raise ValueError("MX scale_format must be 'native' or 'rowmajor'")
+    with torch.cuda.device(dev):
+        status = lib().bsgemm_quantize(x.data_ptr(), 1 if x.dtype == torch.float32 else 0, rows, cols,
+                                       x.stride(0), QUANT_FORMATS[fmt], q.data_ptr(), ldq, sf.data_ptr(),
+                                       sff, ld, _stream(dev))
+        _record((x, q, sf), dev)
+    _check(status, "bsgemm_quantize")
+    return q, sf
 
 
 # ---------------------------------------------------------------------------

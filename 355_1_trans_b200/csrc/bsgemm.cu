@@ -23,6 +23,7 @@
 #include "mx_gemm.cuh"
 #include "mx_gemm_2sm.cuh"
 #include "pack.cuh"
+#include "quant.cuh"
 
 namespace {
 
@@ -1062,6 +1063,75 @@ int launch_blockscale_bpreshuffle(const void* kargs, int output_bf16, int tiles,
   bsgemm_args_init(&a);
   std::memcpy(&a, kargs, 96);
   return e8m0b_run(a, output_bf16 == 1, tiles, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int bsgemm_quantize(const void* x, int in_dtype, int rows, int cols, long long ldx, int format, void* q,
+                    long long ldq, void* sf, int sf_format, long long ld_sf, bsg_stream_t stream) {
+  if (!x || !q || !sf || rows <= 0 || cols <= 0) return BSG_ERR_INVALID_VALUE;
+  if (in_dtype != BSG_IN_BF16 && in_dtype != BSG_IN_FP32) return BSG_ERR_INVALID_VALUE;
+  if (format != BSG_QUANT_MXFP8 && format != BSG_QUANT_MXFP4 && format != BSG_QUANT_FP8_BLOCK)
+    return BSG_ERR_INVALID_VALUE;
+  const bool mx = format != BSG_QUANT_FP8_BLOCK;
+  const int group = mx ? 32 : 128;
+  if (cols % group) return BSG_ERR_INVALID_VALUE;
+  const int esz = in_dtype == BSG_IN_FP32 ? 4 : 2;
+  if (ldx < cols || (ldx * esz) % 16 || !aligned16(x)) return BSG_ERR_ALIGNMENT;
+  const long long qcols = format == BSG_QUANT_MXFP4 ? cols / 2 : cols;
+  const int qalign = format == BSG_QUANT_MXFP4 ? 4 : 8;
+  if (ldq < qcols || ldq % qalign || reinterpret_cast<uintptr_t>(q) % qalign) return BSG_ERR_ALIGNMENT;
+  if (mx) {
+    if (sf_format == BSG_SF_NATIVE) {
+      if (cols % 128) return BSG_ERR_INVALID_VALUE;
+    } else if (sf_format != BSG_SF_ROWMAJOR || ld_sf < cols / 32) {
+      return BSG_ERR_INVALID_VALUE;
+    }
+  } else {
+    if (sf_format == BSG_SF_ROWMAJOR) {
+      if (ld_sf < cols / 128) return BSG_ERR_INVALID_VALUE;
+    } else if (sf_format != BSG_SF_KMAJOR_T || ld_sf < rows) {
+      return BSG_ERR_INVALID_VALUE;
+    }
+    if (reinterpret_cast<uintptr_t>(sf) % 4) return BSG_ERR_ALIGNMENT;
+  }
+  // q and the scales must not overlap x
+  const uint64_t xbytes = static_cast<uint64_t>(rows - 1) * ldx * esz + static_cast<uint64_t>(cols) * esz;
+  const uint64_t qbytes = static_cast<uint64_t>(rows - 1) * ldq + static_cast<uint64_t>(qcols);
+  if (overlaps(x, xbytes, q, qbytes)) return BSG_ERR_INVALID_VALUE;
+  bsg::QuantParams p{};
+  p.x = x;
+  p.in_fp32 = in_dtype == BSG_IN_FP32;
+  p.rows = rows;
+  p.cols = cols;
+  p.ldx = ldx;
+  p.q = static_cast<uint8_t*>(q);
+  p.ldq = ldq;
+  p.sf = sf;
+  p.sf_format = sf_format == BSG_SF_NATIVE ? 0 : sf_format == BSG_SF_ROWMAJOR ? 1 : 2;
+  p.ld_sf = ld_sf;
+  p.rows_padded = (rows + 127) / 128 * 128;
+  const int warps_per_row = (cols + bsg::kQuantWarpCols - 1) / bsg::kQuantWarpCols;
+  const int launch_rows = mx && p.sf_format == 0 ? p.rows_padded : rows;
+  const long long warps = static_cast<long long>(launch_rows) * warps_per_row;
+  const long long blocks = (warps + 7) / 8;
+  if (blocks > 0x7fffffffLL) return BSG_ERR_INVALID_VALUE;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const dim3 grid(static_cast<unsigned>(blocks));
+  const bool f32 = in_dtype == BSG_IN_FP32;
+  switch (format) {
+    case BSG_QUANT_MXFP8:
+      if (f32) bsg::quantize_kernel<bsg::kQuantMxfp8, true><<<grid, 256, 0, st>>>(p);
+      else bsg::quantize_kernel<bsg::kQuantMxfp8, false><<<grid, 256, 0, st>>>(p);
+      break;
+    case BSG_QUANT_MXFP4:
+      if (f32) bsg::quantize_kernel<bsg::kQuantMxfp4, true><<<grid, 256, 0, st>>>(p);
+      else bsg::quantize_kernel<bsg::kQuantMxfp4, false><<<grid, 256, 0, st>>>(p);
+      break;
+    default:
+      if (f32) bsg::quantize_kernel<bsg::kQuantFp8Block, true><<<grid, 256, 0, st>>>(p);
+      else bsg::quantize_kernel<bsg::kQuantFp8Block, false><<<grid, 256, 0, st>>>(p);
+      break;
+  }
+  return launch_status();
 }
 
 const char* bsgemm_strerror(int status) {

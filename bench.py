@@ -86,6 +86,8 @@ def parse():
                          "would take as abbreviations of its options")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--quant", action="store_true",
+                    help="activation quantise+pack bandwidth (bf16 -> mxfp8/mxfp4/fp8_block), one JSON line")
     ap.add_argument("--sweep", action="store_true",
                     help="fp8 block-scale sweep, M in {1,16,64,128,1024,8192} x 4 (N,K) shapes, one JSON line")
     args = ap.parse_args()
@@ -662,12 +664,75 @@ def run_sweep(args):
     return 0
 
 
+def run_quant(args):
+    """bsgemm_quantize bandwidth: bf16 activations [M, 7168] -> each format with
+    its default scale layout, L2 flushed before every call, graph-difference
+    timing as in the sweep.  Bytes = bf16 read + elements + scales written."""
+    import torch
+    dev = torch.device("cuda", 0)
+    bs = importlib.import_module("355_1_trans_b200")
+    peaks, peak_kind = load_peaks()
+    flush = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    sink = torch.empty((), dtype=torch.float32, device=dev)
+    reps = 20
+
+    def graph_time(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(max(3, min(args.steps, 10))):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        del g
+        return statistics.median(ts)
+
+    def flushes():
+        for _ in range(reps):
+            torch.sum(flush, dim=0, out=sink)
+
+    t_flush = graph_time(flushes)
+    rows = []
+    k = 7168
+    for m in (16, 128, 1024, 8192, 32768):
+        x = torch.randn(m, k, device=dev).to(torch.bfloat16)
+        for fmt in ("mxfp8", "mxfp4", "fp8_block"):
+            call = lambda: bs.quantize(x, fmt)
+            call()
+
+            def both():
+                for _ in range(reps):
+                    torch.sum(flush, dim=0, out=sink)
+                    call()
+
+            ms = max(graph_time(both) - t_flush, 1e-6) / reps
+            out_bytes = m * k // (2 if fmt == "mxfp4" else 1) + (m * k // 32 if fmt != "fp8_block" else 4 * m * k // 128)
+            byts = 2 * m * k + out_bytes
+            rows.append({"m": m, "k": k, "format": fmt, "us": ms * 1e3, "gbs": byts / ms / 1e6,
+                         "hbm_frac": byts / ms / 1e6 / peaks["hbm_gbs"]})
+    assert bs.check_device_error() == 0
+    print(json.dumps({"quantize": "bf16 [M, 7168] -> format, default scale layout", "hbm_peak_gbs": peaks["hbm_gbs"],
+                      "peak_kind": peak_kind, "l2": "flushed before every call",
+                      "timing": f"graph of {reps} x (flush, call) minus graph of {reps} flushes", "rows": rows}),
+          flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
     if args.sweep:
         return run_sweep(args)
+    if args.quant:
+        return run_quant(args)
     return run_ours(args)
 
 

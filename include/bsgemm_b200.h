@@ -211,6 +211,34 @@ BSG_API size_t bsgemm_native_scales_size(int rows, int kg);
 BSG_API int launch_blockscale_bpreshuffle(const void *opus_gemm_scale_kargs, int output_bf16,
                                   int tiles, bsg_stream_t stream);
 
+/* ---- activation quantise + pack ----------------------------------------- */
+enum { BSG_QUANT_MXFP8 = 0, BSG_QUANT_MXFP4 = 1, BSG_QUANT_FP8_BLOCK = 2 };
+enum { BSG_IN_BF16 = 0, BSG_IN_FP32 = 1 };
+
+/*
+ * Quantise x [rows, cols] (bf16 or fp32, row stride ldx elements, 16-byte
+ * aligned rows) in one pass, writing elements and scales in layouts the GEMM
+ * entry points read:
+ *   BSG_QUANT_MXFP8     q E4M3 [rows, cols] bytes (row stride ldq bytes, % 8),
+ *                       one E8M0 scale per 32 columns = 2^ceil(log2(amax/448)),
+ *                       elements RNE-saturated from x * 2^-scale; cols % 32;
+ *   BSG_QUANT_MXFP4     q packed E2M1 [rows, cols/2] (even column in the low
+ *                       nibble, ldq % 4), scale 2^ceil(log2(amax/6)); cols % 32;
+ *   BSG_QUANT_FP8_BLOCK q E4M3 [rows, cols], one fp32 scale amax/448 per 128
+ *                       columns (1 for an all-zero block); cols % 128.
+ * MX scales: sf_format BSG_SF_NATIVE (tcgen05 atoms, bsgemm_native_scales_size(
+ * rows, cols/32) bytes, padding rows 0x7F; cols % 128) or BSG_SF_ROWMAJOR
+ * ([rows, cols/32] bytes, row stride ld_sf).  FP8 block scales:
+ * BSG_SF_ROWMAJOR ([rows, cols/128], row stride ld_sf floats) or
+ * BSG_SF_KMAJOR_T ([cols/128, rows], stride ld_sf floats).
+ * Bit-identical to the reference drivers' host quantisation recipes (E8M0
+ * codec: mxfp8_gemm/gemm_a8w8_mxfp8_host.cc:35-47).  No reference entry
+ * point: the reference quantises on the host only.
+ */
+BSG_API int bsgemm_quantize(const void *x, int in_dtype, int rows, int cols, long long ldx, int format,
+                            void *q, long long ldq, void *sf, int sf_format, long long ld_sf,
+                            bsg_stream_t stream);
+
 /* Human-readable status. */
 BSG_API const char *bsgemm_strerror(int status);
 
