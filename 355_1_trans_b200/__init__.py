@@ -161,8 +161,9 @@ def gemm_a8w8_mxfp8(A, B, A_scale, B_scale, *, layout: str = "tn", out_dtype=tor
     optional leading batch dim.  A_scale/B_scale: E8M0 bytes, [rows, K/32]
     row-major (scale_format="rowmajor") or native atoms from pack_scales
     (scale_format="native").  Returns C [M,N] (or [batch,M,N]) of out_dtype.
-    kernel: "auto", "1cta" (128 x BN tiles, one CTA each) or "pair" (256 x 256
-    tiles on CTA pairs, cta_group::2).  b_format "shuffle16": B holds aiter's
+    kernel: "auto", "1cta" (128 x BN tiles, one CTA each), "pair" (256 x 256
+    tiles on CTA pairs, cta_group::2) or "swap" (transposed decode kernel,
+    M <= 64, layout tn).  b_format "shuffle16": B holds aiter's
     shuffle_weight(16,16) bytes of a K-major [N,K] B (read in place).
     """
     return _mx(A, B, A_scale, B_scale, fp4=False, layout=layout, out_dtype=out_dtype, out=out,

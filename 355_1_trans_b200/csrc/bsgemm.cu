@@ -22,6 +22,7 @@
 #include "fp8_block_swap.cuh"
 #include "mx_gemm.cuh"
 #include "mx_gemm_2sm.cuh"
+#include "mx_gemm_swap.cuh"
 #include "pack.cuh"
 #include "quant.cuh"
 
@@ -228,15 +229,33 @@ struct MxPlan : Plan {
   size_t ws_sfa = 0, ws_sfb = 0;  // bytes of packed scales in the workspace
 };
 
+// Activation rows per transposed-kernel tile (the MMA's N side): 16, 32 or 64.
+int swap_mn(int m) { return m <= 16 ? 16 : m <= 32 ? 32 : 64; }
+
+// Transposed MX kernel: decode-shaped M (one activation tile), both operands
+// K-major (B raw or shuffle_weight(16,16)).
+bool mx_use_swap(const bsgemm_args& a) {
+  const bool eligible = a.m <= 64 && a.layout == BSG_LAYOUT_TN &&
+                        (a.b_format == BSG_B_RAW || a.b_format == BSG_B_SHUFFLE16);
+  return eligible && (a.kernel == BSG_KERNEL_SWAP || a.kernel == BSG_KERNEL_AUTO);
+}
+
 int mx_plan(const bsgemm_args& a, bool fp4, const DevInfo& dev, MxPlan& pl, bool allow_auto) {
   const int kg = a.k / 32;
-  pl.tiles_m = (a.m + 127) / 128;
   pl.num_kb = fp4 ? a.k / 256 : a.k / 128;
-  pl.bn = 256;
-  if (static_cast<long long>(pl.tiles_m) * ((a.n + 255) / 256) * a.batch < dev.sms / 2 || a.n <= 128)
-    pl.bn = 128;
-  pl.tiles_n = (a.n + pl.bn - 1) / pl.bn;
-  plan_split(pl, a, dev.sms, allow_auto, 128.0 * (128 + pl.bn));
+  if (mx_use_swap(a)) {
+    pl.bn = swap_mn(a.m);   // activation rows per tile
+    pl.tiles_m = 1;
+    pl.tiles_n = (a.n + 127) / 128;
+    plan_split(pl, a, dev.sms, allow_auto, 128.0 * (128 + pl.bn));
+  } else {
+    pl.tiles_m = (a.m + 127) / 128;
+    pl.bn = 256;
+    if (static_cast<long long>(pl.tiles_m) * ((a.n + 255) / 256) * a.batch < dev.sms / 2 || a.n <= 128)
+      pl.bn = 128;
+    pl.tiles_n = (a.n + pl.bn - 1) / pl.bn;
+    plan_split(pl, a, dev.sms, allow_auto, 128.0 * (128 + pl.bn));
+  }
   pl.ws_sfa = a.sfa_format == BSG_SF_ROWMAJOR ? align256(native_sf_bytes(a.m, kg) * a.batch) : 0;
   pl.ws_sfb = a.sfb_format == BSG_SF_ROWMAJOR ? align256(native_sf_bytes(a.n, kg) * a.batch) : 0;
   return BSG_OK;
@@ -445,6 +464,35 @@ bool make_b_tmap(CUtensorMap* m, const bsgemm_args& a, const MxOperands& o, uint
                            o.bmode == bsg::kBMNMajor ? 128u : box_rows);
 }
 
+template <int MN, int kFp4, int kBMode, bool kOutF32>
+int mxs_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p, int grid, cudaStream_t st) {
+  using Cfg = bsg::MxSwapCfg<MN, kFp4>;
+  auto* kern = bsg::mx_gemm_swap_kernel<MN, kFp4, kBMode, kOutF32>;
+  if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
+  kern<<<grid, 256, Cfg::kSmemBytes, st>>>(ta, tb, p);
+  return launch_status();
+}
+
+template <int MN, int kFp4>
+int mxs_launch_mn(int bmode, bool f32, const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p, int grid,
+                  cudaStream_t st) {
+  if (bmode == bsg::kBShuffle16)
+    return f32 ? mxs_launch_t<MN, kFp4, bsg::kBShuffle16, true>(ta, tb, p, grid, st)
+               : mxs_launch_t<MN, kFp4, bsg::kBShuffle16, false>(ta, tb, p, grid, st);
+  return f32 ? mxs_launch_t<MN, kFp4, bsg::kBKMajor, true>(ta, tb, p, grid, st)
+             : mxs_launch_t<MN, kFp4, bsg::kBKMajor, false>(ta, tb, p, grid, st);
+}
+
+template <int kFp4>
+int mxs_launch(int mn, int bmode, bool f32, const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p,
+               int grid, cudaStream_t st) {
+  switch (mn) {
+    case 16: return mxs_launch_mn<16, kFp4>(bmode, f32, ta, tb, p, grid, st);
+    case 32: return mxs_launch_mn<32, kFp4>(bmode, f32, ta, tb, p, grid, st);
+    default: return mxs_launch_mn<64, kFp4>(bmode, f32, ta, tb, p, grid, st);
+  }
+}
+
 bool mx_use_pair(const bsgemm_args& a, const MxPlan& pl, const DevInfo& dev) {
   const long long pair_tiles = static_cast<long long>((a.m + 255) / 256) * ((a.n + 255) / 256) * a.batch;
   return a.kernel == BSG_KERNEL_PAIR ||
@@ -457,6 +505,45 @@ int mx_launch_planned(const bsgemm_args& a, const MxOperands& o, const MxPlan& p
                       cudaStream_t st) {
   const bool e8m0b = o.sfmode == bsg::kSfE8m0Block128;
   const int kg = a.k / 32;
+  if (!e8m0b && mx_use_swap(a)) {
+    // transposed decode kernel: activations box MN rows, weights box 128 rows
+    CUtensorMap ta, tb;
+    if (!make_operand_tmap(&ta, a.ptr_a, o.a_cols, o.a_rows, a.stride_a, a.stride_a_batch, a.batch,
+                           static_cast<uint32_t>(pl.bn)) ||
+        !make_b_tmap(&tb, a, o, 128u))
+      return BSG_ERR_CUDA;
+    MxParams p{};
+    p.m = a.m;
+    p.n = a.n;
+    p.k = a.k;
+    p.batch = a.batch;
+    p.num_kb = pl.num_kb;
+    p.tiles_m = 1;
+    p.tiles_n = pl.tiles_n;
+    p.split_k = pl.split;
+    p.kb_per_split = pl.kb_per;
+    p.total_units = pl.tiles_n * a.batch * pl.split;
+    p.group_m = 1;
+    p.sfa = o.sfa;
+    p.sfb = o.sfb;
+    p.sfa_batch_stride = o.sfa_bs;
+    p.sfb_batch_stride = o.sfb_bs;
+    p.sf_kb_total = (kg + 3) / 4;
+    p.sfb_row_blocks = (a.n + 127) / 128;
+    p.c = a.ptr_c;
+    p.ldc = a.stride_c;
+    p.c_batch_stride = a.stride_c_batch;
+    p.ws = pl.split > 1 ? o.partials : nullptr;
+    p.timeout_ns = kTimeoutNs;
+    const int grid = grid_for(p.total_units, dev, a.grid_blocks);
+    const bool f32 = a.out_dtype == BSG_OUT_FP32;
+    const int rc = o.fp4 ? mxs_launch<1>(pl.bn, o.bmode, f32, ta, tb, p, grid, st)
+                         : mxs_launch<0>(pl.bn, o.bmode, f32, ta, tb, p, grid, st);
+    if (rc != BSG_OK) return rc;
+    if (pl.split > 1) return splitk_reduce(p.ws, a, pl.split, dev.sms, st);
+    return BSG_OK;
+  }
+  if (a.kernel == BSG_KERNEL_SWAP) return BSG_ERR_UNSUPPORTED;
   if (mx_use_pair(a, pl, dev)) {
     if (pl.split > 1 || a.out_dtype != BSG_OUT_BF16) return BSG_ERR_UNSUPPORTED;
     if (!e8m0b && (o.sfa_bs % 512 || o.sfb_bs % 512)) return BSG_ERR_UNSUPPORTED;
@@ -728,7 +815,9 @@ int e8m0b_run(const bsgemm_args& in, bool bf16, int tiles, cudaStream_t st) {
   g.workspace = nullptr;
   g.workspace_bytes = 0;
   g.grid_blocks = 0;
-  g.kernel = tiles == 1 ? BSG_KERNEL_1CTA : BSG_KERNEL_AUTO;
+  // decode-sized M also takes the single-CTA kernel (its scale builder is
+  // the one that reads per-128 E8M0 bytes)
+  g.kernel = tiles == 1 || a.m <= 64 ? BSG_KERNEL_1CTA : BSG_KERNEL_AUTO;
   MxOperands o;
   o.bmode = bsg::kBShuffle16;
   o.sfmode = bsg::kSfE8m0Block128;
@@ -764,9 +853,6 @@ int fp8b_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockPa
   kern<<<grid, 256, Cfg::kSmemBytes, st>>>(ta, tb, p);
   return launch_status();
 }
-
-// Rows of A per transposed-kernel tile (the MMA's N side): 16, 32 or 64.
-int swap_mn(int m) { return m <= 16 ? 16 : m <= 32 ? 32 : 64; }
 
 bool fp8b_use_swap(const bsgemm_args& a) {
   return a.kernel == BSG_KERNEL_SWAP || (a.kernel == BSG_KERNEL_AUTO && a.m <= 64);

@@ -555,13 +555,25 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* __restr
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total4;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const long long e = i * 4;
-    float4 acc = reinterpret_cast<const float4*>(ws)[i];
-    for (int s = 1; s < split; ++s) {
-      const float4 v = reinterpret_cast<const float4*>(ws + s * slice)[i];
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
+    // up to 8 slices' loads in flight at once, summed in slice order
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int s0 = 0; s0 < split; s0 += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (s0 + j < split) v[j] = __ldcg(reinterpret_cast<const float4*>(ws + (s0 + j) * slice) + i);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (s0 + j >= split) break;
+        if (s0 + j == 0) {
+          acc = v[0];
+        } else {
+          acc.x += v[j].x;
+          acc.y += v[j].y;
+          acc.z += v[j].z;
+          acc.w += v[j].w;
+        }
+      }
     }
     const long long bb = e / per_batch;
     const long long rem = e - bb * per_batch;

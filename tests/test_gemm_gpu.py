@@ -216,6 +216,33 @@ def test_mxfp8_shuffled_b_in_place(bs, orc, cuda, kernel, out_dtype):
         assert_close(orc, ref, shuf.float().cpu().numpy(), mag, f"mxfp8 shuffled {kernel} {m}x{n}x{k}")
 
 
+# ---- transposed (swap-AB) MX decode kernel -------------------------------------------
+
+@pytest.mark.parametrize("m", [1, 16, 30, 64])
+def test_mxfp8_swap_decode(bs, orc, cuda, m):
+    run_mxfp8(bs, orc, cuda, m, 640, 1024, seed=80 + m, sf_mode="rowpattern", kernel="swap")
+
+
+def test_mxfp8_swap_variants(bs, orc, cuda):
+    """fp32 out, forced split-K, native scales, batch 2 through the swap kernel."""
+    run_mxfp8(bs, orc, cuda, 24, 520, 2048, seed=90, out_dtype=torch.float32, split_k=3, kernel="swap")
+    run_mxfp8(bs, orc, cuda, 40, 384, 512, seed=91, native=True, kernel="swap")
+    run_mxfp8(bs, orc, cuda, 8, 256, 1024, seed=92, batch=2, kernel="swap")
+
+
+@pytest.mark.parametrize("m", [1, 16, 64])
+def test_mxfp4_swap_decode_shuffled(bs, orc, cuda, m):
+    qa, qb, sa, sb = mxfp4_problem(orc, m, 768, 2048, 95 + m, "kpattern")
+    ref, mag = orc.gemm_mxfp4(qa, qb, sa, sb)
+    A, SA, SB = dev_u8(qa, cuda), dev_u8(sa, cuda), dev_u8(sb, cuda)
+    for b_format, Bh in (("raw", qb), ("shuffle16", orc.shuffle_weight16(qb))):
+        out = poisoned((m, 768), torch.bfloat16, cuda)
+        bs.gemm_a4w4_mxfp4(A, dev_u8(Bh, cuda), SA, SB, out=out, kernel="swap", b_format=b_format)
+        torch.cuda.synchronize()
+        assert bs.check_device_error() == 0
+        assert_close(orc, ref, out.float().cpu().numpy(), mag, f"mxfp4 swap {m} {b_format}")
+
+
 # ---- E8M0 1x128 / 128x128 block scale: the reference's launch_blockscale_bpreshuffle --
 
 def e8m0_block_problem(orc, m, n, k, seed):
