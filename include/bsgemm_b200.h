@@ -122,7 +122,7 @@ typedef struct bsgemm_args {
                                (the reference's PERSIST_GRID / m10 grid_blocks) */
     int kernel;             /* BSG_KERNEL_*: 0 = auto, 1 = single-CTA tiles,
                                2 = CTA-pair (cta_group::2) 256x256 tiles (MX),
-                               3 = transposed decode kernel (fp32 block scale, M <= 64) */
+                               3 = transposed decode kernel (M <= 64; MX: layout tn) */
 } bsgemm_args;
 
 enum { BSG_KERNEL_AUTO = 0, BSG_KERNEL_1CTA = 1, BSG_KERNEL_PAIR = 2, BSG_KERNEL_SWAP = 3 };
