@@ -442,10 +442,12 @@ def run_ours(args):
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
+    torch.cuda.nvtx.range_push(f"bsgemm {wl} timed x{args.steps}")   # one range per timed region
     for i in range(args.steps):
         starts[i].record(stream)
         call()
         ends[i].record(stream)
+    torch.cuda.nvtx.range_pop()
     t_end.record(stream)
     torch.cuda.synchronize()
     clk = clocks.stop()

@@ -82,3 +82,41 @@ def test_shard_bounds_cover_columns_once():
         assert np.all(cols == 1), (n, world, gran)
     with pytest.raises(ValueError):
         sh.shard_bounds(128, 2, 2)
+
+
+def _dead_peer_main(rank, port, result_path):
+    """Rank 1 leaves right after joining; rank 0's gather must fail with an
+    error (connection to the peer lost or the group timeout), not hang."""
+    import time
+    from datetime import timedelta
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD, timeout=timedelta(seconds=10))
+    if rank == 1:
+        os._exit(0)   # dies between steps, no collective in flight
+    sh = importlib.import_module("355_1_trans_b200.sharding")
+    time.sleep(1.0)
+    t0 = time.time()
+    try:
+        sh.allgather_columns(torch.zeros(4, 8))
+        outcome = "no error"
+    except Exception as e:   # noqa: BLE001 -- any collective failure is the expected outcome
+        outcome = f"error after {time.time() - t0:.1f}s: {type(e).__name__}"
+    with open(result_path, "w") as f:
+        f.write(outcome)
+    os._exit(0)
+
+
+@pytest.mark.timeout(180)
+def test_lost_rank_fails_fast(tmp_path):
+    result = tmp_path / "result.txt"
+    ctx = mp.start_processes(_dead_peer_main, args=(_free_port(), str(result)), nprocs=WORLD, join=False,
+                             start_method="spawn")
+    for p in ctx.processes:
+        p.join(120)
+    alive = [p for p in ctx.processes if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung"
+    text = result.read_text()
+    assert text.startswith("error after"), text
