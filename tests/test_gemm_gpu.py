@@ -448,7 +448,7 @@ def test_bounded_wait_reports_timeout(bs, cuda):
 
 @pytest.mark.parametrize("layout,kernel", [("tn", "auto"), ("nt", "auto"), ("tn", "1cta")])
 def test_mxfp8_8192_row_sample(bs, orc, cuda, layout, kernel):
-    """MXFP4 8192^3 at full size: every output row is produced by the GPU;
+    """MXFP8 8192^3 at full size: every output row is produced by the GPU;
     64 sampled rows are checked against the oracle."""
     m = n = k = 8192
     x = orc.normal((m, k), seed=81)
@@ -479,3 +479,68 @@ def test_mxfp4_8192_row_sample(bs, orc, cuda):
     got = out[torch.from_numpy(rows).to(cuda)].float().cpu().numpy()
     assert_close(orc, ref, got, mag, "mxfp4 8192^3 sample")
     assert not torch.isnan(out).any()
+
+
+def test_mxfp4_8192_shuffled_b_row_sample(bs, orc, cuda):
+    """The benchmark configuration: MXFP4 8192^3 with B in shuffle_weight(16,16)
+    read in place, native scales, CTA pairs."""
+    m = n = k = 8192
+    qa, qb, sa, sb = mxfp4_problem(orc, m, n, k, 12)
+    SA = bs.pack_scales(dev_u8(sa, cuda))
+    SB = bs.pack_scales(dev_u8(sb, cuda))
+    out = bs.gemm_a4w4_mxfp4(dev_u8(qa, cuda), dev_u8(orc.shuffle_weight16(qb), cuda), SA, SB,
+                             scale_format="native", b_format="shuffle16")
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    rows = np.random.default_rng(2).choice(m, 64, replace=False)
+    rows.sort()
+    ref, mag = orc.gemm_mxfp4(qa[rows], qb, sa[rows], sb)
+    got = out[torch.from_numpy(rows).to(cuda)].float().cpu().numpy()
+    assert_close(orc, ref, got, mag, "mxfp4 8192^3 shuffled sample")
+    assert not torch.isnan(out).any()
+
+
+def test_e8m0_block_8192_row_sample(bs, orc, cuda):
+    """launch_blockscale_bpreshuffle at 8192^3 (CTA pairs, scale builders):
+    64 sampled rows against the oracle under the reference's valid_vector rule."""
+    m = n = k = 8192
+    qa, qb, sfa_t, sfb = e8m0_block_problem(orc, m, n, k, 13)
+    A = dev_u8(qa, cuda).view(torch.float8_e4m3fn)
+    B = dev_u8(orc.shuffle_weight16(qb), cuda).view(torch.float8_e4m3fn)
+    out = bs.gemm_a8w8_blockscale_bpreshuffle(A, B, dev_u8(sfa_t, cuda).t(), dev_u8(sfb, cuda))
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    rows = np.random.default_rng(3).choice(m, 64, replace=False)
+    rows.sort()
+    ref, mag = orc.gemm_e8m0_block(qa[rows], qb, np.ascontiguousarray(sfa_t[:, rows]), sfb)
+    got = out[torch.from_numpy(rows).to(cuda)].float().cpu().numpy()
+    errors, ratio = orc.check_e8m0_rule(ref, got, mag, bf16=True)
+    assert errors == 0, f"{errors} errors, max ratio {ratio}"
+    assert_close(orc, ref, got, mag, "e8m0 block 8192^3 sample")
+
+
+def test_fp8_block_largest_sweep_shape_row_sample(bs, orc, cuda):
+    """The largest fp32 block-scale sweep shape, M=8192 N=7168 K=18432, K-panel B:
+    32 sampled rows against the oracle."""
+    m, n, k = 8192, 7168, 18432
+    x = orc.normal((m, k), seed=14)
+    w = orc.normal((n, k), seed=15)
+    qa, sa = orc.quant_fp8_block(x, 1)
+    qb, sb = orc.quant_fp8_block(w, 128)
+    A = dev_u8(qa, cuda).view(torch.float8_e4m3fn)
+    B = dev_u8(orc.shuffle_kpanel(qb), cuda).view(torch.float8_e4m3fn)
+    out = bs.gemm_a8w8_bpreshuffle(A, B, torch.from_numpy(sa).to(cuda), torch.from_numpy(sb).to(cuda))
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    rows = np.random.default_rng(4).choice(m, 32, replace=False)
+    rows.sort()
+    ref, mag = orc.gemm_fp8_block(qa[rows], qb, sa[rows], sb)
+    got = out[torch.from_numpy(rows).to(cuda)].float().cpu().numpy()
+    assert_close(orc, ref, got, mag, "fp8 block 8192x7168x18432 sample")
+    assert not torch.isnan(out).any()
+
+
+def test_fp8_block_decode_full_shape(bs, orc, cuda):
+    """Decode at full size, M=16 N=7168 K=18432 (transposed kernel, auto split-K),
+    every element checked."""
+    run_fp8_block(bs, orc, cuda, 16, 7168, 18432, seed=16)
