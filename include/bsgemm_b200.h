@@ -64,7 +64,7 @@ enum { BSG_LAYOUT_NT = 0, BSG_LAYOUT_TT = 1, BSG_LAYOUT_NN = 2, BSG_LAYOUT_TN = 
 enum {
     BSG_B_RAW = 0,          /* plain [N,K] (K-major) or [K,N] (N-major) */
     BSG_B_KPANEL128 = 1,    /* B'[K/128][N][128] (reference shuffle_b) */
-    BSG_B_SHUFFLE16 = 2     /* aiter shuffle_weight(16,16): needs bsgemm_pack_b first */
+    BSG_B_SHUFFLE16 = 2     /* aiter shuffle_weight(16,16) [N/16][Kb/16][16][16], read in place */
 };
 
 enum {
@@ -133,9 +133,11 @@ BSG_API void bsgemm_args_init(bsgemm_args *args);
 /*
  * MXFP8: C[b,m,n] = sum_g 2^(sfa[m,g]-127) 2^(sfb[n,g]-127) sum_{k in g} A*B,
  * g = 32 consecutive K.  A/B E4M3FN bytes in any of the four layouts
- * (args->layout); SFA/SFB in BSG_SF_NATIVE or BSG_SF_ROWMAJOR ([rows,K/32]
- * bytes, row stride stride_sf*).  Requires K % 128 == 0, N % 8 == 0 (bf16) or
- * N % 4 == 0 (fp32); M arbitrary.
+ * (args->layout); B also as BSG_B_SHUFFLE16 (K-major layouts, read in place);
+ * SFA/SFB in BSG_SF_NATIVE or BSG_SF_ROWMAJOR ([rows,K/32] bytes, row stride
+ * stride_sf*).  Requires K % 128 == 0, N % 8 == 0 (bf16) or N % 4 == 0 (fp32);
+ * M arbitrary.  kernel: AUTO (M <= 64 tn -> transposed decode kernel; large
+ * bf16 problems -> CTA pairs; else single-CTA tiles), 1CTA, PAIR or SWAP.
  * Replaces the launch of gemm_a8w8_mxfp8_kernel in
  * mxfp8_gemm/gemm_a8w8_mxfp8_host.cc:287-295 (its kargs at :265-285), without
  * the reference's K == 256 and M/N % 256 limits.
@@ -145,8 +147,9 @@ BSG_API int bsgemm_a8w8_mxfp8(const bsgemm_args *args, bsg_stream_t stream);
 /*
  * MXFP4: same contraction with E2M1 elements packed two per byte, even k in
  * the low nibble; A [M,K/2] and B [N,K/2] bytes, K-major only (layout TN).
- * B may be BSG_B_RAW or, after bsgemm_pack_b, the raw form of an aiter
- * shuffle_weight(16,16) buffer.  Requires K % 128 == 0.
+ * B may be BSG_B_RAW or BSG_B_SHUFFLE16 (aiter shuffle_weight(16,16) bytes,
+ * stride_b = K/2, read in place).  Requires K % 256 == 0.  kernel: AUTO,
+ * 1CTA, PAIR, or SWAP (transposed decode kernel, M <= 64).
  * Replaces gemm_a4w4_mxfp4_4wave_kernel's launch in
  * mxfp4_gemm_4wave_20261112/gemm_a4w4_mxfp4_4wave_host.cc:211-213 and the
  * persistent launch of candidate_m10/gemm_a4w4_mxfp4_4wave_host.cc:242-250.
@@ -173,7 +176,9 @@ BSG_API int bsgemm_a8w8_blockscale_bpreshuffle(const bsgemm_args *args, bsg_stre
 BSG_API size_t bsgemm_workspace_size(int family, const bsgemm_args *args);
 
 /*
- * Device repack of B into the raw layout the kernels read (async on stream).
+ * Device repack of B between a reference preshuffle and the raw layout
+ * (async on stream).  The GEMMs read BSG_B_SHUFFLE16 and BSG_B_KPANEL128 in
+ * place; this converts weights for other consumers, or raw -> preshuffled.
  *   src_format BSG_B_KPANEL128 or BSG_B_SHUFFLE16; dst is [rows, kbytes] bytes
  *   (kbytes = K for fp8, K/2 for fp4).  rows % 16 == 0 and kbytes % 16 == 0
  *   for SHUFFLE16; kbytes % 128 == 0 for KPANEL128.  unpack = 1 runs the
