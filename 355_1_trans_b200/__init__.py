@@ -187,6 +187,16 @@ def gemm_a4w4_mxfp4(A, B, A_scale, B_scale, *, out_dtype=torch.bfloat16, out=Non
 _B_FORMATS = {"raw": B_RAW, "shuffle16": B_SHUFFLE16}
 
 
+def _tuned(family: str, m: int, n: int, k: int, kernel: str, split_k: int):
+    """(kernel, split_k) from the installed tuned table for "auto" calls."""
+    if kernel != "auto" or split_k != 0:
+        return kernel, split_k
+    from . import tuning
+    table = tuning.active()
+    sel = table.lookup(family, m, n, k) if table is not None else None
+    return sel if sel is not None else (kernel, split_k)
+
+
 def _mx(A, B, A_scale, B_scale, *, fp4, layout, out_dtype, out, scale_format, split_k,
         workspace, grid_blocks, kernel="auto", b_format="raw"):
     if layout not in LAYOUTS:
@@ -225,6 +235,7 @@ def _mx(A, B, A_scale, B_scale, *, fp4, layout, out_dtype, out, scale_format, sp
         if t.stride(-1) != 1:
             raise ValueError("A and B must have unit stride in the last dimension")
     out = _out(out, m, n, out_dtype, A.device, batch)
+    kernel, split_k = _tuned("mxfp4" if fp4 else "mxfp8", m, n, k, kernel, split_k)
     args = Args()
     lib().bsgemm_args_init(ctypes.byref(args))
     args.ptr_a, args.ptr_b, args.ptr_c = A.data_ptr(), B.data_ptr(), out.data_ptr()
@@ -322,6 +333,7 @@ def gemm_a8w8_bpreshuffle(A, B, x_scale, w_scale, out_dtype=torch.bfloat16, *,
     if tuple(w_scale.shape) != ((n + 127) // 128, kblk) or w_scale.stride(1) != 1:
         raise ValueError("w_scale must be [N/128, K/128]")
     out = _out(out, m, n, out_dtype, A.device, 1)
+    kernel, split_k = _tuned("fp8_block", m, n, k, kernel, split_k)
     args = Args()
     lib().bsgemm_args_init(ctypes.byref(args))
     args.ptr_a, args.ptr_b, args.ptr_c = A.data_ptr(), B.data_ptr(), out.data_ptr()

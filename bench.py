@@ -86,6 +86,11 @@ def parse():
                          "would take as abbreviations of its options")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tune", default=None, metavar="CSV",
+                    help="tune kernel / split-K per shape (fp8 block-scale sweep shapes and skinny MX "
+                         "shapes) and write the tuned table (aiter CSV schema) to CSV")
+    ap.add_argument("--tuned", default=None, metavar="CSV",
+                    help="use a tuned table for the library's auto calls (--sweep)")
     ap.add_argument("--quant", action="store_true",
                     help="activation quantise+pack bandwidth (bf16 -> mxfp8/mxfp4/fp8_block), one JSON line")
     ap.add_argument("--sweep", action="store_true",
@@ -736,10 +741,60 @@ def run_quant(args):
     return 0
 
 
+def run_tune(args):
+    """Tuned table for the fp8 block-scale sweep shapes (M <= 8192 of the
+    decode/prefill grid) and the skinny MX shapes M in {1, 16, 64, 128, 1024},
+    N = K = 8192; written in the aiter tuned-CSV schema."""
+    import torch
+    dev = torch.device("cuda", 0)
+    bs = importlib.import_module("355_1_trans_b200")
+    tuning = importlib.import_module("355_1_trans_b200.tuning")
+    rows = []
+    for (n, k) in ((7168, 2048), (4096, 7168), (24576, 1536), (7168, 18432)):
+        qa_full, qb, sa_full, sb = make_fp8block_inputs(8192, n, k, dev, 7)
+
+        def make_call(m, n_, k_, kernel, split):
+            qa, sa = qa_full[:m].contiguous(), sa_full[:m].contiguous()
+            out = torch.empty(m, n_, dtype=torch.bfloat16, device=dev)
+            return lambda: bs.gemm_a8w8_bpreshuffle(qa, qb, sa, sb, torch.bfloat16, preshuffled=True, out=out,
+                                                    kernel=kernel, split_k=split)
+
+        rows += tuning.tune("fp8_block", [(m, n, k) for m in (1, 16, 64, 128, 1024)], make_call)
+    for fp4 in (False, True):
+        n = k = 8192
+        qa_full, qb, sa_full, sb = make_mx_inputs(bs, 1024, n, k, fp4, "tn", dev, 3)
+        sb_n = bs.pack_scales(sb)
+        if fp4:
+            qb = bs.pack_b(qb.view(torch.uint8), "shuffle16", unpack=True)
+
+        def make_call(m, n_, k_, kernel, split, fp4=fp4, qa_full=qa_full, sa_full=sa_full, qb=qb, sb_n=sb_n):
+            qa = qa_full[:m].contiguous()
+            sa_n = bs.pack_scales(sa_full[:m].contiguous())
+            out = torch.empty(m, n_, dtype=torch.bfloat16, device=dev)
+            if fp4:
+                return lambda: bs.gemm_a4w4_mxfp4(qa, qb, sa_n, sb_n, out=out, scale_format="native",
+                                                  b_format="shuffle16", kernel=kernel, split_k=split)
+            return lambda: bs.gemm_a8w8_mxfp8(qa, qb, sa_n, sb_n, out=out, scale_format="native",
+                                              kernel=kernel, split_k=split)
+
+        rows += tuning.tune("mxfp4" if fp4 else "mxfp8", [(m, n, k) for m in (1, 16, 64, 128, 1024)], make_call)
+    with open(args.tune, "w", newline="", encoding="utf-8") as f:
+        import csv
+        w = csv.DictWriter(f, fieldnames=tuning.TUNED_HEADER)
+        w.writeheader()
+        w.writerows(rows)
+    print(json.dumps({"tuned_rows": len(rows), "csv": args.tune}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.tuned:
+        importlib.import_module("355_1_trans_b200.tuning").use_tuned(args.tuned)
     if args.impl == "reference":
         return run_reference(args)
+    if args.tune:
+        return run_tune(args)
     if args.sweep:
         return run_sweep(args)
     if args.quant:

@@ -113,3 +113,36 @@ def test_launch_blockscale_bpreshuffle_validation(bs):
     assert fn(ctypes.byref(c), 0, 0, None) == INVALID
     d = _opus_kargs(bs, m=1 << 16, n=1 << 16, k=1 << 16)       # int32 element-count overflow
     assert fn(ctypes.byref(d), 1, 0, None) == INVALID
+
+
+def test_tuned_table_lookup(tmp_path):
+    """aiter-schema tuned CSV: exact M, next bucket up, largest for big M,
+    None for an untuned (N, K)."""
+    import importlib
+    tuning = importlib.import_module("355_1_trans_b200.tuning")
+    path = tmp_path / "t.csv"
+    rows = []
+    for m, solidx, split in ((1, 3, 8), (16, 3, 4), (128, 1, 2), (1024, 1, 1)):
+        r = {c: "" for c in tuning.TUNED_HEADER}
+        r.update({"gfx": "sm_100a", "cu_num": 148, "M": m, "N": 7168, "K": 2048, "dtype": "fp8_block",
+                  "solidx": solidx, "splitK": split})
+        rows.append(r)
+    import csv
+    with open(path, "w", newline="") as f:
+        w = csv.DictWriter(f, fieldnames=tuning.TUNED_HEADER)
+        w.writeheader()
+        w.writerows(rows)
+    t = tuning.TunedTable.load(path)
+    assert t.lookup("fp8_block", 16, 7168, 2048) == ("swap", 4)
+    assert t.lookup("fp8_block", 17, 7168, 2048) == ("1cta", 2)
+    assert t.lookup("fp8_block", 5000, 7168, 2048) == ("1cta", 1)
+    assert t.lookup("fp8_block", 16, 4096, 2048) is None
+    assert t.lookup("mxfp8", 16, 7168, 2048) is None
+
+
+def test_shipped_tuned_table_loads():
+    import importlib
+    tuning = importlib.import_module("355_1_trans_b200.tuning")
+    t = tuning.TunedTable.load(tuning.DEFAULT_TABLE)
+    sel = t.lookup("fp8_block", 16, 7168, 18432)
+    assert sel is not None and sel[0] in tuning.KERNEL_NAMES.values()
