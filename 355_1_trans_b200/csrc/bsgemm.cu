@@ -145,13 +145,41 @@ bool overlaps(const void* a, uint64_t a_bytes, const void* b, uint64_t b_bytes) 
 // reference-compatible entry point returns CUDA error codes).
 thread_local cudaError_t t_last_cuda_error = cudaSuccess;
 
+// Dynamic shared memory opt-in of a kernel, set once per (kernel, device):
+// the attribute persists, so a launch that needs no more than the largest
+// value already set skips the driver call.  Keyed on the kernel's address,
+// since kernels of one signature share a template instantiation here.
+struct SmemOptIn {
+  const void* fn;
+  int dev;
+  uint32_t bytes;
+};
+
 template <typename K>
 int set_smem(K kernel, uint32_t bytes) {
+  static std::mutex mu;
+  static SmemOptIn done[256];
+  static int count = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return BSG_ERR_CUDA;
+  const void* fn = reinterpret_cast<const void*>(kernel);
+  std::lock_guard<std::mutex> lock(mu);
+  int slot = -1;
+  for (int i = 0; i < count; ++i)
+    if (done[i].fn == fn && done[i].dev == dev) slot = i;
+  if (slot >= 0 && done[slot].bytes >= bytes) return BSG_OK;
   const cudaError_t e =
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
-  if (e == cudaSuccess) return BSG_OK;
-  t_last_cuda_error = e;
-  return BSG_ERR_CUDA;
+  if (e != cudaSuccess) {
+    t_last_cuda_error = e;
+    return BSG_ERR_CUDA;
+  }
+  if (slot >= 0) {
+    done[slot].bytes = bytes;
+  } else if (count < 256) {
+    done[count++] = SmemOptIn{fn, dev, bytes};
+  }
+  return BSG_OK;
 }
 
 int launch_status() {
