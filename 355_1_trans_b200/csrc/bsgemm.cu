@@ -182,6 +182,31 @@ int set_smem(K kernel, uint32_t bytes) {
   return BSG_OK;
 }
 
+// Launch with programmatic stream serialization: the grid may launch while
+// the previous kernel on the stream drains, so its prologue (barriers, TMEM,
+// tensor-map prefetch, L2 prefetch of weights) overlaps that kernel.  Every
+// GEMM kernel of this library runs griddepcontrol.wait before it reads or
+// writes global memory that an earlier kernel may still own.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), int grid, int block, uint32_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(static_cast<unsigned>(block));
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+  if (e != cudaSuccess) {
+    t_last_cuda_error = e;
+    return BSG_ERR_CUDA;
+  }
+  return BSG_OK;
+}
+
 int launch_status() {
   const cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) return BSG_OK;
@@ -317,8 +342,8 @@ int mx_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p,
   using Cfg = MxCfg<BN, kFp4>;
   auto* kern = bsg::mx_gemm_kernel<BN, kFp4, kAMN, kBMode, kOutF32, kSfMode>;
   if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
-  kern<<<grid, bsg::kMxThreads, Cfg::kSmemBytes, st>>>(ta, tb, p);
-  return launch_status();
+  const int rc = launch_pdl(kern, grid, bsg::kMxThreads, Cfg::kSmemBytes, st, ta, tb, p);
+  return rc != BSG_OK ? rc : launch_status();
 }
 
 template <int BN, int kFp4, bool kAMN, int kBMode>
@@ -371,8 +396,8 @@ int mx2_launch_t(const Mx2Maps& t, const bsg::Mx2Params& p, int grid, cudaStream
   using Cfg = bsg::Mx2Cfg<kFp4>;
   auto* kern = bsg::mx_gemm_2sm_kernel<kFp4, kAMN, kBMode, kSfMode>;
   if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
-  kern<<<grid, bsg::kMxThreads, Cfg::kSmemBytes, st>>>(t.a, t.b, t.sfa, t.sfb, t.c, p);
-  return launch_status();
+  const int rc = launch_pdl(kern, grid, bsg::kMxThreads, Cfg::kSmemBytes, st, t.a, t.b, t.sfa, t.sfb, t.c, p);
+  return rc != BSG_OK ? rc : launch_status();
 }
 
 int mx2_launch(bool fp4, bool amn, int bmode, int sfmode, const Mx2Maps& t, const bsg::Mx2Params& p, int grid,
@@ -497,8 +522,8 @@ int mxs_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p
   using Cfg = bsg::MxSwapCfg<MN, kFp4>;
   auto* kern = bsg::mx_gemm_swap_kernel<MN, kFp4, kBMode, kOutF32>;
   if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
-  kern<<<grid, 256, Cfg::kSmemBytes, st>>>(ta, tb, p);
-  return launch_status();
+  const int rc = launch_pdl(kern, grid, 256, Cfg::kSmemBytes, st, ta, tb, p);
+  return rc != BSG_OK ? rc : launch_status();
 }
 
 template <int MN, int kFp4>
@@ -881,8 +906,8 @@ int fp8b_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockPa
   using Cfg = Fp8BlockCfg<128>;
   auto* kern = bsg::fp8_block_gemm_kernel<128, kBFmt, kOutF32>;
   if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
-  kern<<<grid, 256, Cfg::kSmemBytes, st>>>(ta, tb, p);
-  return launch_status();
+  const int rc = launch_pdl(kern, grid, 256, Cfg::kSmemBytes, st, ta, tb, p);
+  return rc != BSG_OK ? rc : launch_status();
 }
 
 bool fp8b_use_swap(const bsgemm_args& a) {
@@ -910,8 +935,8 @@ int swap_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockPa
   using Cfg = bsg::SwapCfg<MN>;
   auto* kern = bsg::fp8_block_swap_kernel<MN, kBFmt, kOutF32>;
   if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
-  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(ta, tb, p);
-  return launch_status();
+  const int rc = launch_pdl(kern, grid, Cfg::kThreads, Cfg::kSmemBytes, st, ta, tb, p);
+  return rc != BSG_OK ? rc : launch_status();
 }
 
 template <int kBFmt>

@@ -126,6 +126,10 @@ __global__ void __launch_bounds__(256, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   if (threadIdx.x == 0) griddep_launch_dependents();   // a split-K reduce may launch now
+  // Launched with programmatic dependent launch, the prologue above overlaps
+  // the previous kernel on the stream; nothing of global memory is touched
+  // before that kernel has completed.
+  griddep_wait();
 
   if (warp == 0) {
     // producer warp: all lanes run the loop, the elected lane issues the copies
@@ -175,8 +179,12 @@ __global__ void __launch_bounds__(256, 1)
     // MMA warp: all lanes run the loop, the elected lane issues
     const bool issuer = elect_one();
     // ------------------------------------------------------------------ MMA issuer
+    // The descriptors of stage 0 are built once; a stage's are a constant
+    // offset from them, so the issue path between two MMAs stays a few adds.
     const uint32_t idesc = idesc_f8f6f4(false, false, 128, BN);
-    const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
+    const uint64_t adesc0 = make_sdesc(smem_u32(sA), 16u, 1024u, kLayoutSW128);
+    const uint64_t bdesc0 = weight_sdesc<kBFmt>(smem_u32(sB), 0);
+    constexpr uint64_t kBStep = (kBFmt == kFmtShuffle16 ? 256u : 32u) >> 4;   // one K step, 16-byte units
     int stage = 0;
     uint32_t phase = 0;
     uint32_t kbi = 0;   // K blocks issued by this CTA, selects the TMEM buffer
@@ -198,16 +206,15 @@ __global__ void __launch_bounds__(256, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t a_addr = sA0 + stage * Cfg::kABytes;
-        const uint32_t b_addr = sB0 + stage * Cfg::kBBytes;
-        const uint32_t d = tmem_base + buf * BN;
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const uint64_t adesc = make_sdesc(a_addr + 32u * t, 16u, 1024u, kLayoutSW128);
-          const uint64_t bdesc = weight_sdesc<kBFmt>(b_addr, t);
-          if (issuer) umma_f8f6f4(d, adesc, bdesc, idesc, t > 0 ? 1u : 0u);
-        }
         if (issuer) {
+          const uint32_t ust = static_cast<uint32_t>(stage);
+          const uint64_t ad = adesc0 + static_cast<uint64_t>(ust * (Cfg::kABytes >> 4));
+          const uint64_t bd = bdesc0 + static_cast<uint64_t>(ust * (Cfg::kBBytes >> 4));
+          const uint32_t d = tmem_base + buf * BN;
+          umma_f8f6f4(d, ad, bd, idesc, 0u);
+          umma_f8f6f4(d, ad + 2u, bd + kBStep, idesc, 1u);
+          umma_f8f6f4(d, ad + 4u, bd + 2u * kBStep, idesc, 1u);
+          umma_f8f6f4(d, ad + 6u, bd + 3u * kBStep, idesc, 1u);
           tc_commit(&empty_bar[stage]);
           tc_commit(&acc_full[buf]);
         }

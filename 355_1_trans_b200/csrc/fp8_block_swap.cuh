@@ -19,6 +19,9 @@
 // copies into a ring of kStages + kAccBufs slots -- as many K blocks as can be
 // between the producer and the promotion -- so neither the producer nor the
 // promotion ever waits on a global scale load.
+//
+// Roles: warps 0, 2 and 3 TMA producers (every third K block each, with its
+// scales), warp 1 MMA, warp 2 also allocates TMEM, warps 4.. promotion.
 #pragma once
 
 #include "fp8_block_gemm.cuh"
@@ -36,6 +39,55 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         "=r"(r[14]), "=r"(r[15])
       : "r"(taddr)
       : "memory");
+}
+
+constexpr uint32_t kSwapProducers = 3;   // TMA producer warps 0, 2 and 3
+
+// L2 prefetch of the weight tile (N tile nt, K block kb, batch b) in each B layout.
+template <int kBFmt>
+__device__ __forceinline__ void prefetch_weight_tile(const CUtensorMap* tmB, int nt, int kb, int b) {
+  if constexpr (kBFmt == kFmtKPanel)
+    tma_prefetch_4d(tmB, 0, nt * 128, kb, b);
+  else if constexpr (kBFmt == kFmtShuffle16)
+    tma_prefetch_5d(tmB, 0, kb * 8, 0, nt * 8, b);
+  else
+    tma_prefetch_3d(tmB, kb * 128, nt * 128, b);
+}
+
+// tcgen05.ld of 32 lanes x 16 columns without the wait: the registers hold
+// the data only after tmem_wait_ld16 (or, for a later group, after
+// tmem_reg_fence16 placed behind that wait).
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32"
+      " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+// Wait for this thread's TMEM loads.  The "+r" operands make every use of r
+// depend on the wait, so the compiler cannot hoist a use above it.
+__device__ __forceinline__ void tmem_wait_ld16(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]),
+                 "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+
+// Ties the uses of r to a position after an earlier tmem_wait_ld16 (volatile
+// asm statements keep their program order).
+__device__ __forceinline__ void tmem_reg_fence16(uint32_t (&r)[16]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]),
+                 "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
 }
 
 template <int MN>
@@ -57,7 +109,10 @@ struct SwapCfg {
   static constexpr uint32_t kTmemCols = static_cast<uint32_t>(kAccBufs * MN) < 32 ? 32u
                                         : static_cast<uint32_t>(kAccBufs * MN);
   static constexpr uint32_t kOffX = kWBytes * kStages;
-  static constexpr int kScaleSlots = kStages + kAccBufs;
+  // scale ring: at least kStages + kAccBufs slots (the K blocks that can sit
+  // between the producer and the promotion), a power of two so that the slot
+  // and parity of a K block are a mask and a shift
+  static constexpr int kScaleSlots = 32;
   static constexpr uint32_t kScaleSlot = static_cast<uint32_t>(MN + 4);   // floats: MN sfa, 1 sfb
   static constexpr uint32_t kOffScale = kOffX + kXBytes * kStages;
   static constexpr uint32_t kScaleBytes = static_cast<uint32_t>(kScaleSlots) * kScaleSlot * 4u;
@@ -65,6 +120,7 @@ struct SwapCfg {
   static constexpr uint32_t kSmemBytes = kOffBar + 1024u + 1024u;
   static_assert(8u * (2u * kStages + 2u * kAccBufs + 2u * kScaleSlots + 1u) + 8u <= 1024u, "barrier area");
   static_assert(kSmemBytes <= 227u * 1024u, "shared memory");
+  static_assert(kScaleSlots >= kStages + kAccBufs, "scale ring shorter than the pipeline");
 };
 
 template <int MN, int kBFmt, bool kOutF32>
@@ -126,8 +182,13 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
   if (threadIdx.x == 0) griddep_launch_dependents();   // a split-K reduce may launch now
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+  if (warp == 0 || warp == 2 || warp == 3) {
+    // ------------------------------------------------------------------ TMA producers
+    // Three warps take every third K block each.  One warp's issue chain per
+    // K block (two barrier waits, the scale copies, two TMA issues) lasts
+    // ~600 cycles, which alone would cap the weight stream at ~28 B/clk per
+    // SM; three chains in flight keep a CTA near the TMA rate.
+    const uint32_t pidx = warp == 0 ? 0u : static_cast<uint32_t>(warp - 1);
     const bool issuer = elect_one();
     const uint64_t pol_w = l2_policy_evict_first();   // weights stream through once
     const uint64_t pol_x = l2_policy_evict_last();    // activations are reread by every tile
@@ -135,6 +196,21 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
     uint32_t phase = 0;
     uint32_t kbi = 0;
     bool ok = true;
+    int last_stage = -1;
+    uint32_t last_phase = 0;
+    // The weights do not come from the previous kernel on the stream: pull
+    // this warp's share of the first unit's first S K blocks into L2, then
+    // wait for that kernel (programmatic dependent launch) before anything is
+    // read into shared memory.
+    if (issuer && static_cast<int>(blockIdx.x) < p.total_units) {
+      int b, mt, nt, s;
+      decode_unit(blockIdx.x, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+      const int kb0 = s * p.kb_per_split;
+      const int kb1 = min(kb0 + min(p.kb_per_split, S), p.num_kb);
+      for (int kb = kb0 + static_cast<int>(pidx); kb < kb1; kb += static_cast<int>(kSwapProducers))
+        prefetch_weight_tile<kBFmt>(&tmB, nt, kb, b);
+    }
+    griddep_wait();
     for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
       int b, mt, nt, s;
       decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
@@ -145,6 +221,13 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
       const float* sfa_t = p.sfa + b * p.sfa_batch + static_cast<long long>(m0) * p.sfa_m;
       const float* sfb_blk = p.sfb + b * p.sfb_batch + static_cast<long long>(nt) * p.sfb_n;
       for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
+        if (kbi % kSwapProducers != pidx) {
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          continue;
+        }
         if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
           ok = false;
           break;
@@ -175,17 +258,29 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
           tma_load_3d_hint(sX + stage * Cfg::kXBytes, &tmA, fb, kb * 128, mt * MN, b, pol_x);
         }
         __syncwarp();
+        last_stage = stage;
+        last_phase = phase;
         if (++stage == S) {
           stage = 0;
           phase ^= 1u;
         }
       }
     }
+    if (!ok && last_stage >= 0) {   // let this warp's last copies land before the CTA exits
+      int dummy = 0;
+      mbar_wait(&full_bar[last_stage], last_phase, &dummy, p.timeout_ns);
+    }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
+    // An M=128 N<=64 MMA occupies the tensor pipe for well under 100 cycles,
+    // so the instructions between two MMAs set the pace: the descriptors of
+    // stage 0 are built once, a stage's are a constant offset from them, and
+    // the four K steps of a K block are one branch of immediate adds.
     const bool issuer = elect_one();
     const uint32_t idesc = idesc_f8f6f4(false, false, 128, MN);
-    const uint32_t sW0 = smem_u32(sW), sX0 = smem_u32(sX);
+    const uint64_t wdesc0 = weight_sdesc<kBFmt>(smem_u32(sW), 0);
+    const uint64_t xdesc0 = make_sdesc(smem_u32(sX), 16u, 1024u, kLayoutSW128);
+    constexpr uint64_t kWStep = (kBFmt == kFmtShuffle16 ? 256u : 32u) >> 4;   // one K step, 16-byte units
     int stage = 0;
     uint32_t phase = 0;
     uint32_t kbi = 0;
@@ -197,26 +292,20 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
       const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
       for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
         const uint32_t buf = kbi % NB;
-        const uint32_t use = kbi / NB;
-        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, abort_flag, p.timeout_ns)) {
-          ok = false;
-          break;
-        }
-        if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) {
+        if (!mbar_wait(&acc_empty[buf], ((kbi / NB) & 1u) ^ 1u, abort_flag, p.timeout_ns) ||
+            !mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t w_addr = sW0 + stage * Cfg::kWBytes;
-        const uint32_t x_addr = sX0 + stage * Cfg::kXBytes;
-        const uint32_t d = tmem_base + buf * MN;
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const uint64_t adesc = weight_sdesc<kBFmt>(w_addr, t);
-          const uint64_t bdesc = make_sdesc(x_addr + 32u * t, 16u, 1024u, kLayoutSW128);
-          if (issuer) umma_f8f6f4(d, adesc, bdesc, idesc, t > 0 ? 1u : 0u);
-        }
         if (issuer) {
+          const uint64_t wd = wdesc0 + static_cast<uint64_t>(static_cast<uint32_t>(stage) * (Cfg::kWBytes >> 4));
+          const uint64_t xd = xdesc0 + static_cast<uint64_t>(static_cast<uint32_t>(stage) * (Cfg::kXBytes >> 4));
+          const uint32_t d = tmem_base + buf * MN;
+          umma_f8f6f4(d, wd, xd, idesc, 0u);
+          umma_f8f6f4(d, wd + kWStep, xd + 2u, idesc, 1u);
+          umma_f8f6f4(d, wd + 2u * kWStep, xd + 4u, idesc, 1u);
+          umma_f8f6f4(d, wd + 3u * kWStep, xd + 6u, idesc, 1u);
           tc_commit(&empty_bar[stage]);
           tc_commit(&acc_full[buf]);
         }
@@ -240,6 +329,7 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     uint32_t kbi = 0;
     bool ok = true;
+    griddep_wait();   // C and the split-K partials may still be read by the previous kernel
     for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
       int b, mt, nt, s;
       decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
@@ -251,43 +341,38 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
       float acc[HC];
 #pragma unroll
       for (int i = 0; i < HC; ++i) acc[i] = 0.0f;
+      constexpr int CH = HC / 16;   // 16-column TMEM loads per K block
       for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
         const uint32_t buf = kbi % NB;
-        const uint32_t use = kbi / NB;
         const uint32_t sl = kbi % R;
-        if (!mbar_wait(&scale_full[sl], (kbi / R) & 1u, abort_flag, p.timeout_ns) ||
-            !mbar_wait(&acc_full[buf], use & 1u, abort_flag, p.timeout_ns)) {
+        if (!mbar_wait(&acc_full[buf], (kbi / NB) & 1u, abort_flag, p.timeout_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        // the partial's TMEM loads are in flight while this K block's scales
+        // are checked (they landed long before the MMA ran)
+        uint32_t r[CH][16];
+        const uint32_t taddr = tmem_base + lane_base + buf * MN + static_cast<uint32_t>(c0);
+#pragma unroll
+        for (int c = 0; c < CH; ++c) tmem_ld16_async(taddr + static_cast<uint32_t>(c * 16), r[c]);
+        const bool sc_ok = mbar_wait(&scale_full[sl], (kbi / R) & 1u, abort_flag, p.timeout_ns);
+        tmem_wait_ld16(r[0]);
+#pragma unroll
+        for (int c = 1; c < CH; ++c) tmem_reg_fence16(r[c]);
+        if (!sc_ok) {
+          ok = false;
+          break;
+        }
         const float* slot = sScale + sl * Cfg::kScaleSlot;
         const float sb = slot[MN];
-        const uint32_t taddr = tmem_base + lane_base + buf * MN + static_cast<uint32_t>(c0);
-        // 32 (or 16) columns per TMEM load: the load, the combined scales, the FMAs
-        if constexpr (HC % 32 == 0) {
 #pragma unroll
-          for (int c = 0; c < HC / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(taddr + static_cast<uint32_t>(c * 32), r);
+        for (int c = 0; c < CH; ++c) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int row = c0 + c * 32 + i;
-              const float comb = row < rows ? sb * slot[row] : 0.0f;
-              acc[c * 32 + i] = fmaf(__uint_as_float(r[i]), comb, acc[c * 32 + i]);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < HC / 16; ++c) {
-            uint32_t r[16];
-            tmem_ld16(taddr + static_cast<uint32_t>(c * 16), r);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int row = c0 + c * 16 + i;
-              const float comb = row < rows ? sb * slot[row] : 0.0f;
-              acc[c * 16 + i] = fmaf(__uint_as_float(r[i]), comb, acc[c * 16 + i]);
-            }
+          for (int i = 0; i < 16; ++i) {
+            const int row = c0 + c * 16 + i;
+            const float comb = row < rows ? sb * slot[row] : 0.0f;
+            acc[c * 16 + i] = fmaf(__uint_as_float(r[c][i]), comb, acc[c * 16 + i]);
           }
         }
         tc_fence_before();

@@ -251,6 +251,10 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   if (threadIdx.x == 0) griddep_launch_dependents();   // a split-K reduce may launch now
+  // Launched with programmatic dependent launch, the prologue above overlaps
+  // the previous kernel on the stream; nothing of global memory is touched
+  // before that kernel has completed.
+  griddep_wait();
 
   if (warp == 0) {
     // producer warp: all lanes run the loop, the elected lane issues the copies
@@ -334,7 +338,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     const bool issuer = elect_one();
     // ------------------------------------------------------------------ MMA issuer
     constexpr uint32_t kFmt = kFp4 ? 1u : 0u;
-    const uint32_t idesc0 = idesc_block_scaled(kFmt, kFmt, kAMN, kBMN, 128, BN);
+    constexpr uint32_t idesc0 = idesc_block_scaled(kFmt, kFmt, kAMN, kBMN, 128, BN);
     // K-major: SBO = 8 rows x 128 B; MN-major: LBO = next 128-element MN slab,
     // SBO = next 8 K rows.
     // Shuffled B (no swizzle): LBO = next 16-byte K chunk (128 B), SBO = next
@@ -346,7 +350,11 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     constexpr uint32_t kKStep = kAMN ? 32u * 128u : 32u;   // bytes per MMA along K (A)
     constexpr uint32_t kKStepB = kBMN ? 32u * 128u : kBShuf ? 256u : 32u;
     constexpr uint32_t kBLayout = kBShuf ? kLayoutNone : kLayoutSW128;
-    const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
+    // The descriptors of stage 0 are built once; a stage's are a constant
+    // offset from them, so the issue path between two MMAs stays a few adds
+    // (at N <= 128 the tensor pipe outruns a longer issue path).
+    const uint64_t adesc0 = make_sdesc(smem_u32(sA), kALbo, kSbo, kLayoutSW128);
+    const uint64_t bdesc0 = make_sdesc(smem_u32(sB), kBLbo, kSbo, kBLayout);
     const uint32_t sSfa0 = smem_u32(sSfa), sSfb0 = smem_u32(sSfb);
     int stage = 0;
     uint32_t phase = 0;
@@ -370,34 +378,36 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t sf_off = sf_region * Cfg::kSfRegionCols;
+        const uint32_t tsf = tmem_base + sf_region * Cfg::kSfRegionCols;
         sf_region ^= 1u;
+        if (issuer) {
+          const uint32_t ust = static_cast<uint32_t>(stage);
 #pragma unroll
-        for (int j = 0; j < Cfg::kSfAtomsK; ++j) {
-          if (issuer) tmem_cp_sf_atom(tmem_base + sf_off + Cfg::kColSfa + 4u * j,
-                          sSfa0 + stage * Cfg::kSfaBytes + 512u * j);
+          for (int j = 0; j < Cfg::kSfAtomsK; ++j) {
+            tmem_cp_sf_atom(tsf + Cfg::kColSfa + 4u * j, sSfa0 + ust * Cfg::kSfaBytes + 512u * j);
 #pragma unroll
-          for (int r = 0; r < Cfg::kSfbRowBlocks; ++r)
-            if (issuer) tmem_cp_sf_atom(tmem_base + sf_off + Cfg::kColSfb + 4u * (j * Cfg::kSfbRowBlocks + r),
-                            sSfb0 + stage * Cfg::kSfbBytes + 512u * (r * Cfg::kSfAtomsK + j));
-        }
-        const uint32_t a_addr = sA0 + stage * Cfg::kABytes;
-        const uint32_t b_addr = sB0 + stage * Cfg::kBBytes;
+            for (int r = 0; r < Cfg::kSfbRowBlocks; ++r)
+              tmem_cp_sf_atom(tsf + Cfg::kColSfb + 4u * (j * Cfg::kSfbRowBlocks + r),
+                              sSfb0 + ust * Cfg::kSfbBytes + 512u * (r * Cfg::kSfAtomsK + j));
+          }
+          const uint64_t ad = adesc0 + static_cast<uint64_t>(ust * (Cfg::kABytes >> 4));
+          const uint64_t bd = bdesc0 + static_cast<uint64_t>(ust * (Cfg::kBBytes >> 4));
+          const uint32_t acc0 = kb > kb0 ? 1u : 0u;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const uint32_t j = kFp4 ? static_cast<uint32_t>(t >> 1) : 0u;
-          const uint32_t sf_id = kFp4 ? static_cast<uint32_t>((t & 1) * 2) : static_cast<uint32_t>(t);
-          const uint64_t adesc = make_sdesc(a_addr + t * kKStep, kALbo, kSbo, kLayoutSW128);
-          const uint64_t bdesc = make_sdesc(b_addr + t * kKStepB, kBLbo, kSbo, kBLayout);
-          const uint32_t idesc = idesc_with_sf_id(idesc0, sf_id, sf_id);
-          const uint32_t tsfa = tmem_base + sf_off + Cfg::kColSfa + 4u * j;
-          const uint32_t tsfb = tmem_base + sf_off + Cfg::kColSfb + 4u * j * Cfg::kSfbRowBlocks;
-          const uint32_t acc = (kb > kb0 || t > 0) ? 1u : 0u;
-          if (!issuer) continue;
-          if constexpr (kFp4)
-            umma_mxf4(tmem_base, adesc, bdesc, idesc, tsfa, tsfb, acc);
-          else
-            umma_mxf8f6f4(tmem_base, adesc, bdesc, idesc, tsfa, tsfb, acc);
+          for (int t = 0; t < 4; ++t) {
+            const uint32_t j = kFp4 ? static_cast<uint32_t>(t >> 1) : 0u;
+            const uint32_t sf_id = kFp4 ? static_cast<uint32_t>((t & 1) * 2) : static_cast<uint32_t>(t);
+            const uint64_t adesc = ad + static_cast<uint64_t>((t * kKStep) >> 4);
+            const uint64_t bdesc = bd + static_cast<uint64_t>((t * kKStepB) >> 4);
+            const uint32_t idesc = idesc_with_sf_id(idesc0, sf_id, sf_id);
+            const uint32_t tsfa = tsf + Cfg::kColSfa + 4u * j;
+            const uint32_t tsfb = tsf + Cfg::kColSfb + 4u * j * Cfg::kSfbRowBlocks;
+            const uint32_t acc = t > 0 ? 1u : acc0;
+            if constexpr (kFp4)
+              umma_mxf4(tmem_base, adesc, bdesc, idesc, tsfa, tsfb, acc);
+            else
+              umma_mxf8f6f4(tmem_base, adesc, bdesc, idesc, tsfa, tsfb, acc);
+          }
         }
         if (issuer) tc_commit(&empty_bar[stage]);
         __syncwarp();

@@ -161,6 +161,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
   cluster_sync_all();   // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  if (threadIdx.x == 0) griddep_launch_dependents();   // the next kernel's prologue may start
+  // Launched with programmatic dependent launch, the prologue above overlaps
+  // the previous kernel on the stream; nothing of global memory is touched
+  // before that kernel has completed.
+  griddep_wait();
   const int cluster_id = static_cast<int>(blockIdx.x >> 1);
   const int num_clusters = static_cast<int>(gridDim.x >> 1);
 

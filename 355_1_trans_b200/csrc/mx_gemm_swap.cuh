@@ -15,12 +15,13 @@
 // the weights at HBM speed.  The activation rows of one batch all lie in the
 // first 128-row scale atom (M <= 64), so the activation scales are that atom.
 //
-// Roles as in mx_gemm.cuh: warp 0 TMA producer, warp 1 MMA, warp 2 TMEM
-// allocator, warps 4-7 epilogue.  Two TMEM accumulators (MN columns each)
-// alternate between units, so the MMA starts the next unit while the
-// epilogue drains the last one: lane n of the accumulator is output column
-// n, column m is output row m; a thread stores its column for every row
-// (64 contiguous bytes per warp per row), or its split-K partial.
+// Roles: warps 0, 2 and 3 TMA producers (every third K block each), warp 1
+// MMA, warp 2 also allocates TMEM, warps 4-7 epilogue.  Two TMEM
+// accumulators (MN columns each) alternate between units, so the MMA starts
+// the next unit while the epilogue drains the last one: lane n of the
+// accumulator is output column n, column m is output row m; a thread stores
+// its column for every row (64 contiguous bytes per warp per row), or its
+// split-K partial.
 #pragma once
 
 #include "mx_gemm.cuh"
@@ -36,6 +37,8 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
       : "r"(taddr)
       : "memory");
 }
+
+constexpr uint32_t kMxSwapProducers = 3;   // TMA producer warps 0, 2 and 3
 
 template <int MN, int kFp4>
 struct MxSwapCfg {
@@ -119,16 +122,38 @@ __global__ void __launch_bounds__(256, 1)
   if (threadIdx.x == 0) griddep_launch_dependents();   // a split-K reduce may launch now
 
   // units: (batch, N tile, K slice); the activation tile is the batch's rows 0..MN-1
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+  if (warp == 0 || warp == 2 || warp == 3) {
+    // ------------------------------------------------------------------ TMA producers
+    // Three warps take every third K block each: one warp's issue chain per
+    // K block (a barrier wait and four copies) would alone cap the weight
+    // stream well below the TMA rate of an SM.
+    const uint32_t pidx = warp == 0 ? 0u : static_cast<uint32_t>(warp - 1);
     const bool issuer = elect_one();
     const uint64_t pol_w = l2_policy_evict_first();   // weights stream through once
     const uint64_t pol_x = l2_policy_evict_last();    // activations are reread by every tile
     int stage = 0;
     uint32_t phase = 0;
+    uint32_t kbi = 0;
     bool ok = true;
     int last_stage = -1;
     uint32_t last_phase = 0;
+    // The weights do not come from the previous kernel on the stream: pull
+    // this warp's share of the first unit's first S K blocks into L2, then
+    // wait for that kernel (programmatic dependent launch) before anything is
+    // read into shared memory.
+    if (issuer && static_cast<int>(blockIdx.x) < p.total_units) {
+      int b, mt, nt, s;
+      decode_unit(blockIdx.x, 1, p.tiles_n, p.split_k, 1, b, mt, nt, s);
+      const int kb0 = s * p.kb_per_split;
+      const int kb1 = min(kb0 + min(p.kb_per_split, S), p.num_kb);
+      for (int kb = kb0 + static_cast<int>(pidx); kb < kb1; kb += static_cast<int>(kMxSwapProducers)) {
+        if constexpr (kBMode == kBShuffle16)
+          tma_prefetch_5d(&tmB, 0, kb * 8, 0, nt * 8, b);
+        else
+          tma_prefetch_3d(&tmB, kb * 128, nt * 128, b);
+      }
+    }
+    griddep_wait();
     for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
       int b, mt, nt, s;
       decode_unit(u, 1, p.tiles_n, p.split_k, 1, b, mt, nt, s);
@@ -136,7 +161,14 @@ __global__ void __launch_bounds__(256, 1)
       const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
       const uint8_t* sfw_tile = p.sfb + b * p.sfb_batch_stride + static_cast<long long>(nt) * p.sf_kb_total * 512;
       const uint8_t* sfx_tile = p.sfa + b * p.sfa_batch_stride;
-      for (int kb = kb0; kb < kb1; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
+        if (kbi % kMxSwapProducers != pidx) {
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          continue;
+        }
         if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
           ok = false;
           break;
@@ -169,14 +201,19 @@ __global__ void __launch_bounds__(256, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
+    // An M=128 N<=64 MMA occupies the tensor pipe for well under 100 cycles,
+    // so the instructions between two MMAs set the pace: the descriptors of
+    // stage 0 are built once, a stage's are a constant offset from them, and
+    // a K block's scale copies and MMAs are one branch of immediate adds.
     const bool issuer = elect_one();
     constexpr uint32_t kFmt = kFp4 ? 1u : 0u;
-    const uint32_t idesc0 = idesc_block_scaled(kFmt, kFmt, false, false, 128, MN);
+    constexpr uint32_t idesc0 = idesc_block_scaled(kFmt, kFmt, false, false, 128, MN);
     constexpr bool kWShuf = kBMode == kBShuffle16;
     constexpr uint32_t kWLbo = kWShuf ? 128u : 16u;
-    constexpr uint32_t kWStep = kWShuf ? 256u : 32u;
+    constexpr uint64_t kWStep = (kWShuf ? 256u : 32u) >> 4;   // one K step, 16-byte units
     constexpr uint32_t kWLayout = kWShuf ? kLayoutNone : kLayoutSW128;
-    const uint32_t sW0 = smem_u32(sW), sX0 = smem_u32(sX);
+    const uint64_t wdesc0 = make_sdesc(smem_u32(sW), kWLbo, 1024u, kWLayout);
+    const uint64_t xdesc0 = make_sdesc(smem_u32(sX), 16u, 1024u, kLayoutSW128);
     const uint32_t sSfw0 = smem_u32(sSfw), sSfx0 = smem_u32(sSfx);
     int stage = 0;
     uint32_t phase = 0;
@@ -201,32 +238,31 @@ __global__ void __launch_bounds__(256, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t sf_off = Cfg::kColSf + sf_region * Cfg::kSfRegionCols;
+        const uint32_t tsf = tmem_base + Cfg::kColSf + sf_region * Cfg::kSfRegionCols;
         sf_region ^= 1u;
+        if (issuer) {
+          const uint32_t ust = static_cast<uint32_t>(stage);
 #pragma unroll
-        for (int j = 0; j < Cfg::kSfAtomsK; ++j) {
-          if (issuer) {
-            tmem_cp_sf_atom(tmem_base + sf_off + 4u * j, sSfw0 + stage * Cfg::kSfwBytes + 512u * j);
-            tmem_cp_sf_atom(tmem_base + sf_off + 4u * (Cfg::kSfAtomsK + j), sSfx0 + stage * Cfg::kSfxBytes + 512u * j);
+          for (int j = 0; j < Cfg::kSfAtomsK; ++j) {
+            tmem_cp_sf_atom(tsf + 4u * j, sSfw0 + ust * Cfg::kSfwBytes + 512u * j);
+            tmem_cp_sf_atom(tsf + 4u * (Cfg::kSfAtomsK + j), sSfx0 + ust * Cfg::kSfxBytes + 512u * j);
           }
-        }
-        const uint32_t w_addr = sW0 + stage * Cfg::kWBytes;
-        const uint32_t x_addr = sX0 + stage * Cfg::kXBytes;
+          const uint64_t wd = wdesc0 + static_cast<uint64_t>(ust * (Cfg::kWBytes >> 4));
+          const uint64_t xd = xdesc0 + static_cast<uint64_t>(ust * (Cfg::kXBytes >> 4));
+          const uint32_t acc0 = kb > kb0 ? 1u : 0u;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const uint32_t j = kFp4 ? static_cast<uint32_t>(t >> 1) : 0u;
-          const uint32_t sf_id = kFp4 ? static_cast<uint32_t>((t & 1) * 2) : static_cast<uint32_t>(t);
-          const uint64_t adesc = make_sdesc(w_addr + t * kWStep, kWLbo, 1024u, kWLayout);
-          const uint64_t bdesc = make_sdesc(x_addr + 32u * t, 16u, 1024u, kLayoutSW128);
-          const uint32_t idesc = idesc_with_sf_id(idesc0, sf_id, sf_id);
-          const uint32_t tsfa = tmem_base + sf_off + 4u * j;
-          const uint32_t tsfb = tmem_base + sf_off + 4u * (Cfg::kSfAtomsK + j);
-          const uint32_t acc = (kb > kb0 || t > 0) ? 1u : 0u;
-          if (!issuer) continue;
-          if constexpr (kFp4)
-            umma_mxf4(d, adesc, bdesc, idesc, tsfa, tsfb, acc);
-          else
-            umma_mxf8f6f4(d, adesc, bdesc, idesc, tsfa, tsfb, acc);
+          for (int t = 0; t < 4; ++t) {
+            const uint32_t j = kFp4 ? static_cast<uint32_t>(t >> 1) : 0u;
+            const uint32_t sf_id = kFp4 ? static_cast<uint32_t>((t & 1) * 2) : static_cast<uint32_t>(t);
+            const uint32_t idesc = idesc_with_sf_id(idesc0, sf_id, sf_id);
+            const uint64_t adesc = wd + static_cast<uint64_t>(t) * kWStep;
+            const uint64_t bdesc = xd + 2u * static_cast<uint64_t>(t);
+            const uint32_t acc = t > 0 ? 1u : acc0;
+            if constexpr (kFp4)
+              umma_mxf4(d, adesc, bdesc, idesc, tsf + 4u * j, tsf + 4u * (Cfg::kSfAtomsK + j), acc);
+            else
+              umma_mxf8f6f4(d, adesc, bdesc, idesc, tsf + 4u * j, tsf + 4u * (Cfg::kSfAtomsK + j), acc);
+          }
         }
         if (issuer) tc_commit(&empty_bar[stage]);
         __syncwarp();
@@ -246,6 +282,7 @@ __global__ void __launch_bounds__(256, 1)
     const int q = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     int iter = 0;
+    griddep_wait();   // C and the split-K partials may still be read by the previous kernel
     for (int u = blockIdx.x; u < p.total_units; u += gridDim.x, ++iter) {
       int b, mt, nt, s;
       decode_unit(u, 1, p.tiles_n, p.split_k, 1, b, mt, nt, s);

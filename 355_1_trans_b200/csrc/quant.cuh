@@ -90,6 +90,10 @@ __global__ void __launch_bounds__(256) quantize_kernel(const QuantParams p) {
   const int row = static_cast<int>(gw / warps_per_row);
   const int col0 = static_cast<int>(gw % warps_per_row) * kQuantWarpCols + lane * 8;
   const int limit_rows = kFormat != kQuantFp8Block && p.sf_format == 0 ? p.rows_padded : p.rows;
+  // A GEMM that consumes these activations may launch now (programmatic
+  // dependent launch): its prologue and weight prefetch overlap this kernel,
+  // and it waits for this grid's completion before it reads the outputs.
+  griddep_launch_dependents();
   if (row >= limit_rows) return;
   // all loads first
   float v[kQuantItems][8];

@@ -236,6 +236,31 @@ __device__ __forceinline__ void tma_load_5d_hint(void* dst, const CUtensorMap* m
       : "memory");
 }
 
+// Tiled prefetch of a tensor-map box into L2 only (nothing lands in shared
+// memory, no barrier).  L2 is the coherence point of device memory, so a
+// prefetch issued before griddep_wait cannot expose data that the
+// predecessor grid is still writing: the later load reads L2 after the wait.
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* m, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* m, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_5d(const CUtensorMap* m, int c0, int c1, int c2, int c3, int c4) {
+  asm volatile("cp.async.bulk.prefetch.tensor.5d.L2.global [%0, {%1, %2, %3, %4, %5}];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+               : "memory");
+}
+
 // Make this thread's generic-proxy shared-memory writes visible to the async
 // proxy (TMA, tcgen05.cp, tcgen05.mma operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
