@@ -93,18 +93,26 @@ __device__ __forceinline__ void tmem_reg_fence16(uint32_t (&r)[16]) {
 template <int MN>
 struct SwapCfg {
   static_assert(MN == 16 || MN == 32 || MN == 64, "MN must be 16, 32 or 64");
-  // promotion warps: one per TMEM lane quarter, two (each half of the MN
-  // columns) for MN = 64, so a warp's TMEM-load -> FMA chain per K block
-  // stays short
-  static constexpr int kPromoWarps = MN >= 64 ? 8 : 4;
+  // Promotion: eight warps, two per TMEM lane quarter.  A warp's chain per
+  // K block (barrier wait, TMEM load, scale reads, FMAs, arrivals) is ~600
+  // cycles of latency, longer than the MMA and the weight stream need per
+  // K block, so two warps share each lane quarter: for MN = 64 each takes
+  // half of the columns of every K block; for MN <= 32 two sets of four
+  // warps take alternate K blocks, and at the end of a unit the second set
+  // hands its sums to the first through shared memory.
+  static constexpr int kPromoWarps = 8;
+  static constexpr int kPromoSets = MN >= 64 ? 1 : 2;
   static constexpr int kThreads = 128 + 32 * kPromoWarps;
-  static constexpr int kCols = MN * 4 / kPromoWarps;   // accumulator columns per thread
+  static constexpr int kCols = MN >= 64 ? MN / 2 : MN;        // accumulator columns per thread
+  static constexpr int kArrivals = kPromoWarps / kPromoSets;  // promotion warps per K block
+  static constexpr uint32_t kRedBytes = kPromoSets > 1 ? 128u * static_cast<uint32_t>(MN) * 4u : 0u;
   static constexpr uint32_t kWBytes = 128u * 128u;                 // weight tile
   static constexpr uint32_t kXBytes = static_cast<uint32_t>(MN) * 128u;
   static constexpr uint32_t kStageBytes = kWBytes + kXBytes;
-  static constexpr int kStages = static_cast<int>((210u * 1024u) / kStageBytes) > 12
+  static constexpr uint32_t kStageBudget = 210u * 1024u - kRedBytes;
+  static constexpr int kStages = static_cast<int>(kStageBudget / kStageBytes) > 12
                                      ? 12
-                                     : static_cast<int>((210u * 1024u) / kStageBytes);
+                                     : static_cast<int>(kStageBudget / kStageBytes);
   static constexpr int kAccBufs = (512 / MN) > 8 ? 8 : 512 / MN;
   static constexpr uint32_t kTmemCols = static_cast<uint32_t>(kAccBufs * MN) < 32 ? 32u
                                         : static_cast<uint32_t>(kAccBufs * MN);
@@ -116,9 +124,10 @@ struct SwapCfg {
   static constexpr uint32_t kScaleSlot = static_cast<uint32_t>(MN + 4);   // floats: MN sfa, 1 sfb
   static constexpr uint32_t kOffScale = kOffX + kXBytes * kStages;
   static constexpr uint32_t kScaleBytes = static_cast<uint32_t>(kScaleSlots) * kScaleSlot * 4u;
-  static constexpr uint32_t kOffBar = kOffScale + ((kScaleBytes + 15u) & ~15u);
+  static constexpr uint32_t kOffRed = kOffScale + ((kScaleBytes + 15u) & ~15u);   // [MN][128] floats
+  static constexpr uint32_t kOffBar = kOffRed + kRedBytes;
   static constexpr uint32_t kSmemBytes = kOffBar + 1024u + 1024u;
-  static_assert(8u * (2u * kStages + 2u * kAccBufs + 2u * kScaleSlots + 1u) + 8u <= 1024u, "barrier area");
+  static_assert(8u * (2u * kStages + 2u * kAccBufs + 2u * kScaleSlots + 1u + 8u) + 8u <= 1024u, "barrier area");
   static_assert(kSmemBytes <= 227u * 1024u, "shared memory");
   static_assert(kScaleSlots >= kStages + kAccBufs, "scale ring shorter than the pipeline");
 };
@@ -145,7 +154,9 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
   uint64_t* scale_full = acc_empty + NB;  // [R]
   uint64_t* scale_empty = scale_full + R;  // [R]
   uint64_t* drain_bar = scale_empty + R;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* red_full = drain_bar + 1;   // [4] second promotion set -> first, per lane quarter
+  uint64_t* red_empty = red_full + 4;   // [4]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(red_empty + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -158,13 +169,17 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
     }
     for (int i = 0; i < NB; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], Cfg::kPromoWarps);   // one arrival per promotion warp
+      mbar_init(&acc_empty[i], Cfg::kArrivals);   // one arrival per promotion warp of the K block
     }
     for (int i = 0; i < R; ++i) {
       mbar_init(&scale_full[i], 32);  // one cp.async arrival per producer lane
-      mbar_init(&scale_empty[i], Cfg::kPromoWarps);  // one arrival per promotion warp
+      mbar_init(&scale_empty[i], Cfg::kArrivals);
     }
     mbar_init(drain_bar, 1);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&red_full[i], 1);
+      mbar_init(&red_empty[i], 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -273,32 +288,32 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     // An M=128 N<=64 MMA occupies the tensor pipe for well under 100 cycles,
-    // so the instructions between two MMAs set the pace: the descriptors of
-    // stage 0 are built once, a stage's are a constant offset from them, and
-    // the four K steps of a K block are one branch of immediate adds.
-    const bool issuer = elect_one();
-    const uint32_t idesc = idesc_f8f6f4(false, false, 128, MN);
-    const uint64_t wdesc0 = weight_sdesc<kBFmt>(smem_u32(sW), 0);
-    const uint64_t xdesc0 = make_sdesc(smem_u32(sX), 16u, 1024u, kLayoutSW128);
-    constexpr uint64_t kWStep = (kBFmt == kFmtShuffle16 ? 256u : 32u) >> 4;   // one K step, 16-byte units
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t kbi = 0;
-    bool ok = true;
-    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
-      int b, mt, nt, s;
-      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
-      const int kb0 = s * p.kb_per_split;
-      const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
-      for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
-        const uint32_t buf = kbi % NB;
-        if (!mbar_wait(&acc_empty[buf], ((kbi / NB) & 1u) ^ 1u, abort_flag, p.timeout_ns) ||
-            !mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (issuer) {
+    // so the issue loop sets the pace.  One elected thread runs the whole
+    // role (its barrier waits cost a fraction of a 32-lane wait; the tcgen05
+    // instructions are single-thread anyway), the descriptors of stage 0 are
+    // built once and a stage's are a constant offset from them.
+    if (elect_one()) {
+      const uint32_t idesc = idesc_f8f6f4(false, false, 128, MN);
+      const uint64_t wdesc0 = weight_sdesc<kBFmt>(smem_u32(sW), 0);
+      const uint64_t xdesc0 = make_sdesc(smem_u32(sX), 16u, 1024u, kLayoutSW128);
+      constexpr uint64_t kWStep = (kBFmt == kFmtShuffle16 ? 256u : 32u) >> 4;   // one K step, 16-byte units
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t kbi = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+        int b, mt, nt, s;
+        decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+        const int kb0 = s * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
+        for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
+          const uint32_t buf = kbi % NB;
+          if (!mbar_wait(&acc_empty[buf], ((kbi / NB) & 1u) ^ 1u, abort_flag, p.timeout_ns) ||
+              !mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
           const uint64_t wd = wdesc0 + static_cast<uint64_t>(static_cast<uint32_t>(stage) * (Cfg::kWBytes >> 4));
           const uint64_t xd = xdesc0 + static_cast<uint64_t>(static_cast<uint32_t>(stage) * (Cfg::kXBytes >> 4));
           const uint32_t d = tmem_base + buf * MN;
@@ -308,29 +323,35 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
           umma_f8f6f4(d, wd + 3u * kWStep, xd + 6u, idesc, 1u);
           tc_commit(&empty_bar[stage]);
           tc_commit(&acc_full[buf]);
-        }
-        __syncwarp();
-        if (++stage == S) {
-          stage = 0;
-          phase ^= 1u;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
+      tc_commit(drain_bar);
+      int dummy = 0;
+      mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
     }
-    if (issuer) tc_commit(drain_bar);
-    int dummy = 0;
-    mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
+    __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ promotion + store
-    // warp w: TMEM lane quarter w % 4 (= output columns), activation rows
-    // [c0, c0 + HC) of the tile
+    // warp w: TMEM lane quarter w % 4 (= output columns); MN = 64: activation
+    // rows [c0, c0 + HC) of every K block; MN <= 32: all rows of the K blocks
+    // whose parity is the warp's set
     constexpr int HC = Cfg::kCols;
+    constexpr int PS = Cfg::kPromoSets;
     const int q = warp & 3;
-    const int c0 = ((warp - 4) >> 2) * HC;
+    const int half = (warp - 4) >> 2;
+    const uint32_t set = PS > 1 ? static_cast<uint32_t>(half) : 0u;
+    const int c0 = PS > 1 ? 0 : half * HC;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    float* red = reinterpret_cast<float*>(smem + Cfg::kOffRed);   // [HC][128]: conflict-free per column
     uint32_t kbi = 0;
+    uint32_t ui = 0;   // units done, for the hand-off barriers' parity
     bool ok = true;
     griddep_wait();   // C and the split-K partials may still be read by the previous kernel
-    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
+    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x, ++ui) {
       int b, mt, nt, s;
       decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
       const int kb0 = s * p.kb_per_split;
@@ -343,6 +364,7 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
       for (int i = 0; i < HC; ++i) acc[i] = 0.0f;
       constexpr int CH = HC / 16;   // 16-column TMEM loads per K block
       for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
+        if (PS > 1 && (kbi & 1u) != set) continue;
         const uint32_t buf = kbi % NB;
         const uint32_t sl = kbi % R;
         if (!mbar_wait(&acc_full[buf], (kbi / NB) & 1u, abort_flag, p.timeout_ns)) {
@@ -383,6 +405,24 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
         }
       }
       if (!ok) break;
+      if constexpr (PS > 1) {
+        // the second set hands its sums to the first (per lane quarter,
+        // through [HC][128] floats of shared memory)
+        const int lrow = q * 32 + static_cast<int>(lane);
+        if (set == 1) {
+          if (!mbar_wait(&red_empty[q], (ui & 1u) ^ 1u, abort_flag, p.timeout_ns)) break;
+#pragma unroll
+          for (int i = 0; i < HC; ++i) red[i * 128 + lrow] = acc[i];
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&red_full[q]);
+          continue;
+        }
+        if (!mbar_wait(&red_full[q], ui & 1u, abort_flag, p.timeout_ns)) break;
+#pragma unroll
+        for (int i = 0; i < HC; ++i) acc[i] += red[i * 128 + lrow];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&red_empty[q]);
+      }
       if (n >= p.n) continue;
       // store: lane n writes column n of every valid row (64 B per warp per row)
 #pragma unroll
