@@ -32,11 +32,11 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// One lane of a fully converged warp (the lowest active lane).  The MMA warps
-// run their loops on all 32 lanes -- so barrier waits and descriptor
-// arithmetic stay warp-uniform -- and only the elected lane issues tcgen05
-// instructions; issuing from a lane-divergent single-thread loop costs tens
-// of cycles per instruction more.
+// One lane of a fully converged warp (the lowest active lane).  Loops whose
+// waits and descriptor arithmetic must stay warp-uniform elect the issuing
+// lane per instruction; the decode kernels instead run their whole MMA role
+// on the elected lane, where a barrier wait costs a fraction of a 32-lane
+// one and the instructions between two MMAs are a few adds.
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(
@@ -85,12 +85,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// Non-blocking test of a phase (cheaper than try_wait when the phase has
+// already completed, the common case for a pipeline that runs ahead).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete.  Gives up
 // when the CTA-wide abort word is set by another role, or after timeout_ns,
 // in which case it sets the abort word and the device error word.  Returns
 // false on give-up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           uint64_t timeout_ns) {
+  if (mbar_test_wait(bar, parity)) return true;
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 1; it < 0x7fffffffu; ++it) {
