@@ -39,6 +39,7 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
 }
 
 constexpr uint32_t kMxSwapProducers = 3;   // TMA producer warps 0, 2 and 3
+constexpr uint32_t kMxSwapChains = 2;      // accumulators per unit (alternate K blocks)
 
 template <int MN, int kFp4>
 struct MxSwapCfg {
@@ -59,10 +60,19 @@ struct MxSwapCfg {
   static constexpr uint32_t kSmemBytes = kOffBar + 256u + 1024u;
   // TMEM: two accumulators [0, 2 MN), then two alternating scale regions
   // (weight atoms: 4 columns per K atom, activation atoms: 4 per K atom)
-  static constexpr uint32_t kColSf = 2u * MN;
+  // Each unit accumulates its K blocks alternately into kMxSwapChains TMEM
+  // accumulators (summed in the epilogue): consecutive MMAs of one
+  // accumulator wait for each other, so two chains keep the tensor pipe
+  // busy at these small N.  Two units alternate, so the MMA starts the next
+  // unit while the epilogue drains the last one.
+  static constexpr uint32_t kChains = kMxSwapChains;
+  static constexpr uint32_t kAccCols = kChains * static_cast<uint32_t>(MN);   // one unit's accumulators
+  static constexpr uint32_t kColSf = 2u * kAccCols;
   static constexpr uint32_t kSfRegionCols = 8u * kSfAtomsK;
   static constexpr uint32_t kColsUsed = kColSf + 2u * kSfRegionCols;
-  static constexpr uint32_t kTmemCols = kColsUsed <= 32 ? 32 : kColsUsed <= 64 ? 64 : kColsUsed <= 128 ? 128 : 256;
+  static constexpr uint32_t kTmemCols =
+      kColsUsed <= 32 ? 32 : kColsUsed <= 64 ? 64 : kColsUsed <= 128 ? 128 : kColsUsed <= 256 ? 256 : 512;
+  static_assert(kColsUsed <= 512, "TMEM columns");
   static_assert(kStages >= 4, "pipeline too shallow");
   static_assert(kSmemBytes <= 227u * 1024u, "shared memory");
   static_assert(8u * (2u * kStages + 5u) + 8u <= 256u, "barrier area");
@@ -202,45 +212,47 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     // An M=128 N<=64 MMA occupies the tensor pipe for well under 100 cycles,
-    // so the instructions between two MMAs set the pace: the descriptors of
-    // stage 0 are built once, a stage's are a constant offset from them, and
-    // a K block's scale copies and MMAs are one branch of immediate adds.
-    const bool issuer = elect_one();
-    constexpr uint32_t kFmt = kFp4 ? 1u : 0u;
-    constexpr uint32_t idesc0 = idesc_block_scaled(kFmt, kFmt, false, false, 128, MN);
-    constexpr bool kWShuf = kBMode == kBShuffle16;
-    constexpr uint32_t kWLbo = kWShuf ? 128u : 16u;
-    constexpr uint64_t kWStep = (kWShuf ? 256u : 32u) >> 4;   // one K step, 16-byte units
-    constexpr uint32_t kWLayout = kWShuf ? kLayoutNone : kLayoutSW128;
-    const uint64_t wdesc0 = make_sdesc(smem_u32(sW), kWLbo, 1024u, kWLayout);
-    const uint64_t xdesc0 = make_sdesc(smem_u32(sX), 16u, 1024u, kLayoutSW128);
-    const uint32_t sSfw0 = smem_u32(sSfw), sSfx0 = smem_u32(sSfx);
-    int stage = 0;
-    uint32_t phase = 0;
-    int iter = 0;
-    uint32_t sf_region = 0;
-    bool ok = true;
-    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x, ++iter) {
-      int b, mt, nt, s;
-      decode_unit(u, 1, p.tiles_n, p.split_k, 1, b, mt, nt, s);
-      const int kb0 = s * p.kb_per_split;
-      const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
-      const uint32_t ub = static_cast<uint32_t>(iter) & 1u;
-      if (!mbar_wait(&acc_empty[ub], ((static_cast<uint32_t>(iter) >> 1) & 1u) ^ 1u, abort_flag, p.timeout_ns)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t d = tmem_base + ub * MN;
-      for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) {
+    // so the issue loop sets the pace.  One elected thread runs the whole
+    // role (its barrier waits cost a fraction of a 32-lane wait; the tcgen05
+    // instructions are single-thread anyway), the descriptors of stage 0 are
+    // built once and a stage's are a constant offset from them.
+    if (elect_one()) {
+      constexpr uint32_t kFmt = kFp4 ? 1u : 0u;
+      constexpr uint32_t idesc0 = idesc_block_scaled(kFmt, kFmt, false, false, 128, MN);
+      constexpr bool kWShuf = kBMode == kBShuffle16;
+      constexpr uint32_t kWLbo = kWShuf ? 128u : 16u;
+      constexpr uint64_t kWStep = (kWShuf ? 256u : 32u) >> 4;   // one K step, 16-byte units
+      constexpr uint32_t kWLayout = kWShuf ? kLayoutNone : kLayoutSW128;
+      const uint64_t wdesc0 = make_sdesc(smem_u32(sW), kWLbo, 1024u, kWLayout);
+      const uint64_t xdesc0 = make_sdesc(smem_u32(sX), 16u, 1024u, kLayoutSW128);
+      const uint32_t sSfw0 = smem_u32(sSfw), sSfx0 = smem_u32(sSfx);
+      int stage = 0;
+      uint32_t phase = 0;
+      int iter = 0;
+      uint32_t sf_region = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x, ++iter) {
+        int b, mt, nt, s;
+        decode_unit(u, 1, p.tiles_n, p.split_k, 1, b, mt, nt, s);
+        const int kb0 = s * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
+        const uint32_t ub = static_cast<uint32_t>(iter) & 1u;
+        if (!mbar_wait(&acc_empty[ub], ((static_cast<uint32_t>(iter) >> 1) & 1u) ^ 1u, abort_flag, p.timeout_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t tsf = tmem_base + Cfg::kColSf + sf_region * Cfg::kSfRegionCols;
-        sf_region ^= 1u;
-        if (issuer) {
+        const uint32_t dunit = tmem_base + ub * Cfg::kAccCols;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          const uint32_t chain = static_cast<uint32_t>(kb - kb0) % Cfg::kChains;
+          const uint32_t d = dunit + chain * MN;
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t tsf = tmem_base + Cfg::kColSf + sf_region * Cfg::kSfRegionCols;
+          sf_region ^= 1u;
           const uint32_t ust = static_cast<uint32_t>(stage);
 #pragma unroll
           for (int j = 0; j < Cfg::kSfAtomsK; ++j) {
@@ -249,7 +261,7 @@ __global__ void __launch_bounds__(256, 1)
           }
           const uint64_t wd = wdesc0 + static_cast<uint64_t>(ust * (Cfg::kWBytes >> 4));
           const uint64_t xd = xdesc0 + static_cast<uint64_t>(ust * (Cfg::kXBytes >> 4));
-          const uint32_t acc0 = kb > kb0 ? 1u : 0u;
+          const uint32_t acc0 = kb - kb0 >= static_cast<int>(Cfg::kChains) ? 1u : 0u;   // first K block of its chain
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
             const uint32_t j = kFp4 ? static_cast<uint32_t>(t >> 1) : 0u;
@@ -263,20 +275,20 @@ __global__ void __launch_bounds__(256, 1)
             else
               umma_mxf8f6f4(d, adesc, bdesc, idesc, tsf + 4u * j, tsf + 4u * (Cfg::kSfAtomsK + j), acc);
           }
+          tc_commit(&empty_bar[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
-        if (issuer) tc_commit(&empty_bar[stage]);
-        __syncwarp();
-        if (++stage == S) {
-          stage = 0;
-          phase ^= 1u;
-        }
+        if (!ok) break;
+        tc_commit(&acc_full[ub]);
       }
-      if (!ok) break;
-      if (issuer) tc_commit(&acc_full[ub]);
+      tc_commit(drain_bar);
+      int dummy = 0;
+      mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
     }
-    if (issuer) tc_commit(drain_bar);
-    int dummy = 0;
-    mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
+    __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;
@@ -290,22 +302,33 @@ __global__ void __launch_bounds__(256, 1)
       if (!mbar_wait(&acc_full[ub], (static_cast<uint32_t>(iter) >> 1) & 1u, abort_flag, p.timeout_ns)) break;
       tc_fence_after();
       float v[MN];
-      const uint32_t taddr = tmem_base + lane_base + ub * MN;
-      if constexpr (MN >= 32) {
+      const int kb0 = s * p.kb_per_split;
+      const int nkb = min(kb0 + p.kb_per_split, p.num_kb) - kb0;
+      // chain c holds the unit's K blocks c, c + kChains, ...; chains the
+      // unit did not reach hold nothing of it
+      const uint32_t chains = static_cast<uint32_t>(min(nkb, static_cast<int>(Cfg::kChains)));
+      const uint32_t taddr = tmem_base + lane_base + ub * Cfg::kAccCols;
 #pragma unroll
-        for (int c = 0; c < MN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(taddr + static_cast<uint32_t>(c * 32), r);
+      for (uint32_t ch = 0; ch < Cfg::kChains; ++ch) {
+        if (ch >= chains) break;
+        if constexpr (MN >= 32) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[c * 32 + i] = __uint_as_float(r[i]);
-        }
-      } else {
+          for (int c = 0; c < MN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(taddr + ch * MN + static_cast<uint32_t>(c * 32), r);
 #pragma unroll
-        for (int c = 0; c < MN / 8; ++c) {
-          uint32_t r[8];
-          tmem_ld8(taddr + static_cast<uint32_t>(c * 8), r);
+            for (int i = 0; i < 32; ++i)
+              v[c * 32 + i] = ch == 0 ? __uint_as_float(r[i]) : v[c * 32 + i] + __uint_as_float(r[i]);
+          }
+        } else {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) v[c * 8 + i] = __uint_as_float(r[i]);
+          for (int c = 0; c < MN / 8; ++c) {
+            uint32_t r[8];
+            tmem_ld8(taddr + ch * MN + static_cast<uint32_t>(c * 8), r);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              v[c * 8 + i] = ch == 0 ? __uint_as_float(r[i]) : v[c * 8 + i] + __uint_as_float(r[i]);
+          }
         }
       }
       tc_fence_before();
