@@ -242,7 +242,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
     const bool issuer = elect_one();
     // ------------------------------------------------------------------ MMA issuer (leader)
     constexpr uint32_t kFmt = kFp4 ? 1u : 0u;
-    const uint32_t idesc0 = idesc_block_scaled(kFmt, kFmt, kAMN, kBMN, 256, 256);
+    constexpr uint32_t idesc0 = idesc_block_scaled(kFmt, kFmt, kAMN, kBMN, 256, 256);
     constexpr bool kBShuf = kBMode == kBShuffle16;
     constexpr uint32_t kALbo = kAMN ? 128u * 128u : 16u;
     constexpr uint32_t kBLbo = kBMN ? 128u * 128u : kBShuf ? 128u : 16u;
@@ -250,7 +250,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
     constexpr uint32_t kKStep = kAMN ? 32u * 128u : 32u;
     constexpr uint32_t kKStepB = kBMN ? 32u * 128u : kBShuf ? 256u : 32u;
     constexpr uint32_t kBLayout = kBShuf ? kLayoutNone : kLayoutSW128;
-    const uint32_t sA0 = smem_u32(sA), sB0 = smem_u32(sB);
+    // The descriptors of stage 0 are built once; a stage's are a constant
+    // offset from them, and a stage's scale copies and MMAs are one branch,
+    // so the issue path per stage stays short of the MMAs' own time.
+    const uint64_t adesc0 = make_sdesc(smem_u32(sA), kALbo, kSbo, kLayoutSW128);
+    const uint64_t bdesc0 = make_sdesc(smem_u32(sB), kBLbo, kSbo, kBLayout);
     const uint32_t sSfa0 = smem_u32(sSfa), sSfb0 = smem_u32(sSfb);
     int stage = 0;
     uint32_t phase = 0;
@@ -270,36 +274,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t sf_off = sf_region * Cfg::kSfRegionCols;
+        const uint32_t tsf = tmem_base + sf_region * Cfg::kSfRegionCols;
         sf_region ^= 1u;
+        if (issuer) {
+          const uint32_t ust = static_cast<uint32_t>(stage);
 #pragma unroll
-        for (int j = 0; j < Cfg::kSfAtomsK; ++j) {
-          // A scales: 4 columns per K atom (each CTA's own rows)
-          if (issuer) tmem_cp_sf_atom_pair(tmem_base + sf_off + Cfg::kColSfa + 4u * j,
-                               sSfa0 + stage * Cfg::kSfaBytes + 512u * j);
-          // B scales: 8 columns per K atom (all 256 columns, in both CTAs)
+          for (int j = 0; j < Cfg::kSfAtomsK; ++j) {
+            // A scales: 4 columns per K atom (each CTA's own rows)
+            tmem_cp_sf_atom_pair(tsf + Cfg::kColSfa + 4u * j, sSfa0 + ust * Cfg::kSfaBytes + 512u * j);
+            // B scales: 8 columns per K atom (all 256 columns, in both CTAs)
 #pragma unroll
-          for (int r = 0; r < 2; ++r)
-            if (issuer) tmem_cp_sf_atom_pair(tmem_base + sf_off + Cfg::kColSfb + 4u * (j * 2 + r),
-                                 sSfb0 + stage * Cfg::kSfbBytes + 512u * (r * Cfg::kSfAtomsK + j));
-        }
-        const uint32_t a_addr = sA0 + stage * Cfg::kABytes;
-        const uint32_t b_addr = sB0 + stage * Cfg::kBBytes;
+            for (int r = 0; r < 2; ++r)
+              tmem_cp_sf_atom_pair(tsf + Cfg::kColSfb + 4u * (j * 2 + r),
+                                   sSfb0 + ust * Cfg::kSfbBytes + 512u * (r * Cfg::kSfAtomsK + j));
+          }
+          const uint64_t ad = adesc0 + static_cast<uint64_t>(ust * (Cfg::kABytes >> 4));
+          const uint64_t bd = bdesc0 + static_cast<uint64_t>(ust * (Cfg::kBBytes >> 4));
+          const uint32_t acc0 = kb > 0 ? 1u : 0u;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const uint32_t j = kFp4 ? static_cast<uint32_t>(t >> 1) : 0u;
-          const uint32_t sf_id = kFp4 ? static_cast<uint32_t>((t & 1) * 2) : static_cast<uint32_t>(t);
-          const uint64_t adesc = make_sdesc(a_addr + t * kKStep, kALbo, kSbo, kLayoutSW128);
-          const uint64_t bdesc = make_sdesc(b_addr + t * kKStepB, kBLbo, kSbo, kBLayout);
-          const uint32_t idesc = idesc_with_sf_id(idesc0, sf_id, sf_id);
-          const uint32_t tsfa = tmem_base + sf_off + Cfg::kColSfa + 4u * j;
-          const uint32_t tsfb = tmem_base + sf_off + Cfg::kColSfb + 8u * j;
-          const uint32_t acc = (kb > 0 || t > 0) ? 1u : 0u;
-          if (!issuer) continue;
-          if constexpr (kFp4)
-            umma_mxf4_pair(tmem_base, adesc, bdesc, idesc, tsfa, tsfb, acc);
-          else
-            umma_mxf8f6f4_pair(tmem_base, adesc, bdesc, idesc, tsfa, tsfb, acc);
+          for (int t = 0; t < 4; ++t) {
+            const uint32_t j = kFp4 ? static_cast<uint32_t>(t >> 1) : 0u;
+            const uint32_t sf_id = kFp4 ? static_cast<uint32_t>((t & 1) * 2) : static_cast<uint32_t>(t);
+            const uint64_t adesc = ad + static_cast<uint64_t>((t * kKStep) >> 4);
+            const uint64_t bdesc = bd + static_cast<uint64_t>((t * kKStepB) >> 4);
+            const uint32_t idesc = idesc_with_sf_id(idesc0, sf_id, sf_id);
+            const uint32_t tsfa = tsf + Cfg::kColSfa + 4u * j;
+            const uint32_t tsfb = tsf + Cfg::kColSfb + 8u * j;
+            const uint32_t acc = t > 0 ? 1u : acc0;
+            if constexpr (kFp4)
+              umma_mxf4_pair(tmem_base, adesc, bdesc, idesc, tsfa, tsfb, acc);
+            else
+              umma_mxf8f6f4_pair(tmem_base, adesc, bdesc, idesc, tsfa, tsfb, acc);
+          }
         }
         if (issuer) tc_commit_pair(&empty_bar[stage], 0x3);
         __syncwarp();
