@@ -390,7 +390,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMxThreads, 1)
       decode_unit(u, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
       if (!mbar_wait(tmem_full, static_cast<uint32_t>(iter) & 1u, abort_flag, p.timeout_ns)) break;
       tc_fence_after();
-      const int row = mt * 256 + static_cast<int>(rank) * 128 + q * 32 + static_cast<int>(lane);
       const int col_base = nt * 256 + half * 128;
       const int valid_cols = p.n - col_base;
       uint32_t w[64];
