@@ -230,6 +230,27 @@ def test_mxfp8_swap_variants(bs, orc, cuda):
     run_mxfp8(bs, orc, cuda, 8, 256, 1024, seed=92, batch=2, kernel="swap")
 
 
+@pytest.mark.parametrize("m,k,split_k", [(16, 128, 1), (5, 384, 1), (32, 640, 5), (64, 896, 2), (16, 1152, 9)])
+def test_mxfp8_swap_short_units(bs, orc, cuda, m, k, split_k):
+    """Units of 1, 3 and odd numbers of K blocks (including split-K slices of one K block): the
+    transposed kernel accumulates alternate K blocks in two TMEM chains and sums only the chains a
+    unit reached."""
+    run_mxfp8(bs, orc, cuda, m, 384, k, seed=200 + k + split_k, sf_mode="rowpattern", split_k=split_k,
+              kernel="swap")
+
+
+@pytest.mark.parametrize("m,k,split_k", [(1, 256, 1), (16, 768, 1), (40, 1280, 5)])
+def test_mxfp4_swap_short_units(bs, orc, cuda, m, k, split_k):
+    qa, qb, sa, sb = mxfp4_problem(orc, m, 512, k, 300 + k, "kpattern")
+    ref, mag = orc.gemm_mxfp4(qa, qb, sa, sb)
+    out = poisoned((m, 512), torch.bfloat16, cuda)
+    bs.gemm_a4w4_mxfp4(dev_u8(qa, cuda), dev_u8(orc.shuffle_weight16(qb), cuda), dev_u8(sa, cuda), dev_u8(sb, cuda),
+                       out=out, kernel="swap", b_format="shuffle16", split_k=split_k)
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    assert_close(orc, ref, out.float().cpu().numpy(), mag, f"mxfp4 swap {m}x512x{k} split {split_k}")
+
+
 @pytest.mark.parametrize("m", [1, 16, 64])
 def test_mxfp4_swap_decode_shuffled(bs, orc, cuda, m):
     qa, qb, sa, sb = mxfp4_problem(orc, m, 768, 2048, 95 + m, "kpattern")
@@ -370,6 +391,13 @@ def test_fp8_block_swap_raw_b_fp32_split(bs, orc, cuda):
     ref, got = run_fp8_block(bs, orc, cuda, 24, 640, 1536, seed=50, kpanel=False, kernel="swap",
                              split_k=3, out_dtype=torch.float32)
     np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("m,k,split_k", [(16, 128, 1), (1, 384, 1), (30, 640, 5), (64, 384, 3), (8, 1152, 9)])
+def test_fp8_block_swap_short_units(bs, orc, cuda, m, k, split_k):
+    """Units of 1 and 3 K blocks and split-K slices of one K block: the two promotion sets take
+    alternate K blocks, so a set may see none of a unit's K blocks and still hand over zeros."""
+    run_fp8_block(bs, orc, cuda, m, 640, k, seed=70 + k + split_k, kernel="swap", split_k=split_k)
 
 
 @pytest.mark.parametrize("m,kernel", [(16, "swap"), (48, "swap"), (200, "1cta")])
