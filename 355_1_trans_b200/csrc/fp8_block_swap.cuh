@@ -15,13 +15,14 @@
 // MMA rarely waits for the promotion warps, and the small stages (16 KB of B
 // + MN x 128 B of A) allow a deep TMA pipeline: the kernel is bound by the B
 // stream from HBM.  The per-K-block scales (MN values of sfa and one sfb)
-// are staged into shared memory by the producer warp with asynchronous 4-byte
-// copies into a ring of kStages + kAccBufs slots -- as many K blocks as can be
-// between the producer and the promotion -- so neither the producer nor the
-// promotion ever waits on a global scale load.
+// are staged into shared memory by the producers with asynchronous 4-byte
+// copies into a ring of 32 slots -- more K blocks than can sit between the
+// producers and the promotion -- so neither ever waits on a global scale load.
 //
 // Roles: warps 0, 2 and 3 TMA producers (every third K block each, with its
-// scales), warp 1 MMA, warp 2 also allocates TMEM, warps 4.. promotion.
+// scales), warp 1 MMA (one elected thread runs the role), warp 2 also
+// allocates TMEM, warps 4-11 promotion (two sets on alternate K blocks for
+// MN <= 32, two column halves for MN = 64).
 #pragma once
 
 #include "fp8_block_gemm.cuh"
