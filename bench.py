@@ -55,6 +55,19 @@ def load_peaks():
     return PEAKS_FALLBACK, "fallback"
 
 
+L2_BYTES = 126 * 1024 * 1024
+
+
+def l2_policy(m, in_bytes):
+    """(flush L2 before every timed call, the call is bound by the weight
+    stream).  Inputs that fit in L2 are flushed.  Skinny calls (M <= 128)
+    stream their weights from HBM, so their roofline is bandwidth, and their
+    inputs are flushed unless they exceed twice the L2: weights left in L2 by
+    the previous call would otherwise inflate the bandwidth."""
+    hbm_bound = m <= 128
+    return in_bytes < (2 * L2_BYTES if hbm_bound else L2_BYTES), hbm_bound
+
+
 def load_traffic(workload, m, n, k, b_format):
     """DRAM bytes (read + write) of one launch of the workload's dominant
     kernel from the committed ncu capture (profiles/dram_traffic.json), when
@@ -437,13 +450,8 @@ def run_ours(args):
     # the GEMM alone (the flush also lets the host enqueue the next call, so a
     # short kernel is not timed behind its own launch).  Larger inputs stream
     # from HBM on every call anyway.
-    # Skinny (M <= 128) calls are bound by the weight stream from HBM: their
-    # inputs are flushed unless they exceed twice the L2, so that weights left
-    # in L2 by the previous call cannot inflate the bandwidth.
-    l2_bytes = 126 * 1024 * 1024
-    hbm_bound = m <= 128
     in_bytes = a_bytes + b_bytes + sf_bytes
-    flush_l2 = in_bytes < (2 * l2_bytes if hbm_bound else l2_bytes)
+    flush_l2, hbm_bound = l2_policy(m, in_bytes)
     if flush_l2:
         flush_buf = torch.ones(64 << 20, dtype=torch.float32, device=dev)   # 256 MiB
         flush_sink = torch.empty((), dtype=torch.float32, device=dev)

@@ -146,3 +146,21 @@ def test_shipped_tuned_table_loads():
     t = tuning.TunedTable.load(tuning.DEFAULT_TABLE)
     sel = t.lookup("fp8_block", 16, 7168, 18432)
     assert sel is not None and sel[0] in tuning.KERNEL_NAMES.values()
+
+
+def test_bench_l2_policy():
+    """bench.py flushes L2 before every timed call when the inputs fit in it,
+    and for skinny (weight-stream-bound) calls when they fit in twice the L2."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", Path(__file__).resolve().parents[1] / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    mb = 1024 * 1024
+    # MXFP8 8192^3: 138 MB of inputs, compute-bound -> no flush
+    assert bench.l2_policy(8192, 138 * mb) == (False, False)
+    # MXFP4 8192^3: 71 MB of inputs fit in L2 -> flush
+    assert bench.l2_policy(8192, 71 * mb) == (True, False)
+    # decode M=16 N=7168 K=18432: 132 MB < 2 x L2 -> flush, bandwidth roofline
+    assert bench.l2_policy(16, 132 * mb) == (True, True)
+    # skinny call streaming 300 MB of weights -> no flush needed
+    assert bench.l2_policy(64, 300 * mb) == (False, True)
