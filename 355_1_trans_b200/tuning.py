@@ -21,8 +21,11 @@ installs a table that the "auto" calls of this package consult.
 tuned/b200_sm100a.csv (next to this module) was produced on a B200 by
 `python bench.py --tune <csv>`: the fp8 block-scale decode/prefill shapes
 M in {1, 16, 64, 128, 1024} x (N, K) in {(7168, 2048), (4096, 7168),
-(24576, 1536), (7168, 18432)} and the skinny MX shapes M in {1, 16, 64, 128,
-1024} x N = K = 8192.  It is opt-in: `use_tuned(DEFAULT_TABLE)`.
+(24576, 1536), (7168, 18432)}; the (N, K) groups of the reference's traced
+DeepSeek-V4 a8w8 shapes (dsv4_a8w8_all_traced_shapes.csv) at M in {1, 16,
+64, 128, 256, 512, 1024, 2048, 4096} (and 8192, 16384 for (7168, 7168)); and
+the skinny MX shapes M in {1, 16, 64, 128, 1024} x N = K = 8192.  It is
+opt-in: `use_tuned(DEFAULT_TABLE)`.
 """
 from __future__ import annotations
 
@@ -100,8 +103,9 @@ def _graph_time(fn, reps, rounds):
     return statistics.median(ts)
 
 
-def candidates(family: str, m: int, k: int):
-    """(kernel, split_k) pairs worth timing for a shape."""
+def candidates(family: str, m: int, k: int, n: int | None = None, sms: int = 148):
+    """(kernel, split_k) pairs worth timing for a shape.  Split-K is tried
+    only while a kernel's output tiles leave SMs idle (with n unknown, always)."""
     num_kb = k // (256 if family == "mxfp4" else 128)
     splits = [s for s in (1, 2, 3, 4, 6, 8, 12, 16) if s <= num_kb]
     out = [("auto", 0)]
@@ -111,8 +115,13 @@ def candidates(family: str, m: int, k: int):
     if family != "fp8_block" and m >= 256:
         kernels.append("pair")
     for kern in kernels:
+        tiles = None
+        if n is not None:
+            tiles = -(-n // 128) * (1 if kern == "swap" else -(-m // 128))
         for s in splits:
             if kern == "pair" and s > 1:
+                continue
+            if s > 1 and tiles is not None and tiles >= sms:
                 continue
             out.append((kern, s))
     return out
@@ -137,7 +146,7 @@ def tune(family: str, shapes, make_call, *, reps: int = 10, rounds: int = 5, gfx
     for (m, n, k) in shapes:
         ref = make_call(m, n, k, "1cta", 1)().float()
         best = None
-        for kern, split in candidates(family, m, k):
+        for kern, split in candidates(family, m, k, n, cu_num):
             call = make_call(m, n, k, kern, split)
             try:
                 out = call()

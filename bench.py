@@ -822,25 +822,39 @@ def run_quant(args):
     return 0
 
 
+# (N, K) groups of the reference's traced DeepSeek-V4 a8w8 deployment shapes
+# (dsv4_a8w8_all_traced_shapes.csv: 125 rows, M from 6 to 16384), tuned at
+# power-of-two M buckets: a call takes the row of the smallest tuned M >= its M.
+DSV4_NK = ((1536, 7168), (2048, 7168), (6144, 7168), (7168, 3072), (7168, 7168), (7168, 16384), (7168, 21504),
+           (8192, 1536), (65536, 1536))
+DSV4_M = (1, 16, 64, 128, 256, 512, 1024, 2048, 4096)
+
+
 def run_tune(args):
-    """Tuned table for the fp8 block-scale sweep shapes (M <= 8192 of the
-    decode/prefill grid) and the skinny MX shapes M in {1, 16, 64, 128, 1024},
-    N = K = 8192; written in the aiter tuned-CSV schema."""
+    """Tuned table for the fp8 block-scale sweep shapes (M <= 1024 of the
+    decode/prefill grid), the DeepSeek-V4 (N, K) groups at power-of-two M
+    buckets, and the skinny MX shapes M in {1, 16, 64, 128, 1024}, N = K = 8192;
+    written in the aiter tuned-CSV schema."""
     import torch
     dev = torch.device("cuda", 0)
     bs = importlib.import_module("355_1_trans_b200")
     tuning = importlib.import_module("355_1_trans_b200.tuning")
     rows = []
-    for (n, k) in ((7168, 2048), (4096, 7168), (24576, 1536), (7168, 18432)):
-        qa_full, qb, sa_full, sb = make_fp8block_inputs(8192, n, k, dev, 7)
+    groups = [((n, k), (1, 16, 64, 128, 1024)) for (n, k) in ((7168, 2048), (4096, 7168), (24576, 1536), (7168, 18432))]
+    groups += [((n, k), DSV4_M + ((8192, 16384) if (n, k) == (7168, 7168) else ())) for (n, k) in DSV4_NK
+               if (n, k) not in {g[0] for g in groups}]
+    for (n, k), ms in groups:
+        qa_full, qb, sa_full, sb = make_fp8block_inputs(max(ms), n, k, dev, 7)
 
-        def make_call(m, n_, k_, kernel, split):
+        def make_call(m, n_, k_, kernel, split, qa_full=qa_full, qb=qb, sa_full=sa_full, sb=sb):
             qa, sa = qa_full[:m].contiguous(), sa_full[:m].contiguous()
             out = torch.empty(m, n_, dtype=torch.bfloat16, device=dev)
             return lambda: bs.gemm_a8w8_bpreshuffle(qa, qb, sa, sb, torch.bfloat16, preshuffled=True, out=out,
                                                     kernel=kernel, split_k=split)
 
-        rows += tuning.tune("fp8_block", [(m, n, k) for m in (1, 16, 64, 128, 1024)], make_call)
+        rows += tuning.tune("fp8_block", [(m, n, k) for m in ms], make_call)
+        del qa_full, qb, sa_full, sb
+        torch.cuda.empty_cache()
     for fp4 in (False, True):
         n = k = 8192
         qa_full, qb, sa_full, sb = make_mx_inputs(bs, 1024, n, k, fp4, "tn", dev, 3)
