@@ -146,6 +146,15 @@ def test_shipped_tuned_table_loads():
     t = tuning.TunedTable.load(tuning.DEFAULT_TABLE)
     sel = t.lookup("fp8_block", 16, 7168, 18432)
     assert sel is not None and sel[0] in tuning.KERNEL_NAMES.values()
+    # every (N, K) group of the traced DeepSeek-V4 shapes is tuned, with an M
+    # bucket that covers the traced M range (6 .. 4096, or 16384)
+    for n, k in ((1536, 7168), (2048, 7168), (6144, 7168), (7168, 3072), (7168, 7168), (7168, 16384),
+                 (7168, 21504), (8192, 1536), (65536, 1536)):
+        for m in (6, 66, 300, 4096):
+            sel = t.lookup("fp8_block", m, n, k)
+            assert sel is not None and sel[0] in tuning.KERNEL_NAMES.values(), (m, n, k)
+        # a swap-kernel row is only ever chosen for M <= 64
+        assert t.lookup("fp8_block", 4096, n, k)[0] != "swap"
 
 
 def test_bench_l2_policy():
