@@ -72,6 +72,7 @@ def lib() -> ctypes.CDLL:
         "bsgemm_a8w8_mxfp8": (I, [ctypes.POINTER(Args), P]),
         "bsgemm_a4w4_mxfp4": (I, [ctypes.POINTER(Args), P]),
         "bsgemm_a8w8_blockscale_bpreshuffle": (I, [ctypes.POINTER(Args), P]),
+        "bsgemm_a8w8_blockscale_grouped": (I, [ctypes.POINTER(Args), P, I, P]),
         "bsgemm_workspace_size": (S, [I, ctypes.POINTER(Args)]),
         "bsgemm_pack_b": (I, [P, P, I, I, I, I, P]),
         "bsgemm_pack_scales": (I, [P, I, P, I, I, I, I, P]),
@@ -356,6 +357,70 @@ def gemm_a8w8_bpreshuffle(A, B, x_scale, w_scale, out_dtype=torch.bfloat16, *,
         status = lib().bsgemm_a8w8_blockscale_bpreshuffle(ctypes.byref(args), _stream(A.device))
         _record((*tensors, out, ws), A.device)
     _check(status, "bsgemm_a8w8_blockscale_bpreshuffle")
+    return out
+
+
+def gemm_a8w8_blockscale_grouped(A, B, x_scale, w_scale, group_offsets, max_rows: int,
+                                 out_dtype=torch.bfloat16, *, out=None, b_layout: str = "kpanel",
+                                 grid_blocks: int = 0):
+    """Grouped (MoE) a8w8 GEMM with fp32 1x128 / 128x128 block scales.
+
+    The tokens of all groups (experts) are concatenated: A [T, K] E4M3 and
+    x_scale [T, K/128]; group e owns rows group_offsets[e] .. group_offsets[e+1]
+    (an int32 CUDA tensor of E + 1 offsets, as the routing writes it) and is
+    multiplied by its own weights B[e] (layout b_layout, as in
+    gemm_a8w8_bpreshuffle: B [E, K/128, N, 128] or [E, N, K]) with w_scale[e]
+    [N/128, K/128].  max_rows bounds the rows of any group.  Returns C [T, N];
+    rows outside every group are left unwritten."""
+    if b_layout not in ("kpanel", "shuffle16", "raw"):
+        raise ValueError("b_layout must be 'kpanel', 'shuffle16' or 'raw'")
+    tensors = (A, B, x_scale, w_scale, group_offsets)
+    if A.dim() != 2 or not A.is_cuda or any(t.device != A.device for t in tensors):
+        raise ValueError("A must be [T, K] and all inputs on the same GPU")
+    if A.dtype not in _FP8 or B.dtype not in _FP8:
+        raise ValueError("A/B must hold E4M3FN bytes")
+    if x_scale.dtype != torch.float32 or w_scale.dtype != torch.float32:
+        raise ValueError("scales must be fp32")
+    if group_offsets.dtype != torch.int32 or group_offsets.dim() != 1 or not group_offsets.is_contiguous():
+        raise ValueError("group_offsets must be a contiguous int32 tensor of E + 1 offsets")
+    t_rows, k = A.shape
+    groups = group_offsets.numel() - 1
+    if groups < 1 or B.shape[0] != groups or w_scale.dim() != 3 or w_scale.shape[0] != groups:
+        raise ValueError("B and w_scale need one entry per group")
+    if not B.is_contiguous():
+        raise ValueError("B must be contiguous")
+    n = B.shape[2] if (b_layout == "kpanel" and B.dim() == 4) else B.shape[1]
+    if B[0].numel() != n * k:
+        raise ValueError("B and A disagree on K")
+    kblk = k // 128
+    if tuple(x_scale.shape) != (t_rows, kblk) or x_scale.stride(1) != 1:
+        raise ValueError("x_scale must be [T, K/128]")
+    if tuple(w_scale.shape[1:]) != ((n + 127) // 128, kblk) or w_scale.stride(2) != 1:
+        raise ValueError("w_scale must be [E, N/128, K/128]")
+    if max_rows < 1:
+        raise ValueError("max_rows must be positive")
+    out = _out(out, t_rows, n, out_dtype, A.device, 1)
+    args = Args()
+    lib().bsgemm_args_init(ctypes.byref(args))
+    args.ptr_a, args.ptr_b, args.ptr_c = A.data_ptr(), B.data_ptr(), out.data_ptr()
+    args.m, args.n, args.k, args.batch = int(max_rows), n, k, groups
+    args.stride_a, args.stride_c = A.stride(0), n
+    args.stride_b = 128 if b_layout == "kpanel" else k
+    args.stride_b_batch = B.stride(0)
+    args.b_format = {"kpanel": B_KPANEL128, "shuffle16": B_SHUFFLE16, "raw": B_RAW}[b_layout]
+    args.ptr_sfa, args.ptr_sfb = x_scale.data_ptr(), w_scale.data_ptr()
+    args.sfa_format = args.sfb_format = SF_ROWMAJOR
+    args.stride_sfa = x_scale.stride(0)
+    args.stride_sfb = w_scale.stride(1)
+    args.stride_sfb_batch = w_scale.stride(0)
+    args.layout = LAYOUTS["tn"]
+    args.out_dtype = OUT_BF16 if out_dtype == torch.bfloat16 else OUT_FP32
+    args.grid_blocks = grid_blocks
+    with torch.cuda.device(A.device):
+        status = lib().bsgemm_a8w8_blockscale_grouped(ctypes.byref(args), ctypes.c_void_p(group_offsets.data_ptr()),
+                                                      t_rows, _stream(A.device))
+        _record((*tensors, out), A.device)
+    _check(status, "bsgemm_a8w8_blockscale_grouped")
     return out
 
 

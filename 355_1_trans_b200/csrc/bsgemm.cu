@@ -962,6 +962,27 @@ int swap_launch_mn(int fmt, bool f32, const CUtensorMap& ta, const CUtensorMap& 
   }
 }
 
+// Tensor map of the fp8 block-scale weights (batch = experts for grouped
+// calls): shuffle_weight(16,16), K panels B'[K/128][N][128], or raw [N, K].
+bool make_fp8b_weight_tmap(CUtensorMap* tb, const bsgemm_args& a, bool kpanel, bool shuf, int kb,
+                           long long b_elems) {
+  if (shuf) return make_shuffle16_tmap(tb, a.ptr_b, a.n, a.k, a.stride_b_batch, a.batch, 128u);
+  if (kpanel) {
+    const uint64_t dims[4] = {128u, static_cast<uint64_t>(a.n), static_cast<uint64_t>(kb),
+                              static_cast<uint64_t>(a.batch)};
+    const uint64_t strides[3] = {128u, static_cast<uint64_t>(a.n) * 128u,
+                                 static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch : b_elems)};
+    const uint32_t box[4] = {128u, 128u, 1u, 1u};
+    return make_tmap_u8(tb, a.ptr_b, 4, dims, strides, box, true);
+  }
+  const uint64_t dims[3] = {static_cast<uint64_t>(a.k), static_cast<uint64_t>(a.n),
+                            static_cast<uint64_t>(a.batch)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_b),
+                               static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch : b_elems)};
+  const uint32_t box[3] = {128u, 128u, 1u};
+  return make_tmap_u8(tb, a.ptr_b, 3, dims, strides, box, true);
+}
+
 int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
   int rc = validate_common(args);
   if (rc != BSG_OK) return rc;
@@ -1041,23 +1062,7 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
     const uint32_t box[3] = {128u, swap ? static_cast<uint32_t>(swap_mn(a.m)) : 128u, 1u};
     if (!make_tmap_u8(&ta, a.ptr_a, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
   }
-  if (shuf) {
-    if (!make_shuffle16_tmap(&tb, a.ptr_b, a.n, a.k, a.stride_b_batch, a.batch, 128u)) return BSG_ERR_CUDA;
-  } else if (kpanel) {
-    const uint64_t dims[4] = {128u, static_cast<uint64_t>(a.n), static_cast<uint64_t>(kb),
-                              static_cast<uint64_t>(a.batch)};
-    const uint64_t strides[3] = {128u, static_cast<uint64_t>(a.n) * 128u,
-                                 static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch : b_elems)};
-    const uint32_t box[4] = {128u, 128u, 1u, 1u};
-    if (!make_tmap_u8(&tb, a.ptr_b, 4, dims, strides, box, true)) return BSG_ERR_CUDA;
-  } else {
-    const uint64_t dims[3] = {static_cast<uint64_t>(a.k), static_cast<uint64_t>(a.n),
-                              static_cast<uint64_t>(a.batch)};
-    const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_b),
-                                 static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch : b_elems)};
-    const uint32_t box[3] = {128u, 128u, 1u};
-    if (!make_tmap_u8(&tb, a.ptr_b, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
-  }
+  if (!make_fp8b_weight_tmap(&tb, a, kpanel, shuf, kb, b_elems)) return BSG_ERR_CUDA;
   Fp8BlockParams p{};
   p.m = a.m;
   p.n = a.n;
@@ -1103,6 +1108,119 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
   return BSG_OK;
 }
 
+template <int kBFmt, bool kOutF32>
+int fp8b_grouped_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockParams& p, int grid,
+                          cudaStream_t st) {
+  using Cfg = Fp8BlockCfg<128>;
+  auto* kern = bsg::fp8_block_gemm_kernel<128, kBFmt, kOutF32, true>;
+  if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
+  const int rc = launch_pdl(kern, grid, 256, Cfg::kSmemBytes, st, ta, tb, p);
+  return rc != BSG_OK ? rc : launch_status();
+}
+
+// Grouped (MoE) fp32 block-scale GEMM on the 1-CTA kernel.  a.batch groups
+// (experts): group e multiplies rows [offsets[e], offsets[e + 1]) of the
+// concatenated A [total_rows, K] (and the same rows of x_scale) by its own
+// weights B_e and their scales, and writes the same rows of C [total_rows, N].
+// a.m bounds the rows of one group (it sizes the tile grid); the offsets are
+// read on the device, so the routing needs no host round trip.
+int fp8b_grouped_run(const bsgemm_args* args, const int* group_offsets, int total_rows, cudaStream_t st) {
+  if (!args || !group_offsets || total_rows <= 0) return BSG_ERR_INVALID_VALUE;
+  const bsgemm_args& a = *args;
+  if (!a.ptr_a || !a.ptr_b || !a.ptr_c || !a.ptr_sfa || !a.ptr_sfb) return BSG_ERR_INVALID_VALUE;
+  if (a.m <= 0 || a.n <= 0 || a.k <= 0 || a.batch <= 0 || a.grid_blocks < 0 || a.split_k < 0)
+    return BSG_ERR_INVALID_VALUE;
+  if (a.out_dtype != BSG_OUT_BF16 && a.out_dtype != BSG_OUT_FP32) return BSG_ERR_INVALID_VALUE;
+  if (a.split_k > 1) return BSG_ERR_UNSUPPORTED;
+  if (a.kernel != BSG_KERNEL_AUTO && a.kernel != BSG_KERNEL_1CTA) return BSG_ERR_UNSUPPORTED;
+  if (a.layout != BSG_LAYOUT_TN) return BSG_ERR_UNSUPPORTED;
+  if (a.sfa_format != BSG_SF_ROWMAJOR || a.sfb_format != BSG_SF_ROWMAJOR) return BSG_ERR_UNSUPPORTED;
+  if (a.b_format != BSG_B_RAW && a.b_format != BSG_B_KPANEL128 && a.b_format != BSG_B_SHUFFLE16)
+    return BSG_ERR_UNSUPPORTED;
+  DevInfo dev;
+  int rc;
+  if ((rc = device_info(&dev)) != BSG_OK) return rc;
+  if (!dev.sm100) return BSG_ERR_ARCH;
+  if (a.k % 128) return BSG_ERR_INVALID_VALUE;
+  const int vec = a.out_dtype == BSG_OUT_BF16 ? 8 : 4;
+  if (a.n % vec || a.stride_c < a.n || a.stride_c % vec || !aligned16(a.ptr_c)) return BSG_ERR_ALIGNMENT;
+  const bool kpanel = a.b_format == BSG_B_KPANEL128;
+  const bool shuf = a.b_format == BSG_B_SHUFFLE16;
+  const int bfmt = kpanel ? bsg::kFmtKPanel : shuf ? bsg::kFmtShuffle16 : bsg::kFmtRaw;
+  const int kb = a.k / 128, nb = (a.n + 127) / 128;
+  if (a.stride_a < a.k || a.stride_a % 16 || !aligned16(a.ptr_a) || !aligned16(a.ptr_b))
+    return BSG_ERR_ALIGNMENT;
+  if (kpanel ? a.stride_b != 128 : (a.stride_b < a.k || a.stride_b % 16)) return BSG_ERR_ALIGNMENT;
+  if (shuf && (a.stride_b != a.k || a.n % 16)) return BSG_ERR_INVALID_VALUE;
+  const long long b_elems = kpanel ? static_cast<long long>(a.n) * a.k : static_cast<long long>(a.n) * a.stride_b;
+  if (a.batch > 1 && (a.stride_b_batch < b_elems || a.stride_b_batch % 16)) return BSG_ERR_INVALID_VALUE;
+  if (a.stride_sfa < kb || a.stride_sfb < kb) return BSG_ERR_INVALID_VALUE;
+  if (a.batch > 1 && a.stride_sfb_batch < static_cast<long long>(nb) * kb) return BSG_ERR_INVALID_VALUE;
+  const uint64_t c_bytes =
+      static_cast<uint64_t>(total_rows) * a.stride_c * (a.out_dtype == BSG_OUT_BF16 ? 2 : 4);
+  const uint64_t b_bytes = static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch * (a.batch - 1) : 0) + b_elems;
+  const uint64_t sfb_bytes = 4ull * (a.batch > 1 ? a.stride_sfb_batch * a.batch : static_cast<long long>(nb) * kb);
+  if (overlaps(a.ptr_c, c_bytes, a.ptr_a, static_cast<uint64_t>(total_rows) * a.stride_a) ||
+      overlaps(a.ptr_c, c_bytes, a.ptr_b, b_bytes) ||
+      overlaps(a.ptr_c, c_bytes, a.ptr_sfa, 4ull * total_rows * a.stride_sfa) ||
+      overlaps(a.ptr_c, c_bytes, a.ptr_sfb, sfb_bytes) ||
+      overlaps(a.ptr_c, c_bytes, group_offsets, 4ull * (a.batch + 1)))
+    return BSG_ERR_INVALID_VALUE;
+
+  CUtensorMap ta, tb;
+  {
+    // A over all rows of all groups; a tile that runs past its group's last
+    // row reads the next group's rows (or zero fill past total_rows), and
+    // those rows are not stored
+    const uint64_t dims[3] = {static_cast<uint64_t>(a.k), static_cast<uint64_t>(total_rows), 1u};
+    const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_a),
+                                 static_cast<uint64_t>(total_rows) * static_cast<uint64_t>(a.stride_a)};
+    const uint32_t box[3] = {128u, 128u, 1u};
+    if (!make_tmap_u8(&ta, a.ptr_a, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
+  }
+  if (!make_fp8b_weight_tmap(&tb, a, kpanel, shuf, kb, b_elems)) return BSG_ERR_CUDA;
+  Fp8BlockParams p{};
+  p.m = a.m;
+  p.n = a.n;
+  p.k = a.k;
+  p.batch = a.batch;
+  p.num_kb = kb;
+  p.tiles_m = (a.m + 127) / 128;
+  p.tiles_n = nb;
+  p.split_k = 1;
+  p.kb_per_split = kb;
+  p.total_units = p.tiles_m * p.tiles_n * a.batch;
+  p.group_m = std::min(p.tiles_m, kGroupM);
+  p.sfa = static_cast<const float*>(a.ptr_sfa);
+  p.sfa_m = a.stride_sfa;
+  p.sfa_k = 1;
+  p.sfa_batch = 0;
+  p.sfb = static_cast<const float*>(a.ptr_sfb);
+  p.sfb_n = a.stride_sfb;
+  p.sfb_k = 1;
+  p.sfb_batch = a.stride_sfb_batch;
+  p.c = a.ptr_c;
+  p.ldc = a.stride_c;
+  p.c_batch_stride = 0;
+  p.ws = nullptr;
+  p.timeout_ns = kTimeoutNs;
+  p.group_offsets = group_offsets;
+  p.total_rows = total_rows;
+  const int grid = grid_for(p.total_units, dev, a.grid_blocks);
+  const bool f32 = a.out_dtype == BSG_OUT_FP32;
+  switch (bfmt) {
+    case bsg::kFmtKPanel:
+      return f32 ? fp8b_grouped_launch_t<bsg::kFmtKPanel, true>(ta, tb, p, grid, st)
+                 : fp8b_grouped_launch_t<bsg::kFmtKPanel, false>(ta, tb, p, grid, st);
+    case bsg::kFmtShuffle16:
+      return f32 ? fp8b_grouped_launch_t<bsg::kFmtShuffle16, true>(ta, tb, p, grid, st)
+                 : fp8b_grouped_launch_t<bsg::kFmtShuffle16, false>(ta, tb, p, grid, st);
+    default:
+      return f32 ? fp8b_grouped_launch_t<bsg::kFmtRaw, true>(ta, tb, p, grid, st)
+                 : fp8b_grouped_launch_t<bsg::kFmtRaw, false>(ta, tb, p, grid, st);
+  }
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -1131,6 +1249,11 @@ int bsgemm_a4w4_mxfp4(const bsgemm_args* args, bsg_stream_t stream) {
 
 int bsgemm_a8w8_blockscale_bpreshuffle(const bsgemm_args* args, bsg_stream_t stream) {
   return fp8b_run(args, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int bsgemm_a8w8_blockscale_grouped(const bsgemm_args* args, const int* group_offsets, int total_rows,
+                                   bsg_stream_t stream) {
+  return fp8b_grouped_run(args, group_offsets, total_rows, reinterpret_cast<cudaStream_t>(stream));
 }
 
 size_t bsgemm_workspace_size(int family, const bsgemm_args* args) {

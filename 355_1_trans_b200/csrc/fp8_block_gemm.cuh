@@ -42,7 +42,24 @@ struct Fp8BlockParams {
   long long c_batch_stride;
   float* ws;
   unsigned long long timeout_ns;
+  // grouped (MoE) calls: group b owns rows [offsets[b], offsets[b + 1]) of the
+  // concatenated A, its scales and C; total_rows bounds those arrays
+  const int* group_offsets;
+  int total_rows;
 };
+
+// First row and row count of group b in a grouped call.  The offsets come
+// from device memory written by the caller (the token routing); they are
+// clamped to [0, total_rows] and a group to p.m rows, so an inconsistent
+// offsets array cannot address outside A, its scales or C.
+__device__ __forceinline__ void group_rows(const Fp8BlockParams& p, int b, int& row0, int& rows) {
+  int a0 = __ldg(p.group_offsets + b);
+  int a1 = __ldg(p.group_offsets + b + 1);
+  a0 = min(max(a0, 0), p.total_rows);
+  a1 = min(max(a1, a0), p.total_rows);
+  row0 = a0;
+  rows = min(a1 - a0, p.m);
+}
 
 // Weight (B) storage formats read in place:
 //   kFmtRaw        [N, K] K-major rows (128B-swizzled stage tiles);
@@ -77,7 +94,11 @@ struct Fp8BlockCfg {
   static constexpr uint32_t kTmemCols = 2u * BN;  // two accumulator buffers
 };
 
-template <int BN, int kBFmt, bool kOutF32>
+// kGrouped: the batch index is a group (expert) whose rows of A, sfa and C
+// start at group_offsets[b] (A's tensor map spans all total_rows); tiles past
+// a group's rows are skipped by every role alike, and B, sfb keep their
+// per-group batch strides.  Grouped calls run without split-K.
+template <int BN, int kBFmt, bool kOutF32, bool kGrouped = false>
 __global__ void __launch_bounds__(256, 1)
     fp8_block_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                           const __grid_constant__ CUtensorMap tmB, const Fp8BlockParams p) {
@@ -143,6 +164,14 @@ __global__ void __launch_bounds__(256, 1)
     for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
       int b, mt, nt, s;
       decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+      int a_row = mt * 128, a_batch = b;
+      if constexpr (kGrouped) {
+        int row0, rows;
+        group_rows(p, b, row0, rows);
+        if (mt * 128 >= rows) continue;   // this group has no rows in the tile
+        a_row = row0 + mt * 128;
+        a_batch = 0;
+      }
       const int kb0 = s * p.kb_per_split;
       const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
       for (int kb = kb0; kb < kb1; ++kb) {
@@ -153,7 +182,7 @@ __global__ void __launch_bounds__(256, 1)
         uint64_t* fb = &full_bar[stage];
         if (issuer) {
           mbar_arrive_expect_tx(fb, Cfg::kStageBytes);
-          tma_load_3d(sA + stage * Cfg::kABytes, &tmA, fb, kb * 128, mt * 128, b);
+          tma_load_3d(sA + stage * Cfg::kABytes, &tmA, fb, kb * 128, a_row, a_batch);
           if constexpr (kBFmt == kFmtKPanel)
             tma_load_4d(sB + stage * Cfg::kBBytes, &tmB, fb, 0, nt * BN, kb, b);
           else if constexpr (kBFmt == kFmtShuffle16)
@@ -192,6 +221,11 @@ __global__ void __launch_bounds__(256, 1)
     for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
       int b, mt, nt, s;
       decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+      if constexpr (kGrouped) {
+        int row0, rows;
+        group_rows(p, b, row0, rows);
+        if (mt * 128 >= rows) continue;
+      }
       const int kb0 = s * p.kb_per_split;
       const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
       for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
@@ -239,13 +273,19 @@ __global__ void __launch_bounds__(256, 1)
       decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
       const int kb0 = s * p.kb_per_split;
       const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
+      int row0 = 0, rows = p.m;   // the group's first row and rows (the whole M when not grouped)
+      if constexpr (kGrouped) {
+        group_rows(p, b, row0, rows);
+        if (mt * 128 >= rows) continue;
+      }
       const int row = mt * 128 + q * 32 + static_cast<int>(lane);
-      const bool row_ok = row < p.m;
+      const bool row_ok = row < rows;
       // a lane quarter whose 32 rows all lie beyond M (decode shapes) skips
       // the promotion work but still releases the buffers
-      const bool quarter_live = mt * 128 + q * 32 < p.m;
+      const bool quarter_live = mt * 128 + q * 32 < rows;
       const int n0 = nt * BN;
-      const float* sfa_row = p.sfa + b * p.sfa_batch + static_cast<long long>(row_ok ? row : 0) * p.sfa_m;
+      const long long grow = static_cast<long long>(row0) + row;   // row in A, sfa and C
+      const float* sfa_row = (kGrouped ? p.sfa : p.sfa + b * p.sfa_batch) + (row_ok ? grow : 0) * p.sfa_m;
       const float* sfb_blk = p.sfb + b * p.sfb_batch + static_cast<long long>(n0 / 128) * p.sfb_n;
       float acc[BN];
 #pragma unroll
@@ -301,8 +341,7 @@ __global__ void __launch_bounds__(256, 1)
               if (col0 + v < p.n) dst[v] = acc[c * 32 + v];
           }
         } else if constexpr (kOutF32) {
-          float* dst = reinterpret_cast<float*>(p.c) + b * p.c_batch_stride +
-                       static_cast<long long>(row) * p.ldc + col0;
+          float* dst = reinterpret_cast<float*>(p.c) + (kGrouped ? 0 : b * p.c_batch_stride) + grow * p.ldc + col0;
           if (full) {
 #pragma unroll
             for (int v = 0; v < 8; ++v)
@@ -316,8 +355,7 @@ __global__ void __launch_bounds__(256, 1)
               if (col0 + v < p.n) dst[v] = acc[c * 32 + v];
           }
         } else {
-          uint16_t* dst = reinterpret_cast<uint16_t*>(p.c) + b * p.c_batch_stride +
-                          static_cast<long long>(row) * p.ldc + col0;
+          uint16_t* dst = reinterpret_cast<uint16_t*>(p.c) + (kGrouped ? 0 : b * p.c_batch_stride) + grow * p.ldc + col0;
           if (full) {
             uint32_t w[16];
 #pragma unroll

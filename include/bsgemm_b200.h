@@ -170,6 +170,25 @@ BSG_API int bsgemm_a4w4_mxfp4(const bsgemm_args *args, bsg_stream_t stream);
 BSG_API int bsgemm_a8w8_blockscale_bpreshuffle(const bsgemm_args *args, bsg_stream_t stream);
 
 /*
+ * Grouped (MoE) FP8 block-scale GEMM: args->batch groups (experts), group e
+ * multiplying rows [group_offsets[e], group_offsets[e+1]) of a concatenated
+ * A E4M3 [total_rows, K] (and the same rows of SFA fp32 [total_rows, K/128],
+ * BSG_SF_ROWMAJOR) by its own weights (args->ptr_b + e * stride_b_batch in any
+ * B format above; SFB fp32 [N/128, K/128] at ptr_sfb + e * stride_sfb_batch)
+ * and writing the same rows of C [total_rows, N].  group_offsets is a DEVICE
+ * array of batch + 1 non-decreasing int32 row offsets (the token routing, so
+ * no host round trip); args->m is the most rows any group can hold (it sizes
+ * the tile grid; tiles past a group's rows are skipped).  Offsets are clamped
+ * to [0, total_rows] and a group to args->m rows, so an inconsistent array
+ * gives wrong rows, never an out-of-bounds access.  split_k must be 0 or 1;
+ * kernel AUTO or 1CTA.
+ * No launcher in the reference; its notes point at a batched mxscale GEMM
+ * (opus_gemm_splitk_and_interface_refactor.md:10, aiter PR #4320).
+ */
+BSG_API int bsgemm_a8w8_blockscale_grouped(const bsgemm_args *args, const int *group_offsets, int total_rows,
+                                           bsg_stream_t stream);
+
+/*
  * Bytes of split-K workspace the call would need (0 when it runs without
  * split-K).  family = BSG_FAMILY_*.
  */

@@ -400,6 +400,64 @@ def test_fp8_block_swap_short_units(bs, orc, cuda, m, k, split_k):
     run_fp8_block(bs, orc, cuda, m, 640, k, seed=70 + k + split_k, kernel="swap", split_k=split_k)
 
 
+# ---- grouped (MoE) fp32 block-scale GEMM ----------------------------------------------
+
+def run_fp8_block_grouped(bs, orc, cuda, sizes, n, k, *, seed, b_layout="kpanel", tail=0, max_rows=None,
+                          out_dtype=torch.bfloat16):
+    """Groups of `sizes` rows concatenated (then `tail` rows in no group); each
+    group against its own weights through the oracle.  Returns the output."""
+    offs = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int32)
+    t_rows = int(offs[-1]) + tail
+    qa, sa = orc.quant_fp8_block(orc.normal((t_rows, k), seed=seed), 1)
+    qbs, sbs = zip(*[orc.quant_fp8_block(orc.normal((n, k), seed=seed * 31 + e + 1), 128) for e in range(len(sizes))])
+    if b_layout == "kpanel":
+        bh = np.stack([orc.shuffle_kpanel(qb) for qb in qbs])
+    elif b_layout == "shuffle16":
+        bh = np.stack([orc.shuffle_weight16(qb) for qb in qbs])
+    else:
+        bh = np.stack(qbs)
+    A = dev_u8(qa, cuda).view(torch.float8_e4m3fn)
+    B = dev_u8(bh, cuda).view(torch.float8_e4m3fn)
+    SA = torch.from_numpy(sa).to(cuda)
+    SB = torch.from_numpy(np.stack(sbs)).to(cuda)
+    G = torch.from_numpy(offs).to(cuda)
+    max_rows = max_rows or max(max(sizes), 1)
+    out = poisoned((t_rows, n), out_dtype, cuda)
+    bs.gemm_a8w8_blockscale_grouped(A, B, SA, SB, G, max_rows, out_dtype, out=out, b_layout=b_layout)
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    got = out.float().cpu().numpy()
+    for e, sz in enumerate(sizes):
+        o0, done = int(offs[e]), min(sz, max_rows)
+        if done:
+            ref, mag = orc.gemm_fp8_block(qa[o0:o0 + done], qbs[e], sa[o0:o0 + done], sbs[e])
+            assert_close(orc, ref, got[o0:o0 + done], mag, f"grouped e{e} rows {sz} {b_layout}")
+        # rows of the group beyond max_rows are not computed
+        assert np.isnan(got[o0 + done:o0 + sz]).all(), f"group {e} wrote past max_rows"
+    assert np.isnan(got[int(offs[-1]):]).all(), "rows outside every group were written"
+    return got
+
+
+@pytest.mark.parametrize("sizes,n,k,b_layout,out_dtype", [
+    ((0, 5, 130, 17, 256, 1), 384, 512, "kpanel", torch.bfloat16),
+    ((64, 64, 3), 256, 1024, "raw", torch.float32),
+    ((200, 0, 40), 512, 384, "shuffle16", torch.bfloat16),
+    ((1,), 128, 128, "kpanel", torch.bfloat16),
+])
+def test_fp8_block_grouped(bs, orc, cuda, sizes, n, k, b_layout, out_dtype):
+    """Ragged groups (empty, single-row, several 128-row tiles), each against
+    its own weights, with rows after the last group left untouched."""
+    run_fp8_block_grouped(bs, orc, cuda, sizes, n, k, seed=400 + n + k, b_layout=b_layout, tail=9,
+                          out_dtype=out_dtype)
+
+
+def test_fp8_block_grouped_caps_rows_at_max_rows(bs, orc, cuda):
+    """A group longer than max_rows is computed up to max_rows rows only: the
+    kernel clamps groups, so routing offsets beyond the bound never reach
+    past the tile grid."""
+    run_fp8_block_grouped(bs, orc, cuda, (300, 20), 256, 512, seed=5, max_rows=256)
+
+
 @pytest.mark.parametrize("m,kernel", [(16, "swap"), (48, "swap"), (200, "1cta")])
 def test_fp8_block_shuffle16_b(bs, orc, cuda, m, kernel):
     """aiter shuffle_weight(16,16) weights read in place by both kernels."""
