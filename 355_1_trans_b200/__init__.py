@@ -73,6 +73,9 @@ def lib() -> ctypes.CDLL:
         "bsgemm_a4w4_mxfp4": (I, [ctypes.POINTER(Args), P]),
         "bsgemm_a8w8_blockscale_bpreshuffle": (I, [ctypes.POINTER(Args), P]),
         "bsgemm_a8w8_blockscale_grouped": (I, [ctypes.POINTER(Args), P, I, P]),
+        "bsgemm_a8w8_mxfp8_grouped": (I, [ctypes.POINTER(Args), P, I, P]),
+        "bsgemm_a4w4_mxfp4_grouped": (I, [ctypes.POINTER(Args), P, I, P]),
+        "bsgemm_mx_grouped_workspace_size": (S, [ctypes.POINTER(Args)]),
         "bsgemm_workspace_size": (S, [I, ctypes.POINTER(Args)]),
         "bsgemm_pack_b": (I, [P, P, I, I, I, I, P]),
         "bsgemm_pack_scales": (I, [P, I, P, I, I, I, I, P]),
@@ -421,6 +424,103 @@ def gemm_a8w8_blockscale_grouped(A, B, x_scale, w_scale, group_offsets, max_rows
                                                       t_rows, _stream(A.device))
         _record((*tensors, out), A.device)
     _check(status, "bsgemm_a8w8_blockscale_grouped")
+    return out
+
+
+def gemm_a8w8_mxfp8_grouped(A, B, A_scale, B_scale, group_offsets, max_rows: int,
+                            out_dtype=torch.bfloat16, *, out=None, b_format: str = "raw",
+                            b_scale_format: str = "rowmajor", workspace=None, grid_blocks: int = 0):
+    """Grouped (MoE) MXFP8 GEMM.
+
+    A [T, K] E4M3 with A_scale E8M0 [T, K/32]; group e owns rows
+    group_offsets[e] .. group_offsets[e+1] (int32 CUDA tensor of E + 1
+    offsets) and multiplies them by B[e] ([E, N, K], raw or shuffle_weight(16,16)
+    bytes per b_format) with B_scale[e] (E8M0 [E, N, K/32] row-major, or native
+    atoms per expert [E, bytes] with b_scale_format="native").  max_rows bounds
+    the rows of any group.  Returns C [T, N]; rows outside every group are left
+    unwritten."""
+    return _mx_grouped(A, B, A_scale, B_scale, group_offsets, max_rows, fp4=False, out_dtype=out_dtype,
+                       out=out, b_format=b_format, b_scale_format=b_scale_format, workspace=workspace,
+                       grid_blocks=grid_blocks)
+
+
+def gemm_a4w4_mxfp4_grouped(A, B, A_scale, B_scale, group_offsets, max_rows: int,
+                            out_dtype=torch.bfloat16, *, out=None, b_format: str = "raw",
+                            b_scale_format: str = "rowmajor", workspace=None, grid_blocks: int = 0):
+    """Grouped (MoE) MXFP4 GEMM: as gemm_a8w8_mxfp8_grouped with A [T, K/2]
+    and B [E, N, K/2] packed E2M1 bytes (even k in the low nibble)."""
+    return _mx_grouped(A, B, A_scale, B_scale, group_offsets, max_rows, fp4=True, out_dtype=out_dtype,
+                       out=out, b_format=b_format, b_scale_format=b_scale_format, workspace=workspace,
+                       grid_blocks=grid_blocks)
+
+
+def _mx_grouped(A, B, A_scale, B_scale, group_offsets, max_rows, *, fp4, out_dtype, out, b_format,
+                b_scale_format, workspace, grid_blocks):
+    if b_format not in _B_FORMATS:
+        raise ValueError(f"b_format must be one of {sorted(_B_FORMATS)}")
+    if b_scale_format not in ("rowmajor", "native"):
+        raise ValueError("b_scale_format must be 'rowmajor' or 'native'")
+    tensors = (A, B, A_scale, B_scale, group_offsets)
+    if A.dim() != 2 or B.dim() != 3 or not A.is_cuda or any(t.device != A.device for t in tensors):
+        raise ValueError("A must be [T, K], B [E, N, K], all on the same GPU")
+    ok_types = _FP4 if fp4 else _FP8
+    if A.dtype not in ok_types or B.dtype not in ok_types:
+        raise ValueError("A/B must hold %s bytes" % ("packed E2M1" if fp4 else "E4M3FN"))
+    if A_scale.dtype not in _SCALE_U8 or B_scale.dtype not in _SCALE_U8:
+        raise ValueError("scales must be E8M0 bytes")
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("out_dtype must be bfloat16 or float32")
+    if group_offsets.dtype != torch.int32 or group_offsets.dim() != 1 or not group_offsets.is_contiguous():
+        raise ValueError("group_offsets must be a contiguous int32 tensor of E + 1 offsets")
+    t_rows, kb = A.shape
+    k = 2 * kb if fp4 else kb
+    groups = group_offsets.numel() - 1
+    if groups < 1 or B.shape[0] != groups:
+        raise ValueError("B needs one entry per group")
+    n = B.shape[1]
+    if B.shape[2] != kb or not B.is_contiguous() or A.stride(1) != 1:
+        raise ValueError("B must be a contiguous [E, N, K] and agree with A on K")
+    kg = k // 32
+    if tuple(A_scale.shape) != (t_rows, kg) or A_scale.stride(1) != 1:
+        raise ValueError(f"A_scale must be [{t_rows}, {kg}]")
+    if b_scale_format == "rowmajor" and (tuple(B_scale.shape) != (groups, n, kg) or B_scale.stride(2) != 1):
+        raise ValueError(f"B_scale must be [{groups}, {n}, {kg}]")
+    if b_scale_format == "native" and (B_scale.dim() != 2 or B_scale.shape[0] != groups):
+        raise ValueError("native B_scale must be [E, bytes] (pack_scales per expert)")
+    if max_rows < 1:
+        raise ValueError("max_rows must be positive")
+    out = _out(out, t_rows, n, out_dtype, A.device, 1)
+    args = Args()
+    lib().bsgemm_args_init(ctypes.byref(args))
+    args.ptr_a, args.ptr_b, args.ptr_c = A.data_ptr(), B.data_ptr(), out.data_ptr()
+    args.m, args.n, args.k, args.batch = int(max_rows), n, k, groups
+    args.stride_a, args.stride_b, args.stride_c = A.stride(0), B.stride(1), n
+    args.stride_b_batch = B.stride(0)
+    args.b_format = _B_FORMATS[b_format]
+    args.ptr_sfa, args.ptr_sfb = A_scale.data_ptr(), B_scale.data_ptr()
+    args.sfa_format = SF_ROWMAJOR
+    args.stride_sfa = A_scale.stride(0)
+    if b_scale_format == "rowmajor":
+        args.sfb_format = SF_ROWMAJOR
+        args.stride_sfb, args.stride_sfb_batch = B_scale.stride(1), B_scale.stride(0)
+    else:
+        args.sfb_format = SF_NATIVE
+        args.stride_sfb_batch = B_scale.stride(0)
+    args.layout = LAYOUTS["tn"]
+    args.out_dtype = OUT_BF16 if out_dtype == torch.bfloat16 else OUT_FP32
+    args.grid_blocks = grid_blocks
+    need = int(lib().bsgemm_mx_grouped_workspace_size(ctypes.byref(args)))
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=A.device)
+    elif workspace.numel() * workspace.element_size() < need:
+        raise ValueError(f"workspace needs {need} bytes")
+    args.workspace = workspace.data_ptr()
+    args.workspace_bytes = workspace.numel() * workspace.element_size()
+    fn = lib().bsgemm_a4w4_mxfp4_grouped if fp4 else lib().bsgemm_a8w8_mxfp8_grouped
+    with torch.cuda.device(A.device):
+        status = fn(ctypes.byref(args), ctypes.c_void_p(group_offsets.data_ptr()), t_rows, _stream(A.device))
+        _record((*tensors, out, workspace), A.device)
+    _check(status, "bsgemm_a4w4_mxfp4_grouped" if fp4 else "bsgemm_a8w8_mxfp8_grouped")
     return out
 
 

@@ -346,6 +346,17 @@ int mx_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p,
   return rc != BSG_OK ? rc : launch_status();
 }
 
+// Grouped (MoE) mode of the single-CTA kernel: K-major A, native scales.
+template <int BN, int kFp4, int kBMode, bool kOutF32>
+int mx_launch_t_grouped(const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p, int grid,
+                        cudaStream_t st) {
+  using Cfg = MxCfg<BN, kFp4>;
+  auto* kern = bsg::mx_gemm_kernel<BN, kFp4, false, kBMode, kOutF32, bsg::kSfNative, true>;
+  if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
+  const int rc = launch_pdl(kern, grid, bsg::kMxThreads, Cfg::kSmemBytes, st, ta, tb, p);
+  return rc != BSG_OK ? rc : launch_status();
+}
+
 template <int BN, int kFp4, bool kAMN, int kBMode>
 int mx_launch_out(bool f32, const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p, int grid,
                   cudaStream_t st) {
@@ -1221,6 +1232,167 @@ int fp8b_grouped_run(const bsgemm_args* args, const int* group_offsets, int tota
   }
 }
 
+// ---------------------------------------------------------------------------
+// Grouped (MoE) MXFP8 / MXFP4: the grouped mode of the single-CTA MX kernel
+// ---------------------------------------------------------------------------
+template <int BN, int kFp4, int kBMode>
+int mx_grouped_launch_t(bool f32, const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p, int grid,
+                        cudaStream_t st) {
+  return f32 ? mx_launch_t_grouped<BN, kFp4, kBMode, true>(ta, tb, p, grid, st)
+             : mx_launch_t_grouped<BN, kFp4, kBMode, false>(ta, tb, p, grid, st);
+}
+
+template <int kFp4>
+int mx_grouped_launch(int bn, int bmode, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
+                      const MxParams& p, int grid, cudaStream_t st) {
+  if (bn == 256)
+    return bmode == bsg::kBShuffle16 ? mx_grouped_launch_t<256, kFp4, bsg::kBShuffle16>(f32, ta, tb, p, grid, st)
+                                     : mx_grouped_launch_t<256, kFp4, bsg::kBKMajor>(f32, ta, tb, p, grid, st);
+  return bmode == bsg::kBShuffle16 ? mx_grouped_launch_t<128, kFp4, bsg::kBShuffle16>(f32, ta, tb, p, grid, st)
+                                   : mx_grouped_launch_t<128, kFp4, bsg::kBKMajor>(f32, ta, tb, p, grid, st);
+}
+
+// args: m = the most rows any group may have, batch = groups; A [total_rows,
+// K] (packed bytes for fp4) with row-major E8M0 scales [total_rows, K/32]
+// (stride_sfa), which are packed per group into the workspace; B [groups, N,
+// K] raw or shuffle_weight(16,16) at stride_b_batch, its scales native or
+// row-major per group.
+int mx_grouped_run(const bsgemm_args* args, bool fp4, const int* group_offsets, int total_rows,
+                   cudaStream_t st) {
+  if (!args || !group_offsets || total_rows <= 0) return BSG_ERR_INVALID_VALUE;
+  const bsgemm_args& a = *args;
+  if (!a.ptr_a || !a.ptr_b || !a.ptr_c || !a.ptr_sfa || !a.ptr_sfb) return BSG_ERR_INVALID_VALUE;
+  if (a.m <= 0 || a.n <= 0 || a.k <= 0 || a.batch <= 0 || a.grid_blocks < 0 || a.split_k < 0)
+    return BSG_ERR_INVALID_VALUE;
+  if (a.out_dtype != BSG_OUT_BF16 && a.out_dtype != BSG_OUT_FP32) return BSG_ERR_INVALID_VALUE;
+  if (a.split_k > 1) return BSG_ERR_UNSUPPORTED;
+  if (a.kernel != BSG_KERNEL_AUTO && a.kernel != BSG_KERNEL_1CTA) return BSG_ERR_UNSUPPORTED;
+  if (a.layout != BSG_LAYOUT_TN) return BSG_ERR_UNSUPPORTED;
+  if (a.b_format != BSG_B_RAW && a.b_format != BSG_B_SHUFFLE16) return BSG_ERR_UNSUPPORTED;
+  if (a.sfa_format != BSG_SF_ROWMAJOR) return BSG_ERR_UNSUPPORTED;
+  if (a.sfb_format != BSG_SF_NATIVE && a.sfb_format != BSG_SF_ROWMAJOR) return BSG_ERR_UNSUPPORTED;
+  DevInfo dev;
+  int rc;
+  if ((rc = device_info(&dev)) != BSG_OK) return rc;
+  if (!dev.sm100) return BSG_ERR_ARCH;
+  if (a.k % (fp4 ? 256 : 128)) return BSG_ERR_INVALID_VALUE;
+  const int vec = a.out_dtype == BSG_OUT_BF16 ? 8 : 4;
+  if (a.n % vec || a.stride_c < a.n || a.stride_c % vec || !aligned16(a.ptr_c)) return BSG_ERR_ALIGNMENT;
+  const bool shuffled = a.b_format == BSG_B_SHUFFLE16;
+  const long long kbytes = fp4 ? a.k / 2 : a.k;
+  const int kg = a.k / 32;
+  if (a.stride_a < kbytes || a.stride_a % 16 || a.stride_b < kbytes || a.stride_b % 16 || !aligned16(a.ptr_a) ||
+      !aligned16(a.ptr_b))
+    return BSG_ERR_ALIGNMENT;
+  if (shuffled && (a.n % 16 || a.stride_b != kbytes)) return BSG_ERR_INVALID_VALUE;
+  const long long b_bytes1 = static_cast<long long>(a.n) * a.stride_b;
+  if (a.batch > 1 && (a.stride_b_batch < b_bytes1 || a.stride_b_batch % 16)) return BSG_ERR_INVALID_VALUE;
+  if (a.stride_sfa < kg) return BSG_ERR_INVALID_VALUE;
+  const size_t sfa_nat = native_sf_bytes(a.m, kg), sfb_nat = native_sf_bytes(a.n, kg);
+  long long sfb_bs = 0;
+  uint64_t sfb_bytes;
+  if (a.sfb_format == BSG_SF_NATIVE) {
+    if (!aligned16(a.ptr_sfb)) return BSG_ERR_ALIGNMENT;
+    sfb_bs = a.batch > 1 ? (a.stride_sfb_batch ? a.stride_sfb_batch : static_cast<long long>(sfb_nat)) : 0;
+    if (sfb_bs % 16 || (a.batch > 1 && sfb_bs < static_cast<long long>(sfb_nat))) return BSG_ERR_INVALID_VALUE;
+    sfb_bytes = static_cast<uint64_t>(sfb_bs) * (a.batch - 1) + sfb_nat;
+  } else {
+    if (a.stride_sfb < kg || (a.batch > 1 && a.stride_sfb_batch < static_cast<long long>(a.n) * a.stride_sfb))
+      return BSG_ERR_INVALID_VALUE;
+    sfb_bytes = static_cast<uint64_t>(a.batch > 1 ? a.stride_sfb_batch * (a.batch - 1) : 0) +
+                static_cast<uint64_t>(a.n) * a.stride_sfb;
+  }
+  // workspace: the per-group A scale atoms, (row-major B scales) B's atoms,
+  // then the prefix of the groups' M tiles
+  const size_t ws_sfa = align256(sfa_nat * a.batch);
+  const size_t ws_sfb = a.sfb_format == BSG_SF_ROWMAJOR ? align256(sfb_nat * a.batch) : 0;
+  const size_t need = ws_sfa + ws_sfb + align256(4u * (static_cast<size_t>(a.batch) + 1));
+  if (need > a.workspace_bytes || !a.workspace) return BSG_ERR_WORKSPACE;
+  if (!aligned16(a.workspace)) return BSG_ERR_ALIGNMENT;
+  uint8_t* ws = static_cast<uint8_t*>(a.workspace);
+  const uint64_t c_bytes =
+      static_cast<uint64_t>(total_rows) * a.stride_c * (a.out_dtype == BSG_OUT_BF16 ? 2 : 4);
+  const uint64_t b_bytes = static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch * (a.batch - 1) : 0) + b_bytes1;
+  const uint64_t sfa_bytes = static_cast<uint64_t>(total_rows) * a.stride_sfa;
+  const uint64_t off_bytes = 4ull * (a.batch + 1);
+  if (overlaps(a.ptr_c, c_bytes, a.ptr_a, static_cast<uint64_t>(total_rows) * a.stride_a) ||
+      overlaps(a.ptr_c, c_bytes, a.ptr_b, b_bytes) || overlaps(a.ptr_c, c_bytes, a.ptr_sfa, sfa_bytes) ||
+      overlaps(a.ptr_c, c_bytes, a.ptr_sfb, sfb_bytes) || overlaps(a.ptr_c, c_bytes, group_offsets, off_bytes) ||
+      overlaps(a.ptr_c, c_bytes, ws, need) || overlaps(ws, need, a.ptr_a, static_cast<uint64_t>(total_rows) * a.stride_a) ||
+      overlaps(ws, need, a.ptr_b, b_bytes) || overlaps(ws, need, a.ptr_sfa, sfa_bytes) ||
+      overlaps(ws, need, a.ptr_sfb, sfb_bytes) || overlaps(ws, need, group_offsets, off_bytes))
+    return BSG_ERR_INVALID_VALUE;
+
+  CUtensorMap ta, tb;
+  // A over all rows of all groups; a tile that runs past its group's last row
+  // reads the next group's rows (or zero fill past total_rows), and those
+  // rows are not stored
+  if (!make_operand_tmap(&ta, a.ptr_a, kbytes, total_rows, a.stride_a, 0, 1, 128u)) return BSG_ERR_CUDA;
+  const int tiles_m = (a.m + 127) / 128;
+  int bn = 256;
+  if (static_cast<long long>(tiles_m) * ((a.n + 255) / 256) * a.batch < dev.sms / 2 || a.n <= 128) bn = 128;
+  MxOperands o;
+  o.fp4 = fp4;
+  o.bmode = shuffled ? bsg::kBShuffle16 : bsg::kBKMajor;
+  o.kbytes = kbytes;
+  o.b_rows = a.n;
+  o.b_cols = kbytes;
+  if (!make_b_tmap(&tb, a, o, static_cast<uint32_t>(bn))) return BSG_ERR_CUDA;
+
+  // scale atoms: A per group (device offsets) with the M-tile prefix, B per
+  // batch when row-major
+  int* tile_prefix = reinterpret_cast<int*>(ws + ws_sfa + ws_sfb);
+  {
+    const long long words = static_cast<long long>(sfa_nat / 4) * a.batch;
+    const int grid = static_cast<int>(std::min<long long>((words + 255) / 256, 4096));
+    bsg::pack_sf_grouped_kernel<<<grid, 256, 0, st>>>(static_cast<const uint8_t*>(a.ptr_sfa), a.stride_sfa,
+                                                     group_offsets, a.batch, total_rows, a.m, kg, ws,
+                                                     tile_prefix);
+    if ((rc = launch_status()) != BSG_OK) return rc;
+  }
+  const uint8_t* sfb = static_cast<const uint8_t*>(a.ptr_sfb);
+  if (a.sfb_format == BSG_SF_ROWMAJOR) {
+    for (int bb = 0; bb < a.batch; ++bb)
+      if ((rc = pack_sf_launch(sfb + static_cast<long long>(bb) * a.stride_sfb_batch, a.stride_sfb,
+                               ws + ws_sfa + bb * sfb_nat, a.n, kg, BSG_SF_ROWMAJOR, 0, st)) != BSG_OK)
+        return rc;
+    sfb = ws + ws_sfa;
+    sfb_bs = static_cast<long long>(sfb_nat);
+  }
+
+  MxParams p{};
+  p.m = a.m;
+  p.n = a.n;
+  p.k = a.k;
+  p.batch = a.batch;
+  p.num_kb = fp4 ? a.k / 256 : a.k / 128;
+  p.tiles_m = tiles_m;
+  p.tiles_n = (a.n + bn - 1) / bn;
+  p.split_k = 1;
+  p.kb_per_split = p.num_kb;
+  p.total_units = p.tiles_m * p.tiles_n * a.batch;
+  p.group_m = std::min(p.tiles_m, kGroupM);
+  p.sfa = ws;
+  p.sfb = sfb;
+  p.sfa_batch_stride = static_cast<long long>(sfa_nat);
+  p.sfb_batch_stride = sfb_bs;
+  p.sf_kb_total = (kg + 3) / 4;
+  p.sfb_row_blocks = (a.n + 127) / 128;
+  p.c = a.ptr_c;
+  p.ldc = a.stride_c;
+  p.c_batch_stride = 0;
+  p.ws = nullptr;
+  p.timeout_ns = kTimeoutNs;
+  p.group_offsets = group_offsets;
+  p.total_rows = total_rows;
+  p.tile_prefix = tile_prefix;
+  p.group_m = kGroupM;   // over the live M tiles, whose count only the device knows
+  const int grid = grid_for(p.total_units, dev, a.grid_blocks);
+  const bool f32 = a.out_dtype == BSG_OUT_FP32;
+  return fp4 ? mx_grouped_launch<1>(bn, o.bmode, f32, ta, tb, p, grid, st)
+             : mx_grouped_launch<0>(bn, o.bmode, f32, ta, tb, p, grid, st);
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -1254,6 +1426,24 @@ int bsgemm_a8w8_blockscale_bpreshuffle(const bsgemm_args* args, bsg_stream_t str
 int bsgemm_a8w8_blockscale_grouped(const bsgemm_args* args, const int* group_offsets, int total_rows,
                                    bsg_stream_t stream) {
   return fp8b_grouped_run(args, group_offsets, total_rows, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int bsgemm_a8w8_mxfp8_grouped(const bsgemm_args* args, const int* group_offsets, int total_rows,
+                              bsg_stream_t stream) {
+  return mx_grouped_run(args, false, group_offsets, total_rows, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int bsgemm_a4w4_mxfp4_grouped(const bsgemm_args* args, const int* group_offsets, int total_rows,
+                              bsg_stream_t stream) {
+  return mx_grouped_run(args, true, group_offsets, total_rows, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t bsgemm_mx_grouped_workspace_size(const bsgemm_args* args) {
+  if (!args || args->m <= 0 || args->n <= 0 || args->k <= 0 || args->batch <= 0) return 0;
+  const int kg = args->k / 32;
+  return align256(native_sf_bytes(args->m, kg) * args->batch) +
+         (args->sfb_format == BSG_SF_ROWMAJOR ? align256(native_sf_bytes(args->n, kg) * args->batch) : 0) +
+         align256(4u * (static_cast<size_t>(args->batch) + 1));
 }
 
 size_t bsgemm_workspace_size(int family, const bsgemm_args* args) {

@@ -75,7 +75,50 @@ struct MxParams {
   long long c_batch_stride;      // elements
   float* ws;                     // split-K partials [split][batch][m][n]
   unsigned long long timeout_ns;
+  const int* group_offsets;      // grouped mode: batch + 1 row offsets (device); else unused
+  int total_rows;                // grouped mode: rows of A and C over all groups
+  const int* tile_prefix;        // grouped mode: batch + 1 exclusive prefix of the groups' M tiles
 };
+
+// Grouped mode: group b owns rows group_offsets[b] .. group_offsets[b+1] of A
+// and C, clamped to [0, total_rows] and to at most m rows (the tile grid's
+// bound), so corrupt or oversized offsets never reach past the tensors.
+__device__ __forceinline__ void mx_group_rows(const MxParams& p, int b, int& row0, int& rows) {
+  int a0 = __ldg(p.group_offsets + b);
+  int a1 = __ldg(p.group_offsets + b + 1);
+  a0 = min(max(a0, 0), p.total_rows);
+  a1 = min(max(a1, a0), p.total_rows);
+  row0 = a0;
+  rows = min(a1 - a0, p.m);
+}
+
+// Grouped mode enumerates only the M tiles that hold rows: unit u is (global
+// M tile gm, N tile nt) over prefix[batch] M tiles (rasterised as a plain
+// GEMM of that many M tiles), and gm belongs to the last group e with
+// prefix[e] <= gm (empty groups share their successor's prefix), as its M
+// tile gm - prefix[e].  Returns false for a tile past the group's rows, which
+// the prefix never produces; every role skips such a unit alike.
+__device__ __forceinline__ int mx_grouped_units(const MxParams& p) {
+  const int live = min(__ldg(p.tile_prefix + p.batch), p.tiles_m * p.batch);
+  return max(live, 0) * p.tiles_n;
+}
+
+__device__ __forceinline__ bool mx_grouped_unit(const MxParams& p, int u, int& e, int& mt, int& nt, int& row0,
+                                                int& rows) {
+  const int live = min(__ldg(p.tile_prefix + p.batch), p.tiles_m * p.batch);
+  int b, gm, s;
+  decode_unit(u, live, p.tiles_n, 1, p.group_m, b, gm, nt, s);
+  int lo = 0, hi = p.batch - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(p.tile_prefix + mid) <= gm) lo = mid;
+    else hi = mid - 1;
+  }
+  e = lo;
+  mt = gm - __ldg(p.tile_prefix + lo);
+  mx_group_rows(p, e, row0, rows);
+  return mt >= 0 && mt * 128 < rows;
+}
 
 constexpr int kMxThreads = 384;     // 4 control warps + 8 epilogue warps
 constexpr int kMxEpiThreads = 256;
@@ -198,7 +241,13 @@ __device__ __forceinline__ void store_row32_f32(float* dst, const uint32_t (&r)[
   }
 }
 
-template <int BN, int kFp4, bool kAMN, int kBMode, bool kOutF32, int kSfMode>
+// kGrouped: the batch index is a group (expert) whose rows of A and C start
+// at group_offsets[b] (mx_group_rows); A is one [total_rows, K] matrix, the
+// group's A scales are native atoms at batch stride sfa_batch_stride (packed
+// per group), and the units are only the M tiles that hold rows
+// (mx_grouped_unit), so the persistent grid stays balanced however ragged
+// the groups are.
+template <int BN, int kFp4, bool kAMN, int kBMode, bool kOutF32, int kSfMode, bool kGrouped = false>
 __global__ void __launch_bounds__(kMxThreads, 1)
     mx_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const MxParams p) {
@@ -207,6 +256,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   constexpr bool kBMN = kBMode == kBMNMajor;
   constexpr bool kBuildSf = kSfMode == kSfE8m0Block128;
   static_assert(!kBuildSf || !kFp4, "per-128 E8M0 scales are an fp8 format");
+  static_assert(!kGrouped || (!kBuildSf && !kAMN), "grouped mode: K-major A, native scales");
 
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzled operand tiles
@@ -267,9 +317,20 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     bool ok = true;
     int last_stage = -1;
     uint32_t last_phase = 0;
-    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
-      int b, mt, nt, s;
-      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+    const int units = kGrouped ? mx_grouped_units(p) : p.total_units;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      int b, mt, nt, s = 0;
+      int a_row, a_batch;
+      if constexpr (kGrouped) {
+        int row0, rows;
+        if (!mx_grouped_unit(p, u, b, mt, nt, row0, rows)) continue;
+        a_row = row0 + mt * 128;
+        a_batch = 0;
+      } else {
+        decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+        a_row = mt * 128;
+        a_batch = b;
+      }
       const int kb0 = s * p.kb_per_split;
       const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
       const uint8_t* sfa_tile = p.sfa + b * p.sfa_batch_stride +
@@ -294,9 +355,9 @@ __global__ void __launch_bounds__(kMxThreads, 1)
         const int kbyte = kb * 128;
         if (issuer) {
           if constexpr (!kAMN) {
-            tma_load_3d_hint(a_dst, &tmA, fb, kbyte, mt * 128, b, pol_a);
+            tma_load_3d_hint(a_dst, &tmA, fb, kbyte, a_row, a_batch, pol_a);
           } else {
-            tma_load_3d_hint(a_dst, &tmA, fb, mt * 128, kbyte, b, pol_a);
+            tma_load_3d_hint(a_dst, &tmA, fb, a_row, kbyte, a_batch, pol_a);
           }
           if constexpr (kBMode == kBKMajor) {
             tma_load_3d_hint(b_dst, &tmB, fb, kbyte, nt * BN, b, pol_b);
@@ -361,9 +422,15 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     int iter = 0;
     uint32_t sf_region = 0;   // alternates every stage
     bool ok = true;
-    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x, ++iter) {
-      int b, mt, nt, s;
-      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+    const int units = kGrouped ? mx_grouped_units(p) : p.total_units;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      int b, mt, nt, s = 0;
+      if constexpr (kGrouped) {
+        int row0, rows;
+        if (!mx_grouped_unit(p, u, b, mt, nt, row0, rows)) continue;   // uses no accumulator phase
+      } else {
+        decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+      }
       const int kb0 = s * p.kb_per_split;
       const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
       if (!mbar_wait(tmem_empty, (static_cast<uint32_t>(iter) & 1u) ^ 1u, abort_flag,
@@ -418,6 +485,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       }
       if (!ok) break;
       if (issuer) tc_commit(tmem_full);
+      ++iter;
     }
     // drain: wait until every tcgen05 op issued above has completed
     if (issuer) tc_commit(drain_bar);
@@ -489,21 +557,30 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     const uint32_t t_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                             static_cast<uint32_t>(half * HC);
     int iter = 0;
-    for (int u = blockIdx.x; u < p.total_units; u += gridDim.x, ++iter) {
-      int b, mt, nt, s;
-      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+    const int units = kGrouped ? mx_grouped_units(p) : p.total_units;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      int b, mt, nt, s = 0;
+      int row0 = 0, rows = p.m;   // the group's first row and rows (all of M when not grouped)
+      if constexpr (kGrouped) {
+        if (!mx_grouped_unit(p, u, b, mt, nt, row0, rows)) continue;
+      } else {
+        decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+      }
       if (!mbar_wait(tmem_full, static_cast<uint32_t>(iter) & 1u, abort_flag, p.timeout_ns)) break;
+      ++iter;
       tc_fence_after();
       const int row = mt * 128 + q * 32 + static_cast<int>(lane);
-      const bool row_ok = row < p.m;
+      const bool row_ok = row < rows;
+      // C row of this lane and the batch's C origin (a group's rows live in one C)
+      const long long crow = static_cast<long long>(row0) + row;
+      const long long cbatch = kGrouped ? 0 : b * p.c_batch_stride;
       const int col_base = nt * BN + half * HC;
       const int valid_cols = p.n - col_base;   // may be <= 0 or > HC
       if (p.split_k > 1 || kOutF32) {
         float* dst = p.split_k > 1
                          ? p.ws + ((static_cast<long long>(s) * p.batch + b) * p.m + row) *
                                       static_cast<long long>(p.n) + col_base
-                         : reinterpret_cast<float*>(p.c) + b * p.c_batch_stride +
-                               static_cast<long long>(row) * p.ldc + col_base;
+                         : reinterpret_cast<float*>(p.c) + cbatch + crow * p.ldc + col_base;
 #pragma unroll 1
         for (int c = 0; c < HC / 32; ++c) {
           uint32_t r[32];
@@ -529,8 +606,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(tmem_empty);
         if (row_ok && valid_cols > 0) {
-          uint16_t* dst = reinterpret_cast<uint16_t*>(p.c) + b * p.c_batch_stride +
-                          static_cast<long long>(row) * p.ldc + col_base;
+          uint16_t* dst = reinterpret_cast<uint16_t*>(p.c) + cbatch + crow * p.ldc + col_base;
           if (valid_cols >= HC) {
 #pragma unroll
             for (int v = 0; v < HC / 8; ++v)

@@ -88,6 +88,70 @@ __global__ void pack_sf_native_kernel(const uint8_t* __restrict__ src, int src_s
   }
 }
 
+// Row-major E8M0 scales of a grouped (MoE) activation [total_rows][kg] into
+// native atoms per group: group e (rows offsets[e] .. offsets[e+1], clamped to
+// [0, total_rows] and to at most max_rows rows, as the grouped GEMM clamps
+// them) gets its own ceil(max_rows/128) row blocks, so the GEMM finds group
+// e's atoms at batch stride tiles * ceil(kg/4) * 512 bytes.  Rows past a
+// group's end and groups past kg read 0x7F (2^0).
+//
+// The first warp of block 0 also writes tile_prefix[0 .. groups]: the
+// exclusive prefix sum of the groups' 128-row tiles (ceil(rows / 128)), which
+// the grouped GEMM uses to enumerate only the tiles that hold rows.
+__global__ void pack_sf_grouped_kernel(const uint8_t* __restrict__ src, int src_stride,
+                                       const int* __restrict__ offsets, int groups, int total_rows,
+                                       int max_rows, int kg, uint8_t* __restrict__ dst,
+                                       int* __restrict__ tile_prefix) {
+  if (blockIdx.x == 0 && threadIdx.x < 32) {
+    const int lane = static_cast<int>(threadIdx.x);
+    int carry = 0;
+    for (int base = 0; base < groups; base += 32) {
+      const int e = base + lane;
+      int t = 0;
+      if (e < groups) {
+        int a0 = __ldg(offsets + e), a1 = __ldg(offsets + e + 1);
+        a0 = min(max(a0, 0), total_rows);
+        a1 = min(max(a1, a0), total_rows);
+        t = (min(a1 - a0, max_rows) + 127) / 128;
+      }
+      int v = t;   // inclusive warp scan
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) v += y;
+      }
+      if (e < groups) tile_prefix[e] = carry + v - t;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) tile_prefix[groups] = carry;
+  }
+  const int kb_total = (kg + 3) / 4;
+  const int tiles = (max_rows + 127) / 128;
+  const long long atoms_per_group = static_cast<long long>(tiles) * kb_total;
+  const long long words = atoms_per_group * groups * 128;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < words;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long atom = i / 128;
+    const int w = static_cast<int>(i % 128);
+    const int e = static_cast<int>(atom / atoms_per_group);
+    const long long rem = atom - e * atoms_per_group;
+    const int rb = static_cast<int>(rem / kb_total), kb = static_cast<int>(rem % kb_total);
+    int a0 = __ldg(offsets + e), a1 = __ldg(offsets + e + 1);
+    a0 = min(max(a0, 0), total_rows);
+    a1 = min(max(a1, a0), total_rows);
+    const int rows = min(a1 - a0, max_rows);
+    const int r = rb * 128 + (w % 4) * 32 + w / 4;
+    uint32_t word = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int g = kb * 4 + j;
+      const uint32_t v = r < rows && g < kg ? src[static_cast<long long>(a0 + r) * src_stride + g] : 0x7Fu;
+      word |= v << (8 * j);
+    }
+    reinterpret_cast<uint32_t*>(dst)[i] = word;
+  }
+}
+
 // Pads of an aiter e8m0_shuffle buffer are 0x7F; unpack writes them first.
 __global__ void fill_u8_kernel(uint8_t* __restrict__ dst, long long n, uint8_t v) {
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;

@@ -189,6 +189,25 @@ BSG_API int bsgemm_a8w8_blockscale_grouped(const bsgemm_args *args, const int *g
                                            bsg_stream_t stream);
 
 /*
+ * Grouped (MoE) MXFP8 / MXFP4 GEMM, with the groups given as in
+ * bsgemm_a8w8_blockscale_grouped: A [total_rows, K] E4M3 (MXFP4: packed E2M1
+ * [total_rows, K/2] bytes), layout TN, with SFA E8M0 [total_rows, K/32]
+ * (BSG_SF_ROWMAJOR, row stride stride_sfa bytes); group e's weights B
+ * [N, K] (raw or BSG_B_SHUFFLE16) at ptr_b + e * stride_b_batch and their SFB
+ * E8M0 in BSG_SF_ROWMAJOR or BSG_SF_NATIVE, per group at stride_sfb_batch.
+ * The row-major scales are packed into tcgen05 atoms (A per group, from the
+ * device offsets) in the caller's workspace, which must hold
+ * bsgemm_mx_grouped_workspace_size(args) bytes.  Offsets are clamped as in
+ * bsgemm_a8w8_blockscale_grouped.  split_k 0 or 1; kernel AUTO or 1CTA.
+ * No launcher in the reference (same note as the FP8 block-scale form).
+ */
+BSG_API int bsgemm_a8w8_mxfp8_grouped(const bsgemm_args *args, const int *group_offsets, int total_rows,
+                                      bsg_stream_t stream);
+BSG_API int bsgemm_a4w4_mxfp4_grouped(const bsgemm_args *args, const int *group_offsets, int total_rows,
+                                      bsg_stream_t stream);
+BSG_API size_t bsgemm_mx_grouped_workspace_size(const bsgemm_args *args);
+
+/*
  * Bytes of split-K workspace the call would need (0 when it runs without
  * split-K).  family = BSG_FAMILY_*.
  */

@@ -66,6 +66,27 @@ def test_invalid_arguments_rejected_without_gpu(bs):
     assert lib.bsgemm_native_scales_size(200, 12) == 2 * 3 * 512
 
 
+def test_mx_grouped_workspace_and_rejections(bs):
+    """Grouped MX: workspace = per-group A atoms (+ B atoms when row-major)
+    + the groups' M-tile prefix, and missing arguments are rejected before any CUDA call."""
+    lib = bs.lib()
+    a = bs.Args()
+    lib.bsgemm_args_init(ctypes.byref(a))
+    a.m, a.n, a.k, a.batch = 200, 384, 1024, 8
+    per_a = lib.bsgemm_native_scales_size(200, 32)
+    per_b = lib.bsgemm_native_scales_size(384, 32)
+    prefix = 256   # nine int32 M-tile prefix entries, 256-byte aligned
+    assert lib.bsgemm_mx_grouped_workspace_size(ctypes.byref(a)) == 8 * per_a + 8 * per_b + prefix
+    a.sfb_format = bs.SF_NATIVE
+    assert lib.bsgemm_mx_grouped_workspace_size(ctypes.byref(a)) == 8 * per_a + prefix
+    offs = (ctypes.c_int * 9)()
+    for fn in (lib.bsgemm_a8w8_mxfp8_grouped, lib.bsgemm_a4w4_mxfp4_grouped):
+        assert fn(None, offs, 100, None) == bs.ERR_INVALID_VALUE
+        assert fn(ctypes.byref(a), None, 100, None) == bs.ERR_INVALID_VALUE
+        assert fn(ctypes.byref(a), offs, 0, None) == bs.ERR_INVALID_VALUE
+        assert fn(ctypes.byref(a), offs, 100, None) == bs.ERR_INVALID_VALUE   # null operands
+
+
 def test_python_api_rejects_cpu_tensors(bs):
     import torch
     a = torch.zeros(128, 128, dtype=torch.float8_e4m3fn)

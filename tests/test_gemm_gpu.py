@@ -458,6 +458,85 @@ def test_fp8_block_grouped_caps_rows_at_max_rows(bs, orc, cuda):
     run_fp8_block_grouped(bs, orc, cuda, (300, 20), 256, 512, seed=5, max_rows=256)
 
 
+def run_mx_grouped(bs, orc, cuda, sizes, n, k, *, fp4, seed, b_format="raw", b_scale_format="rowmajor",
+                   tail=0, max_rows=None, out_dtype=torch.bfloat16, sf_mode="data"):
+    """Grouped MXFP8 / MXFP4: groups of `sizes` rows concatenated (then `tail`
+    rows in no group), each checked against its own weights through the oracle."""
+    quant = orc.quant_mxfp4 if fp4 else orc.quant_mxfp8
+    offs = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int32)
+    t_rows = int(offs[-1]) + tail
+    qa, sa = quant(orc.normal((t_rows, k), seed=seed))
+    sa = scale_mode(sa, sf_mode)
+    qbs, sbs = zip(*[quant(orc.normal((n, k), seed=seed * 31 + e + 1)) for e in range(len(sizes))])
+    sbs = [scale_mode(sb, sf_mode) for sb in sbs]
+    bh = np.stack([orc.shuffle_weight16(qb) for qb in qbs]) if b_format == "shuffle16" else np.stack(qbs)
+    A, B = dev_u8(qa, cuda), dev_u8(bh, cuda)
+    if not fp4:
+        A, B = A.view(torch.float8_e4m3fn), B.view(torch.float8_e4m3fn)
+    SA = dev_u8(sa, cuda)
+    SB = dev_u8(np.stack(sbs), cuda)
+    if b_scale_format == "native":
+        SB = torch.stack([bs.pack_scales(SB[e]) for e in range(len(sizes))])
+    G = torch.from_numpy(offs).to(cuda)
+    max_rows = max_rows or max(max(sizes), 1)
+    out = poisoned((t_rows, n), out_dtype, cuda)
+    fn = bs.gemm_a4w4_mxfp4_grouped if fp4 else bs.gemm_a8w8_mxfp8_grouped
+    fn(A, B, SA, SB, G, max_rows, out_dtype, out=out, b_format=b_format, b_scale_format=b_scale_format)
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    got = out.float().cpu().numpy()
+    for e, sz in enumerate(sizes):
+        o0, done = int(offs[e]), min(sz, max_rows)
+        if done:
+            rows = slice(o0, o0 + done)
+            ref, mag = (orc.gemm_mxfp4(qa[rows], qbs[e], sa[rows], sbs[e]) if fp4
+                        else orc.gemm_mxfp8(qa[rows], qbs[e], sa[rows], sbs[e], f64=True))
+            assert_close(orc, ref, got[rows], mag, f"mx grouped fp4={fp4} e{e} rows {sz} {b_format}")
+        assert np.isnan(got[o0 + done:o0 + sz]).all(), f"group {e} wrote past max_rows"
+    assert np.isnan(got[int(offs[-1]):]).all(), "rows outside every group were written"
+    return got
+
+
+@pytest.mark.parametrize("fp4,sizes,n,k,b_format,b_sf,out_dtype", [
+    (False, (0, 5, 130, 17, 256, 1), 384, 512, "raw", "rowmajor", torch.bfloat16),
+    (False, (64, 64, 3), 256, 1024, "shuffle16", "native", torch.float32),
+    (False, (200, 0, 40), 272, 384, "raw", "native", torch.bfloat16),
+    (True, (0, 7, 129, 33), 256, 1024, "raw", "rowmajor", torch.bfloat16),
+    (True, (96, 1, 250), 384, 512, "shuffle16", "native", torch.float32),
+])
+def test_mx_grouped(bs, orc, cuda, fp4, sizes, n, k, b_format, b_sf, out_dtype):
+    """Ragged groups (empty, single-row, several 128-row tiles, N not a
+    multiple of the tile), each against its own weights, with rows after the
+    last group left untouched; B raw or shuffle_weight(16,16), B scales
+    row-major or native atoms per expert."""
+    run_mx_grouped(bs, orc, cuda, sizes, n, k, fp4=fp4, seed=700 + n + k + fp4, b_format=b_format,
+                   b_scale_format=b_sf, tail=9, out_dtype=out_dtype)
+
+
+@pytest.mark.parametrize("fp4", [False, True])
+def test_mx_grouped_scale_patterns_and_cap(bs, orc, cuda, fp4):
+    """The reference's row-pattern scales (a wrong row-to-group scale mapping
+    shows at once) and a group longer than max_rows, computed up to max_rows."""
+    run_mx_grouped(bs, orc, cuda, (300, 20, 77), 256, 512, fp4=fp4, seed=9, max_rows=256,
+                   sf_mode="rowpattern")
+
+
+def test_mx_grouped_matches_dense(bs, orc, cuda):
+    """A single group covering all rows equals the dense MXFP8 GEMM bit for bit."""
+    x = orc.normal((200, 1024), seed=77)
+    w = orc.normal((384, 1024), seed=78)
+    qa, sa = orc.quant_mxfp8(x)
+    qb, sb = orc.quant_mxfp8(w)
+    A = dev_u8(qa, cuda).view(torch.float8_e4m3fn)
+    B = dev_u8(qb, cuda).view(torch.float8_e4m3fn)
+    SA, SB = dev_u8(sa, cuda), dev_u8(sb, cuda)
+    dense = bs.gemm_a8w8_mxfp8(A, B, SA, SB, kernel="1cta", split_k=1)
+    G = torch.tensor([0, 200], dtype=torch.int32, device=cuda)
+    grouped = bs.gemm_a8w8_mxfp8_grouped(A, B[None], SA, SB[None], G, 200)
+    torch.cuda.synchronize()
+    assert torch.equal(dense, grouped)
+
+
 @pytest.mark.parametrize("m,kernel", [(16, "swap"), (48, "swap"), (200, "1cta")])
 def test_fp8_block_shuffle16_b(bs, orc, cuda, m, kernel):
     """aiter shuffle_weight(16,16) weights read in place by both kernels."""
