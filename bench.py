@@ -4,6 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload mxfp8|mxfp4|fp8block|e8m0block] [--layout tn|nn|tt|nt]
                     [--b-format raw|shuffle16]
+    python bench.py --sweep | --quant | --grouped | --tune CSV     (one JSON line each)
 
 Default workload (the headline metric): MXFP8 GEMM M=N=K=8192, layout
 tn, E4M3 with E8M0 scales per 32 K, bf16 out, fp32 accumulation.  One step is
@@ -112,6 +113,10 @@ def parse():
                     help="activation quantise+pack bandwidth (bf16 -> mxfp8/mxfp4/fp8_block), one JSON line")
     ap.add_argument("--sweep", action="store_true",
                     help="fp8 block-scale sweep, M in {1,16,64,128,1024,8192} x 4 (N,K) shapes, one JSON line")
+    ap.add_argument("--grouped", action="store_true",
+                    help="grouped (MoE) GEMMs of the three families on decode and prefill expert mixes, one JSON line")
+    ap.add_argument("--families", default="fp8block,mxfp8,mxfp4",
+                    help="comma-separated families for --grouped")
     args = ap.parse_args()
     if args.shape:
         args.m, args.n, args.k = (int(v) for v in args.shape.split(","))
@@ -822,6 +827,111 @@ def run_quant(args):
     return 0
 
 
+def run_grouped(args):
+    """Grouped (MoE) GEMMs: fp32 block-scale (K-panel B), MXFP8 (raw B) and
+    MXFP4 (shuffle_weight(16,16) B), native expert scales for MX, on
+    (experts x tokens, N, K) mixes: decode (32 x 4), prefill (8 x 512) and
+    ragged prefill (4096 tokens over 32 experts, multinomial, seed 0).
+    Every expert has its own weights in HBM.  L2 flushed before every call,
+    graph-difference timing as in the sweep; one call includes the scale
+    packing the grouped entry point does.  Bytes = weights + activations +
+    scales + bf16 C; hbm_frac relates them to the measured copy bandwidth."""
+    import numpy as np
+    import torch
+    dev = torch.device("cuda", 0)
+    bs = importlib.import_module("355_1_trans_b200")
+    peaks, peak_kind = load_peaks()
+    flush = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    sink = torch.empty((), dtype=torch.float32, device=dev)
+    reps = 10
+
+    def graph_time(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(max(3, min(args.steps, 10))):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        del g
+        return statistics.median(ts)
+
+    def flushes():
+        for _ in range(reps):
+            torch.sum(flush, dim=0, out=sink)
+
+    t_flush = graph_time(flushes)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11)
+    ragged = np.random.default_rng(0).multinomial(4096, np.ones(32) / 32)
+    mixes = (("decode", [4] * 32, 4096, 7168), ("decode", [4] * 32, 7168, 2048),
+             ("prefill", [512] * 8, 4096, 7168), ("ragged prefill", list(ragged), 4096, 7168))
+    rows = []
+    for family in args.families.split(","):
+        if family not in ("fp8block", "mxfp8", "mxfp4"):
+            raise SystemExit(f"unknown family {family}")
+        for label, sizes, n, k in mixes:
+            e, t = len(sizes), int(sum(sizes))
+            offs = torch.tensor(np.concatenate([[0], np.cumsum(sizes)]).astype(np.int32), device=dev)
+            out = torch.empty(t, n, dtype=torch.bfloat16, device=dev)
+            fp4 = family == "mxfp4"
+            kb = k // 2 if fp4 else k
+            if family == "fp8block":
+                qa, _, sa, _ = make_fp8block_inputs(t, 128, k, dev, 1)
+                _, qb1, _, sb1 = make_fp8block_inputs(1, n, k, dev, 2)
+                B = qb1.view(torch.uint8).reshape(1, -1).repeat(e, 1).view(torch.float8_e4m3fn)
+                B = B.reshape(e, k // 128, n, 128)
+                SB = sb1.unsqueeze(0).repeat(e, 1, 1).contiguous()
+                call = lambda: bs.gemm_a8w8_blockscale_grouped(qa, B, sa, SB, offs, max(sizes), out=out)
+                sf_bytes = 4 * t * (k // 128) + 4 * e * (n // 128) * (k // 128)
+            else:
+                hi = 256 if fp4 else 0x70   # any packed E2M1 byte; E4M3 bytes below the NaN codes
+                qa = torch.randint(0, hi, (t, kb), device=dev, generator=gen, dtype=torch.uint8)
+                B = torch.randint(0, hi, (e, n, kb), device=dev, generator=gen, dtype=torch.uint8)
+                if not fp4:
+                    qa, B = qa.view(torch.float8_e4m3fn), B.view(torch.float8_e4m3fn)
+                else:
+                    B = torch.stack([bs.pack_b(B[i], "shuffle16", unpack=True) for i in range(e)])
+                sa = torch.randint(120, 134, (t, k // 32), device=dev, generator=gen, dtype=torch.uint8)
+                sb1 = torch.randint(120, 134, (n, k // 32), device=dev, generator=gen, dtype=torch.uint8)
+                SB = torch.stack([bs.pack_scales(sb1)] * e)
+                ws = torch.empty(1 << 26, dtype=torch.uint8, device=dev)
+                fn = bs.gemm_a4w4_mxfp4_grouped if fp4 else bs.gemm_a8w8_mxfp8_grouped
+                bfmt = "shuffle16" if fp4 else "raw"
+                call = lambda: fn(qa, B, sa, SB, offs, max(sizes), out=out, b_format=bfmt,
+                                  b_scale_format="native", workspace=ws)
+                sf_bytes = t * (k // 32) + e * n * (k // 32)
+            for _ in range(3):
+                call()
+            torch.cuda.synchronize()
+
+            def both():
+                for _ in range(reps):
+                    torch.sum(flush, dim=0, out=sink)
+                    call()
+
+            ms = max(graph_time(both) - t_flush, 1e-6) / reps
+            byts = e * n * kb + t * kb + sf_bytes + 2 * t * n
+            rows.append({"family": family, "mix": label, "experts": e, "tokens": t, "n": n, "k": k,
+                         "us": ms * 1e3, "tflops": 2.0 * t * n * k / ms / 1e9, "gbs": byts / ms / 1e6,
+                         "hbm_frac": byts / ms / 1e6 / peaks["hbm_gbs"]})
+            del B, SB, qa, sa, out
+    assert bs.check_device_error() == 0
+    print(json.dumps({"grouped": "MoE GEMMs, experts x tokens, each expert its own weights",
+                      "hbm_peak_gbs": peaks["hbm_gbs"], "peak_kind": peak_kind,
+                      "l2": "flushed (256 MiB read) before every call",
+                      "timing": f"graph of {reps} x (flush, call) minus graph of {reps} flushes", "rows": rows}),
+          flush=True)
+    return 0
+
+
 # (N, K) groups of the reference's traced DeepSeek-V4 a8w8 deployment shapes
 # (dsv4_a8w8_all_traced_shapes.csv: 125 rows, M from 6 to 16384), tuned at
 # power-of-two M buckets: a call takes the row of the smallest tuned M >= its M.
@@ -894,6 +1004,8 @@ def main():
         return run_sweep(args)
     if args.quant:
         return run_quant(args)
+    if args.grouped:
+        return run_grouped(args)
     return run_ours(args)
 
 
