@@ -76,6 +76,8 @@ def lib() -> ctypes.CDLL:
         "bsgemm_a8w8_mxfp8_grouped": (I, [ctypes.POINTER(Args), P, I, P]),
         "bsgemm_a4w4_mxfp4_grouped": (I, [ctypes.POINTER(Args), P, I, P]),
         "bsgemm_mx_grouped_workspace_size": (S, [ctypes.POINTER(Args)]),
+        "bsgemm_mx_host_workspace_size": (S, [I, ctypes.POINTER(Args)]),
+        "bsgemm_mx_host_gemm": (I, [I, ctypes.POINTER(Args), P, S, I, P]),
         "bsgemm_workspace_size": (S, [I, ctypes.POINTER(Args)]),
         "bsgemm_pack_b": (I, [P, P, I, I, I, I, P]),
         "bsgemm_pack_scales": (I, [P, I, P, I, I, I, I, P]),
@@ -452,6 +454,67 @@ def gemm_a4w4_mxfp4_grouped(A, B, A_scale, B_scale, group_offsets, max_rows: int
     return _mx_grouped(A, B, A_scale, B_scale, group_offsets, max_rows, fp4=True, out_dtype=out_dtype,
                        out=out, b_format=b_format, b_scale_format=b_scale_format, workspace=workspace,
                        grid_blocks=grid_blocks)
+
+
+def gemm_mx_from_host(A, B, A_scale, B_scale, *, fp4: bool, out_dtype=torch.bfloat16, out=None,
+                      b_format: str = "raw", chunks: int = 0, workspace=None, device=None):
+    """MXFP8 (fp4=False) or MXFP4 GEMM on host-resident operands, the
+    reference drivers' copy-in / launch / copy-out sequence with the copies
+    pipelined against the GEMM blocks (bsgemm_mx_host_gemm).
+
+    A [M,K] E4M3 or [M,K/2] packed E2M1 bytes, B [N,K] (or its
+    shuffle_weight(16,16) bytes with b_format="shuffle16") and row-major E8M0
+    scales [rows, K/32], all CPU tensors (pinned for overlap).  Returns C
+    [M,N] in host memory (pinned, unless `out` is given); the call returns once
+    C is complete.  workspace: a CUDA uint8 tensor of at least
+    bsgemm_mx_host_workspace_size bytes, allocated when omitted."""
+    if b_format not in _B_FORMATS:
+        raise ValueError(f"b_format must be one of {sorted(_B_FORMATS)}")
+    tensors = (A, B, A_scale, B_scale)
+    if any(t.is_cuda for t in tensors) or A.dim() != 2 or B.dim() != 2:
+        raise ValueError("A, B and the scales must be 2-D host (CPU) tensors")
+    ok_types = _FP4 if fp4 else _FP8
+    if A.dtype not in ok_types or B.dtype not in ok_types:
+        raise ValueError("A/B must hold %s bytes" % ("packed E2M1" if fp4 else "E4M3FN"))
+    if A_scale.dtype not in _SCALE_U8 or B_scale.dtype not in _SCALE_U8:
+        raise ValueError("scales must be E8M0 bytes")
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("out_dtype must be bfloat16 or float32")
+    m, kb = A.shape
+    n = B.shape[0]
+    k = 2 * kb if fp4 else kb
+    if B.shape[1] != kb or any(t.stride(-1) != 1 for t in tensors):
+        raise ValueError("A and B must agree on K and have unit inner stride")
+    if tuple(A_scale.shape) != (m, k // 32) or tuple(B_scale.shape) != (n, k // 32):
+        raise ValueError("scales must be [rows, K/32]")
+    device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if out is None:
+        out = torch.empty(m, n, dtype=out_dtype, pin_memory=True)
+    elif out.is_cuda or tuple(out.shape) != (m, n) or out.dtype != out_dtype or out.stride(1) != 1:
+        raise ValueError("out must be a host tensor [M, N] of out_dtype with unit inner stride")
+    args = Args()
+    lib().bsgemm_args_init(ctypes.byref(args))
+    args.ptr_a, args.ptr_b, args.ptr_c = A.data_ptr(), B.data_ptr(), out.data_ptr()
+    args.m, args.n, args.k = m, n, k
+    args.stride_a, args.stride_b, args.stride_c = A.stride(0), B.stride(0), out.stride(0)
+    args.ptr_sfa, args.ptr_sfb = A_scale.data_ptr(), B_scale.data_ptr()
+    args.stride_sfa, args.stride_sfb = A_scale.stride(0), B_scale.stride(0)
+    args.b_format = _B_FORMATS[b_format]
+    args.out_dtype = OUT_BF16 if out_dtype == torch.bfloat16 else OUT_FP32
+    family = FAMILY_MXFP4 if fp4 else FAMILY_MXFP8
+    need = int(lib().bsgemm_mx_host_workspace_size(family, ctypes.byref(args)))
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=device)
+    elif not workspace.is_cuda or workspace.numel() * workspace.element_size() < need:
+        raise ValueError(f"workspace must be a CUDA tensor of at least {need} bytes")
+    with torch.cuda.device(workspace.device):
+        stream = torch.cuda.current_stream(workspace.device)
+        status = lib().bsgemm_mx_host_gemm(family, ctypes.byref(args), ctypes.c_void_p(workspace.data_ptr()),
+                                           workspace.numel() * workspace.element_size(), int(chunks),
+                                           ctypes.c_void_p(stream.cuda_stream))
+        _check(status, "bsgemm_mx_host_gemm")
+        stream.synchronize()
+    return out
 
 
 def _mx_grouped(A, B, A_scale, B_scale, group_offsets, max_rows, *, fp4, out_dtype, out, b_format,

@@ -1393,6 +1393,230 @@ int mx_grouped_run(const bsgemm_args* args, bool fp4, const int* group_offsets, 
              : mx_grouped_launch<0>(bn, o.bmode, f32, ta, tb, p, grid, st);
 }
 
+// ---------------------------------------------------------------------------
+// Host-staged MX GEMM: operands and C in host memory, copies pipelined with
+// the GEMM blocks (the reference drivers' copy-in / launch / copy-out flow)
+// ---------------------------------------------------------------------------
+constexpr int kHostMaxChunks = 8;
+
+// Per-device streams and events of the pipeline, created once.  The whole
+// enqueue sequence of a call holds the device's mutex, so two host threads
+// never interleave their records and waits on the shared events.
+struct HostPipe {
+  bool ready = false;
+  cudaStream_t comp = nullptr, d2h = nullptr;
+  cudaEvent_t start = nullptr, end = nullptr;
+  cudaEvent_t in_a[kHostMaxChunks] = {}, in_b[kHostMaxChunks] = {};
+  cudaEvent_t blk[2 * kHostMaxChunks] = {};   // the two strips of each step
+  std::mutex mu;
+};
+
+int host_pipe(HostPipe** out) {
+  static HostPipe pipes[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return BSG_ERR_CUDA;
+  HostPipe& hp = pipes[dev];
+  *out = &hp;
+  std::lock_guard<std::mutex> lock(hp.mu);
+  if (hp.ready) return BSG_OK;
+  auto ev = [](cudaEvent_t* e) { return cudaEventCreateWithFlags(e, cudaEventDisableTiming) == cudaSuccess; };
+  bool ok = cudaStreamCreateWithFlags(&hp.comp, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&hp.d2h, cudaStreamNonBlocking) == cudaSuccess && ev(&hp.start) &&
+            ev(&hp.end);
+  for (int i = 0; ok && i < kHostMaxChunks; ++i) ok = ev(&hp.in_a[i]) && ev(&hp.in_b[i]);
+  for (int i = 0; ok && i < 2 * kHostMaxChunks; ++i) ok = ev(&hp.blk[i]);
+  if (!ok) {
+    t_last_cuda_error = cudaGetLastError();
+    return BSG_ERR_CUDA;
+  }
+  hp.ready = true;
+  return BSG_OK;
+}
+
+// Device workspace of the host-staged call: A, B, their row-major scales,
+// their native scale atoms and C, each 256-byte aligned.
+struct HostLayout {
+  size_t a, b, sa, sb, na, nb, c, total;
+};
+
+HostLayout host_layout(const bsgemm_args& a, bool fp4) {
+  const size_t kbytes = fp4 ? a.k / 2 : a.k, kg = a.k / 32;
+  HostLayout l;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off += align256(bytes);
+    return at;
+  };
+  l.a = take(static_cast<size_t>(a.m) * kbytes);
+  l.b = take(static_cast<size_t>(a.n) * kbytes);
+  l.sa = take(static_cast<size_t>(a.m) * kg);
+  l.sb = take(static_cast<size_t>(a.n) * kg);
+  l.na = take(native_sf_bytes(a.m, static_cast<int>(kg)));
+  l.nb = take(native_sf_bytes(a.n, static_cast<int>(kg)));
+  l.c = take(static_cast<size_t>(a.m) * a.n * (a.out_dtype == BSG_OUT_FP32 ? 4 : 2));
+  l.total = off;
+  return l;
+}
+
+// Chunk boundaries along one dimension: `chunks` pieces, multiples of 256
+// rows except the last (native scale atoms and C columns stay aligned).
+int chunk_bounds(int extent, int chunks, int* bounds) {
+  const int step = std::max(256, (extent + chunks - 1) / chunks + 255) / 256 * 256;
+  int c = 0;
+  bounds[0] = 0;
+  while (bounds[c] < extent && c < kHostMaxChunks) {
+    bounds[c + 1] = std::min(extent, bounds[c] + step);
+    ++c;
+  }
+  return c;
+}
+
+int host_gemm_run(int family, const bsgemm_args* args, void* dev_ws, size_t dev_ws_bytes, int chunks,
+                  cudaStream_t st) {
+  if (!args) return BSG_ERR_INVALID_VALUE;
+  if (family != BSG_FAMILY_MXFP8 && family != BSG_FAMILY_MXFP4) return BSG_ERR_UNSUPPORTED;
+  const bool fp4 = family == BSG_FAMILY_MXFP4;
+  const bsgemm_args& a = *args;
+  if (!a.ptr_a || !a.ptr_b || !a.ptr_c || !a.ptr_sfa || !a.ptr_sfb || !dev_ws) return BSG_ERR_INVALID_VALUE;
+  if (a.m <= 0 || a.n <= 0 || a.k <= 0 || a.batch != 1 || chunks < 0 || chunks > kHostMaxChunks)
+    return BSG_ERR_INVALID_VALUE;
+  if (a.out_dtype != BSG_OUT_BF16 && a.out_dtype != BSG_OUT_FP32) return BSG_ERR_INVALID_VALUE;
+  if (a.layout != BSG_LAYOUT_TN || a.sfa_format != BSG_SF_ROWMAJOR || a.sfb_format != BSG_SF_ROWMAJOR)
+    return BSG_ERR_UNSUPPORTED;
+  if (a.b_format != BSG_B_RAW && a.b_format != BSG_B_SHUFFLE16) return BSG_ERR_UNSUPPORTED;
+  if (a.k % (fp4 ? 256 : 128)) return BSG_ERR_INVALID_VALUE;
+  const int vec = a.out_dtype == BSG_OUT_BF16 ? 8 : 4;
+  if (a.n % vec || a.stride_c < a.n) return BSG_ERR_ALIGNMENT;
+  const size_t kbytes = fp4 ? a.k / 2 : a.k, kg = a.k / 32;
+  const bool shuffled = a.b_format == BSG_B_SHUFFLE16;
+  if (a.stride_a < static_cast<long long>(kbytes) || a.stride_b < static_cast<long long>(kbytes) ||
+      a.stride_sfa < static_cast<long long>(kg) || a.stride_sfb < static_cast<long long>(kg))
+    return BSG_ERR_INVALID_VALUE;
+  if (shuffled && (a.n % 16 || a.stride_b != static_cast<long long>(kbytes))) return BSG_ERR_INVALID_VALUE;
+  const HostLayout l = host_layout(a, fp4);
+  if (dev_ws_bytes < l.total) return BSG_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(dev_ws) & 255u) return BSG_ERR_ALIGNMENT;
+  DevInfo dev;
+  int rc;
+  if ((rc = device_info(&dev)) != BSG_OK) return rc;
+  if (!dev.sm100) return BSG_ERR_ARCH;
+
+  int mb[kHostMaxChunks + 1], nb[kHostMaxChunks + 1];
+  const int auto_m = std::min(4, std::max(1, a.m / 1024)), auto_n = std::min(4, std::max(1, a.n / 1024));
+  const int cm = chunk_bounds(a.m, chunks ? chunks : auto_m, mb);
+  const int cn = chunk_bounds(a.n, chunks ? chunks : auto_n, nb);
+  HostPipe* hp = nullptr;
+  if ((rc = host_pipe(&hp)) != BSG_OK) return rc;
+  std::lock_guard<std::mutex> lock(hp->mu);
+
+  uint8_t* ws = static_cast<uint8_t*>(dev_ws);
+  const uint8_t* ha = static_cast<const uint8_t*>(a.ptr_a);
+  const uint8_t* hb = static_cast<const uint8_t*>(a.ptr_b);
+  const uint8_t* hsa = static_cast<const uint8_t*>(a.ptr_sfa);
+  const uint8_t* hsb = static_cast<const uint8_t*>(a.ptr_sfb);
+  const size_t esz = a.out_dtype == BSG_OUT_FP32 ? 4 : 2;
+  const int kb_atoms = static_cast<int>((kg + 3) / 4);
+  cudaError_t e = cudaSuccess;
+  auto chk = [&](cudaError_t r) {
+    if (r != cudaSuccess && e == cudaSuccess) e = r;
+    return r == cudaSuccess;
+  };
+  // rows [r0, r1) of a host matrix (pitch `ld` bytes) into dense device rows
+  auto h2d_rows = [&](uint8_t* dst, const uint8_t* src, long long ld, size_t width, int r0, int r1) {
+    return chk(cudaMemcpy2DAsync(dst + static_cast<size_t>(r0) * width, width, src + static_cast<size_t>(r0) * ld,
+                                 static_cast<size_t>(ld), width, static_cast<size_t>(r1 - r0),
+                                 cudaMemcpyHostToDevice, st));
+  };
+
+  chk(cudaEventRecord(hp->start, st));
+  chk(cudaStreamWaitEvent(hp->comp, hp->start, 0));
+  chk(cudaStreamWaitEvent(hp->d2h, hp->start, 0));
+  const long long b_ld = shuffled ? static_cast<long long>(kbytes) : a.stride_b;
+  int status = BSG_OK;   // a failed launch stops the enqueueing; the join below always runs
+  // One GEMM over rows [r0, r1) x columns [c0, c1) of C from the device
+  // copies, then its copy back to the host C (strided rows).
+  auto strip = [&](int r0, int r1, int c0, int c1, cudaEvent_t done) {
+    if (r1 <= r0 || c1 <= c0 || status != BSG_OK || e != cudaSuccess) return;
+    bsgemm_args g = a;
+    g.ptr_a = ws + l.a + static_cast<size_t>(r0) * kbytes;
+    g.ptr_b = ws + l.b + static_cast<size_t>(c0) * kbytes;
+    g.ptr_c = ws + l.c + (static_cast<size_t>(r0) * a.n + c0) * esz;
+    g.ptr_sfa = ws + l.na + static_cast<size_t>(r0 / 128) * kb_atoms * 512;
+    g.ptr_sfb = ws + l.nb + static_cast<size_t>(c0 / 128) * kb_atoms * 512;
+    g.m = r1 - r0;
+    g.n = c1 - c0;
+    g.stride_a = static_cast<int>(kbytes);
+    g.stride_b = static_cast<int>(kbytes);
+    g.stride_c = a.n;
+    g.sfa_format = g.sfb_format = BSG_SF_NATIVE;
+    g.split_k = 1;
+    g.workspace = nullptr;
+    g.workspace_bytes = 0;
+    const int r = mx_run(&g, fp4, hp->comp);
+    if (r != BSG_OK) {
+      status = r;
+      return;
+    }
+    chk(cudaEventRecord(done, hp->comp));
+    chk(cudaStreamWaitEvent(hp->d2h, done, 0));
+    chk(cudaMemcpy2DAsync(static_cast<uint8_t*>(a.ptr_c) + (static_cast<size_t>(r0) * a.stride_c + c0) * esz,
+                          static_cast<size_t>(a.stride_c) * esz,
+                          ws + l.c + (static_cast<size_t>(r0) * a.n + c0) * esz, static_cast<size_t>(a.n) * esz,
+                          static_cast<size_t>(c1 - c0) * esz, static_cast<size_t>(r1 - r0),
+                          cudaMemcpyDeviceToHost, hp->d2h));
+  };
+  // Step t brings B chunk t, then A chunk t.  The C blocks that become
+  // computable are the column strip (A chunks < t) x (B chunk t), which runs
+  // while A chunk t is still in flight, and the row strip (A chunk t) x (B
+  // chunks <= t): two GEMMs per step whatever the chunk count.
+  // Every input copy is queued first, so the copy engine never waits for
+  // the host to enqueue GEMMs.
+  for (int t = 0; t < std::max(cm, cn) && e == cudaSuccess; ++t) {
+    if (t < cn) {
+      // shuffle_weight(16,16) bytes of rows [n0, n1) are contiguous (n0 % 16 == 0)
+      h2d_rows(ws + l.b, hb, b_ld, kbytes, nb[t], nb[t + 1]);
+      h2d_rows(ws + l.sb, hsb, a.stride_sfb, kg, nb[t], nb[t + 1]);
+      chk(cudaEventRecord(hp->in_b[t], st));
+    }
+    if (t < cm) {
+      h2d_rows(ws + l.a, ha, a.stride_a, kbytes, mb[t], mb[t + 1]);
+      h2d_rows(ws + l.sa, hsa, a.stride_sfa, kg, mb[t], mb[t + 1]);
+      chk(cudaEventRecord(hp->in_a[t], st));
+    }
+  }
+  for (int t = 0; t < std::max(cm, cn) && e == cudaSuccess && status == BSG_OK; ++t) {
+    if (t < cn) {
+      chk(cudaStreamWaitEvent(hp->comp, hp->in_b[t], 0));
+      const int rc2 = pack_sf_launch(ws + l.sb + static_cast<size_t>(nb[t]) * kg, static_cast<int>(kg),
+                                     ws + l.nb + static_cast<size_t>(nb[t] / 128) * kb_atoms * 512, nb[t + 1] - nb[t],
+                                     static_cast<int>(kg), BSG_SF_ROWMAJOR, 0, hp->comp);
+      if (rc2 != BSG_OK) status = rc2;
+      strip(0, mb[std::min(t, cm)], nb[t], nb[t + 1], hp->blk[2 * t]);
+    }
+    if (t < cm) {
+      chk(cudaStreamWaitEvent(hp->comp, hp->in_a[t], 0));
+      const int rc2 = pack_sf_launch(ws + l.sa + static_cast<size_t>(mb[t]) * kg, static_cast<int>(kg),
+                                     ws + l.na + static_cast<size_t>(mb[t] / 128) * kb_atoms * 512, mb[t + 1] - mb[t],
+                                     static_cast<int>(kg), BSG_SF_ROWMAJOR, 0, hp->comp);
+      if (rc2 != BSG_OK && status == BSG_OK) status = rc2;
+      strip(mb[t], mb[t + 1], 0, nb[std::min(t, cn - 1) + 1], hp->blk[2 * t + 1]);
+    }
+  }
+  // the caller's stream resumes after every block is back in host memory
+  // (and, after a failure, after whatever was enqueued on either stream)
+  chk(cudaEventRecord(hp->end, hp->comp));
+  chk(cudaStreamWaitEvent(hp->d2h, hp->end, 0));
+  chk(cudaEventRecord(hp->end, hp->d2h));
+  chk(cudaStreamWaitEvent(st, hp->end, 0));
+  if (status != BSG_OK) return status;
+  if (e != cudaSuccess) {
+    t_last_cuda_error = e;
+    return BSG_ERR_CUDA;
+  }
+  return BSG_OK;
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -1436,6 +1660,18 @@ int bsgemm_a8w8_mxfp8_grouped(const bsgemm_args* args, const int* group_offsets,
 int bsgemm_a4w4_mxfp4_grouped(const bsgemm_args* args, const int* group_offsets, int total_rows,
                               bsg_stream_t stream) {
   return mx_grouped_run(args, true, group_offsets, total_rows, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t bsgemm_mx_host_workspace_size(int family, const bsgemm_args* args) {
+  if (!args || args->m <= 0 || args->n <= 0 || args->k <= 0) return 0;
+  if (family != BSG_FAMILY_MXFP8 && family != BSG_FAMILY_MXFP4) return 0;
+  return host_layout(*args, family == BSG_FAMILY_MXFP4).total;
+}
+
+int bsgemm_mx_host_gemm(int family, const bsgemm_args* args, void* dev_workspace, size_t dev_workspace_bytes,
+                        int chunks, bsg_stream_t stream) {
+  return host_gemm_run(family, args, dev_workspace, dev_workspace_bytes, chunks,
+                       reinterpret_cast<cudaStream_t>(stream));
 }
 
 size_t bsgemm_mx_grouped_workspace_size(const bsgemm_args* args) {

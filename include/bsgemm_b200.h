@@ -208,6 +208,29 @@ BSG_API int bsgemm_a4w4_mxfp4_grouped(const bsgemm_args *args, const int *group_
 BSG_API size_t bsgemm_mx_grouped_workspace_size(const bsgemm_args *args);
 
 /*
+ * Host-staged MXFP8 / MXFP4 GEMM (family BSG_FAMILY_MXFP8 or _MXFP4): A, B,
+ * their E8M0 scales (BSG_SF_ROWMAJOR) and C are HOST pointers (pinned for
+ * asynchronous copies), with the strides of bsgemm_a8w8_mxfp8; layout TN,
+ * batch 1, B raw or BSG_B_SHUFFLE16.  The call copies the operands in
+ * row chunks (chunks per dimension, 1..8; 0 = one per 1024 rows, at most 4)
+ * on `stream`, runs each C block's GEMM on an internal stream as soon as its
+ * A and B chunks have arrived, and copies each finished block back on a
+ * second internal stream, so both copy directions and the GEMMs overlap.
+ * dev_workspace (256-byte aligned) holds the device copies and C:
+ * bsgemm_mx_host_workspace_size(family, args) bytes.  Asynchronous: C is
+ * complete when `stream` reaches this point.  The block GEMMs run without
+ * split-K (args->split_k and args->workspace are ignored).  The first call
+ * on a device creates the two internal streams and their events (no device
+ * memory); calls on one device are serialised while they enqueue.
+ * Replaces the reference drivers' hipMemcpy-in / launch / hipMemcpy-out
+ * sequence (mxfp8_gemm/gemm_a8w8_mxfp8_host.cc:261-301,
+ * mxfp4_gemm_4wave_20261112/gemm_a4w4_mxfp4_4wave_host.cc:195-224).
+ */
+BSG_API size_t bsgemm_mx_host_workspace_size(int family, const bsgemm_args *args);
+BSG_API int bsgemm_mx_host_gemm(int family, const bsgemm_args *args, void *dev_workspace,
+                                size_t dev_workspace_bytes, int chunks, bsg_stream_t stream);
+
+/*
  * Bytes of split-K workspace the call would need (0 when it runs without
  * split-K).  family = BSG_FAMILY_*.
  */

@@ -87,6 +87,35 @@ def test_mx_grouped_workspace_and_rejections(bs):
         assert fn(ctypes.byref(a), offs, 100, None) == bs.ERR_INVALID_VALUE   # null operands
 
 
+def test_mx_host_workspace_and_rejections(bs):
+    """Host-staged MX GEMM: the device workspace holds A, B, both scale forms
+    and C (256-byte aligned pieces); bad arguments fail before any CUDA call."""
+    lib = bs.lib()
+    a = bs.Args()
+    lib.bsgemm_args_init(ctypes.byref(a))
+    a.m, a.n, a.k = 700, 640, 512
+
+    def al(x):
+        return (x + 255) // 256 * 256
+
+    want = (al(700 * 512) + al(640 * 512) + al(700 * 16) + al(640 * 16) + al(lib.bsgemm_native_scales_size(700, 16))
+            + al(lib.bsgemm_native_scales_size(640, 16)) + al(700 * 640 * 2))
+    assert lib.bsgemm_mx_host_workspace_size(bs.FAMILY_MXFP8, ctypes.byref(a)) == want
+    assert lib.bsgemm_mx_host_workspace_size(bs.FAMILY_FP8_BLOCK, ctypes.byref(a)) == 0
+    fn = lib.bsgemm_mx_host_gemm
+    assert fn(bs.FAMILY_MXFP8, None, None, 0, 0, None) == bs.ERR_INVALID_VALUE
+    assert fn(bs.FAMILY_FP8_BLOCK, ctypes.byref(a), None, 0, 0, None) == bs.ERR_UNSUPPORTED
+    assert fn(bs.FAMILY_MXFP8, ctypes.byref(a), None, 0, 0, None) == bs.ERR_INVALID_VALUE   # null pointers
+    a.ptr_a = a.ptr_b = a.ptr_c = a.ptr_sfa = a.ptr_sfb = 4096
+    a.stride_a = a.stride_b = 512
+    a.stride_c = 640
+    a.stride_sfa = a.stride_sfb = 16
+    assert fn(bs.FAMILY_MXFP8, ctypes.byref(a), ctypes.c_void_p(1 << 20), 0, 9, None) == bs.ERR_INVALID_VALUE
+    assert fn(bs.FAMILY_MXFP8, ctypes.byref(a), ctypes.c_void_p(1 << 20), 1024, 0, None) == bs.ERR_WORKSPACE
+    a.layout = bs.LAYOUTS["nn"]
+    assert fn(bs.FAMILY_MXFP8, ctypes.byref(a), ctypes.c_void_p(1 << 20), 1 << 30, 0, None) == bs.ERR_UNSUPPORTED
+
+
 def test_python_api_rejects_cpu_tensors(bs):
     import torch
     a = torch.zeros(128, 128, dtype=torch.float8_e4m3fn)

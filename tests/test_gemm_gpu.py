@@ -537,6 +537,44 @@ def test_mx_grouped_matches_dense(bs, orc, cuda):
     assert torch.equal(dense, grouped)
 
 
+@pytest.mark.parametrize("fp4,m,n,k,chunks,b_format,out_dtype,pinned", [
+    (False, 700, 640, 512, 3, "raw", torch.bfloat16, True),
+    (False, 128, 256, 256, 1, "raw", torch.float32, False),
+    (True, 300, 512, 1024, 2, "shuffle16", torch.bfloat16, True),
+    (True, 1100, 1280, 512, 0, "raw", torch.bfloat16, True),
+])
+def test_mx_host_staged(bs, orc, cuda, fp4, m, n, k, chunks, b_format, out_dtype, pinned):
+    """Host-resident operands through the pipelined copy-in / GEMM blocks /
+    copy-out entry point: ragged last chunks in both dimensions, pinned and
+    pageable host memory, against the oracle; a host C with a wider row pitch
+    keeps its padding untouched."""
+    if fp4:
+        qa, qb, sa, sb = mxfp4_problem(orc, m, n, k, 40 + m, "rowpattern")
+        ref, mag = orc.gemm_mxfp4(qa, qb, sa, sb)
+    else:
+        qa_l, qb_l, sa_l, sb_l = mxfp8_problem(orc, m, n, k, 40 + m, "rowpattern")
+        qa, qb, sa, sb = qa_l[0], qb_l[0], sa_l[0], sb_l[0]
+        ref, mag = orc.gemm_mxfp8(qa, qb, sa, sb, f64=True)
+    bh = orc.shuffle_weight16(qb) if b_format == "shuffle16" else qb
+
+    def host(x):
+        t = torch.from_numpy(np.ascontiguousarray(x))
+        return t.pin_memory() if pinned else t
+
+    A, B, SA, SB = host(qa), host(bh), host(sa), host(sb)
+    if not fp4:
+        A, B = A.view(torch.float8_e4m3fn), B.view(torch.float8_e4m3fn)
+    wide = torch.full((m, n + 8), float("nan"), dtype=out_dtype)
+    out = wide[:, :n]
+    with torch.cuda.device(cuda):
+        got = bs.gemm_mx_from_host(A, B, SA, SB, fp4=fp4, out_dtype=out_dtype, out=out, b_format=b_format,
+                                   chunks=chunks)
+    assert bs.check_device_error() == 0
+    assert got.data_ptr() == out.data_ptr()
+    assert_close(orc, ref, got.float().numpy(), mag, f"host-staged fp4={fp4} {m}x{n}x{k} chunks={chunks}")
+    assert torch.isnan(wide[:, n:]).all(), "the row padding of C was written"
+
+
 @pytest.mark.parametrize("m,kernel", [(16, "swap"), (48, "swap"), (200, "1cta")])
 def test_fp8_block_shuffle16_b(bs, orc, cuda, m, kernel):
     """aiter shuffle_weight(16,16) weights read in place by both kernels."""
