@@ -1522,11 +1522,16 @@ int host_gemm_run(int family, const bsgemm_args* args, void* dev_ws, size_t dev_
     if (r != cudaSuccess && e == cudaSuccess) e = r;
     return r == cudaSuccess;
   };
-  // rows [r0, r1) of a host matrix (pitch `ld` bytes) into dense device rows
+  // rows [r0, r1) of a host matrix (pitch `ld` bytes) into dense device rows;
+  // dense rows go as one linear copy (strided 2-D copies ran at half the
+  // PCIe rate while copies in the other direction were running)
   auto h2d_rows = [&](uint8_t* dst, const uint8_t* src, long long ld, size_t width, int r0, int r1) {
-    return chk(cudaMemcpy2DAsync(dst + static_cast<size_t>(r0) * width, width, src + static_cast<size_t>(r0) * ld,
-                                 static_cast<size_t>(ld), width, static_cast<size_t>(r1 - r0),
-                                 cudaMemcpyHostToDevice, st));
+    uint8_t* d = dst + static_cast<size_t>(r0) * width;
+    const uint8_t* h = src + static_cast<size_t>(r0) * ld;
+    const size_t rows = static_cast<size_t>(r1 - r0);
+    if (static_cast<size_t>(ld) == width)
+      return chk(cudaMemcpyAsync(d, h, rows * width, cudaMemcpyHostToDevice, st));
+    return chk(cudaMemcpy2DAsync(d, width, h, static_cast<size_t>(ld), width, rows, cudaMemcpyHostToDevice, st));
   };
 
   chk(cudaEventRecord(hp->start, st));
@@ -1560,11 +1565,14 @@ int host_gemm_run(int family, const bsgemm_args* args, void* dev_ws, size_t dev_
     }
     chk(cudaEventRecord(done, hp->comp));
     chk(cudaStreamWaitEvent(hp->d2h, done, 0));
-    chk(cudaMemcpy2DAsync(static_cast<uint8_t*>(a.ptr_c) + (static_cast<size_t>(r0) * a.stride_c + c0) * esz,
-                          static_cast<size_t>(a.stride_c) * esz,
-                          ws + l.c + (static_cast<size_t>(r0) * a.n + c0) * esz, static_cast<size_t>(a.n) * esz,
-                          static_cast<size_t>(c1 - c0) * esz, static_cast<size_t>(r1 - r0),
-                          cudaMemcpyDeviceToHost, hp->d2h));
+    uint8_t* hc = static_cast<uint8_t*>(a.ptr_c) + (static_cast<size_t>(r0) * a.stride_c + c0) * esz;
+    const uint8_t* dc = ws + l.c + (static_cast<size_t>(r0) * a.n + c0) * esz;
+    if (c0 == 0 && c1 == a.n && a.stride_c == a.n)   // whole rows: one linear copy
+      chk(cudaMemcpyAsync(hc, dc, static_cast<size_t>(r1 - r0) * a.n * esz, cudaMemcpyDeviceToHost, hp->d2h));
+    else
+      chk(cudaMemcpy2DAsync(hc, static_cast<size_t>(a.stride_c) * esz, dc, static_cast<size_t>(a.n) * esz,
+                            static_cast<size_t>(c1 - c0) * esz, static_cast<size_t>(r1 - r0),
+                            cudaMemcpyDeviceToHost, hp->d2h));
   };
   // Step t brings B chunk t, then A chunk t.  The C blocks that become
   // computable are the column strip (A chunks < t) x (B chunk t), which runs
