@@ -11,8 +11,8 @@
 // Because the scales are arbitrary fp32 (not powers of two) they cannot be
 // folded into a block-scaled MMA.  Instead:
 //   - the single-thread issuer runs 4 x .kind::f8f6f4 MMAs (K = 32 each) per
-//     128-K block into one of two TMEM buffers (128 x BN fp32 each), so the
-//     tensor core fills buffer kb+1 while buffer kb is being promoted;
+//     128-K block into one of four TMEM buffers (128 x BN fp32 each), so the
+//     tensor core fills the next buffers while buffer kb is being promoted;
 //   - the epilogue warps (the "promotion" warps) tcgen05.ld each finished
 //     partial and FMA it into a register accumulator with the per-row A scale
 //     times the per-tile B scale, then release the buffer; after the last K
@@ -91,7 +91,11 @@ struct Fp8BlockCfg {
   static constexpr uint32_t kOffB = kABytes * kStages;
   static constexpr uint32_t kOffBar = kOffB + kBBytes * kStages;
   static constexpr uint32_t kSmemBytes = kOffBar + 256u + 1024u;
-  static constexpr uint32_t kTmemCols = 2u * BN;  // two accumulator buffers
+  // Four TMEM partial buffers (all 512 columns): the MMA runs up to four K
+  // blocks ahead of the promotion (two buffers: 1666 against 1736 TFLOPS at
+  // M=8192 N=7168 K=8192, together with the batched loads below).
+  static constexpr int kAccBufs = 4;
+  static constexpr uint32_t kTmemCols = kAccBufs * BN;
 };
 
 // kGrouped: the batch index is a group (expert) whose rows of A, sfa and C
@@ -112,9 +116,11 @@ __global__ void __launch_bounds__(256, 1)
   uint8_t* sB = smem + Cfg::kOffB;
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
   uint64_t* empty_bar = full_bar + S;
-  uint64_t* acc_full = empty_bar + S;    // [2]
-  uint64_t* acc_empty = acc_full + 2;    // [2]
-  uint64_t* drain_bar = acc_empty + 2;
+  constexpr int NB = Cfg::kAccBufs;
+  uint64_t* acc_full = empty_bar + S;    // [NB]
+  uint64_t* acc_empty = acc_full + NB;   // [NB]
+  uint64_t* drain_bar = acc_empty + NB;
+  static_assert(8 * (2 * Cfg::kStages + 2 * Cfg::kAccBufs + 1) + 8 <= 256, "barrier area");
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -126,7 +132,7 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(&full_bar[i], 1);
       mbar_init(&empty_bar[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NB; ++i) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 4);   // one arrival per promotion warp
     }
@@ -229,8 +235,8 @@ __global__ void __launch_bounds__(256, 1)
       const int kb0 = s * p.kb_per_split;
       const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
       for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
-        const uint32_t buf = kbi & 1u;
-        const uint32_t use = kbi >> 1;   // how many times this buffer was used before
+        const uint32_t buf = kbi % NB;
+        const uint32_t use = kbi / NB;   // how many times this buffer was used before
         if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, abort_flag, p.timeout_ns)) {
           ok = false;
           break;
@@ -298,20 +304,29 @@ __global__ void __launch_bounds__(256, 1)
           sa_next = row_ok ? __ldg(sfa_row + (kb + 1) * p.sfa_k) : 0.0f;
           sb_next = __ldg(sfb_blk + (kb + 1) * p.sfb_k);
         }
-        const uint32_t buf = kbi & 1u;
-        const uint32_t use = kbi >> 1;
+        const uint32_t buf = kbi % NB;
+        const uint32_t use = kbi / NB;
         if (!mbar_wait(&acc_full[buf], use & 1u, abort_flag, p.timeout_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
         if (quarter_live) {
+          // two rounds of four 16-column loads in flight behind one wait
 #pragma unroll
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tmem_base + lane_base + buf * BN + static_cast<uint32_t>(c * 32), r);
+          for (int c = 0; c < BN / 64; ++c) {
+            uint32_t r[4][16];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc[c * 32 + i] = fmaf(__uint_as_float(r[i]), scale, acc[c * 32 + i]);
+            for (int j = 0; j < 4; ++j)
+              tmem_ld16_async(tmem_base + lane_base + buf * BN + static_cast<uint32_t>(c * 64 + j * 16), r[j]);
+            tmem_wait_ld16(r[0]);
+#pragma unroll
+            for (int j = 1; j < 4; ++j) tmem_reg_fence16(r[j]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                acc[c * 64 + j * 16 + i] = fmaf(__uint_as_float(r[j][i]), scale, acc[c * 64 + j * 16 + i]);
           }
         }
         tc_fence_before();

@@ -55,42 +55,6 @@ __device__ __forceinline__ void prefetch_weight_tile(const CUtensorMap* tmB, int
     tma_prefetch_3d(tmB, kb * 128, nt * 128, b);
 }
 
-// tcgen05.ld of 32 lanes x 16 columns without the wait: the registers hold
-// the data only after tmem_wait_ld16 (or, for a later group, after
-// tmem_reg_fence16 placed behind that wait).
-__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32"
-      " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-}
-
-// Wait for this thread's TMEM loads.  The "+r" operands make every use of r
-// depend on the wait, so the compiler cannot hoist a use above it.
-__device__ __forceinline__ void tmem_wait_ld16(uint32_t (&r)[16]) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
-                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]),
-                 "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
-               :
-               : "memory");
-}
-
-// Ties the uses of r to a position after an earlier tmem_wait_ld16 (volatile
-// asm statements keep their program order).
-__device__ __forceinline__ void tmem_reg_fence16(uint32_t (&r)[16]) {
-  asm volatile(""
-               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
-                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]),
-                 "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
-               :
-               : "memory");
-}
-
 template <int MN>
 struct SwapCfg {
   static_assert(MN == 16 || MN == 32 || MN == 64, "MN must be 16, 32 or 64");
