@@ -293,13 +293,16 @@ __global__ void __launch_bounds__(256, 1)
       const long long grow = static_cast<long long>(row0) + row;   // row in A, sfa and C
       const float* sfa_row = (kGrouped ? p.sfa : p.sfa + b * p.sfa_batch) + (row_ok ? grow : 0) * p.sfa_m;
       const float* sfb_blk = p.sfb + b * p.sfb_batch + static_cast<long long>(n0 / 128) * p.sfb_n;
-      float acc[BN];
+      // column pairs as fp32 x 2 for fma.rn.f32x2: half the FMA instructions
+      // in each warp's serial promotion round, and the same RN result per
+      // element as two fmaf
+      uint64_t accp[BN / 2];
 #pragma unroll
-      for (int i = 0; i < BN; ++i) acc[i] = 0.0f;
+      for (int i = 0; i < BN / 2; ++i) accp[i] = 0ull;
       float sa_next = row_ok ? __ldg(sfa_row + kb0 * p.sfa_k) : 0.0f;
       float sb_next = __ldg(sfb_blk + kb0 * p.sfb_k);
       for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
-        const float scale = sa_next * sb_next;
+        const uint64_t scale2 = pack_f32x2(sa_next * sb_next);
         if (kb + 1 < kb1) {
           sa_next = row_ok ? __ldg(sfa_row + (kb + 1) * p.sfa_k) : 0.0f;
           sb_next = __ldg(sfb_blk + (kb + 1) * p.sfb_k);
@@ -325,8 +328,7 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
             for (int j = 0; j < 4; ++j)
 #pragma unroll
-              for (int i = 0; i < 16; ++i)
-                acc[c * 64 + j * 16 + i] = fmaf(__uint_as_float(r[j][i]), scale, acc[c * 64 + j * 16 + i]);
+              for (int i = 0; i < 8; ++i) fma_f32x2(accp[(c * 64 + j * 16) / 2 + i], r[j][2 * i], r[j][2 * i + 1], scale2);
           }
         }
         tc_fence_before();
@@ -335,6 +337,9 @@ __global__ void __launch_bounds__(256, 1)
       }
       if (!ok) break;
       if (!row_ok) continue;
+      float acc[BN];
+#pragma unroll
+      for (int i = 0; i < BN / 2; ++i) unpack_f32x2(accp[i], acc[2 * i], acc[2 * i + 1]);
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
         const int col0 = n0 + c * 32;

@@ -597,6 +597,24 @@ __device__ __forceinline__ void tmem_reg_fence16(uint32_t (&r)[16]) {
                : "memory");
 }
 
+// Packed fp32 pairs (sm_100 fma.rn.f32x2: two independent round-to-nearest
+// FMAs per instruction).  acc += {lo, hi} * s2, lanes elementwise.
+__device__ __forceinline__ uint64_t pack_f32x2(float v) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(v));
+  return r;
+}
+
+__device__ __forceinline__ void fma_f32x2(uint64_t& acc, uint32_t lo, uint32_t hi, uint64_t s2) {
+  asm("{\n\t.reg .b64 t;\n\tmov.b64 t, {%1, %2};\n\tfma.rn.f32x2 %0, t, %3, %0;\n\t}"
+      : "+l"(acc)
+      : "r"(lo), "r"(hi), "l"(s2));
+}
+
+__device__ __forceinline__ void unpack_f32x2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
 __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
   asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d)
