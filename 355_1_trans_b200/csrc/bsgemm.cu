@@ -1201,7 +1201,7 @@ int fp8b_grouped_run(const bsgemm_args* args, const int* group_offsets, int tota
   p.split_k = 1;
   p.kb_per_split = kb;
   p.total_units = p.tiles_m * p.tiles_n * a.batch;
-  p.group_m = std::min(p.tiles_m, kGroupM);
+  p.group_m = kGroupM;   // rasterises the live M tiles, whose count only the device knows
   p.sfa = static_cast<const float*>(a.ptr_sfa);
   p.sfa_m = a.stride_sfa;
   p.sfa_k = 1;

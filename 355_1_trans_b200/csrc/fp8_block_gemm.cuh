@@ -61,6 +61,42 @@ __device__ __forceinline__ void group_rows(const Fp8BlockParams& p, int b, int& 
   rows = min(a1 - a0, p.m);
 }
 
+// The unit a persistent CTA works on.  Plain calls decode the tile grid.  A
+// grouped call with its groups' 128-row tile prefix in shared memory
+// (`pre`, live = prefix[batch] M tiles) enumerates only the M tiles that hold
+// rows, so ragged groups leave no CTA idle: gm belongs to the last group e
+// with pre[e] <= gm (empty groups share their successor's prefix), as its M
+// tile gm - pre[e].  Without the prefix (more groups than it holds), grouped
+// calls decode the full grid and skip the tiles past a group's rows.
+// Returns false for a unit to skip; every role skips the same units.
+template <bool kGrouped>
+__device__ __forceinline__ bool fp8b_unit(const Fp8BlockParams& p, const int* pre, int live, int u, int& b,
+                                          int& mt, int& nt, int& s, int& row0, int& rows) {
+  row0 = 0;
+  rows = p.m;
+  if constexpr (kGrouped) {
+    if (pre != nullptr) {
+      int gb, gm;
+      decode_unit(u, live, p.tiles_n, 1, p.group_m, gb, gm, nt, s);
+      int lo = 0, hi = p.batch - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (pre[mid] <= gm) lo = mid;
+        else hi = mid - 1;
+      }
+      b = lo;
+      mt = gm - pre[lo];
+    } else {
+      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+    }
+    group_rows(p, b, row0, rows);
+    return mt >= 0 && mt * 128 < rows;
+  } else {
+    decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+    return true;
+  }
+}
+
 // Weight (B) storage formats read in place:
 //   kFmtRaw        [N, K] K-major rows (128B-swizzled stage tiles);
 //   kFmtKPanel     the reference's shuffle_b K panels B'[K/128][N][128]
@@ -90,7 +126,10 @@ struct Fp8BlockCfg {
   static constexpr int kStages = 6;
   static constexpr uint32_t kOffB = kABytes * kStages;
   static constexpr uint32_t kOffBar = kOffB + kBBytes * kStages;
-  static constexpr uint32_t kSmemBytes = kOffBar + 256u + 1024u;
+  // grouped calls: the groups' M-tile prefix (up to kMaxPrefixGroups groups)
+  static constexpr int kMaxPrefixGroups = 1024;
+  static constexpr uint32_t kOffPrefix = kOffBar + 256u;
+  static constexpr uint32_t kSmemBytes = kOffPrefix + 4u * (kMaxPrefixGroups + 1) + 1024u;
   // Four TMEM partial buffers (all 512 columns): the MMA runs up to four K
   // blocks ahead of the promotion (two buffers: 1666 against 1736 TFLOPS at
   // M=8192 N=7168 K=8192, together with the batched loads below).
@@ -158,6 +197,42 @@ __global__ void __launch_bounds__(256, 1)
   // before that kernel has completed.
   griddep_wait();
 
+  // Grouped calls: warp 0 writes the exclusive prefix of the groups' 128-row
+  // tiles (clamped as group_rows clamps) for fp8b_unit.
+  const int* pre = nullptr;
+  int live = 0;
+  int units = p.total_units;
+  if constexpr (kGrouped) {
+    if (p.batch <= Cfg::kMaxPrefixGroups) {
+      int* pre_s = reinterpret_cast<int*>(smem + Cfg::kOffPrefix);
+      if (warp == 0) {
+        int carry = 0;
+        for (int base = 0; base < p.batch; base += 32) {
+          const int g = base + static_cast<int>(lane);
+          int t = 0;
+          if (g < p.batch) {
+            int row0, rows;
+            group_rows(p, g, row0, rows);
+            t = (rows + 127) / 128;
+          }
+          int v = t;   // inclusive warp scan
+#pragma unroll
+          for (int d = 1; d < 32; d <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, v, d);
+            if (static_cast<int>(lane) >= d) v += y;
+          }
+          if (g < p.batch) pre_s[g] = carry + v - t;
+          carry += __shfl_sync(0xffffffffu, v, 31);
+        }
+        if (lane == 0) pre_s[p.batch] = carry;
+      }
+      __syncthreads();
+      pre = pre_s;
+      live = min(pre_s[p.batch], p.tiles_m * p.batch);
+      units = live * p.tiles_n;
+    }
+  }
+
   if (warp == 0) {
     // producer warp: all lanes run the loop, the elected lane issues the copies
     const bool issuer = elect_one();
@@ -167,14 +242,11 @@ __global__ void __launch_bounds__(256, 1)
     bool ok = true;
     int last_stage = -1;
     uint32_t last_phase = 0;
-    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
-      int b, mt, nt, s;
-      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      int b, mt, nt, s, row0, rows;
+      if (!fp8b_unit<kGrouped>(p, pre, live, u, b, mt, nt, s, row0, rows)) continue;
       int a_row = mt * 128, a_batch = b;
       if constexpr (kGrouped) {
-        int row0, rows;
-        group_rows(p, b, row0, rows);
-        if (mt * 128 >= rows) continue;   // this group has no rows in the tile
         a_row = row0 + mt * 128;
         a_batch = 0;
       }
@@ -224,14 +296,9 @@ __global__ void __launch_bounds__(256, 1)
     uint32_t phase = 0;
     uint32_t kbi = 0;   // K blocks issued by this CTA, selects the TMEM buffer
     bool ok = true;
-    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
-      int b, mt, nt, s;
-      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
-      if constexpr (kGrouped) {
-        int row0, rows;
-        group_rows(p, b, row0, rows);
-        if (mt * 128 >= rows) continue;
-      }
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      int b, mt, nt, s, row0, rows;
+      if (!fp8b_unit<kGrouped>(p, pre, live, u, b, mt, nt, s, row0, rows)) continue;
       const int kb0 = s * p.kb_per_split;
       const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
       for (int kb = kb0; kb < kb1; ++kb, ++kbi) {
@@ -274,16 +341,12 @@ __global__ void __launch_bounds__(256, 1)
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     uint32_t kbi = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < p.total_units && ok; u += gridDim.x) {
-      int b, mt, nt, s;
-      decode_unit(u, p.tiles_m, p.tiles_n, p.split_k, p.group_m, b, mt, nt, s);
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      // row0, rows: the group's first row and rows (the whole M when not grouped)
+      int b, mt, nt, s, row0, rows;
+      if (!fp8b_unit<kGrouped>(p, pre, live, u, b, mt, nt, s, row0, rows)) continue;
       const int kb0 = s * p.kb_per_split;
       const int kb1 = min(kb0 + p.kb_per_split, p.num_kb);
-      int row0 = 0, rows = p.m;   // the group's first row and rows (the whole M when not grouped)
-      if constexpr (kGrouped) {
-        group_rows(p, b, row0, rows);
-        if (mt * 128 >= rows) continue;
-      }
       const int row = mt * 128 + q * 32 + static_cast<int>(lane);
       const bool row_ok = row < rows;
       // a lane quarter whose 32 rows all lie beyond M (decode shapes) skips
