@@ -451,6 +451,16 @@ def test_fp8_block_grouped(bs, orc, cuda, sizes, n, k, b_layout, out_dtype):
                           out_dtype=out_dtype)
 
 
+def test_fp8_block_grouped_many_experts(bs, orc, cuda):
+    """More experts than the kernel's shared-memory tile prefix holds (1024):
+    the grouped kernel falls back to decoding the full tile grid and skipping
+    tiles past each expert's rows."""
+    sizes = [0] * 1100
+    for e, sz in ((3, 5), (500, 130), (1023, 1), (1024, 64), (1099, 200)):
+        sizes[e] = sz
+    run_fp8_block_grouped(bs, orc, cuda, tuple(sizes), 128, 256, seed=77, b_layout="raw", tail=3)
+
+
 def test_fp8_block_grouped_caps_rows_at_max_rows(bs, orc, cuda):
     """A group longer than max_rows is computed up to max_rows rows only: the
     kernel clamps groups, so routing offsets beyond the bound never reach
