@@ -24,7 +24,8 @@ _PKG = Path(__file__).resolve().parent
 LIB_PATH = _PKG / "_build" / "libbsgemm_b200.so"
 
 # ---- C enums (include/bsgemm_b200.h) -----------------------------------------
-OK, ERR_INVALID_VALUE, ERR_UNSUPPORTED, ERR_ARCH, ERR_WORKSPACE, ERR_CUDA, ERR_TIMEOUT, ERR_ALIGNMENT = range(8)
+(OK, ERR_INVALID_VALUE, ERR_UNSUPPORTED, ERR_ARCH, ERR_WORKSPACE, ERR_CUDA, ERR_TIMEOUT, ERR_ALIGNMENT,
+ ERR_SCRATCH_LIMIT) = range(9)
 LAYOUTS = {"nt": 0, "tt": 1, "nn": 2, "tn": 3}
 B_RAW, B_KPANEL128, B_SHUFFLE16 = 0, 1, 2
 SF_NATIVE, SF_ROWMAJOR, SF_KMAJOR_T, SF_E8M0_SHUFFLE = 0, 1, 2, 3

@@ -24,10 +24,13 @@ replay of the K steps so that host launch overhead stays out (config.l2 and
 config.timing say which).  e2e = the same GEMM through the public C-ABI call
 with pinned host buffers (inputs H2D + output D2H inside the timed region),
 roofline of the GEMM kernel, cpu_baseline = the reference's CPU verification
-GEMM (restated in oracle/, "port") on a row sample, and sampled clocks.
+GEMM (oracle/_ref, "reference", or its restatement in oracle/, "port") on a
+row sample, and sampled clocks.
 
---impl reference times the reference's CPU GEMM (the oracle port; the
-reference itself is HIP-only and cannot be built here) on the same metric.
+--impl reference times the reference's CPU verification GEMM on the same
+metric: its own CPU functions compiled from its sources (oracle/_ref) when that
+library is built, else their restatement in oracle/ (its GPU kernels are
+HIP/gfx950-only).
 """
 from __future__ import annotations
 
@@ -265,54 +268,62 @@ def use_all_host_cores():
     return n
 
 
-def cpu_baseline(workload, m, n, k, target_s=12.0, max_rows=None):
+def cpu_gemm(workload, rows, n, k, seed=0):
+    """One CPU verification GEMM of `rows` activation rows against the whole
+    N x K weight matrix, ready to time: returns (fn, kind, module).  The
+    reference's own CPU functions (oracle/_ref, compiled from its host
+    drivers) are used when that library is built ("reference"); otherwise the
+    restatement in oracle/ ("port").  Inputs are quantised by the oracle."""
     import numpy as np
-    use_all_host_cores()
     from oracle import oracle as orc
+    from oracle import ref as rlib
     orc.build()
-    cores = orc.num_threads()
-    rng = np.random.default_rng(0)
+    use_ref = rlib.available()
+    g = rlib if use_ref else orc
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((rows, k)).astype(np.float32)
+    w = rng.standard_normal((n, k)).astype(np.float32)
+    if workload == "mxfp8":
+        (qa, sa), (qb, sb) = orc.quant_mxfp8(x), orc.quant_mxfp8(w)
+        fn = lambda: g.gemm_mxfp8(qa, qb, sa, sb)
+    elif workload == "mxfp4":
+        (qa, sa), (qb, sb) = orc.quant_mxfp4(x), orc.quant_mxfp4(w)
+        fn = lambda: g.gemm_mxfp4(qa, qb, sa, sb)
+    elif workload == "e8m0block":
+        qa, qb = orc.quant_mxfp8(x)[0], orc.quant_mxfp8(w)[0]
+        sfa_t = rng.integers(124, 131, size=(k // 128, rows)).astype(np.uint8)
+        sfb = rng.integers(124, 131, size=(n // 128, k // 128)).astype(np.uint8)
+        fn = lambda: g.gemm_e8m0_block(qa, qb, sfa_t, sfb)
+    else:
+        (qa, sa), (qb, sb) = orc.quant_fp8_block(x, 1), orc.quant_fp8_block(w, 128)
+        fn = lambda: g.gemm_fp8_block(qa, qb, sa, sb)
+    return fn, ("reference" if use_ref else "port"), g
 
-    def sample(rows):
-        if workload == "mxfp8":
-            qa, sa = orc.quant_mxfp8(rng.standard_normal((rows, k)).astype(np.float32))
-            qb, sb = orc.quant_mxfp8(rng.standard_normal((n, k)).astype(np.float32)) if not hasattr(sample, "b") else sample.b
-            sample.b = (qb, sb)
-            t0 = time.perf_counter()
-            orc.gemm_mxfp8(qa, qb, sa, sb)
-            return time.perf_counter() - t0
-        if workload == "mxfp4":
-            qa, sa = orc.quant_mxfp4(rng.standard_normal((rows, k)).astype(np.float32))
-            if not hasattr(sample, "b"):
-                sample.b = orc.quant_mxfp4(rng.standard_normal((n, k)).astype(np.float32))
-            qb, sb = sample.b
-            t0 = time.perf_counter()
-            orc.gemm_mxfp4(qa, qb, sa, sb)
-            return time.perf_counter() - t0
-        if workload == "e8m0block":
-            qa, _ = orc.quant_mxfp8(rng.standard_normal((rows, k)).astype(np.float32))
-            sfa_t = rng.integers(124, 131, size=(k // 128, rows)).astype(np.uint8)
-            if not hasattr(sample, "b"):
-                qb, _ = orc.quant_mxfp8(rng.standard_normal((n, k)).astype(np.float32))
-                sample.b = (qb, rng.integers(124, 131, size=(n // 128, k // 128)).astype(np.uint8))
-            qb, sfb = sample.b
-            t0 = time.perf_counter()
-            orc.gemm_e8m0_block(qa, qb, sfa_t, sfb)
-            return time.perf_counter() - t0
-        qa, sa = orc.quant_fp8_block(rng.standard_normal((rows, k)).astype(np.float32), 1)
-        if not hasattr(sample, "b"):
-            sample.b = orc.quant_fp8_block(rng.standard_normal((n, k)).astype(np.float32), 128)
-        qb, sb = sample.b
-        t0 = time.perf_counter()
-        orc.gemm_fp8_block(qa, qb, sa, sb)
-        return time.perf_counter() - t0
 
-    t1 = sample(1)
+CPU_KIND_NOTE = {
+    "reference": "the reference's own CPU verification GEMM (compiled from its host-driver sources into "
+                 "oracle/_ref with g++ -O3 -fopenmp)",
+    "port": "the reference's CPU verification GEMM restated in oracle/ (oracle/_ref not built)",
+}
+
+
+def cpu_baseline(workload, m, n, k, target_s=12.0, max_rows=None):
+    use_all_host_cores()
+    fn1, kind, g = cpu_gemm(workload, 1, n, k)
+    t0 = time.perf_counter()
+    fn1()
+    t1 = time.perf_counter() - t0
     rows = max(1, min(int(target_s / max(t1, 1e-6)), max_rows or m, m))
-    t = sample(rows) if rows > 1 else t1
+    t = t1
+    if rows > 1:
+        fn, _, _ = cpu_gemm(workload, rows, n, k)
+        t0 = time.perf_counter()
+        fn()
+        t = time.perf_counter() - t0
     tflops = 2.0 * rows * n * k / t / 1e12
-    return {"value": tflops, "unit": "TFLOPS", "cores": cores, "kind": "port",
-            "sample": f"{rows} of {m} rows x N={n} x K={k} ({t:.1f} s, extrapolated to TFLOPS)"}
+    return {"value": tflops, "unit": "TFLOPS", "cores": g.num_threads(), "kind": kind,
+            "sample": f"{rows} of {m} rows x N={n} x K={k} ({t:.1f} s, extrapolated to TFLOPS); "
+                      f"{CPU_KIND_NOTE[kind]}"}
 
 
 def metric_name(workload):
@@ -330,31 +341,10 @@ def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return 0
-    import numpy as np
     use_all_host_cores()
-    from oracle import oracle as orc
-    orc.build()
     m, n, k = args.m, args.n * world, args.k
-    rng = np.random.default_rng(0)
     rows = 1
-    if args.workload == "mxfp8":
-        qb, sb = orc.quant_mxfp8(rng.standard_normal((n, k)).astype(np.float32))
-        qa, sa = orc.quant_mxfp8(rng.standard_normal((rows, k)).astype(np.float32))
-        fn = lambda: orc.gemm_mxfp8(qa, qb, sa, sb)
-    elif args.workload == "mxfp4":
-        qb, sb = orc.quant_mxfp4(rng.standard_normal((n, k)).astype(np.float32))
-        qa, sa = orc.quant_mxfp4(rng.standard_normal((rows, k)).astype(np.float32))
-        fn = lambda: orc.gemm_mxfp4(qa, qb, sa, sb)
-    elif args.workload == "e8m0block":
-        qb, _ = orc.quant_mxfp8(rng.standard_normal((n, k)).astype(np.float32))
-        qa, _ = orc.quant_mxfp8(rng.standard_normal((rows, k)).astype(np.float32))
-        sfa_t = rng.integers(124, 131, size=(k // 128, rows)).astype(np.uint8)
-        sfb = rng.integers(124, 131, size=(n // 128, k // 128)).astype(np.uint8)
-        fn = lambda: orc.gemm_e8m0_block(qa, qb, sfa_t, sfb)
-    else:
-        qb, sb = orc.quant_fp8_block(rng.standard_normal((n, k)).astype(np.float32), 128)
-        qa, sa = orc.quant_fp8_block(rng.standard_normal((rows, k)).astype(np.float32), 1)
-        fn = lambda: orc.gemm_fp8_block(qa, qb, sa, sb)
+    fn, kind, g = cpu_gemm(args.workload, rows, n, k)
     # bound the whole run to a few minutes
     t0 = time.perf_counter()
     fn()
@@ -368,7 +358,7 @@ def run_reference(args):
         fn()
     dt = (time.perf_counter() - t0) / steps
     value = 2.0 * rows * n * k / dt / 1e12
-    cores = orc.num_threads()
+    cores = g.num_threads()
     line = {
         "impl": "reference", "metric": metric_name(args.workload), "value": value, "unit": "TFLOPS",
         "n_gpus": world, "steps": steps, "warmup": min(args.warmup, 2), "ms_per_step": dt * 1e3,
@@ -377,11 +367,10 @@ def run_reference(args):
         "data": "synthetic",
         "config": {"workload": f"{args.workload} M={m} N={n} K={k} layout={args.layout}",
                    "sample_rows_per_step": rows},
-        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": cores, "kind": "port",
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": cores, "kind": kind,
                          "sample": f"{rows} row x N={n} x K={k} per step, {steps} steps"},
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "reference CPU verification GEMM restated in oracle/ (the reference is HIP/gfx950-only "
-                "and cannot be built here)",
+        "note": CPU_KIND_NOTE[kind] + "; the reference's GPU kernels are HIP/gfx950-only",
     }
     print(json.dumps(line), flush=True)
     return 0

@@ -221,7 +221,12 @@ BSG_API size_t bsgemm_mx_grouped_workspace_size(const bsgemm_args *args);
  * complete when `stream` reaches this point.  The block GEMMs run without
  * split-K (args->split_k and args->workspace are ignored).  The first call
  * on a device creates the two internal streams and their events (no device
- * memory); calls on one device are serialised while they enqueue.
+ * memory); calls on one device are serialised while they enqueue.  C
+ * should be pinned: with pageable host C each strip's copy-back is
+ * synchronous, so the host waits for that strip's GEMM before it queues the
+ * next one and the copies no longer overlap the GEMMs.  The internal streams
+ * and events are cached per device ordinal for the life of the process: do
+ * not use the library across cudaDeviceReset on that device.
  * Replaces the reference drivers' hipMemcpy-in / launch / hipMemcpy-out
  * sequence (mxfp8_gemm/gemm_a8w8_mxfp8_host.cc:261-301,
  * mxfp4_gemm_4wave_20261112/gemm_a4w4_mxfp4_4wave_host.cc:195-224).
@@ -334,8 +339,10 @@ BSG_API int bsgemm_selftest_timeout(int timeout_us);
  * BSG_ERR_SCRATCH_LIMIT.  All calls on a device share that one array: calls
  * that overlap on the GPU race and corrupt each other.  The first call on a
  * device looks the array's address up (once per device); make it before any
- * stream capture.  No counterpart in the reference, whose launchers need no
- * scratch.
+ * stream capture.  That address is cached per device ordinal for the life of
+ * the process: do not call this entry point across cudaDeviceReset on that
+ * device (the reset unloads the module that holds the array).  No
+ * counterpart in the reference, whose launchers need no scratch.
  */
 BSG_API int bsgemm_a8w8_mxfp8_noalloc(const bsgemm_args *args, bsg_stream_t stream);
 /* Size of that fixed scratch array in bytes. */

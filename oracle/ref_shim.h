@@ -42,11 +42,17 @@ struct __hip_fp8_e4m3 {
     explicit __hip_fp8_e4m3(float f) : __x(encode(f)) {}
 
     explicit operator float() const {
-        const int s = __x >> 7, e = (__x >> 3) & 15, m = __x & 7;
+        // built from the bit fields: no libm call in the GEMM loops
+        const std::uint32_t s = (__x & 0x80u) << 24, e = (__x >> 3) & 15u, m = __x & 7u;
         if (e == 15 && m == 7) return std::numeric_limits<float>::quiet_NaN();
-        const float mag = e == 0 ? std::ldexp(static_cast<float>(m), -9)
-                                 : std::ldexp(static_cast<float>(8 + m), e - 10);
-        return s ? -mag : mag;
+        if (e == 0) {                                    // subnormal: m * 2^-9
+            const float mag = static_cast<float>(m) * 0.001953125f;
+            return s ? -mag : mag;
+        }
+        const std::uint32_t bits = s | ((e + 120u) << 23) | (m << 20);
+        float f;
+        std::memcpy(&f, &bits, 4);
+        return f;
     }
 
   private:

@@ -72,6 +72,33 @@ def test_noalloc_matches_workspace_entry_twice(bs, orc, cuda):
             assert_close(orc, ref, got, mag, f"noalloc vs oracle {m}x{n}x{k} call {call}")
 
 
+def test_noalloc_drops_auto_split_that_exceeds_its_scratch(bs, orc, cuda):
+    """A skinny problem whose automatic split-K partials would not fit in the
+    fixed scratch runs unsplit instead of failing, with the same results."""
+    fn = noalloc_fn(bs)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
+    m, n, k = 128, 8192, 8192
+    qa, qb, sa, sb = [x[0] for x in mxfp8_problem(orc, m, n, k, 23, "rowpattern")]
+    A = dev_u8(qa, cuda).view(torch.float8_e4m3fn)
+    B = dev_u8(qb, cuda).view(torch.float8_e4m3fn)
+    SA, SB = dev_u8(sa, cuda), dev_u8(sb, cuda)
+    out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device=cuda)
+    args = fill_args(bs, A, B, SA, SB, out)
+    size = bs.lib().bsgemm_workspace_size
+    limit = bs.lib().bsgemm_noalloc_scratch_bytes
+    limit.restype = ctypes.c_size_t
+    assert size(bs.FAMILY_MXFP8, ctypes.byref(args)) > limit()      # the automatic plan splits K
+    expected = bs.gemm_a8w8_mxfp8(A, B, SA, SB)
+    assert fn(ctypes.byref(args), stream) == bs.OK
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    got = out.float().cpu().numpy()
+    assert_close(orc, expected.float().cpu().numpy().astype(np.float64), got, None, "noalloc unsplit vs entry")
+    rows = np.arange(0, m, 9)
+    ref, mag = orc.gemm_mxfp8(qa[rows], qb, sa[rows], sb, f64=True)
+    assert_close(orc, ref, got[rows], mag, "noalloc unsplit vs oracle")
+
+
 def test_noalloc_rejects_problems_beyond_its_scratch(bs, cuda):
     fn = noalloc_fn(bs)
     limit = bs.lib().bsgemm_noalloc_scratch_bytes
@@ -87,7 +114,7 @@ def test_noalloc_rejects_problems_beyond_its_scratch(bs, cuda):
     # forced split of 4: 4 * 1024 * 1024 * 4 bytes of partials = 16 MiB > 8 MiB
     args = fill_args(bs, A, B, SA, SB, out, split_k=4)
     stream = ctypes.c_void_p(torch.cuda.current_stream(cuda).cuda_stream)
-    assert fn(ctypes.byref(args), stream) == 8          # BSG_ERR_SCRATCH_LIMIT
-    assert "scratch" in bs.strerror(8)
+    assert fn(ctypes.byref(args), stream) == bs.ERR_SCRATCH_LIMIT
+    assert "scratch" in bs.strerror(bs.ERR_SCRATCH_LIMIT)
     torch.cuda.synchronize()
     assert torch.count_nonzero(out) == 0                # nothing ran
