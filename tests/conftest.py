@@ -5,6 +5,8 @@ loading and argument validation).  `-m gpu` needs an sm_100 GPU and calls the
 CUDA library through its C ABI.
 """
 import importlib
+import json
+import os
 import sys
 from pathlib import Path
 
@@ -41,3 +43,26 @@ def cuda():
     if (major, minor) != (10, 0):
         pytest.skip(f"needs sm_100, found sm_{major}{minor}")
     return torch.device("cuda:0")
+
+
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    """Per parity check: how many elements passed only through the
+    fp32-accumulation floor (1e-6 * sum|term|) of the tolerance.  Written as
+    JSON to $BSG_PARITY_REPORT when that is set."""
+    from helpers import PARITY_LOG
+    if not PARITY_LOG:
+        return
+    total = sum(n for _, _, n, _, _ in PARITY_LOG)
+    floor = sum(f for _, f, _, _, _ in PARITY_LOG)
+    tr = terminalreporter
+    tr.section("parity: elements passing only through the fp32-accumulation floor")
+    tr.write_line(f"{len(PARITY_LOG)} checks, {total} elements, {floor} pass only through the floor "
+                  f"({floor / max(total, 1):.2e})")
+    for what, f, n, max_rel, cd in PARITY_LOG:
+        if f:
+            tr.write_line(f"  {what}: {f} of {n}")
+    path = os.environ.get("BSG_PARITY_REPORT")
+    if path:
+        Path(path).write_text(json.dumps(
+            [{"check": w, "floor_only": f, "elements": n, "max_rel": r, "calc_diff": c}
+             for w, f, n, r, c in PARITY_LOG], indent=1))

@@ -50,13 +50,31 @@ def to_f32(out):
     return out.float().cpu().numpy()
 
 
+# (what, elements passing only through the fp32-accumulation floor, elements,
+#  max relative error, calc_diff) of every assert_close call in this session;
+# conftest.py prints it at the end of the run
+PARITY_LOG = []
+
+
+def floor_only_count(ref, got, mag):
+    """Elements within 2^-7|ref| + 1e-3 + 1e-6*sum|term| but NOT within the
+    target rule 2^-7|ref| + 1e-3 alone: the ones the floor lets through."""
+    if mag is None:
+        return 0
+    err = np.abs(np.asarray(got, np.float64) - ref)
+    base = (2.0 ** -7) * np.abs(ref) + 1e-3
+    return int(np.count_nonzero((err > base) & (err <= base + 1e-6 * mag)))
+
+
 def assert_close(orc, ref, got, mag=None, what=""):
     """Tolerance of every parity test (bf16 outputs):
          |err| <= 2^-7 |ref| + 1e-3 + 1e-6 * sum|a*b*s|   per element,
          max relative error <= 1e-2 over non-cancelling elements.
     The target rule plus an fp32-accumulation floor; see
-    oracle.check_baseline_rule."""
+    oracle.check_baseline_rule.  The number of elements that pass only
+    through the floor is logged in PARITY_LOG."""
     bad, max_rel, calc_diff = orc.check_baseline_rule(ref, got, mag)
+    PARITY_LOG.append((what, floor_only_count(ref, got, mag), int(np.size(ref)), max_rel, calc_diff))
     if bad:
         err = np.abs(got.astype(np.float64) - ref)
         floor = 0.0 if mag is None else 1e-6 * mag

@@ -92,11 +92,14 @@ def test_noalloc_drops_auto_split_that_exceeds_its_scratch(bs, orc, cuda):
     assert fn(ctypes.byref(args), stream) == bs.OK
     torch.cuda.synchronize()
     assert bs.check_device_error() == 0
-    got = out.float().cpu().numpy()
-    assert_close(orc, expected.float().cpu().numpy().astype(np.float64), got, None, "noalloc unsplit vs entry")
+    assert torch.isfinite(out).all()
     rows = np.arange(0, m, 9)
+    got = out.float().cpu().numpy()[rows]
     ref, mag = orc.gemm_mxfp8(qa[rows], qb, sa[rows], sb, f64=True)
-    assert_close(orc, ref, got[rows], mag, "noalloc unsplit vs oracle")
+    # the workspace entry splits K and this one does not: they agree within
+    # the fp32-accumulation tolerance, not bit for bit
+    assert_close(orc, expected.float().cpu().numpy()[rows].astype(np.float64), got, mag, "noalloc unsplit vs entry")
+    assert_close(orc, ref, got, mag, "noalloc unsplit vs oracle")
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch(bs, cuda):
