@@ -121,6 +121,15 @@ def parse():
                     help="grouped (MoE) GEMMs of the three families on decode and prefill expert mixes, one JSON line")
     ap.add_argument("--families", default="fp8block,mxfp8,mxfp4",
                     help="comma-separated families for --grouped")
+    ap.add_argument("--no-configs4", action="store_true",
+                    help="skip the configs[4] sub-record (N-sharded M=16384 N=57344 K=8192 MXFP4 and "
+                         "fp32 block-scale, GEMM and GEMM + all-gather)")
+    ap.add_argument("--c4-steps", type=int, default=8)
+    ap.add_argument("--c4-strips", type=int, default=4, help="M strips of the overlapped GEMM + all-gather")
+    ap.add_argument("--c4-grid", type=int, default=0,
+                    help="CTA cap of the configs[4] GEMMs (0 = one per SM; a cap leaves SMs to NCCL)")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the N=1 mxfp4 and sustained sub-records")
     args = ap.parse_args()
     if args.shape:
         args.m, args.n, args.k = (int(v) for v in args.shape.split(","))
@@ -567,7 +576,7 @@ def run_ours(args):
     d_sa, d_sb = torch.empty_like(sa), torch.empty_like(sb)
     # MX, layout tn: the host-staged entry point pipelines the copies with the
     # GEMM blocks (bsgemm_mx_host_gemm); the other workloads copy, call, copy back
-    host_staged = wl in ("mxfp8", "mxfp4") and args.layout == "tn"
+    host_staged = wl in ("mxfp8", "mxfp4") and args.layout == "tn" and world == 1
     if host_staged:
         del d_a, d_b, d_sa, d_sb
         fdt = torch.uint8 if fp4 else torch.float8_e4m3fn
@@ -584,10 +593,16 @@ def run_ours(args):
             bs.gemm_mx_from_host(h_a8, h_b8, h_sa, h_sb, fp4=fp4, out=h_out, b_format=b_format,
                                  workspace=host_ws)
             return
-        d_a.copy_(h_a, non_blocking=True)
         d_b.copy_(h_b, non_blocking=True)
-        d_sa.copy_(h_sa, non_blocking=True)
         d_sb.copy_(h_sb, non_blocking=True)
+        if world == 1 or rank == 0:
+            d_a.copy_(h_a, non_blocking=True)
+            d_sa.copy_(h_sa, non_blocking=True)
+        if world > 1:
+            # the replicated activations cross the host link once (rank 0) and
+            # reach the other ranks over NVLink
+            dist.broadcast(d_a, 0)
+            dist.broadcast(d_sa, 0)
         if wl == "mxfp8":
             r = bs.gemm_a8w8_mxfp8(d_a.view(torch.float8_e4m3fn), d_b.view(torch.float8_e4m3fn), d_sa, d_sb,
                                    layout=args.layout, out=out, b_format=b_format)
@@ -616,13 +631,19 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(et, op=dist.ReduceOp.MAX)
     e2e_ms = float(et[0])
-    h2d = h_a.numel() + h_b.numel() + h_sa.numel() * h_sa.element_size() + h_sb.numel() * h_sb.element_size()
+    a_host = h_a.numel() + h_sa.numel() * h_sa.element_size()
+    b_host = h_b.numel() + h_sb.numel() * h_sb.element_size()
+    h2d = a_host + world * b_host          # the whole job: A once, every rank its own B
     e2e = {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS", "ms_per_step": e2e_ms,
-           "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(m * n * 2),
+           "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(world * m * n * 2),
+           "host_bytes_per_rank": {"rank0_h2d": int(a_host + b_host), "other_h2d": int(b_host) if world > 1 else None,
+                                   "d2h": int(m * n * 2)},
            "path": ("bsgemm_mx_host_gemm (host-staged C-ABI call: pinned host A, B, row-major scales and C; "
                     "H2D chunks, GEMM blocks and D2H blocks pipelined, result complete on return)"
                     if host_staged else
-                    "C-ABI call with pinned host buffers, reference-facing row-major scales")}
+                    "C-ABI call with pinned host buffers, reference-facing row-major scales" +
+                    ("; A and its scales copied to rank 0 only and NCCL-broadcast, each rank copies its own "
+                     "B shard and reads back its own C shard" if world > 1 else ""))}
 
     # roofline of the GEMM kernel
     if hbm_bound:
@@ -653,6 +674,23 @@ def run_ours(args):
     if bound == "tensor":
         roofline["frac_of_burst_peak"] = achieved / burst
         roofline["frac_of_sustained_peak"] = achieved / sustained
+
+    extra = {}
+    if world == 1 and not args.no_extra and wl == "mxfp8" and (m, n, k) == (8192, 8192, 8192):
+        extra["sustained"] = sustained_record(call, kern_ms, stream, local, flops, peaks, peak_kind)
+    # free the headline's device buffers before the other sub-records
+    out = qa = qb = sa = sb = call = None
+    sa_n = sb_n = flush_buf = host_ws = d_a = d_b = d_sa = d_sb = None
+    graph_main = graph_flush = None
+    torch.cuda.empty_cache()
+    if world == 1 and not args.no_extra and wl == "mxfp8" and (m, n, k) == (8192, 8192, 8192):
+        extra["mxfp4"] = mxfp4_record(bs, dev, stream, peaks, peak_kind, args.layout)
+    if not args.no_configs4:
+        import bench_configs4
+        c4 = bench_configs4.run(sys.modules[__name__], bs, dev, world, rank, dist if world > 1 else None, peaks,
+                                steps=args.c4_steps, strips=args.c4_strips, grid_blocks=args.c4_grid)
+        if c4 is not None:
+            extra["configs4"] = c4
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -686,11 +724,72 @@ def run_ours(args):
         }
         if allgather_ms is not None:
             line["allgather_ms"] = allgather_ms
+        line.update(extra)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def sustained_record(call, kern_ms, stream, local, flops, peaks, peak_kind, seconds=2.5):
+    """The headline GEMM back to back for a timed region of `seconds` (long
+    enough to reach the 1 kW power cap), with its own clock samples; compared
+    with the measured sustained GEMM peak."""
+    import torch
+    steps = max(1, int(seconds * 1e3 / max(kern_ms, 1e-3)))
+    for _ in range(20):
+        call()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        call()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / steps
+    tflops = flops / (ms * 1e-3) / 1e12
+    sustained = 2.0 * (peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops"))
+    return {"steps": steps, "timed_s": ms * steps / 1e3, "ms_per_step": ms, "tflops": tflops,
+            "peak": sustained, "frac": tflops / sustained, "frac_of_burst_peak": tflops / (2.0 * peaks["bf16_tflops"]),
+            "peak_basis": f"2 x bf16_tflops_sustained ({peak_kind})", "clocks": clk}
+
+
+def mxfp4_record(bs, dev, stream, peaks, peak_kind, layout, steps=20):
+    """configs[3]'s 8192^3 MXFP4 GEMM (B in shuffle_weight(16,16), native
+    scales): its 71 MB of inputs fit in L2, so a 256 MiB read flushes L2
+    before every call and the per-call events exclude the flushes."""
+    import torch
+    m = n = k = 8192
+    qa, qb, sa, sb = make_mx_inputs(bs, m, n, k, True, "tn", dev, 4321)
+    qb = bs.pack_b(qb, "shuffle16", unpack=True)
+    sa_n, sb_n = bs.pack_scales(sa), bs.pack_scales(sb)
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    call = lambda: bs.gemm_a4w4_mxfp4(qa, qb, sa_n, sb_n, out=out, scale_format="native", b_format="shuffle16")
+    flush_buf = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    sink = torch.empty((), dtype=torch.float32, device=dev)
+    for _ in range(5):
+        call()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in evs:
+        torch.sum(flush_buf, dim=0, out=sink)
+        a.record(stream)
+        call()
+        b.record(stream)
+    torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    flops = 2.0 * m * n * k
+    tflops = flops / (ms * 1e-3) / 1e12
+    peak = 4.0 * peaks["bf16_tflops"]
+    return {"workload": "mxfp4 M=N=K=8192 layout=tn, B shuffle_weight(16,16) read in place, native scales, bf16 out",
+            "steps": steps, "ms_per_step": ms, "tflops": tflops, "peak": peak, "frac": tflops / peak,
+            "peak_basis": f"4 x bf16_tflops burst ({peak_kind}): dense MXFP4 tensor rate is 4x bf16 on B200",
+            "l2": "256 MiB read flushes L2 before every call; excluded", "target_frac": 0.60}
 
 
 def run_sweep(args):

@@ -141,6 +141,12 @@ BSG_API void bsgemm_args_init(bsgemm_args *args);
  * Replaces the launch of gemm_a8w8_mxfp8_kernel in
  * mxfp8_gemm/gemm_a8w8_mxfp8_host.cc:287-295 (its kargs at :265-285), without
  * the reference's K == 256 and M/N % 256 limits.
+ * E8M0 edge bytes (all MX and E8M0 block-scale entry points): byte 0 is
+ * 2^-127, as on the reference host (gemm_a8w8_mxfp8_host.cc:35-37); byte 255
+ * is NaN (OCP MX, what the block-scaled tensor cores implement), where the
+ * reference host's ldexp gives 2^128 (+inf in fp32), so every output of a
+ * row or column whose scales hold a 255 byte is NaN.  E4M3 0x7F / 0xFF
+ * operands are NaN and propagate to their outputs.
  */
 BSG_API int bsgemm_a8w8_mxfp8(const bsgemm_args *args, bsg_stream_t stream);
 

@@ -263,6 +263,36 @@ def sf_to_native(sf):
     return out
 
 
+# ---- E8M0 edge bytes: the library's semantics ------------------------------------
+
+def as_library_e8m0(ref: np.ndarray, nan_rows=(), nan_cols=()) -> np.ndarray:
+    """Map a reference-host result onto what the block-scaled tensor cores
+    produce for the two E8M0 edge bytes and for NaN operands.
+
+    The reference host decodes a scale byte with ldexp(1, e - 127): byte 0 is
+    2^-127, and byte 255 is 2^128 -- +inf in fp32
+    (mxfp8_gemm/gemm_a8w8_mxfp8_host.cc:35-37), a finite double in the MXFP4
+    driver (mxfp4_gemm_4wave_20261112/gemm_a4w4_mxfp4_4wave_host.cc:44).
+    tcgen05's block-scaled MMA follows the OCP MX encoding: byte 0 is also
+    2^-127, but byte 255 is NaN, so every output of a row whose activation
+    scales hold a 255 byte, or of a column whose weight scales do, is NaN; an
+    E4M3 NaN operand (0x7F / 0xFF) makes its output row or column NaN on both.
+    (The reference's own device decode,
+    mxfp8_gemm/gemm_a8w8_mxfp8_kernel_template.hpp:23-25, reads byte 0 as 0.0
+    and 255 as +inf; neither is what this library does.)  All other outputs
+    are the reference's values.  nan_rows / nan_cols: the rows and columns
+    such a byte or operand reaches."""
+    out = np.array(ref, dtype=np.float64, copy=True)
+    out[np.asarray(nan_rows, dtype=np.int64), :] = np.nan
+    out[:, np.asarray(nan_cols, dtype=np.int64)] = np.nan
+    return out
+
+
+def e4m3_nan_rows(q: np.ndarray) -> np.ndarray:
+    """Rows of an E4M3 byte matrix holding a NaN code (0x7F or 0xFF)."""
+    return np.where(((q & 0x7F) == 0x7F).any(axis=1))[0]
+
+
 # ---- reference acceptance rules ---------------------------------------------------
 
 def check_e8m0_rule(ref: np.ndarray, got: np.ndarray, mag: np.ndarray, bf16: bool,
