@@ -135,6 +135,11 @@ def _out(out, m, n, dtype, device, batch):
 
 
 def _workspace(family: int, args: Args, workspace, device):
+    """workspace None: allocate what the call needs; a tensor: use it;
+    False: pass none (a decode-shaped call then splits K inside CTA clusters,
+    up to 4 slices, or runs unsplit; row-major MX scales still need one)."""
+    if workspace is False:
+        return None
     need = int(lib().bsgemm_workspace_size(family, ctypes.byref(args)))
     if need == 0:
         return None

@@ -207,6 +207,70 @@ int launch_pdl(void (*kern)(KArgs...), int grid, int block, uint32_t smem, cudaS
   return BSG_OK;
 }
 
+// Same, as 1-D clusters of `cluster` CTAs (the grid a multiple of it).
+template <typename... KArgs, typename... Args>
+int launch_pdl_cluster(void (*kern)(KArgs...), int grid, int cluster, int block, uint32_t smem, cudaStream_t st,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(static_cast<unsigned>(block));
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+  if (e != cudaSuccess) {
+    t_last_cuda_error = e;
+    return BSG_ERR_CUDA;
+  }
+  return BSG_OK;
+}
+
+// Clusters of `cluster` CTAs of `kern` that fit on the device at once (0 when
+// none does or the query fails).  Cached per (kernel, device, cluster size).
+template <typename K>
+int cluster_capacity(K kern, int cluster, int block, uint32_t smem) {
+  struct Entry {
+    const void* fn;
+    int dev, cluster, n;
+  };
+  static std::mutex mu;
+  static Entry done[64];
+  static int count = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const void* fn = reinterpret_cast<const void*>(kern);
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < count; ++i)
+    if (done[i].fn == fn && done[i].dev == dev && done[i].cluster == cluster) return done[i].n;
+  if (set_smem(kern, smem) != BSG_OK) return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(cluster * 64));
+  cfg.blockDim = dim3(static_cast<unsigned>(block));
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    n = 0;
+  }
+  if (count < 64) done[count++] = Entry{fn, dev, cluster, n};
+  return n;
+}
+
 int launch_status() {
   const cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) return BSG_OK;
@@ -229,6 +293,8 @@ struct Plan {
   int split = 1, kb_per = 1;
   int num_kb = 1;
   size_t ws_partials = 0;       // bytes of fp32 partials
+  bool cluster = false;         // split-K slices of a tile reduced inside a CTA cluster
+  int clusters = 0;             // co-resident clusters used (grid = clusters * split)
 };
 
 // Split-K choice for a persistent grid of `sms` CTAs: the wall time is set by
@@ -292,6 +358,14 @@ bool mx_use_swap(const bsgemm_args& a) {
                         (a.b_format == BSG_B_RAW || a.b_format == BSG_B_SHUFFLE16);
   return eligible && (a.kernel == BSG_KERNEL_SWAP || a.kernel == BSG_KERNEL_AUTO);
 }
+
+// In-cluster split-K of the transposed decode kernels (for calls without the
+// workspace a split needs) and the cluster capacities it consults; defined
+// with the kernels' launchers below.
+bool swap_split_in_cluster(Plan& pl, const bsgemm_args& a, int (*capacity)(int mn, int split));
+int swap_cluster_capacity(int mn, int split);
+int mxs_cluster_capacity_fp8(int mn, int split);
+int mxs_cluster_capacity_fp4(int mn, int split);
 
 int mx_plan(const bsgemm_args& a, bool fp4, const DevInfo& dev, MxPlan& pl, bool allow_auto) {
   const int kg = a.k / 32;
@@ -529,7 +603,15 @@ bool make_b_tmap(CUtensorMap* m, const bsgemm_args& a, const MxOperands& o, uint
 }
 
 template <int MN, int kFp4, int kBMode, bool kOutF32>
-int mxs_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p, int grid, cudaStream_t st) {
+int mxs_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p, int grid, cudaStream_t st,
+                 int cluster) {
+  if (cluster > 1) {
+    using Cfg = bsg::MxSwapCfg<MN, kFp4, true>;
+    auto* kern = bsg::mx_gemm_swap_kernel<MN, kFp4, kBMode, kOutF32, true>;
+    if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
+    const int rc = launch_pdl_cluster(kern, grid, cluster, 256, Cfg::kSmemBytes, st, ta, tb, p);
+    return rc != BSG_OK ? rc : launch_status();
+  }
   using Cfg = bsg::MxSwapCfg<MN, kFp4>;
   auto* kern = bsg::mx_gemm_swap_kernel<MN, kFp4, kBMode, kOutF32>;
   if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
@@ -539,23 +621,42 @@ int mxs_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p
 
 template <int MN, int kFp4>
 int mxs_launch_mn(int bmode, bool f32, const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p, int grid,
-                  cudaStream_t st) {
+                  cudaStream_t st, int cluster) {
   if (bmode == bsg::kBShuffle16)
-    return f32 ? mxs_launch_t<MN, kFp4, bsg::kBShuffle16, true>(ta, tb, p, grid, st)
-               : mxs_launch_t<MN, kFp4, bsg::kBShuffle16, false>(ta, tb, p, grid, st);
-  return f32 ? mxs_launch_t<MN, kFp4, bsg::kBKMajor, true>(ta, tb, p, grid, st)
-             : mxs_launch_t<MN, kFp4, bsg::kBKMajor, false>(ta, tb, p, grid, st);
+    return f32 ? mxs_launch_t<MN, kFp4, bsg::kBShuffle16, true>(ta, tb, p, grid, st, cluster)
+               : mxs_launch_t<MN, kFp4, bsg::kBShuffle16, false>(ta, tb, p, grid, st, cluster);
+  return f32 ? mxs_launch_t<MN, kFp4, bsg::kBKMajor, true>(ta, tb, p, grid, st, cluster)
+             : mxs_launch_t<MN, kFp4, bsg::kBKMajor, false>(ta, tb, p, grid, st, cluster);
 }
 
 template <int kFp4>
 int mxs_launch(int mn, int bmode, bool f32, const CUtensorMap& ta, const CUtensorMap& tb, const MxParams& p,
-               int grid, cudaStream_t st) {
+               int grid, cudaStream_t st, int cluster) {
   switch (mn) {
-    case 16: return mxs_launch_mn<16, kFp4>(bmode, f32, ta, tb, p, grid, st);
-    case 32: return mxs_launch_mn<32, kFp4>(bmode, f32, ta, tb, p, grid, st);
-    default: return mxs_launch_mn<64, kFp4>(bmode, f32, ta, tb, p, grid, st);
+    case 16: return mxs_launch_mn<16, kFp4>(bmode, f32, ta, tb, p, grid, st, cluster);
+    case 32: return mxs_launch_mn<32, kFp4>(bmode, f32, ta, tb, p, grid, st, cluster);
+    default: return mxs_launch_mn<64, kFp4>(bmode, f32, ta, tb, p, grid, st, cluster);
   }
 }
+
+// Co-resident clusters of the MX decode kernel; all variants of one (MN,
+// element type) share the shared-memory size, so one instantiation answers.
+template <int kFp4>
+int mxs_cluster_capacity(int mn, int split) {
+  switch (mn) {
+    case 16:
+      return cluster_capacity(bsg::mx_gemm_swap_kernel<16, kFp4, bsg::kBKMajor, false, true>, split, 256,
+                              bsg::MxSwapCfg<16, kFp4, true>::kSmemBytes);
+    case 32:
+      return cluster_capacity(bsg::mx_gemm_swap_kernel<32, kFp4, bsg::kBKMajor, false, true>, split, 256,
+                              bsg::MxSwapCfg<32, kFp4, true>::kSmemBytes);
+    default:
+      return cluster_capacity(bsg::mx_gemm_swap_kernel<64, kFp4, bsg::kBKMajor, false, true>, split, 256,
+                              bsg::MxSwapCfg<64, kFp4, true>::kSmemBytes);
+  }
+}
+int mxs_cluster_capacity_fp8(int mn, int split) { return mxs_cluster_capacity<0>(mn, split); }
+int mxs_cluster_capacity_fp4(int mn, int split) { return mxs_cluster_capacity<1>(mn, split); }
 
 bool mx_use_pair(const bsgemm_args& a, const MxPlan& pl, const DevInfo& dev) {
   const long long pair_tiles = static_cast<long long>((a.m + 255) / 256) * ((a.n + 255) / 256) * a.batch;
@@ -597,14 +698,15 @@ int mx_launch_planned(const bsgemm_args& a, const MxOperands& o, const MxPlan& p
     p.c = a.ptr_c;
     p.ldc = a.stride_c;
     p.c_batch_stride = a.stride_c_batch;
-    p.ws = pl.split > 1 ? o.partials : nullptr;
+    p.ws = pl.split > 1 && !pl.cluster ? o.partials : nullptr;
     p.timeout_ns = kTimeoutNs;
-    const int grid = grid_for(p.total_units, dev, a.grid_blocks);
+    const int grid = pl.cluster ? pl.clusters * pl.split : grid_for(p.total_units, dev, a.grid_blocks);
+    const int cluster = pl.cluster ? pl.split : 1;
     const bool f32 = a.out_dtype == BSG_OUT_FP32;
-    const int rc = o.fp4 ? mxs_launch<1>(pl.bn, o.bmode, f32, ta, tb, p, grid, st)
-                         : mxs_launch<0>(pl.bn, o.bmode, f32, ta, tb, p, grid, st);
+    const int rc = o.fp4 ? mxs_launch<1>(pl.bn, o.bmode, f32, ta, tb, p, grid, st, cluster)
+                         : mxs_launch<0>(pl.bn, o.bmode, f32, ta, tb, p, grid, st, cluster);
     if (rc != BSG_OK) return rc;
-    if (pl.split > 1) return splitk_reduce(p.ws, a, pl.split, dev.sms, st);
+    if (pl.split > 1 && !pl.cluster) return splitk_reduce(p.ws, a, pl.split, dev.sms, st);
     return BSG_OK;
   }
   if (a.kernel == BSG_KERNEL_SWAP) return BSG_ERR_UNSUPPORTED;
@@ -790,7 +892,11 @@ int mx_run(const bsgemm_args* args, bool fp4, cudaStream_t st) {
   mx_plan(a, fp4, dev, pl, true);
   size_t need = pl.ws_sfa + pl.ws_sfb + pl.ws_partials;
   if (need > a.workspace_bytes || (need && !a.workspace)) {
-    if (a.split_k == 0 && pl.split > 1) {   // auto split-K: drop it rather than fail
+    const size_t scales = pl.ws_sfa + pl.ws_sfb;
+    if (mx_use_swap(a) && scales <= a.workspace_bytes && (scales == 0 || a.workspace) &&
+        swap_split_in_cluster(pl, a, fp4 ? mxs_cluster_capacity_fp4 : mxs_cluster_capacity_fp8)) {
+      need = scales;   // split inside clusters: no partials in the workspace
+    } else if (a.split_k == 0 && pl.split > 1) {   // auto split-K: drop it rather than fail
       bsgemm_args b2 = a;
       b2.split_k = 1;
       mx_plan(b2, fp4, dev, pl, false);
@@ -925,6 +1031,31 @@ bool fp8b_use_swap(const bsgemm_args& a) {
   return a.kernel == BSG_KERNEL_SWAP || (a.kernel == BSG_KERNEL_AUTO && a.m <= 64);
 }
 
+// Split-K of the transposed decode kernels for a call without the workspace
+// its split needs: the K slices of a tile run on the CTAs of one cluster and
+// are summed through distributed shared memory, so no partials leave the
+// chip.  (With a workspace the partials plus the reduce kernel measured as
+// fast or faster, so that stays the first choice.)  An automatic split is
+// capped at kSwapMaxClusterSplit; a forced one must not exceed it.  Returns
+// false (plan unchanged) when no cluster of that size fits.
+bool swap_split_in_cluster(Plan& pl, const bsgemm_args& a, int (*capacity)(int mn, int split)) {
+  if (pl.split < 2 || (a.split_k > 1 && pl.split > bsg::kSwapMaxClusterSplit)) return false;
+  const int want = std::min(pl.split, bsg::kSwapMaxClusterSplit);
+  const int kb_per = (pl.num_kb + want - 1) / want;
+  const int split = (pl.num_kb + kb_per - 1) / kb_per;   // no empty slice
+  if (split < 2) return false;
+  int cap = capacity(pl.bn, split);
+  if (a.grid_blocks > 0) cap = std::min(cap, a.grid_blocks / split);
+  if (cap <= 0) return false;
+  const long long tiles = static_cast<long long>(pl.tiles_m) * pl.tiles_n * a.batch;
+  pl.kb_per = kb_per;
+  pl.split = split;
+  pl.cluster = true;
+  pl.clusters = static_cast<int>(std::min<long long>(tiles, cap));
+  pl.ws_partials = 0;
+  return true;
+}
+
 void fp8b_plan(const bsgemm_args& a, const DevInfo& dev, Plan& pl, bool allow_auto) {
   pl.num_kb = a.k / 128;
   pl.tiles_n = (a.n + 127) / 128;
@@ -942,12 +1073,36 @@ void fp8b_plan(const bsgemm_args& a, const DevInfo& dev, Plan& pl, bool allow_au
 
 template <int MN, int kBFmt, bool kOutF32>
 int swap_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockParams& p, int grid,
-                  cudaStream_t st) {
+                  cudaStream_t st, int cluster) {
+  if (cluster > 1) {
+    using Cfg = bsg::SwapCfg<MN, true>;
+    auto* kern = bsg::fp8_block_swap_kernel<MN, kBFmt, kOutF32, true>;
+    if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
+    const int rc = launch_pdl_cluster(kern, grid, cluster, Cfg::kThreads, Cfg::kSmemBytes, st, ta, tb, p);
+    return rc != BSG_OK ? rc : launch_status();
+  }
   using Cfg = bsg::SwapCfg<MN>;
   auto* kern = bsg::fp8_block_swap_kernel<MN, kBFmt, kOutF32>;
   if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
   const int rc = launch_pdl(kern, grid, Cfg::kThreads, Cfg::kSmemBytes, st, ta, tb, p);
   return rc != BSG_OK ? rc : launch_status();
+}
+
+template <int MN>
+int swap_cluster_capacity_mn(int split) {
+  using Cfg = bsg::SwapCfg<MN, true>;
+  return cluster_capacity(bsg::fp8_block_swap_kernel<MN, bsg::kFmtKPanel, false, true>, split, Cfg::kThreads,
+                          Cfg::kSmemBytes);
+}
+
+// All variants of one MN share the shared-memory size, so one instantiation
+// answers for all.
+int swap_cluster_capacity(int mn, int split) {
+  switch (mn) {
+    case 16: return swap_cluster_capacity_mn<16>(split);
+    case 32: return swap_cluster_capacity_mn<32>(split);
+    default: return swap_cluster_capacity_mn<64>(split);
+  }
 }
 
 template <int kBFmt>
@@ -958,18 +1113,18 @@ int fp8b_launch_fmt(bool f32, const CUtensorMap& ta, const CUtensorMap& tb, cons
 
 template <int MN, int kBFmt>
 int swap_launch_fmt(bool f32, const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockParams& p,
-                    int grid, cudaStream_t st) {
-  return f32 ? swap_launch_t<MN, kBFmt, true>(ta, tb, p, grid, st)
-             : swap_launch_t<MN, kBFmt, false>(ta, tb, p, grid, st);
+                    int grid, cudaStream_t st, int cluster) {
+  return f32 ? swap_launch_t<MN, kBFmt, true>(ta, tb, p, grid, st, cluster)
+             : swap_launch_t<MN, kBFmt, false>(ta, tb, p, grid, st, cluster);
 }
 
 template <int MN>
 int swap_launch_mn(int fmt, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
-                   const Fp8BlockParams& p, int grid, cudaStream_t st) {
+                   const Fp8BlockParams& p, int grid, cudaStream_t st, int cluster) {
   switch (fmt) {
-    case bsg::kFmtKPanel: return swap_launch_fmt<MN, bsg::kFmtKPanel>(f32, ta, tb, p, grid, st);
-    case bsg::kFmtShuffle16: return swap_launch_fmt<MN, bsg::kFmtShuffle16>(f32, ta, tb, p, grid, st);
-    default: return swap_launch_fmt<MN, bsg::kFmtRaw>(f32, ta, tb, p, grid, st);
+    case bsg::kFmtKPanel: return swap_launch_fmt<MN, bsg::kFmtKPanel>(f32, ta, tb, p, grid, st, cluster);
+    case bsg::kFmtShuffle16: return swap_launch_fmt<MN, bsg::kFmtShuffle16>(f32, ta, tb, p, grid, st, cluster);
+    default: return swap_launch_fmt<MN, bsg::kFmtRaw>(f32, ta, tb, p, grid, st, cluster);
   }
 }
 
@@ -1050,7 +1205,9 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
   Plan pl;
   fp8b_plan(a, dev, pl, true);
   if (pl.ws_partials > a.workspace_bytes || (pl.ws_partials && !a.workspace)) {
-    if (a.split_k == 0) {
+    if (fp8b_use_swap(a) && swap_split_in_cluster(pl, a, swap_cluster_capacity)) {
+      // split inside clusters: no workspace
+    } else if (a.split_k == 0) {
       bsgemm_args b2 = a;
       b2.split_k = 1;
       fp8b_plan(b2, dev, pl, false);
@@ -1097,15 +1254,16 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
   p.c = a.ptr_c;
   p.ldc = a.stride_c;
   p.c_batch_stride = a.stride_c_batch;
-  p.ws = pl.split > 1 ? static_cast<float*>(a.workspace) : nullptr;
+  p.ws = pl.split > 1 && !pl.cluster ? static_cast<float*>(a.workspace) : nullptr;
   p.timeout_ns = kTimeoutNs;
-  const int grid = grid_for(p.total_units, dev, a.grid_blocks);
+  const int grid = pl.cluster ? pl.clusters * pl.split : grid_for(p.total_units, dev, a.grid_blocks);
+  const int cluster = pl.cluster ? pl.split : 1;
   const bool f32 = a.out_dtype == BSG_OUT_FP32;
   if (fp8b_use_swap(a)) {
     switch (swap_mn(a.m)) {
-      case 16: rc = swap_launch_mn<16>(bfmt, f32, ta, tb, p, grid, st); break;
-      case 32: rc = swap_launch_mn<32>(bfmt, f32, ta, tb, p, grid, st); break;
-      default: rc = swap_launch_mn<64>(bfmt, f32, ta, tb, p, grid, st); break;
+      case 16: rc = swap_launch_mn<16>(bfmt, f32, ta, tb, p, grid, st, cluster); break;
+      case 32: rc = swap_launch_mn<32>(bfmt, f32, ta, tb, p, grid, st, cluster); break;
+      default: rc = swap_launch_mn<64>(bfmt, f32, ta, tb, p, grid, st, cluster); break;
     }
   } else {
     switch (bfmt) {
@@ -1115,7 +1273,7 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
     }
   }
   if (rc != BSG_OK) return rc;
-  if (pl.split > 1) return splitk_reduce(p.ws, a, pl.split, dev.sms, st);
+  if (pl.split > 1 && !pl.cluster) return splitk_reduce(p.ws, a, pl.split, dev.sms, st);
   return BSG_OK;
 }
 

@@ -55,7 +55,15 @@ __device__ __forceinline__ void prefetch_weight_tile(const CUtensorMap* tmB, int
     tma_prefetch_3d(tmB, kb * 128, nt * 128, b);
 }
 
-template <int MN>
+// Split-K inside the kernel (kCl): the split_k CTAs that share an output tile
+// form one thread-block cluster, each computes one K slice, and the partial
+// tiles are summed through distributed shared memory.  Output columns are
+// dealt out in "channels" (the storing promotion warps: one per TMEM lane
+// quarter for MN <= 32, two per quarter for MN = 64); channel ch is reduced
+// and stored by cluster rank ch % split_k, which receives the other ranks'
+// partials of that channel in slots of its shared memory and adds them in
+// rank order, so the result does not depend on timing.
+template <int MN, bool kCl = false>
 struct SwapCfg {
   static_assert(MN == 16 || MN == 32 || MN == 64, "MN must be 16, 32 or 64");
   // Promotion: eight warps, two per TMEM lane quarter.  A warp's chain per
@@ -74,7 +82,11 @@ struct SwapCfg {
   static constexpr uint32_t kWBytes = 128u * 128u;                 // weight tile
   static constexpr uint32_t kXBytes = static_cast<uint32_t>(MN) * 128u;
   static constexpr uint32_t kStageBytes = kWBytes + kXBytes;
-  static constexpr uint32_t kStageBudget = 210u * 1024u - kRedBytes;
+  static constexpr int kChannels = MN >= 64 ? 8 : 4;
+  static constexpr int kChanFloats = kCols * 32;                  // HC rows x 32 columns
+  static constexpr uint32_t kClBytes =
+      kCl ? static_cast<uint32_t>(swap_cl_slot_count(kChannels) * kChanFloats) * 4u : 0u;
+  static constexpr uint32_t kStageBudget = 210u * 1024u - kRedBytes - kClBytes;
   static constexpr int kStages = static_cast<int>(kStageBudget / kStageBytes) > 12
                                      ? 12
                                      : static_cast<int>(kStageBudget / kStageBytes);
@@ -90,18 +102,22 @@ struct SwapCfg {
   static constexpr uint32_t kOffScale = kOffX + kXBytes * kStages;
   static constexpr uint32_t kScaleBytes = static_cast<uint32_t>(kScaleSlots) * kScaleSlot * 4u;
   static constexpr uint32_t kOffRed = kOffScale + ((kScaleBytes + 15u) & ~15u);   // [MN][128] floats
-  static constexpr uint32_t kOffBar = kOffRed + kRedBytes;
-  static constexpr uint32_t kSmemBytes = kOffBar + 1024u + 1024u;
-  static_assert(8u * (2u * kStages + 2u * kAccBufs + 2u * kScaleSlots + 1u + 8u) + 8u <= 1024u, "barrier area");
+  static constexpr uint32_t kOffCl = kOffRed + kRedBytes;          // cluster split-K slots
+  static constexpr uint32_t kOffBar = kOffCl + kClBytes;
+  static constexpr uint32_t kBarBytes = kCl ? 1536u : 1024u;
+  static constexpr uint32_t kSmemBytes = kOffBar + kBarBytes + 1024u;
+  static_assert(8u * (2u * kStages + 2u * kAccBufs + 2u * kScaleSlots + 1u + 8u + (kCl ? 2u * kChannels : 0u)) +
+                        8u <= kBarBytes,
+                "barrier area");
   static_assert(kSmemBytes <= 227u * 1024u, "shared memory");
   static_assert(kScaleSlots >= kStages + kAccBufs, "scale ring shorter than the pipeline");
 };
 
-template <int MN, int kBFmt, bool kOutF32>
-__global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
+template <int MN, int kBFmt, bool kOutF32, bool kCl = false>
+__global__ void __launch_bounds__(SwapCfg<MN, kCl>::kThreads, 1)
     fp8_block_swap_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const Fp8BlockParams p) {
-  using Cfg = SwapCfg<MN>;
+  using Cfg = SwapCfg<MN, kCl>;
   constexpr int S = Cfg::kStages;
   constexpr int NB = Cfg::kAccBufs;
   constexpr int R = Cfg::kScaleSlots;
@@ -121,8 +137,11 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
   uint64_t* drain_bar = scale_empty + R;
   uint64_t* red_full = drain_bar + 1;   // [4] second promotion set -> first, per lane quarter
   uint64_t* red_empty = red_full + 4;   // [4]
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(red_empty + 4);
+  uint64_t* cl_full = red_empty + 4;                    // [kChannels] partials of the other ranks arrived
+  uint64_t* cl_free = cl_full + (kCl ? Cfg::kChannels : 0);   // [kChannels] owner consumed this rank's partial
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(cl_free + (kCl ? Cfg::kChannels : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* cl_slots = reinterpret_cast<float*>(smem + Cfg::kOffCl);
 
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31u;
@@ -145,6 +164,12 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
       mbar_init(&red_full[i], 1);
       mbar_init(&red_empty[i], 1);
     }
+    if constexpr (kCl) {
+      for (int i = 0; i < Cfg::kChannels; ++i) {
+        mbar_init(&cl_full[i], 32u * static_cast<uint32_t>(p.split_k - 1));   // every lane of the other ranks
+        mbar_init(&cl_free[i], 32u);                                          // every lane of the owner
+      }
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -158,6 +183,7 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (kCl) cluster_sync_all();   // the peers' barriers exist before any remote arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   if (threadIdx.x == 0) griddep_launch_dependents();   // a split-K reduce may launch now
@@ -388,13 +414,54 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&red_empty[q]);
       }
+      if constexpr (kCl) {
+        // split-K across the cluster: this warp's channel goes to its owner
+        const int ch = PS > 1 ? q : warp - 4;
+        const int S_ = p.split_k;
+        const int rank = static_cast<int>(blockIdx.x) % S_;
+        const int owner = ch % S_;
+        const int owned = (Cfg::kChannels + S_ - 1) / S_;
+        const int lch = ch / S_;
+        if (rank != owner) {
+          // the owner has consumed this channel's previous partial from our slot
+          if (ui > 0 && !mbar_wait_cluster(&cl_free[ch], (ui - 1u) & 1u, abort_flag, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          const uint32_t dst =
+              mapa_shared(smem_u32(cl_slots + (rank * owned + lch) * Cfg::kChanFloats + static_cast<int>(lane)),
+                          static_cast<uint32_t>(owner));
+#pragma unroll
+          for (int i = 0; i < HC; ++i) st_cluster_f32(dst + static_cast<uint32_t>(i * 32 * 4), acc[i]);
+          mbar_arrive_cluster(mapa_shared(smem_u32(&cl_full[ch]), static_cast<uint32_t>(owner)));
+          continue;
+        }
+        if (!mbar_wait_cluster(&cl_full[ch], ui & 1u, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        // rank order: partial 0 + partial 1 + ...
+        float sum[HC];
+        for (int r = 0; r < S_; ++r) {
+          const float* src = cl_slots + (r * owned + lch) * Cfg::kChanFloats + static_cast<int>(lane);
+#pragma unroll
+          for (int i = 0; i < HC; ++i) {
+            const float v = r == rank ? acc[i] : src[i * 32];
+            sum[i] = r == 0 ? v : sum[i] + v;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < HC; ++i) acc[i] = sum[i];
+        for (int r = 0; r < S_; ++r)
+          if (r != rank) mbar_arrive_cluster(mapa_shared(smem_u32(&cl_free[ch]), static_cast<uint32_t>(r)));
+      }
       if (n >= p.n) continue;
       // store: lane n writes column n of every valid row (64 B per warp per row)
 #pragma unroll
       for (int i = 0; i < HC; ++i) {
         if (c0 + i >= rows) break;
         const int m = m0 + c0 + i;
-        if (p.split_k > 1) {
+        if (!kCl && p.split_k > 1) {
           p.ws[((static_cast<long long>(s) * p.batch + b) * p.m + m) * static_cast<long long>(p.n) + n] = acc[i];
         } else if constexpr (kOutF32) {
           reinterpret_cast<float*>(p.c)[b * p.c_batch_stride + static_cast<long long>(m) * p.ldc + n] = acc[i];
@@ -408,6 +475,7 @@ __global__ void __launch_bounds__(SwapCfg<MN>::kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (kCl) cluster_sync_all();   // no peer touches this CTA's slots or barriers any more
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem_base, Cfg::kTmemCols);
 }

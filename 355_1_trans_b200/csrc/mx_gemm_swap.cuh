@@ -41,7 +41,12 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
 constexpr uint32_t kMxSwapProducers = 3;   // TMA producer warps 0, 2 and 3
 constexpr uint32_t kMxSwapChains = 2;      // accumulators per unit (alternate K blocks)
 
-template <int MN, int kFp4>
+// Split-K inside the kernel (kCl), as in fp8_block_swap.cuh: the split_k CTAs
+// of a tile form a cluster and sum their partial tiles through distributed
+// shared memory.  The channels are the four epilogue warps (TMEM lane
+// quarters); channel q is reduced and stored by cluster rank q % split_k in
+// rank order.
+template <int MN, int kFp4, bool kCl = false>
 struct MxSwapCfg {
   static_assert(MN == 16 || MN == 32 || MN == 64, "MN must be 16, 32 or 64");
   static constexpr int kSfAtomsK = kFp4 ? 2 : 1;             // scale atoms per stage along K
@@ -50,14 +55,21 @@ struct MxSwapCfg {
   static constexpr uint32_t kSfwBytes = 512u * kSfAtomsK;
   static constexpr uint32_t kSfxBytes = 512u * kSfAtomsK;
   static constexpr uint32_t kStageBytes = kWBytes + kXBytes + kSfwBytes + kSfxBytes;
-  static constexpr int kStages = static_cast<int>((218u * 1024u) / kStageBytes) > 10
+  static constexpr int kChannels = 4;
+  static constexpr int kChanFloats = MN * 32;                // MN rows x 32 columns
+  static constexpr uint32_t kClBytes =
+      kCl ? static_cast<uint32_t>(swap_cl_slot_count(kChannels) * kChanFloats) * 4u : 0u;
+  static constexpr uint32_t kStageBudget = 218u * 1024u - kClBytes;
+  static constexpr int kStages = static_cast<int>(kStageBudget / kStageBytes) > 10
                                      ? 10
-                                     : static_cast<int>((218u * 1024u) / kStageBytes);
+                                     : static_cast<int>(kStageBudget / kStageBytes);
   static constexpr uint32_t kOffX = kWBytes * kStages;
   static constexpr uint32_t kOffSfw = kOffX + kXBytes * kStages;
   static constexpr uint32_t kOffSfx = kOffSfw + kSfwBytes * kStages;
-  static constexpr uint32_t kOffBar = kOffSfx + kSfxBytes * kStages;
-  static constexpr uint32_t kSmemBytes = kOffBar + 256u + 1024u;
+  static constexpr uint32_t kOffCl = kOffSfx + kSfxBytes * kStages;
+  static constexpr uint32_t kOffBar = kOffCl + kClBytes;
+  static constexpr uint32_t kBarBytes = kCl ? 512u : 256u;
+  static constexpr uint32_t kSmemBytes = kOffBar + kBarBytes + 1024u;
   // TMEM: two accumulators [0, 2 MN), then two alternating scale regions
   // (weight atoms: 4 columns per K atom, activation atoms: 4 per K atom)
   // Each unit accumulates its K blocks alternately into kMxSwapChains TMEM
@@ -75,14 +87,14 @@ struct MxSwapCfg {
   static_assert(kColsUsed <= 512, "TMEM columns");
   static_assert(kStages >= 4, "pipeline too shallow");
   static_assert(kSmemBytes <= 227u * 1024u, "shared memory");
-  static_assert(8u * (2u * kStages + 5u) + 8u <= 256u, "barrier area");
+  static_assert(8u * (2u * kStages + 5u + (kCl ? 2u * kChannels : 0u)) + 8u <= kBarBytes, "barrier area");
 };
 
-template <int MN, int kFp4, int kBMode, bool kOutF32>
+template <int MN, int kFp4, int kBMode, bool kOutF32, bool kCl = false>
 __global__ void __launch_bounds__(256, 1)
     mx_gemm_swap_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const MxParams p) {
-  using Cfg = MxSwapCfg<MN, kFp4>;
+  using Cfg = MxSwapCfg<MN, kFp4, kCl>;
   constexpr int S = Cfg::kStages;
   static_assert(kBMode != kBMNMajor, "the weights are the K-major MMA A operand");
 
@@ -98,8 +110,11 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* acc_full = empty_bar + S;   // [2]
   uint64_t* acc_empty = acc_full + 2;   // [2]
   uint64_t* drain_bar = acc_empty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* cl_full = drain_bar + 1;                           // [4] partials of the other ranks arrived
+  uint64_t* cl_free = cl_full + (kCl ? Cfg::kChannels : 0);    // [4] owner consumed this rank's partial
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(cl_free + (kCl ? Cfg::kChannels : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* cl_slots = reinterpret_cast<float*>(smem + Cfg::kOffCl);
 
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31u;
@@ -114,6 +129,12 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(&acc_empty[i], 4);   // one arrival per epilogue warp
     }
     mbar_init(drain_bar, 1);
+    if constexpr (kCl) {
+      for (int i = 0; i < Cfg::kChannels; ++i) {
+        mbar_init(&cl_full[i], 32u * static_cast<uint32_t>(p.split_k - 1));   // every lane of the other ranks
+        mbar_init(&cl_free[i], 32u);                                          // every lane of the owner
+      }
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -127,6 +148,7 @@ __global__ void __launch_bounds__(256, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (kCl) cluster_sync_all();   // the peers' barriers exist before any remote arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   if (threadIdx.x == 0) griddep_launch_dependents();   // a split-K reduce may launch now
@@ -334,12 +356,46 @@ __global__ void __launch_bounds__(256, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[ub]);
+      if constexpr (kCl) {
+        // split-K across the cluster: channel q (this warp's 32 columns) goes to its owner
+        const int S_ = p.split_k;
+        const int rank = static_cast<int>(blockIdx.x) % S_;
+        const int owner = q % S_;
+        const int owned = (Cfg::kChannels + S_ - 1) / S_;
+        const int lch = q / S_;
+        const uint32_t ui = static_cast<uint32_t>(iter);
+        if (rank != owner) {
+          if (ui > 0 && !mbar_wait_cluster(&cl_free[q], (ui - 1u) & 1u, abort_flag, p.timeout_ns)) break;
+          const uint32_t dst =
+              mapa_shared(smem_u32(cl_slots + (rank * owned + lch) * Cfg::kChanFloats + static_cast<int>(lane)),
+                          static_cast<uint32_t>(owner));
+#pragma unroll
+          for (int i = 0; i < MN; ++i) st_cluster_f32(dst + static_cast<uint32_t>(i * 32 * 4), v[i]);
+          mbar_arrive_cluster(mapa_shared(smem_u32(&cl_full[q]), static_cast<uint32_t>(owner)));
+          continue;
+        }
+        if (!mbar_wait_cluster(&cl_full[q], ui & 1u, abort_flag, p.timeout_ns)) break;
+        // rank order: partial 0 + partial 1 + ...
+        float sum[MN];
+        for (int r = 0; r < S_; ++r) {
+          const float* src = cl_slots + (r * owned + lch) * Cfg::kChanFloats + static_cast<int>(lane);
+#pragma unroll
+          for (int i = 0; i < MN; ++i) {
+            const float x = r == rank ? v[i] : src[i * 32];
+            sum[i] = r == 0 ? x : sum[i] + x;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < MN; ++i) v[i] = sum[i];
+        for (int r = 0; r < S_; ++r)
+          if (r != rank) mbar_arrive_cluster(mapa_shared(smem_u32(&cl_free[q]), static_cast<uint32_t>(r)));
+      }
       const int n = nt * 128 + q * 32 + static_cast<int>(lane);   // output column of this lane
       if (n >= p.n) continue;
 #pragma unroll
       for (int i = 0; i < MN; ++i) {
         if (i >= p.m) break;
-        if (p.split_k > 1) {
+        if (!kCl && p.split_k > 1) {
           p.ws[((static_cast<long long>(s) * p.batch + b) * p.m + i) * static_cast<long long>(p.n) + n] = v[i];
         } else if constexpr (kOutF32) {
           reinterpret_cast<float*>(p.c)[b * p.c_batch_stride + static_cast<long long>(i) * p.ldc + n] = v[i];
@@ -353,6 +409,7 @@ __global__ void __launch_bounds__(256, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (kCl) cluster_sync_all();   // no peer touches this CTA's slots or barriers any more
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem_base, Cfg::kTmemCols);
 }

@@ -296,6 +296,11 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, uint32_t a,
                : "memory");
 }
 
+// 4-byte store to shared memory at a cluster address (e.g. a peer CTA's).
+__device__ __forceinline__ void st_cluster_f32(uint32_t cluster_addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+
 // Generic-proxy writes to shared memory of the cluster (this CTA's or a
 // peer's) visible to the async proxy.
 __device__ __forceinline__ void fence_proxy_async_cluster() {
@@ -627,6 +632,20 @@ __device__ __forceinline__ void st_global_cs_v4(void* p, uint32_t a, uint32_t b,
   asm volatile("st.global.cs.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c),
                "r"(d)
                : "memory");
+}
+
+// Split-K reduced inside a thread-block cluster (the transposed decode
+// kernels): at most this many K slices, i.e. CTAs per cluster.
+constexpr int kSwapMaxClusterSplit = 4;
+
+constexpr int swap_cl_slot_count(int channels) {
+  // slots a CTA holds: split * ceil(channels / split), largest over split 2..4
+  int best = 0;
+  for (int s = 2; s <= kSwapMaxClusterSplit; ++s) {
+    const int v = s * ((channels + s - 1) / s);
+    best = v > best ? v : best;
+  }
+  return best;
 }
 
 // Grouped rasterisation of output tiles: consecutive work units walk the

@@ -757,3 +757,61 @@ def test_fp8_block_decode_full_shape(bs, orc, cuda):
     """Decode at full size, M=16 N=7168 K=18432 (transposed kernel, auto split-K),
     every element checked."""
     run_fp8_block(bs, orc, cuda, 16, 7168, 18432, seed=16)
+
+
+# ---- split-K inside CTA clusters (decode calls without a workspace) ---------------------
+
+@pytest.mark.parametrize("m,n,k,split_k,out_dtype", [
+    (16, 7168, 2048, 0, torch.bfloat16), (1, 4096, 7168, 3, torch.bfloat16), (30, 896, 1536, 2, torch.float32),
+    (48, 1000, 1152, 4, torch.bfloat16), (64, 640, 640, 3, torch.bfloat16), (7, 24576, 1536, 2, torch.bfloat16)])
+def test_fp8_block_cluster_split_without_workspace(bs, orc, cuda, m, n, k, split_k, out_dtype):
+    """No workspace: the K slices of each output tile are summed inside a
+    cluster of CTAs (distributed shared memory), in slice order."""
+    qa, sa = orc.quant_fp8_block(orc.normal((m, k), seed=300 + m), 1)
+    qb, sb = orc.quant_fp8_block(orc.normal((n if n % 128 == 0 else (n + 127) // 128 * 128, k), seed=301 + m), 128)
+    qb, sb = qb[:n], sb
+    ref, mag = orc.gemm_fp8_block(qa, qb, sa, sb)
+    out = poisoned((m, n), out_dtype, cuda)
+    bs.gemm_a8w8_bpreshuffle(dev_u8(qa, cuda).view(torch.float8_e4m3fn),
+                             dev_u8(np.ascontiguousarray(qb), cuda).view(torch.float8_e4m3fn),
+                             torch.from_numpy(sa).to(cuda), torch.from_numpy(sb).to(cuda), out_dtype, b_layout="raw",
+                             out=out, split_k=split_k, kernel="swap", workspace=False)
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    assert_close(orc, ref, out.float().cpu().numpy(), mag, f"fp8 block cluster split {m}x{n}x{k} s{split_k}")
+
+
+def test_fp8_block_cluster_split_more_tiles_than_clusters(bs, orc, cuda):
+    """Persistent clusters: a grid cap of 6 CTAs (3 clusters of 2) walks 56 tiles."""
+    m, n, k = 16, 7168, 1024
+    qa, sa = orc.quant_fp8_block(orc.normal((m, k), seed=310), 1)
+    qb, sb = orc.quant_fp8_block(orc.normal((n, k), seed=311), 128)
+    ref, mag = orc.gemm_fp8_block(qa, qb, sa, sb)
+    out = bs.gemm_a8w8_bpreshuffle(dev_u8(qa, cuda).view(torch.float8_e4m3fn),
+                                   dev_u8(orc.shuffle_kpanel(qb), cuda).view(torch.float8_e4m3fn),
+                                   torch.from_numpy(sa).to(cuda), torch.from_numpy(sb).to(cuda), split_k=2,
+                                   kernel="swap", workspace=False, grid_blocks=6)
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    assert_close(orc, ref, out.float().cpu().numpy(), mag, "fp8 block cluster split, 3 clusters")
+
+
+@pytest.mark.parametrize("fp4,m,split_k", [(False, 16, 0), (False, 40, 3), (True, 1, 2), (True, 64, 4)])
+def test_mx_cluster_split_without_workspace(bs, orc, cuda, fp4, m, split_k):
+    n, k = 2048, 4096
+    if fp4:
+        qa, qb, sa, sb = mxfp4_problem(orc, m, n, k, 320 + m, "kpattern")
+        ref, mag = orc.gemm_mxfp4(qa, qb, sa, sb)
+        A, B = dev_u8(qa, cuda), dev_u8(qb, cuda)
+        fn = bs.gemm_a4w4_mxfp4
+    else:
+        qa, qb, sa, sb = [x[0] for x in mxfp8_problem(orc, m, n, k, 320 + m, "kpattern")]
+        ref, mag = orc.gemm_mxfp8(qa, qb, sa, sb, f64=True)
+        A, B = dev_u8(qa, cuda).view(torch.float8_e4m3fn), dev_u8(qb, cuda).view(torch.float8_e4m3fn)
+        fn = bs.gemm_a8w8_mxfp8
+    SA, SB = bs.pack_scales(dev_u8(sa, cuda)), bs.pack_scales(dev_u8(sb, cuda))
+    out = poisoned((m, n), torch.bfloat16, cuda)
+    fn(A, B, SA, SB, out=out, scale_format="native", split_k=split_k, kernel="swap", workspace=False)
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    assert_close(orc, ref, out.float().cpu().numpy(), mag, f"{'mxfp4' if fp4 else 'mxfp8'} cluster split m{m} s{split_k}")
