@@ -127,7 +127,8 @@ def parse():
     ap.add_argument("--c4-steps", type=int, default=8)
     ap.add_argument("--c4-strips", type=int, default=4, help="M strips of the overlapped GEMM + all-gather")
     ap.add_argument("--c4-grid", type=int, default=0,
-                    help="CTA cap of the configs[4] GEMMs (0 = one per SM; a cap leaves SMs to NCCL)")
+                    help="CTA cap of the overlapped configs[4] strip GEMMs (0 = one per SM; a cap leaves "
+                         "SMs to NCCL's kernels)")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the N=1 mxfp4 and sustained sub-records")
     args = ap.parse_args()
@@ -688,7 +689,7 @@ def run_ours(args):
     if not args.no_configs4:
         import bench_configs4
         c4 = bench_configs4.run(sys.modules[__name__], bs, dev, world, rank, dist if world > 1 else None, peaks,
-                                steps=args.c4_steps, strips=args.c4_strips, grid_blocks=args.c4_grid)
+                                steps=args.c4_steps, strips=args.c4_strips, overlap_grid=args.c4_grid)
         if c4 is not None:
             extra["configs4"] = c4
 

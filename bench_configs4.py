@@ -146,9 +146,11 @@ def _over_ranks(v, dist, world, dev):
     return [float(x) for x in out.cpu()]
 
 
-def run(bench, bs, dev, world, rank, dist, peaks, steps=8, warmup=3, strips=4, grid_blocks=0):
+def run(bench, bs, dev, world, rank, dist, peaks, steps=8, warmup=3, strips=4, overlap_grid=0):
     """Returns the configs4 record on rank 0 (None elsewhere).  Every rank
-    takes the same collective steps in the same order."""
+    takes the same collective steps in the same order.  overlap_grid > 0
+    caps the CTAs of the overlapped strip GEMMs, leaving SMs to NCCL's
+    kernels; the GEMM-only and serial timings always use every SM."""
     import numpy as np
     import torch
     P = world
@@ -157,14 +159,14 @@ def run(bench, bs, dev, world, rank, dist, peaks, steps=8, warmup=3, strips=4, g
     stream = torch.cuda.current_stream(dev)
     dist_ = dist if world > 1 else None
     rec = {"workload": f"M={M} N={N} K={K}, N-sharded over {P} GPU(s) ({nl} columns each), bf16 out",
-           "scaling": "strong", "strips": strips,
+           "scaling": "strong", "strips": strips, "overlap_grid": overlap_grid or "all SMs",
            "gather_layout": {"serial": "[P][M][N/P] rank-major", "overlapped": "[S][P][M/S][N/P] strip-major"},
            "link_gbs": LINK_GBS, "families": {}}
     flops = 2.0 * M * N * K
     for fam in FAMILIES:
         qa, sa = _activations(bench, fam, dev, rank, dist_)
         qb, sb = _weights(bench, fam, n0, n0 + nl, dev)
-        gemm = _Gemm(bs, fam, qa, sa, qb, sb, nl, grid_blocks)
+        gemm = _Gemm(bs, fam, qa, sa, qb, sb, nl)
         del qb, sb
         out = torch.empty(M, nl, dtype=torch.bfloat16, device=dev)
         t_gemm = _time(lambda: gemm(out), steps, warmup, stream)
@@ -188,7 +190,7 @@ def run(bench, bs, dev, world, rank, dist, peaks, steps=8, warmup=3, strips=4, g
             def overlapped():
                 works = []
                 for s in range(strips):
-                    gemm(out, s * ms, (s + 1) * ms)
+                    gemm(out, s * ms, (s + 1) * ms, grid_blocks=overlap_grid)
                     works.append(dist.all_gather_into_tensor(gath_s[s], out[s * ms:(s + 1) * ms], async_op=True))
                 for w in works:
                     w.wait()
