@@ -166,8 +166,8 @@ __global__ void __launch_bounds__(SwapCfg<MN, kCl>::kThreads, 1)
     }
     if constexpr (kCl) {
       for (int i = 0; i < Cfg::kChannels; ++i) {
-        mbar_init(&cl_full[i], 32u * static_cast<uint32_t>(p.split_k - 1));   // every lane of the other ranks
-        mbar_init(&cl_free[i], 32u);                                          // every lane of the owner
+        mbar_init(&cl_full[i], static_cast<uint32_t>(p.split_k - 1));   // one warp of each other rank
+        mbar_init(&cl_free[i], 1u);                                      // the owner's warp
       }
     }
     *abort_flag = 0;
@@ -183,7 +183,10 @@ __global__ void __launch_bounds__(SwapCfg<MN, kCl>::kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if constexpr (kCl) cluster_sync_all();   // the peers' barriers exist before any remote arrival
+  // the peers' barriers must exist before any remote arrival: every thread
+  // arrives here and waits just before its first remote access (or at the end)
+  if constexpr (kCl) cluster_arrive();
+  bool cl_waited = false;
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   if (threadIdx.x == 0) griddep_launch_dependents();   // a split-K reduce may launch now
@@ -422,6 +425,10 @@ __global__ void __launch_bounds__(SwapCfg<MN, kCl>::kThreads, 1)
         const int owner = ch % S_;
         const int owned = (Cfg::kChannels + S_ - 1) / S_;
         const int lch = ch / S_;
+        if (!cl_waited) {   // the peers' barriers are initialised (see the arrival above)
+          cluster_wait();
+          cl_waited = true;
+        }
         if (rank != owner) {
           // the owner has consumed this channel's previous partial from our slot
           if (ui > 0 && !mbar_wait_cluster(&cl_free[ch], (ui - 1u) & 1u, abort_flag, p.timeout_ns)) {
@@ -433,7 +440,9 @@ __global__ void __launch_bounds__(SwapCfg<MN, kCl>::kThreads, 1)
                           static_cast<uint32_t>(owner));
 #pragma unroll
           for (int i = 0; i < HC; ++i) st_cluster_f32(dst + static_cast<uint32_t>(i * 32 * 4), acc[i]);
-          mbar_arrive_cluster(mapa_shared(smem_u32(&cl_full[ch]), static_cast<uint32_t>(owner)));
+          fence_acq_rel_cluster();   // this lane's remote stores before the warp's arrival
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&cl_full[ch]), static_cast<uint32_t>(owner)));
           continue;
         }
         if (!mbar_wait_cluster(&cl_full[ch], ui & 1u, abort_flag, p.timeout_ns)) {
@@ -452,8 +461,9 @@ __global__ void __launch_bounds__(SwapCfg<MN, kCl>::kThreads, 1)
         }
 #pragma unroll
         for (int i = 0; i < HC; ++i) acc[i] = sum[i];
+        __syncwarp();   // every lane has read the slots before they are freed
         for (int r = 0; r < S_; ++r)
-          if (r != rank) mbar_arrive_cluster(mapa_shared(smem_u32(&cl_free[ch]), static_cast<uint32_t>(r)));
+          if (r != rank && lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&cl_free[ch]), static_cast<uint32_t>(r)));
       }
       if (n >= p.n) continue;
       // store: lane n writes column n of every valid row (64 B per warp per row)
@@ -475,7 +485,10 @@ __global__ void __launch_bounds__(SwapCfg<MN, kCl>::kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if constexpr (kCl) cluster_sync_all();   // no peer touches this CTA's slots or barriers any more
+  if constexpr (kCl) {
+    if (!cl_waited) cluster_wait();
+    cluster_sync_all();   // no peer touches this CTA's slots or barriers any more
+  }
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem_base, Cfg::kTmemCols);
 }

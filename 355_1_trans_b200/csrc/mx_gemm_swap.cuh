@@ -131,8 +131,8 @@ __global__ void __launch_bounds__(256, 1)
     mbar_init(drain_bar, 1);
     if constexpr (kCl) {
       for (int i = 0; i < Cfg::kChannels; ++i) {
-        mbar_init(&cl_full[i], 32u * static_cast<uint32_t>(p.split_k - 1));   // every lane of the other ranks
-        mbar_init(&cl_free[i], 32u);                                          // every lane of the owner
+        mbar_init(&cl_full[i], static_cast<uint32_t>(p.split_k - 1));   // one warp of each other rank
+        mbar_init(&cl_free[i], 1u);                                      // the owner's warp
       }
     }
     *abort_flag = 0;
@@ -148,7 +148,10 @@ __global__ void __launch_bounds__(256, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if constexpr (kCl) cluster_sync_all();   // the peers' barriers exist before any remote arrival
+  // the peers' barriers must exist before any remote arrival: every thread
+  // arrives here and waits just before its first remote access (or at the end)
+  if constexpr (kCl) cluster_arrive();
+  bool cl_waited = false;
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   if (threadIdx.x == 0) griddep_launch_dependents();   // a split-K reduce may launch now
@@ -364,6 +367,10 @@ __global__ void __launch_bounds__(256, 1)
         const int owned = (Cfg::kChannels + S_ - 1) / S_;
         const int lch = q / S_;
         const uint32_t ui = static_cast<uint32_t>(iter);
+        if (!cl_waited) {   // the peers' barriers are initialised (see the arrival above)
+          cluster_wait();
+          cl_waited = true;
+        }
         if (rank != owner) {
           if (ui > 0 && !mbar_wait_cluster(&cl_free[q], (ui - 1u) & 1u, abort_flag, p.timeout_ns)) break;
           const uint32_t dst =
@@ -371,7 +378,9 @@ __global__ void __launch_bounds__(256, 1)
                           static_cast<uint32_t>(owner));
 #pragma unroll
           for (int i = 0; i < MN; ++i) st_cluster_f32(dst + static_cast<uint32_t>(i * 32 * 4), v[i]);
-          mbar_arrive_cluster(mapa_shared(smem_u32(&cl_full[q]), static_cast<uint32_t>(owner)));
+          fence_acq_rel_cluster();   // this lane's remote stores before the warp's arrival
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&cl_full[q]), static_cast<uint32_t>(owner)));
           continue;
         }
         if (!mbar_wait_cluster(&cl_full[q], ui & 1u, abort_flag, p.timeout_ns)) break;
@@ -387,8 +396,9 @@ __global__ void __launch_bounds__(256, 1)
         }
 #pragma unroll
         for (int i = 0; i < MN; ++i) v[i] = sum[i];
+        __syncwarp();   // every lane has read the slots before they are freed
         for (int r = 0; r < S_; ++r)
-          if (r != rank) mbar_arrive_cluster(mapa_shared(smem_u32(&cl_free[q]), static_cast<uint32_t>(r)));
+          if (r != rank && lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&cl_free[q]), static_cast<uint32_t>(r)));
       }
       const int n = nt * 128 + q * 32 + static_cast<int>(lane);   // output column of this lane
       if (n >= p.n) continue;
@@ -409,7 +419,10 @@ __global__ void __launch_bounds__(256, 1)
 
   tc_fence_before();
   __syncthreads();
-  if constexpr (kCl) cluster_sync_all();   // no peer touches this CTA's slots or barriers any more
+  if constexpr (kCl) {
+    if (!cl_waited) cluster_wait();
+    cluster_sync_all();   // no peer touches this CTA's slots or barriers any more
+  }
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem_base, Cfg::kTmemCols);
 }
