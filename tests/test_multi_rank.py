@@ -120,3 +120,26 @@ def test_lost_rank_fails_fast(tmp_path):
     assert not alive, "a rank hung"
     text = result.read_text()
     assert text.startswith("error after"), text
+
+
+@pytest.mark.parametrize("fam", ["mxfp4", "fp8block"])
+def test_configs4_weights_are_the_same_for_every_rank_count(fam, monkeypatch):
+    """bench.py's configs[4] record regenerates weight columns from per-block
+    seeds on whichever rank needs them, and checks the gathered C against
+    them: the concatenated shards of P ranks must be the very bytes of the
+    unsharded matrix for P = 1, 2, 4, 8 (here on the CPU at a reduced size)."""
+    import bench
+    import bench_configs4 as c4
+    monkeypatch.setattr(c4, "N", 4096)
+    monkeypatch.setattr(c4, "K", 256)
+    dev = torch.device("cpu")
+    whole_q, whole_s = c4._weights(bench, fam, 0, 4096, dev)
+    for p in (2, 4, 8):
+        nl = 4096 // p
+        parts = [c4._weights(bench, fam, r * nl, (r + 1) * nl, dev) for r in range(p)]
+        assert torch.equal(torch.cat([q for q, _ in parts]), whole_q), (fam, p)
+        assert torch.equal(torch.cat([s for _, s in parts]), whole_s), (fam, p)
+    # a 128-column block regenerated alone (the parity check's unit) matches too
+    q, s = c4._weights(bench, fam, 1664, 1792, dev)
+    assert torch.equal(q, whole_q[1664:1792])
+    assert torch.equal(s, whole_s[1664:1792] if fam == "mxfp4" else whole_s[13:14])
