@@ -1966,7 +1966,8 @@ int bsgemm_quantize(const void* x, int in_dtype, int rows, int cols, long long l
   p.sf_format = sf_format == BSG_SF_NATIVE ? 0 : sf_format == BSG_SF_ROWMAJOR ? 1 : 2;
   p.ld_sf = ld_sf;
   p.rows_padded = (rows + 127) / 128 * 128;
-  const int warps_per_row = (cols + bsg::kQuantWarpCols - 1) / bsg::kQuantWarpCols;
+  const int warp_cols = bsg::quant_warp_cols(in_dtype == BSG_IN_FP32);
+  const int warps_per_row = (cols + warp_cols - 1) / warp_cols;
   const int launch_rows = mx && p.sf_format == 0 ? p.rows_padded : rows;
   const long long warps = static_cast<long long>(launch_rows) * warps_per_row;
   const long long blocks = (warps + 7) / 8;

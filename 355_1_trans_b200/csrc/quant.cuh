@@ -18,11 +18,13 @@
 // (round to nearest even, saturate to the largest finite code, NaN -> NaN).
 //
 // Work split: a thread converts 8 consecutive elements (one 16-byte bf16 or
-// two 16-byte fp32 loads) in each of four 256-column segments, issuing all
-// its loads first (bytes in flight per SM to cover HBM latency); 4 threads
-// form an MX group, 16 a 128-block, and the group maximum is a butterfly of
-// warp shuffles.  A warp covers 1024 consecutive elements of one row, so
-// loads and stores are contiguous.
+// two 16-byte fp32 loads) in each of eight (bf16) or four (fp32) 256-column
+// segments, issuing all its loads first so that 128 bytes per thread are in
+// flight to cover HBM latency (bf16 loads stay packed in 4 registers each
+// until converted); 4 threads form an MX group, 16 a 128-block, and the
+// group maximum is a butterfly of warp shuffles.  A warp covers 2048 (bf16)
+// or 1024 (fp32) consecutive elements of one row, so loads and stores are
+// contiguous.
 #pragma once
 
 #include "sm100.cuh"
@@ -57,15 +59,40 @@ __device__ __forceinline__ uint32_t cvt_e2m1x2(float lo, float hi) {
   return r;
 }
 
-// exponent of 2^ceil(log2(amax / qmax)) for amax > 0, exact (double quotient:
-// a float amax divided by 448 or 6 is never within a double ulp of a power
-// of two unless it is one)
+// exponent of 2^ceil(log2(amax / qmax)) for amax > 0, exact, from the bits.
+// With qmax = c 2^P (448 = 1.75 2^8, 6 = 1.5 2^2) and amax = m 2^e, m in
+// [1, 2) (subnormals normalised first): amax / qmax = (m / c) 2^(e - P) with
+// m / c in (1/2, 2), so the ceiling is e - P + 1 when m > c and e - P
+// otherwise (m == c is an exact power of two).  Identical to ceil(log2())
+// of the double quotient for every finite float (checked exhaustively over
+// mantissas, subnormals and the clamp range); infinities keep that form.
+template <int kP, uint32_t kCFrac>
 __device__ __forceinline__ int mx_scale_exponent(float amax, double qmax) {
   if (!(amax > 0.0f)) return 0;
-  int e;
-  const double f = frexp(static_cast<double>(amax) / qmax, &e);   // f in [0.5, 1)
-  int se = f == 0.5 ? e - 1 : e;
+  const uint32_t bits = __float_as_uint(amax);
+  uint32_t exp_field = bits >> 23, frac = bits & 0x7FFFFFu;
+  int se;
+  if (exp_field == 255u) {   // +inf
+    int e;
+    const double f = frexp(static_cast<double>(amax) / qmax, &e);
+    se = f == 0.5 ? e - 1 : e;
+  } else {
+    int e;
+    if (exp_field == 0u) {   // subnormal: normalise the fraction
+      const int k = __clz(static_cast<int>(frac)) - 8;
+      frac = (frac << k) & 0x7FFFFFu;
+      e = -126 - k;
+    } else {
+      e = static_cast<int>(exp_field) - 127;
+    }
+    se = e - kP + (frac > kCFrac ? 1 : 0);
+  }
   return se < -127 ? -127 : (se > 127 ? 127 : se);
+}
+
+// 2^-se for se in [-127, 127], exactly (2^-127 is subnormal)
+__device__ __forceinline__ float pow2_neg(int se) {
+  return __uint_as_float(se < 127 ? static_cast<uint32_t>(127 - se) << 23 : 0x00400000u);
 }
 
 // byte offset of (row, group) in the native scale layout
@@ -75,15 +102,17 @@ __device__ __forceinline__ long long native_sf_offset(int row, int g, int kg) {
          (((row % 32) * 4 + (row % 128) / 32) * 4 + (g % 4));
 }
 
-// Columns covered by one warp: kQuantItems segments of 256, every thread
-// issuing its kQuantItems 16-byte loads before converting any of them.
-constexpr int kQuantItems = 4;
-constexpr int kQuantWarpCols = 256 * kQuantItems;
+// Columns covered by one warp: quant_items segments of 256, every thread
+// issuing its 16-byte loads (two per segment for fp32) before converting any.
+constexpr int quant_items(bool f32_in) { return f32_in ? 4 : 8; }
+constexpr int quant_warp_cols(bool f32_in) { return 256 * quant_items(f32_in); }
 
 template <int kFormat, bool kF32In>
-__global__ void __launch_bounds__(256) quantize_kernel(const QuantParams p) {
+__global__ void __launch_bounds__(256, 4) quantize_kernel(const QuantParams p) {
   constexpr int kGroup = kFormat == kQuantFp8Block ? 128 : 32;
   constexpr int kLanes = kGroup / 8;   // threads per group
+  constexpr int kQuantItems = quant_items(kF32In);
+  constexpr int kQuantWarpCols = quant_warp_cols(kF32In);
   const int warps_per_row = (p.cols + kQuantWarpCols - 1) / kQuantWarpCols;
   const long long gw = static_cast<long long>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = static_cast<int>(threadIdx.x & 31u);
@@ -95,30 +124,19 @@ __global__ void __launch_bounds__(256) quantize_kernel(const QuantParams p) {
   // and it waits for this grid's completion before it reads the outputs.
   griddep_launch_dependents();
   if (row >= limit_rows) return;
-  // all loads first
-  float v[kQuantItems][8];
+  // all loads first: raw 16-byte words (bf16 stays packed until converted)
+  uint4 raw[kF32In ? 2 * kQuantItems : kQuantItems];
 #pragma unroll
   for (int it = 0; it < kQuantItems; ++it) {
     const int col = col0 + it * 256;
     const bool live = row < p.rows && col < p.cols;   // cols % kGroup == 0: whole groups live or not
-    if (live) {
-      if constexpr (kF32In) {
-        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.x) + row * p.ldx + col);
-        const float4 a = __ldg(src), b = __ldg(src + 1);
-        v[it][0] = a.x; v[it][1] = a.y; v[it][2] = a.z; v[it][3] = a.w;
-        v[it][4] = b.x; v[it][5] = b.y; v[it][6] = b.z; v[it][7] = b.w;
-      } else {
-        const uint4 w = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + row * p.ldx + col));
-        const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          v[it][2 * i] = __uint_as_float(u[i] << 16);
-          v[it][2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
-        }
-      }
+    if constexpr (kF32In) {
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const float*>(p.x) + row * p.ldx + col);
+      raw[2 * it] = live ? __ldg(src) : make_uint4(0u, 0u, 0u, 0u);
+      raw[2 * it + 1] = live ? __ldg(src + 1) : make_uint4(0u, 0u, 0u, 0u);
     } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[it][i] = 0.0f;
+      raw[it] = live ? __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.x) + row * p.ldx + col))
+                     : make_uint4(0u, 0u, 0u, 0u);
     }
   }
 #pragma unroll
@@ -126,9 +144,24 @@ __global__ void __launch_bounds__(256) quantize_kernel(const QuantParams p) {
     const int col = col0 + it * 256;
     if (col - lane * 8 >= p.cols) break;   // the whole warp is past the row end
     const bool live = row < p.rows && col < p.cols;
+    float v[1][8];   // this segment's 8 elements (indexed [0][i] below)
+    if constexpr (kF32In) {
+      const uint4 a = raw[2 * it], b = raw[2 * it + 1];
+      v[0][0] = __uint_as_float(a.x); v[0][1] = __uint_as_float(a.y);
+      v[0][2] = __uint_as_float(a.z); v[0][3] = __uint_as_float(a.w);
+      v[0][4] = __uint_as_float(b.x); v[0][5] = __uint_as_float(b.y);
+      v[0][6] = __uint_as_float(b.z); v[0][7] = __uint_as_float(b.w);
+    } else {
+      const uint32_t u[4] = {raw[it].x, raw[it].y, raw[it].z, raw[it].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[0][2 * i] = __uint_as_float(u[i] << 16);
+        v[0][2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
+      }
+    }
     float amax = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[it][i]));
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[0][i]));
 #pragma unroll
     for (int d = 1; d < kLanes; d <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
     const int g = col / kGroup;
@@ -140,8 +173,8 @@ __global__ void __launch_bounds__(256) quantize_kernel(const QuantParams p) {
       uint32_t w0 = 0, w1 = 0;
 #pragma unroll
       for (int i = 0; i < 4; i += 2) {
-        w0 |= cvt_e4m3x2(v[it][i] / s, v[it][i + 1] / s) << (8 * i);
-        w1 |= cvt_e4m3x2(v[it][i + 4] / s, v[it][i + 5] / s) << (8 * i);
+        w0 |= cvt_e4m3x2(v[0][i] / s, v[0][i + 1] / s) << (8 * i);
+        w1 |= cvt_e4m3x2(v[0][i + 4] / s, v[0][i + 5] / s) << (8 * i);
       }
       *reinterpret_cast<uint2*>(p.q + row * p.ldq + col) = make_uint2(w0, w1);
       if (leader) {
@@ -153,21 +186,22 @@ __global__ void __launch_bounds__(256) quantize_kernel(const QuantParams p) {
       }
     } else {
       constexpr double kQmax = kFormat == kQuantMxfp4 ? 6.0 : 448.0;
-      const int se = mx_scale_exponent(amax, kQmax);
+      const int se = kFormat == kQuantMxfp4 ? mx_scale_exponent<2, 0x400000u>(amax, kQmax)
+                                            : mx_scale_exponent<8, 0x600000u>(amax, kQmax);
       if (live) {
-        const float mul = ldexpf(1.0f, -se);   // exact power of two (2^-127 .. 2^127)
+        const float mul = pow2_neg(se);   // exact power of two (2^-127 .. 2^127)
         if constexpr (kFormat == kQuantMxfp8) {
           uint32_t w0 = 0, w1 = 0;
 #pragma unroll
           for (int i = 0; i < 4; i += 2) {
-            w0 |= cvt_e4m3x2(v[it][i] * mul, v[it][i + 1] * mul) << (8 * i);
-            w1 |= cvt_e4m3x2(v[it][i + 4] * mul, v[it][i + 5] * mul) << (8 * i);
+            w0 |= cvt_e4m3x2(v[0][i] * mul, v[0][i + 1] * mul) << (8 * i);
+            w1 |= cvt_e4m3x2(v[0][i + 4] * mul, v[0][i + 5] * mul) << (8 * i);
           }
           *reinterpret_cast<uint2*>(p.q + row * p.ldq + col) = make_uint2(w0, w1);
         } else {
           uint32_t w = 0;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) w |= cvt_e2m1x2(v[it][2 * i] * mul, v[it][2 * i + 1] * mul) << (8 * i);
+          for (int i = 0; i < 4; ++i) w |= cvt_e2m1x2(v[0][2 * i] * mul, v[0][2 * i + 1] * mul) << (8 * i);
           *reinterpret_cast<uint32_t*>(p.q + row * p.ldq + col / 2) = w;
         }
       }

@@ -115,8 +115,14 @@ def parse():
                     help="use a tuned table for the library's auto calls (--sweep)")
     ap.add_argument("--quant", action="store_true",
                     help="activation quantise+pack bandwidth (bf16 -> mxfp8/mxfp4/fp8_block), one JSON line")
+    ap.add_argument("--quant-m", type=int, default=None, help="--quant: only this row count")
+    ap.add_argument("--quant-fmt", default=None, choices=["mxfp8", "mxfp4", "fp8_block"],
+                    help="--quant: only this format")
     ap.add_argument("--sweep", action="store_true",
                     help="fp8 block-scale sweep, M in {1,16,64,128,1024,8192} x 4 (N,K) shapes, one JSON line")
+    ap.add_argument("--chain", action="store_true",
+                    help="decode chain: the four configs[1] (N,K) GEMMs at M=16 back to back (one L2 flush "
+                         "before the chain) against the same calls one at a time, one JSON line")
     ap.add_argument("--grouped", action="store_true",
                     help="grouped (MoE) GEMMs of the three families on decode and prefill expert mixes, one JSON line")
     ap.add_argument("--families", default="fp8block,mxfp8,mxfp4",
@@ -876,6 +882,84 @@ def run_sweep(args):
     return 0
 
 
+def run_chain(args):
+    """Decode chain: the fp32 block-scale GEMMs of BASELINE configs[1]'s four
+    (N, K) groups at M=16 (K-panel B, bf16 out, the library's automatic
+    kernel and split), issued back to back as one serving step would.  One
+    CUDA graph replays R x (256 MiB L2-flushing read, the four GEMMs); a
+    second replays the flushes alone; the difference / R is the chain's time.
+    Each GEMM launches with programmatic dependent launch, so its prologue
+    and L2 prefetch of weights overlap the GEMM before it.  Compared with the
+    sum of the four calls timed one at a time (a flush before each)."""
+    import torch
+    dev = torch.device("cuda", 0)
+    bs = importlib.import_module("355_1_trans_b200")
+    peaks, peak_kind = load_peaks()
+    flush = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    sink = torch.empty((), dtype=torch.float32, device=dev)
+    reps = 10
+
+    def graph_time(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(max(3, min(args.steps, 10))):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        del g
+        return statistics.median(ts)
+
+    m = 16
+    calls, wbytes = [], 0
+    for i, (n, k) in enumerate(((7168, 2048), (4096, 7168), (24576, 1536), (7168, 18432))):
+        qa, qb, sa, sb = make_fp8block_inputs(m, n, k, dev, 20 + i)
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        calls.append((lambda qa=qa, qb=qb, sa=sa, sb=sb, out=out:
+                      bs.gemm_a8w8_bpreshuffle(qa, qb, sa, sb, torch.bfloat16, preshuffled=True, out=out)))
+        wbytes += n * k + 4 * (n // 128) * (k // 128)
+    for c in calls:
+        c()
+    torch.cuda.synchronize()
+
+    def flushes():
+        for _ in range(reps):
+            torch.sum(flush, dim=0, out=sink)
+
+    def chain():
+        for _ in range(reps):
+            torch.sum(flush, dim=0, out=sink)
+            for c in calls:
+                c()
+
+    t_flush = graph_time(flushes)
+    chain_us = (graph_time(chain) - t_flush) / reps * 1e3
+    single_us = []
+    for c in calls:
+        def one(c=c):
+            for _ in range(reps):
+                torch.sum(flush, dim=0, out=sink)
+                c()
+        single_us.append((graph_time(one) - t_flush) / reps * 1e3)
+    assert bs.check_device_error() == 0
+    hbm = peaks["hbm_gbs"]
+    print(json.dumps({"chain": "fp32 block-scale decode, M=16, (N,K) = (7168,2048), (4096,7168), (24576,1536), "
+                               "(7168,18432), K-panel B, bf16 out, automatic kernel and split",
+                      "l2": "flushed (256 MiB read) once before the chain / before each single call",
+                      "chain_us": chain_us, "single_us": single_us, "sum_single_us": sum(single_us),
+                      "weight_bytes": wbytes, "chain_hbm_frac": wbytes / chain_us / 1e3 / hbm,
+                      "single_hbm_frac": wbytes / sum(single_us) / 1e3 / hbm,
+                      "hbm_peak_gbs": hbm, "peak_kind": peak_kind}), flush=True)
+    return 0
+
+
 def run_quant(args):
     """bsgemm_quantize bandwidth: bf16 activations [M, 7168] -> each format with
     its default scale layout, L2 flushed before every call, graph-difference
@@ -913,9 +997,9 @@ def run_quant(args):
     t_flush = graph_time(flushes)
     rows = []
     k = 7168
-    for m in (16, 128, 1024, 8192, 32768):
+    for m in ((args.quant_m,) if args.quant_m else (16, 128, 1024, 8192, 32768)):
         x = torch.randn(m, k, device=dev).to(torch.bfloat16)
-        for fmt in ("mxfp8", "mxfp4", "fp8_block"):
+        for fmt in ((args.quant_fmt,) if args.quant_fmt else ("mxfp8", "mxfp4", "fp8_block")):
             call = lambda: bs.quantize(x, fmt)
             call()
 
@@ -1114,6 +1198,8 @@ def main():
         return run_sweep(args)
     if args.quant:
         return run_quant(args)
+    if args.chain:
+        return run_chain(args)
     if args.grouped:
         return run_grouped(args)
     return run_ours(args)
