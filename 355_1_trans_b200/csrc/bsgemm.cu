@@ -19,6 +19,7 @@
 
 #include "../../include/bsgemm_b200.h"
 #include "fp8_block_gemm.cuh"
+#include "fp8_block_gemm_2sm.cuh"
 #include "fp8_block_swap.cuh"
 #include "mx_gemm.cuh"
 #include "mx_gemm_2sm.cuh"
@@ -1027,6 +1028,34 @@ int fp8b_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockPa
   return rc != BSG_OK ? rc : launch_status();
 }
 
+template <int kBFmt, bool kOutF32>
+int fp8b2_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockParams& p, int grid,
+                   cudaStream_t st) {
+  using Cfg = bsg::Fp8Block2Cfg;
+  auto* kern = bsg::fp8_block_gemm_2sm_kernel<kBFmt, kOutF32>;
+  if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
+  const int rc = launch_pdl(kern, grid, 256, Cfg::kSmemBytes, st, ta, tb, p);
+  return rc != BSG_OK ? rc : launch_status();
+}
+
+int fp8b2_launch(int fmt, bool f32, const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockParams& p,
+                 int grid, cudaStream_t st) {
+  switch (fmt) {
+    case bsg::kFmtKPanel:
+      return f32 ? fp8b2_launch_t<bsg::kFmtKPanel, true>(ta, tb, p, grid, st)
+                 : fp8b2_launch_t<bsg::kFmtKPanel, false>(ta, tb, p, grid, st);
+    case bsg::kFmtShuffle16:
+      return f32 ? fp8b2_launch_t<bsg::kFmtShuffle16, true>(ta, tb, p, grid, st)
+                 : fp8b2_launch_t<bsg::kFmtShuffle16, false>(ta, tb, p, grid, st);
+    default:
+      return f32 ? fp8b2_launch_t<bsg::kFmtRaw, true>(ta, tb, p, grid, st)
+                 : fp8b2_launch_t<bsg::kFmtRaw, false>(ta, tb, p, grid, st);
+  }
+}
+
+// CTA-pair kernel (256 x 128 tiles, no split-K): on request only.
+bool fp8b_use_pair(const bsgemm_args& a) { return a.kernel == BSG_KERNEL_PAIR; }
+
 bool fp8b_use_swap(const bsgemm_args& a) {
   return a.kernel == BSG_KERNEL_SWAP || (a.kernel == BSG_KERNEL_AUTO && a.m <= 64);
 }
@@ -1131,21 +1160,21 @@ int swap_launch_mn(int fmt, bool f32, const CUtensorMap& ta, const CUtensorMap& 
 // Tensor map of the fp8 block-scale weights (batch = experts for grouped
 // calls): shuffle_weight(16,16), K panels B'[K/128][N][128], or raw [N, K].
 bool make_fp8b_weight_tmap(CUtensorMap* tb, const bsgemm_args& a, bool kpanel, bool shuf, int kb,
-                           long long b_elems) {
-  if (shuf) return make_shuffle16_tmap(tb, a.ptr_b, a.n, a.k, a.stride_b_batch, a.batch, 128u);
+                           long long b_elems, uint32_t box_rows = 128u) {
+  if (shuf) return make_shuffle16_tmap(tb, a.ptr_b, a.n, a.k, a.stride_b_batch, a.batch, box_rows);
   if (kpanel) {
     const uint64_t dims[4] = {128u, static_cast<uint64_t>(a.n), static_cast<uint64_t>(kb),
                               static_cast<uint64_t>(a.batch)};
     const uint64_t strides[3] = {128u, static_cast<uint64_t>(a.n) * 128u,
                                  static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch : b_elems)};
-    const uint32_t box[4] = {128u, 128u, 1u, 1u};
+    const uint32_t box[4] = {128u, box_rows, 1u, 1u};
     return make_tmap_u8(tb, a.ptr_b, 4, dims, strides, box, true);
   }
   const uint64_t dims[3] = {static_cast<uint64_t>(a.k), static_cast<uint64_t>(a.n),
                             static_cast<uint64_t>(a.batch)};
   const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_b),
                                static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch : b_elems)};
-  const uint32_t box[3] = {128u, 128u, 1u};
+  const uint32_t box[3] = {128u, box_rows, 1u};
   return make_tmap_u8(tb, a.ptr_b, 3, dims, strides, box, true);
 }
 
@@ -1161,7 +1190,7 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
   if (a.b_format != BSG_B_RAW && a.b_format != BSG_B_KPANEL128 && a.b_format != BSG_B_SHUFFLE16)
     return BSG_ERR_UNSUPPORTED;
   if (a.kernel == BSG_KERNEL_SWAP && a.m > 64) return BSG_ERR_UNSUPPORTED;
-  if (a.kernel == BSG_KERNEL_PAIR) return BSG_ERR_UNSUPPORTED;
+  if (a.kernel == BSG_KERNEL_PAIR && a.split_k > 1) return BSG_ERR_UNSUPPORTED;
   if (a.sfa_format != BSG_SF_ROWMAJOR && a.sfa_format != BSG_SF_KMAJOR_T) return BSG_ERR_UNSUPPORTED;
   if (a.sfb_format != BSG_SF_ROWMAJOR) return BSG_ERR_UNSUPPORTED;
   const bool kpanel = a.b_format == BSG_B_KPANEL128;
@@ -1204,6 +1233,13 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
 
   Plan pl;
   fp8b_plan(a, dev, pl, true);
+  const bool pair = fp8b_use_pair(a);
+  if (pair) {
+    pl.tiles_m = (a.m + 255) / 256;
+    pl.split = 1;
+    pl.kb_per = pl.num_kb;
+    pl.ws_partials = 0;
+  }
   if (pl.ws_partials > a.workspace_bytes || (pl.ws_partials && !a.workspace)) {
     if (fp8b_use_swap(a) && swap_split_in_cluster(pl, a, swap_cluster_capacity)) {
       // split inside clusters: no workspace
@@ -1230,7 +1266,7 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
     const uint32_t box[3] = {128u, swap ? static_cast<uint32_t>(swap_mn(a.m)) : 128u, 1u};
     if (!make_tmap_u8(&ta, a.ptr_a, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
   }
-  if (!make_fp8b_weight_tmap(&tb, a, kpanel, shuf, kb, b_elems)) return BSG_ERR_CUDA;
+  if (!make_fp8b_weight_tmap(&tb, a, kpanel, shuf, kb, b_elems, pair ? 64u : 128u)) return BSG_ERR_CUDA;
   Fp8BlockParams p{};
   p.m = a.m;
   p.n = a.n;
@@ -1259,6 +1295,11 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
   const int grid = pl.cluster ? pl.clusters * pl.split : grid_for(p.total_units, dev, a.grid_blocks);
   const int cluster = pl.cluster ? pl.split : 1;
   const bool f32 = a.out_dtype == BSG_OUT_FP32;
+  if (pair) {
+    int clusters = std::min(p.total_units, dev.sms / 2);
+    if (a.grid_blocks > 0) clusters = std::min(clusters, std::max(1, a.grid_blocks / 2));
+    return fp8b2_launch(bfmt, f32, ta, tb, p, 2 * clusters, st);
+  }
   if (fp8b_use_swap(a)) {
     switch (swap_mn(a.m)) {
       case 16: rc = swap_launch_mn<16>(bfmt, f32, ta, tb, p, grid, st, cluster); break;

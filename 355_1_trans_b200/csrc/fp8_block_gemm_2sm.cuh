@@ -1,0 +1,331 @@
+// fp8_block_gemm_2sm.cuh -- CTA-pair (tcgen05 cta_group::2) variant of the
+// FP8 GEMM with fp32 block scales: a cluster of two CTAs on two SMs computes
+// one 256 x 128 output tile.
+//
+// Semantics are those of fp8_block_gemm.cuh (reference, paths relative to its
+// project root: block_scale_gemm_bpreshuffle/
+// gemm_a8w8_blockscale_bpreshuffle_kernel_template.hpp:204-601): per 128-K
+// block kb the unscaled partial (A B^T)_kb is multiplied by
+// sfa[m,kb] * sfb[n/128,kb] and added to an fp32 accumulator, in the same
+// order and with the same fma.rn as the 1-CTA kernel.
+//
+// Why pairs: a 1-CTA M=128 N=128 kind::f8f6f4 MMA reads 8 KB of operands
+// from shared memory per 32 K, and the TMA writes of the next stages go
+// through the same shared memory: 64 KB of shared-memory traffic per 128-K
+// block per SM against 256 cycles of MMA.  (The 1-CTA kernel with its
+// promotion switched off runs at about 625 cycles per K block.)  In a pair
+// each SM loads its own 128 rows of A and 64 rows (half) of B's 128 columns,
+// 24 KB per stage, and the pair MMA (M = 256, N = 128) reads each CTA's A rows
+// and B half from that CTA's shared memory: 48 KB of traffic per K block per
+// SM, while each SM still owns a 128 x 128 fp32 partial per K block in its own
+// TMEM, so the promotion is the 1-CTA kernel's.
+//
+// Protocol (rank 0 = leader, rank 1 = peer; identical shared-memory layout):
+//   producer (warp 0, both CTAs)  waits its own empty[s]; loads its A rows and
+//       its B half with the pair form of the TMA load, whose transaction bytes
+//       go to the LEADER's full[s]; the leader arms full[s] with both CTAs'
+//       bytes;
+//   MMA (warp 1 of the leader)     per K block waits acc_empty[buf] (eight
+//       arrivals: four promotion warps in each CTA) and full[s], issues four
+//       pair MMAs (K = 32 each) into TMEM buffer buf of both CTAs, and commits
+//       to empty[s] and acc_full[buf] of both CTAs;
+//   promotion (warps 4-7, both)    as in the 1-CTA kernel, on the CTA's own 128
+//       rows; a buffer is released by a relaxed arrive on the leader's
+//       acc_empty[buf].  The hand-off publishes no memory: the warp's
+//       tcgen05.ld of the buffer have completed (tcgen05.wait::ld) before it
+//       arrives.  A cluster-scope release there waits for the warp's loads and
+//       stores in flight and cost about 2000 cycles per K block (576 against
+//       1708 TFLOPS for the 1-CTA kernel at 8192 x 7168 x 8192); the MMA
+//       thread's wait on it is relaxed for the same reason (with a
+//       cluster-scope acquire per K block: 1182 TFLOPS).  The scale loads run
+//       two K blocks ahead.
+// Split-K and grouped calls stay on the 1-CTA kernel.  Every wait is bounded
+// (sm100.cuh mbar_wait).
+#pragma once
+
+#include "fp8_block_gemm.cuh"
+
+namespace bsg {
+
+struct Fp8Block2Cfg {
+  static constexpr uint32_t kABytes = 128u * 128u;   // this CTA's 128 rows of A, one 128-K block
+  static constexpr uint32_t kBBytes = 64u * 128u;    // this CTA's 64 of the tile's 128 B rows
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = 9;
+  static constexpr uint32_t kOffB = kABytes * kStages;
+  static constexpr uint32_t kOffBar = kOffB + kBBytes * kStages;
+  static constexpr uint32_t kSmemBytes = kOffBar + 256u + 1024u;
+  static constexpr int kAccBufs = 4;
+  static constexpr uint32_t kTmemCols = kAccBufs * 128u;
+  static_assert(kSmemBytes <= 227u * 1024u, "shared memory");
+  static_assert(kOffB % 1024u == 0 && kOffBar % 1024u == 0, "swizzled stages need 1024-byte alignment");
+  static_assert(kTmemCols <= 512u, "TMEM overflow");
+};
+
+// Stores one lane's row of a 128-column tile: acc[0..127] to columns
+// [n0, n0 + 128) of `dst_row` (bf16 RNE or fp32), clipped at n.
+template <bool kOutF32>
+__device__ __forceinline__ void store_row128(const float (&acc)[128], void* dst_row, int n0, int n) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int col0 = n0 + c * 32;
+    if (col0 >= n) continue;
+    const bool full = col0 + 32 <= n;
+    if constexpr (kOutF32) {
+      float* dst = reinterpret_cast<float*>(dst_row) + col0;
+      if (full) {
+#pragma unroll
+        for (int v = 0; v < 8; ++v)
+          st_global_v4(dst + 4 * v, __float_as_uint(acc[c * 32 + 4 * v]), __float_as_uint(acc[c * 32 + 4 * v + 1]),
+                       __float_as_uint(acc[c * 32 + 4 * v + 2]), __float_as_uint(acc[c * 32 + 4 * v + 3]));
+      } else {
+#pragma unroll
+        for (int v = 0; v < 32; ++v)
+          if (col0 + v < n) dst[v] = acc[c * 32 + v];
+      }
+    } else {
+      uint16_t* dst = reinterpret_cast<uint16_t*>(dst_row) + col0;
+      if (full) {
+        uint32_t w[16];
+#pragma unroll
+        for (int v = 0; v < 16; ++v) w[v] = pack_bf16x2(acc[c * 32 + 2 * v], acc[c * 32 + 2 * v + 1]);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) st_global_v4(dst + 8 * v, w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+      } else {
+#pragma unroll
+        for (int v = 0; v < 32; ++v)
+          if (col0 + v < n) dst[v] = static_cast<uint16_t>(pack_bf16x2(acc[c * 32 + v], 0.0f) & 0xFFFFu);
+      }
+    }
+  }
+}
+
+// p.tiles_m counts 256-row pair tiles, p.tiles_n 128-column tiles; split_k 1.
+template <int kBFmt, bool kOutF32>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
+    fp8_block_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                              const Fp8BlockParams p) {
+  using Cfg = Fp8Block2Cfg;
+  constexpr int S = Cfg::kStages;
+  constexpr int NB = Cfg::kAccBufs;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~static_cast<uintptr_t>(1023u));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + Cfg::kOffB;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* acc_full = empty_bar + S;    // [NB]
+  uint64_t* acc_empty = acc_full + NB;   // [NB], the leader's are used
+  uint64_t* drain_bar = acc_empty + NB;
+  static_assert(8 * (2 * S + 2 * NB + 1) + 8 <= 256, "barrier area");
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 32) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < NB; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 8);   // four promotion warps in each CTA
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(tmem_holder, Cfg::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  tc_fence_before();
+  cluster_sync_all();   // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  if (threadIdx.x == 0) griddep_launch_dependents();   // the next kernel's prologue may start
+  // Launched with programmatic dependent launch, the prologue above overlaps
+  // the previous kernel on the stream; nothing of global memory is touched
+  // before that kernel has completed.
+  griddep_wait();
+  const int cluster_id = static_cast<int>(blockIdx.x >> 1);
+  const int num_clusters = static_cast<int>(gridDim.x >> 1);
+
+  if (warp == 0) {
+    // producer warp: all lanes run the loop, the elected lane issues the copies
+    const bool issuer = elect_one();
+    // ------------------------------------------------------------------ TMA producer (both CTAs)
+    const uint64_t pol = l2_policy_evict_normal();
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int u = cluster_id; u < p.total_units; u += num_clusters) {
+      int b, mt, nt, s;
+      decode_unit(u, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
+      const int row_a = mt * 256 + static_cast<int>(rank) * 128;
+      const int row_b = nt * 128 + static_cast<int>(rank) * 64;
+      bool ok = true;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        const uint32_t fb_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
+        if (issuer) {
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2u * Cfg::kStageBytes);
+          tma_load_3d_pair(sA + stage * Cfg::kABytes, &tmA, fb_leader, kb * 128, row_a, b, pol);
+          if constexpr (kBFmt == kFmtKPanel)
+            tma_load_4d_pair(sB + stage * Cfg::kBBytes, &tmB, fb_leader, 0, row_b, kb, b, pol);
+          else if constexpr (kBFmt == kFmtShuffle16)
+            tma_load_5d_pair(sB + stage * Cfg::kBBytes, &tmB, fb_leader, 0, kb * 8, 0, row_b / 16, b, pol);
+          else
+            tma_load_3d_pair(sB + stage * Cfg::kBBytes, &tmB, fb_leader, kb * 128, row_b, b, pol);
+        }
+        __syncwarp();
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+    }
+  } else if (warp == 1 && leader) {
+    // MMA warp: all lanes run the loop, the elected lane issues
+    const bool issuer = elect_one();
+    // ------------------------------------------------------------------ MMA issuer (leader)
+    constexpr uint32_t idesc = idesc_f8f6f4(false, false, 256, 128);
+    const uint64_t adesc0 = make_sdesc(smem_u32(sA), 16u, 1024u, kLayoutSW128);
+    const uint64_t bdesc0 = weight_sdesc<kBFmt>(smem_u32(sB), 0);
+    constexpr uint64_t kBStep = (kBFmt == kFmtShuffle16 ? 256u : 32u) >> 4;   // one K step, 16-byte units
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t kbi = 0;   // K blocks issued by this pair, selects the TMEM buffer
+    bool ok = true;
+    for (int u = cluster_id; u < p.total_units && ok; u += num_clusters) {
+      for (int kb = 0; kb < p.num_kb; ++kb, ++kbi) {
+        const uint32_t buf = kbi % NB;
+        const uint32_t use = kbi / NB;   // how many times this buffer was used before
+        if (!mbar_wait_cluster_relaxed(&acc_empty[buf], (use & 1u) ^ 1u, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (issuer) {
+          const uint32_t ust = static_cast<uint32_t>(stage);
+          const uint64_t ad = adesc0 + static_cast<uint64_t>(ust * (Cfg::kABytes >> 4));
+          const uint64_t bd = bdesc0 + static_cast<uint64_t>(ust * (Cfg::kBBytes >> 4));
+          const uint32_t d = tmem_base + buf * 128u;
+          umma_f8f6f4_pair(d, ad, bd, idesc, 0u);
+          umma_f8f6f4_pair(d, ad + 2u, bd + kBStep, idesc, 1u);
+          umma_f8f6f4_pair(d, ad + 4u, bd + 2u * kBStep, idesc, 1u);
+          umma_f8f6f4_pair(d, ad + 6u, bd + 3u * kBStep, idesc, 1u);
+          tc_commit_pair(&empty_bar[stage], 0x3);
+          tc_commit_pair(&acc_full[buf], 0x3);
+        }
+        __syncwarp();
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (issuer) tc_commit_pair(drain_bar, 0x1);
+    int dummy = 0;
+    mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ promotion + store (both CTAs)
+    const int q = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t ae_leader = mapa_shared(smem_u32(acc_empty), 0);
+    uint32_t kbi = 0;
+    bool ok = true;
+    for (int u = cluster_id; u < p.total_units && ok; u += num_clusters) {
+      int b, mt, nt, s;
+      decode_unit(u, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
+      const int rbase = mt * 256 + static_cast<int>(rank) * 128;
+      const int row = rbase + q * 32 + static_cast<int>(lane);
+      const bool row_ok = row < p.m;
+      // a lane quarter whose 32 rows all lie beyond M skips the promotion
+      // work but still releases the buffers
+      const bool quarter_live = rbase + q * 32 < p.m;
+      const int n0 = nt * 128;
+      const float* sfa_row = p.sfa + b * p.sfa_batch + static_cast<long long>(row_ok ? row : 0) * p.sfa_m;
+      const float* sfb_blk = p.sfb + b * p.sfb_batch + static_cast<long long>(nt) * p.sfb_n;
+      uint64_t accp[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) accp[i] = 0ull;
+      float sa_c = row_ok ? __ldg(sfa_row) : 0.0f;
+      float sb_c = __ldg(sfb_blk);
+      float sa_n = 0.0f, sb_n = 0.0f;
+      if (p.num_kb > 1) {
+        sa_n = row_ok ? __ldg(sfa_row + p.sfa_k) : 0.0f;
+        sb_n = __ldg(sfb_blk + p.sfb_k);
+      }
+      for (int kb = 0; kb < p.num_kb; ++kb, ++kbi) {
+        const uint64_t scale2 = pack_f32x2(sa_c * sb_c);
+        const uint32_t buf = kbi % NB;
+        const uint32_t use = kbi / NB;
+        if (!mbar_wait(&acc_full[buf], use & 1u, abort_flag, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (quarter_live) {
+          // two rounds of four 16-column loads in flight behind one wait
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t r[4][16];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              tmem_ld16_async(tmem_base + lane_base + buf * 128u + static_cast<uint32_t>(c * 64 + j * 16), r[j]);
+            tmem_wait_ld16(r[0]);
+#pragma unroll
+            for (int j = 1; j < 4; ++j) tmem_reg_fence16(r[j]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+              for (int i = 0; i < 8; ++i) fma_f32x2(accp[(c * 64 + j * 16) / 2 + i], r[j][2 * i], r[j][2 * i + 1], scale2);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster_relaxed(ae_leader + buf * 8u);
+        sa_c = sa_n;
+        sb_c = sb_n;
+        if (kb + 2 < p.num_kb) {
+          sa_n = row_ok ? __ldg(sfa_row + (kb + 2) * p.sfa_k) : 0.0f;
+          sb_n = __ldg(sfb_blk + (kb + 2) * p.sfb_k);
+        }
+      }
+      if (!ok || !row_ok) continue;
+      float acc[128];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) unpack_f32x2(accp[i], acc[2 * i], acc[2 * i + 1]);
+      if constexpr (kOutF32)
+        store_row128<true>(acc, reinterpret_cast<float*>(p.c) + b * p.c_batch_stride + row * p.ldc, n0, p.n);
+      else
+        store_row128<false>(acc, reinterpret_cast<uint16_t*>(p.c) + b * p.c_batch_stride + row * p.ldc, n0, p.n);
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();   // both CTAs done with TMEM, barriers and remote arrives
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+}
+
+}  // namespace bsg

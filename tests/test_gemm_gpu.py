@@ -334,7 +334,7 @@ def test_e8m0_block_rejects_like_reference(bs, cuda):
 # ---- FP8 block-scale (fp32 scales) --------------------------------------------------
 
 def run_fp8_block(bs, orc, cuda, m, n, k, *, seed=1, kpanel=True, transposed=False, split_k=0,
-                  out_dtype=torch.bfloat16, kernel="auto", shuffle16=False):
+                  out_dtype=torch.bfloat16, kernel="auto", shuffle16=False, grid_blocks=0):
     x = orc.normal((m, k), seed=seed * 77)
     w = orc.normal((n, k), seed=seed * 77 + 1)
     qa, sa = orc.quant_fp8_block(x, 1)
@@ -354,7 +354,7 @@ def run_fp8_block(bs, orc, cuda, m, n, k, *, seed=1, kpanel=True, transposed=Fal
     SB = torch.from_numpy(sb).to(cuda)
     out = poisoned((m, n), out_dtype, cuda)
     bs.gemm_a8w8_bpreshuffle(A, B, SA, SB, out_dtype, b_layout=b_layout, x_scale_transposed=transposed,
-                             out=out, split_k=split_k, kernel=kernel)
+                             out=out, split_k=split_k, kernel=kernel, grid_blocks=grid_blocks)
     torch.cuda.synchronize()
     assert bs.check_device_error() == 0
     got = out.float().cpu().numpy()
@@ -398,6 +398,47 @@ def test_fp8_block_swap_short_units(bs, orc, cuda, m, k, split_k):
     """Units of 1 and 3 K blocks and split-K slices of one K block: the two promotion sets take
     alternate K blocks, so a set may see none of a unit's K blocks and still hand over zeros."""
     run_fp8_block(bs, orc, cuda, m, 640, k, seed=70 + k + split_k, kernel="swap", split_k=split_k)
+
+
+# ---- CTA-pair fp32 block-scale kernel (256 x 128 tiles) --------------------------------
+
+@pytest.mark.parametrize("m,n,k,layout,out_dtype,transposed", [
+    (256, 256, 512, "kpanel", torch.bfloat16, False),
+    (512, 384, 1024, "raw", torch.bfloat16, True),
+    (384, 768, 640, "shuffle16", torch.bfloat16, False),
+    (300, 200, 384, "kpanel", torch.float32, False),
+    (1, 128, 256, "raw", torch.bfloat16, False),
+    (129, 1000, 1152, "kpanel", torch.bfloat16, True),
+])
+def test_fp8_block_pair(bs, orc, cuda, m, n, k, layout, out_dtype, transposed):
+    """The pair kernel on every weight layout and both outputs.  M = 300 and 129
+    leave the peer CTA's rows of the last pair tile wholly or partly past M; N =
+    200 and 1000 end inside a tile, and 200 leaves the peer's B half past N."""
+    run_fp8_block(bs, orc, cuda, m, n, k, seed=90 + m, kpanel=layout == "kpanel", shuffle16=layout == "shuffle16",
+                  transposed=transposed, out_dtype=out_dtype, kernel="pair")
+
+
+@pytest.mark.parametrize("grid_blocks", [2, 6, 0])
+def test_fp8_block_pair_persistent(bs, orc, cuda, grid_blocks):
+    """More pair tiles (5 x 20) than clusters: 1, 3 and all co-resident pairs walk the tiles."""
+    run_fp8_block(bs, orc, cuda, 1280, 2560, 384, seed=97, kernel="pair", grid_blocks=grid_blocks)
+
+
+def test_fp8_block_pair_matches_1cta(bs, orc, cuda):
+    """Each SM of a pair computes its 128 rows of the 128-K partial from the same
+    bytes in the same K order as the 1-CTA kernel, and promotes them with the same
+    fma.rn, so the two kernels agree bit for bit."""
+    m, n, k = 1024, 1024, 2048
+    qa, sa = orc.quant_fp8_block(orc.normal((m, k), seed=98), 1)
+    qb, sb = orc.quant_fp8_block(orc.normal((n, k), seed=99), 128)
+    A = dev_u8(qa, cuda).view(torch.float8_e4m3fn)
+    B = dev_u8(orc.shuffle_kpanel(qb), cuda).view(torch.float8_e4m3fn)
+    SA, SB = torch.from_numpy(sa).to(cuda), torch.from_numpy(sb).to(cuda)
+    outs = [bs.gemm_a8w8_bpreshuffle(A, B, SA, SB, torch.float32, kernel=kern, split_k=1)
+            for kern in ("1cta", "pair")]
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    assert torch.equal(outs[0], outs[1])
 
 
 # ---- grouped (MoE) fp32 block-scale GEMM ----------------------------------------------
