@@ -1029,32 +1029,55 @@ int fp8b_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockPa
 }
 
 template <int kBFmt, bool kOutF32>
-int fp8b2_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockParams& p, int grid,
-                   cudaStream_t st) {
+int fp8b2_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Fp8BlockParams& p,
+                   int grid, cudaStream_t st) {
   using Cfg = bsg::Fp8Block2Cfg;
   auto* kern = bsg::fp8_block_gemm_2sm_kernel<kBFmt, kOutF32>;
+  // The kernel's warpgroups re-split their registers with setmaxnreg; the
+  // split is sized for exactly Cfg::kLaunchRegs registers per thread at launch
+  // (with fewer, the promotion warps' increase could never be granted).
+  static const int regs = [kern] {
+    cudaFuncAttributes fa{};
+    return cudaFuncGetAttributes(&fa, kern) == cudaSuccess ? fa.numRegs : -1;
+  }();
+  if (regs != Cfg::kLaunchRegs) return BSG_ERR_UNSUPPORTED;
   if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
-  const int rc = launch_pdl(kern, grid, 256, Cfg::kSmemBytes, st, ta, tb, p);
+  const int rc = launch_pdl(kern, grid, Cfg::kThreads, Cfg::kSmemBytes, st, ta, tb, tc, p);
   return rc != BSG_OK ? rc : launch_status();
 }
 
-int fp8b2_launch(int fmt, bool f32, const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockParams& p,
-                 int grid, cudaStream_t st) {
+int fp8b2_launch(int fmt, bool f32, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                 const Fp8BlockParams& p, int grid, cudaStream_t st) {
   switch (fmt) {
     case bsg::kFmtKPanel:
-      return f32 ? fp8b2_launch_t<bsg::kFmtKPanel, true>(ta, tb, p, grid, st)
-                 : fp8b2_launch_t<bsg::kFmtKPanel, false>(ta, tb, p, grid, st);
+      return f32 ? fp8b2_launch_t<bsg::kFmtKPanel, true>(ta, tb, tc, p, grid, st)
+                 : fp8b2_launch_t<bsg::kFmtKPanel, false>(ta, tb, tc, p, grid, st);
     case bsg::kFmtShuffle16:
-      return f32 ? fp8b2_launch_t<bsg::kFmtShuffle16, true>(ta, tb, p, grid, st)
-                 : fp8b2_launch_t<bsg::kFmtShuffle16, false>(ta, tb, p, grid, st);
+      return f32 ? fp8b2_launch_t<bsg::kFmtShuffle16, true>(ta, tb, tc, p, grid, st)
+                 : fp8b2_launch_t<bsg::kFmtShuffle16, false>(ta, tb, tc, p, grid, st);
     default:
-      return f32 ? fp8b2_launch_t<bsg::kFmtRaw, true>(ta, tb, p, grid, st)
-                 : fp8b2_launch_t<bsg::kFmtRaw, false>(ta, tb, p, grid, st);
+      return f32 ? fp8b2_launch_t<bsg::kFmtRaw, true>(ta, tb, tc, p, grid, st)
+                 : fp8b2_launch_t<bsg::kFmtRaw, false>(ta, tb, tc, p, grid, st);
   }
 }
 
-// CTA-pair kernel (256 x 128 tiles, no split-K): on request only.
-bool fp8b_use_pair(const bsgemm_args& a) { return a.kernel == BSG_KERNEL_PAIR; }
+// CTA-pair kernel (256 x 256 tiles, no split-K): on request, or for an
+// automatic call that the 1-CTA kernel (128 x 128 tiles) would cover in more
+// time, counted in waves: a pair unit's K block costs about 1.6 of a 1-CTA
+// tile's (B200, 8192 x 7168 x 8192: 1100 against 680 cycles), and a wave is
+// sms / 2 pair units or sms tiles.  Small tile counts, where the 1-CTA kernel
+// fills the GPU and may split K, stay with it.
+constexpr double kPairKbCost = 1.6;
+bool fp8b_use_pair(const bsgemm_args& a, int sms) {
+  if (a.kernel == BSG_KERNEL_PAIR) return true;
+  if (a.kernel != BSG_KERNEL_AUTO || a.m <= 64 || a.split_k > 1) return false;
+  const long long units = static_cast<long long>((a.m + 255) / 256) * ((a.n + 255) / 256) * a.batch;
+  const long long tiles = static_cast<long long>((a.m + 127) / 128) * ((a.n + 127) / 128) * a.batch;
+  const long long clusters = std::max(1, sms / 2);
+  const double pair_waves = static_cast<double>((units + clusters - 1) / clusters) * kPairKbCost;
+  const double one_waves = static_cast<double>((tiles + sms - 1) / sms);
+  return pair_waves < one_waves;
+}
 
 bool fp8b_use_swap(const bsgemm_args& a) {
   return a.kernel == BSG_KERNEL_SWAP || (a.kernel == BSG_KERNEL_AUTO && a.m <= 64);
@@ -1160,21 +1183,21 @@ int swap_launch_mn(int fmt, bool f32, const CUtensorMap& ta, const CUtensorMap& 
 // Tensor map of the fp8 block-scale weights (batch = experts for grouped
 // calls): shuffle_weight(16,16), K panels B'[K/128][N][128], or raw [N, K].
 bool make_fp8b_weight_tmap(CUtensorMap* tb, const bsgemm_args& a, bool kpanel, bool shuf, int kb,
-                           long long b_elems, uint32_t box_rows = 128u) {
-  if (shuf) return make_shuffle16_tmap(tb, a.ptr_b, a.n, a.k, a.stride_b_batch, a.batch, box_rows);
+                           long long b_elems) {
+  if (shuf) return make_shuffle16_tmap(tb, a.ptr_b, a.n, a.k, a.stride_b_batch, a.batch, 128u);
   if (kpanel) {
     const uint64_t dims[4] = {128u, static_cast<uint64_t>(a.n), static_cast<uint64_t>(kb),
                               static_cast<uint64_t>(a.batch)};
     const uint64_t strides[3] = {128u, static_cast<uint64_t>(a.n) * 128u,
                                  static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch : b_elems)};
-    const uint32_t box[4] = {128u, box_rows, 1u, 1u};
+    const uint32_t box[4] = {128u, 128u, 1u, 1u};
     return make_tmap_u8(tb, a.ptr_b, 4, dims, strides, box, true);
   }
   const uint64_t dims[3] = {static_cast<uint64_t>(a.k), static_cast<uint64_t>(a.n),
                             static_cast<uint64_t>(a.batch)};
   const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_b),
                                static_cast<uint64_t>(a.batch > 1 ? a.stride_b_batch : b_elems)};
-  const uint32_t box[3] = {128u, box_rows, 1u};
+  const uint32_t box[3] = {128u, 128u, 1u};
   return make_tmap_u8(tb, a.ptr_b, 3, dims, strides, box, true);
 }
 
@@ -1233,9 +1256,10 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
 
   Plan pl;
   fp8b_plan(a, dev, pl, true);
-  const bool pair = fp8b_use_pair(a);
+  const bool pair = fp8b_use_pair(a, dev.sms);
   if (pair) {
     pl.tiles_m = (a.m + 255) / 256;
+    pl.tiles_n = (a.n + 255) / 256;
     pl.split = 1;
     pl.kb_per = pl.num_kb;
     pl.ws_partials = 0;
@@ -1266,7 +1290,7 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
     const uint32_t box[3] = {128u, swap ? static_cast<uint32_t>(swap_mn(a.m)) : 128u, 1u};
     if (!make_tmap_u8(&ta, a.ptr_a, 3, dims, strides, box, true)) return BSG_ERR_CUDA;
   }
-  if (!make_fp8b_weight_tmap(&tb, a, kpanel, shuf, kb, b_elems, pair ? 64u : 128u)) return BSG_ERR_CUDA;
+  if (!make_fp8b_weight_tmap(&tb, a, kpanel, shuf, kb, b_elems)) return BSG_ERR_CUDA;
   Fp8BlockParams p{};
   p.m = a.m;
   p.n = a.n;
@@ -1296,9 +1320,25 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
   const int cluster = pl.cluster ? pl.split : 1;
   const bool f32 = a.out_dtype == BSG_OUT_FP32;
   if (pair) {
+    // C (bf16) for the TMA-store epilogue: boxes of 32 columns x 32 rows,
+    // 64-byte swizzle (fp32 C is stored directly)
+    CUtensorMap tc;
+    std::memset(&tc, 0, sizeof(tc));
+    if (!f32) {
+      const uint64_t dims[3] = {static_cast<uint64_t>(a.n), static_cast<uint64_t>(a.m),
+                                static_cast<uint64_t>(a.batch)};
+      const uint64_t strides[2] = {static_cast<uint64_t>(a.stride_c) * 2u,
+                                   static_cast<uint64_t>(a.batch > 1 ? a.stride_c_batch
+                                                                     : static_cast<long long>(a.m) * a.stride_c) *
+                                       2u};
+      const uint32_t box[3] = {32u, 32u, 1u};
+      if (!make_tmap_swz(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.ptr_c, 3, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_64B))
+        return BSG_ERR_CUDA;
+    }
     int clusters = std::min(p.total_units, dev.sms / 2);
     if (a.grid_blocks > 0) clusters = std::min(clusters, std::max(1, a.grid_blocks / 2));
-    return fp8b2_launch(bfmt, f32, ta, tb, p, 2 * clusters, st);
+    return fp8b2_launch(bfmt, f32, ta, tb, tc, p, 2 * clusters, st);
   }
   if (fp8b_use_swap(a)) {
     switch (swap_mn(a.m)) {
@@ -1899,6 +1939,7 @@ size_t bsgemm_workspace_size(int family, const bsgemm_args* args) {
     return pl.ws_sfa + pl.ws_sfb + pl.ws_partials;
   }
   if (family == BSG_FAMILY_FP8_BLOCK) {
+    if (fp8b_use_pair(*args, dev.sms)) return 0;   // the pair kernel does not split K
     Plan pl;
     fp8b_plan(*args, dev, pl, true);
     return pl.ws_partials;

@@ -1,44 +1,45 @@
 // fp8_block_gemm_2sm.cuh -- CTA-pair (tcgen05 cta_group::2) variant of the
 // FP8 GEMM with fp32 block scales: a cluster of two CTAs on two SMs computes
-// one 256 x 128 output tile.
+// one 256 x 256 output tile.
 //
 // Semantics are those of fp8_block_gemm.cuh (reference, paths relative to its
 // project root: block_scale_gemm_bpreshuffle/
 // gemm_a8w8_blockscale_bpreshuffle_kernel_template.hpp:204-601): per 128-K
 // block kb the unscaled partial (A B^T)_kb is multiplied by
 // sfa[m,kb] * sfb[n/128,kb] and added to an fp32 accumulator, in the same
-// order and with the same fma.rn as the 1-CTA kernel.
+// order and with the same fma.rn as the 1-CTA kernel, so the two agree bit for
+// bit.
 //
-// Why pairs: a 1-CTA M=128 N=128 kind::f8f6f4 MMA reads 8 KB of operands
-// from shared memory per 32 K, and the TMA writes of the next stages go
-// through the same shared memory: 64 KB of shared-memory traffic per 128-K
-// block per SM against 256 cycles of MMA.  (The 1-CTA kernel with its
-// promotion switched off runs at about 625 cycles per K block.)  In a pair
-// each SM loads its own 128 rows of A and 64 rows (half) of B's 128 columns,
-// 24 KB per stage, and the pair MMA (M = 256, N = 128) reads each CTA's A rows
-// and B half from that CTA's shared memory: 48 KB of traffic per K block per
-// SM, while each SM still owns a 128 x 128 fp32 partial per K block in its own
-// TMEM, so the promotion is the 1-CTA kernel's.
+// Why pairs of 256 x 256: the 1-CTA kernel's operand pipeline alone (its
+// promotion switched off) reaches 0.57 of the FP8 peak with 128 x 128 tiles,
+// and a pair of 256 x 128 tiles 0.64.  Here each SM loads 128 rows of A and
+// 128 of the tile's 256 B rows per 128-K stage (32 KB) and owns a 128 x 256
+// fp32 partial per K block -- twice the MMA work per stage and per hand-off --
+// which is the MX pair kernel's shape (0.86 of the peak).  TMEM holds two such
+// partials (2 x 256 columns), so the MMA runs one K block ahead of the
+// promotion.
 //
-// Protocol (rank 0 = leader, rank 1 = peer; identical shared-memory layout):
+// Protocol (rank 0 = leader, rank 1 = peer; identical shared-memory layout;
+// 384 threads: warpgroup 0 at 56 registers, warpgroups 1-2 at 224):
 //   producer (warp 0, both CTAs)  waits its own empty[s]; loads its A rows and
-//       its B half with the pair form of the TMA load, whose transaction bytes
+//       its B rows with the pair form of the TMA load, whose transaction bytes
 //       go to the LEADER's full[s]; the leader arms full[s] with both CTAs'
 //       bytes;
-//   MMA (warp 1 of the leader)     per K block waits acc_empty[buf] (eight
-//       arrivals: four promotion warps in each CTA) and full[s], issues four
-//       pair MMAs (K = 32 each) into TMEM buffer buf of both CTAs, and commits
-//       to empty[s] and acc_full[buf] of both CTAs;
-//   promotion (warps 4-7, both)    as in the 1-CTA kernel, on the CTA's own 128
-//       rows; a buffer is released by a relaxed arrive on the leader's
-//       acc_empty[buf].  The hand-off publishes no memory: the warp's
-//       tcgen05.ld of the buffer have completed (tcgen05.wait::ld) before it
-//       arrives.  A cluster-scope release there waits for the warp's loads and
-//       stores in flight and cost about 2000 cycles per K block (576 against
-//       1708 TFLOPS for the 1-CTA kernel at 8192 x 7168 x 8192); the MMA
-//       thread's wait on it is relaxed for the same reason (with a
-//       cluster-scope acquire per K block: 1182 TFLOPS).  The scale loads run
-//       two K blocks ahead.
+//   MMA (warp 1 of the leader)     per K block waits acc_empty[buf] (sixteen
+//       arrivals: eight promotion warps in each CTA) and full[s], issues four
+//       pair MMAs (M = 256, N = 256, K = 32 each) into TMEM buffer buf of both
+//       CTAs, and commits to empty[s] and acc_full[buf] of both CTAs;
+//   promotion (warps 4-11, both)   warp w promotes lane quarter w % 4 and
+//       column half (w - 4) / 4 (128 columns, one B-scale block) of the CTA's
+//       own 128 rows, as the 1-CTA kernel does, then releases the buffer by a
+//       relaxed arrive on the leader's acc_empty[buf].  The hand-off publishes
+//       no memory: the warp's tcgen05.ld of the buffer have completed
+//       (tcgen05.wait::ld) before it arrives.  With a cluster-scope release
+//       (which waits for the warp's loads and stores in flight) and a
+//       cluster-scope acquire on the MMA side, the 256 x 128 pair kernel ran at
+//       576 and 1182 TFLOPS against 1612 relaxed.  The MMA waits for the
+//       slowest of the sixteen warps, so each warp polls for its buffer
+//       (mbar_wait_spin) and has its scales loaded four K blocks ahead.
 // Split-K and grouped calls stay on the 1-CTA kernel.  Every wait is bounded
 // (sm100.cuh mbar_wait).
 #pragma once
@@ -48,17 +49,30 @@
 namespace bsg {
 
 struct Fp8Block2Cfg {
+  static constexpr int kThreads = 384;
+  static constexpr int kLaunchRegs = 168;      // 384 x 168 = 128 x 56 + 256 x 224
+  static constexpr uint32_t kLowRegs = 56u;    // warpgroup 0: producer, MMA, TMEM allocation
+  static constexpr uint32_t kHighRegs = 224u;  // warpgroups 1-2: promotion
+  static_assert(128u * kLowRegs + 256u * kHighRegs <= static_cast<uint32_t>(kThreads * kLaunchRegs),
+                "register split exceeds the launch");
   static constexpr uint32_t kABytes = 128u * 128u;   // this CTA's 128 rows of A, one 128-K block
-  static constexpr uint32_t kBBytes = 64u * 128u;    // this CTA's 64 of the tile's 128 B rows
+  static constexpr uint32_t kBBytes = 128u * 128u;   // this CTA's 128 of the tile's 256 B rows
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = 9;
+  static constexpr int kStages = 6;
   static constexpr uint32_t kOffB = kABytes * kStages;
-  static constexpr uint32_t kOffBar = kOffB + kBBytes * kStages;
+  // bf16 epilogue staging: two 32-row x 32-column boxes (64-byte rows) per promotion warp
+  static constexpr uint32_t kOutBytes = 32u * 64u;
+  static constexpr uint32_t kOffOut = kOffB + kBBytes * kStages;
+  static constexpr uint32_t kOffBar = kOffOut + 8u * 2u * kOutBytes;
+  // next unit's first K blocks prefetched into L2, this many K blocks before the unit ends
+  static constexpr int kPrefetchKb = 8;
+  static constexpr int kPrefetchLead = 16;
   static constexpr uint32_t kSmemBytes = kOffBar + 256u + 1024u;
-  static constexpr int kAccBufs = 4;
-  static constexpr uint32_t kTmemCols = kAccBufs * 128u;
+  static constexpr int kAccBufs = 2;
+  static constexpr uint32_t kBN = 256u;
+  static constexpr uint32_t kTmemCols = kAccBufs * kBN;
   static_assert(kSmemBytes <= 227u * 1024u, "shared memory");
-  static_assert(kOffB % 1024u == 0 && kOffBar % 1024u == 0, "swizzled stages need 1024-byte alignment");
+  static_assert(kOffB % 1024u == 0 && kOffOut % 1024u == 0, "swizzled tiles need 1024-byte alignment");
   static_assert(kTmemCols <= 512u, "TMEM overflow");
 };
 
@@ -100,14 +114,15 @@ __device__ __forceinline__ void store_row128(const float (&acc)[128], void* dst_
   }
 }
 
-// p.tiles_m counts 256-row pair tiles, p.tiles_n 128-column tiles; split_k 1.
+// p.tiles_m counts 256-row pair tiles, p.tiles_n 256-column tiles; split_k 1.
 template <int kBFmt, bool kOutF32>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThreads, 1)
     fp8_block_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                              const Fp8BlockParams p) {
+                              const __grid_constant__ CUtensorMap tmC, const Fp8BlockParams p) {
   using Cfg = Fp8Block2Cfg;
   constexpr int S = Cfg::kStages;
   constexpr int NB = Cfg::kAccBufs;
+  constexpr uint32_t BN = Cfg::kBN;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -135,7 +150,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
     }
     for (int i = 0; i < NB; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 8);   // four promotion warps in each CTA
+      mbar_init(&acc_empty[i], 16);   // eight promotion warps in each CTA
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -148,6 +163,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if constexpr (!kOutF32) prefetch_tmap(&tmC);
   }
   tc_fence_before();
   cluster_sync_all();   // barriers of both CTAs initialised, TMEM allocated
@@ -161,95 +177,122 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
   const int cluster_id = static_cast<int>(blockIdx.x >> 1);
   const int num_clusters = static_cast<int>(gridDim.x >> 1);
 
-  if (warp == 0) {
-    // producer warp: all lanes run the loop, the elected lane issues the copies
-    const bool issuer = elect_one();
-    // ------------------------------------------------------------------ TMA producer (both CTAs)
-    const uint64_t pol = l2_policy_evict_normal();
-    int stage = 0;
-    uint32_t phase = 0;
-    for (int u = cluster_id; u < p.total_units; u += num_clusters) {
-      int b, mt, nt, s;
-      decode_unit(u, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
-      const int row_a = mt * 256 + static_cast<int>(rank) * 128;
-      const int row_b = nt * 128 + static_cast<int>(rank) * 64;
+  if (warp < 4) {
+    setmaxnreg_dec<Cfg::kLowRegs>();
+    if (warp == 0) {
+      // producer warp: all lanes run the loop, the elected lane issues the copies
+      const bool issuer = elect_one();
+      // ---------------------------------------------------------------- TMA producer (both CTAs)
+      const uint64_t pol = l2_policy_evict_normal();
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int u = cluster_id; u < p.total_units; u += num_clusters) {
+        int b, mt, nt, s;
+        decode_unit(u, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
+        const int row_a = mt * 256 + static_cast<int>(rank) * 128;
+        const int row_b = nt * 256 + static_cast<int>(rank) * 128;
+        // every cluster reaches its next unit at about the same time, and the
+        // new unit's A or B panel is often not in L2 yet: this CTA's operands of
+        // that unit's first K blocks go to L2 a while before they are needed
+        const int un = u + num_clusters;
+        const int kb_pf = max(0, p.num_kb - Cfg::kPrefetchLead);
+        bool ok = true;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (kb == kb_pf && un < p.total_units && issuer) {
+            int b2, mt2, nt2, s2;
+            decode_unit(un, p.tiles_m, p.tiles_n, 1, p.group_m, b2, mt2, nt2, s2);
+            const int ra = mt2 * 256 + static_cast<int>(rank) * 128;
+            const int rb = nt2 * 256 + static_cast<int>(rank) * 128;
+            for (int k2 = 0; k2 < min(Cfg::kPrefetchKb, p.num_kb); ++k2) {
+              if (ra < p.m) tma_prefetch_3d(&tmA, k2 * 128, ra, b2);
+              if (rb >= p.n) continue;
+              if constexpr (kBFmt == kFmtKPanel)
+                tma_prefetch_4d(&tmB, 0, rb, k2, b2);
+              else if constexpr (kBFmt == kFmtShuffle16)
+                tma_prefetch_5d(&tmB, 0, k2 * 8, 0, rb / 16, b2);
+              else
+                tma_prefetch_3d(&tmB, k2 * 128, rb, b2);
+            }
+          }
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          if (issuer) {
+            if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2u * Cfg::kStageBytes);
+            tma_load_3d_pair(sA + stage * Cfg::kABytes, &tmA, fb_leader, kb * 128, row_a, b, pol);
+            if constexpr (kBFmt == kFmtKPanel)
+              tma_load_4d_pair(sB + stage * Cfg::kBBytes, &tmB, fb_leader, 0, row_b, kb, b, pol);
+            else if constexpr (kBFmt == kFmtShuffle16)
+              tma_load_5d_pair(sB + stage * Cfg::kBBytes, &tmB, fb_leader, 0, kb * 8, 0, row_b / 16, b, pol);
+            else
+              tma_load_3d_pair(sB + stage * Cfg::kBBytes, &tmB, fb_leader, kb * 128, row_b, b, pol);
+          }
+          __syncwarp();
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+    } else if (warp == 1 && leader) {
+      // MMA warp: all lanes run the loop, the elected lane issues
+      const bool issuer = elect_one();
+      // ---------------------------------------------------------------- MMA issuer (leader)
+      constexpr uint32_t idesc = idesc_f8f6f4(false, false, 256, BN);
+      const uint64_t adesc0 = make_sdesc(smem_u32(sA), 16u, 1024u, kLayoutSW128);
+      const uint64_t bdesc0 = weight_sdesc<kBFmt>(smem_u32(sB), 0);
+      constexpr uint64_t kBStep = (kBFmt == kFmtShuffle16 ? 256u : 32u) >> 4;   // one K step, 16-byte units
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t kbi = 0;   // K blocks issued by this pair, selects the TMEM buffer
       bool ok = true;
-      for (int kb = 0; kb < p.num_kb; ++kb) {
-        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
-          ok = false;
-          break;
-        }
-        const uint32_t fb_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
-        if (issuer) {
-          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2u * Cfg::kStageBytes);
-          tma_load_3d_pair(sA + stage * Cfg::kABytes, &tmA, fb_leader, kb * 128, row_a, b, pol);
-          if constexpr (kBFmt == kFmtKPanel)
-            tma_load_4d_pair(sB + stage * Cfg::kBBytes, &tmB, fb_leader, 0, row_b, kb, b, pol);
-          else if constexpr (kBFmt == kFmtShuffle16)
-            tma_load_5d_pair(sB + stage * Cfg::kBBytes, &tmB, fb_leader, 0, kb * 8, 0, row_b / 16, b, pol);
-          else
-            tma_load_3d_pair(sB + stage * Cfg::kBBytes, &tmB, fb_leader, kb * 128, row_b, b, pol);
-        }
-        __syncwarp();
-        if (++stage == S) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
-      if (!ok) break;
-    }
-  } else if (warp == 1 && leader) {
-    // MMA warp: all lanes run the loop, the elected lane issues
-    const bool issuer = elect_one();
-    // ------------------------------------------------------------------ MMA issuer (leader)
-    constexpr uint32_t idesc = idesc_f8f6f4(false, false, 256, 128);
-    const uint64_t adesc0 = make_sdesc(smem_u32(sA), 16u, 1024u, kLayoutSW128);
-    const uint64_t bdesc0 = weight_sdesc<kBFmt>(smem_u32(sB), 0);
-    constexpr uint64_t kBStep = (kBFmt == kFmtShuffle16 ? 256u : 32u) >> 4;   // one K step, 16-byte units
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t kbi = 0;   // K blocks issued by this pair, selects the TMEM buffer
-    bool ok = true;
-    for (int u = cluster_id; u < p.total_units && ok; u += num_clusters) {
-      for (int kb = 0; kb < p.num_kb; ++kb, ++kbi) {
-        const uint32_t buf = kbi % NB;
-        const uint32_t use = kbi / NB;   // how many times this buffer was used before
-        if (!mbar_wait_cluster_relaxed(&acc_empty[buf], (use & 1u) ^ 1u, abort_flag, p.timeout_ns)) {
-          ok = false;
-          break;
-        }
-        if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (issuer) {
-          const uint32_t ust = static_cast<uint32_t>(stage);
-          const uint64_t ad = adesc0 + static_cast<uint64_t>(ust * (Cfg::kABytes >> 4));
-          const uint64_t bd = bdesc0 + static_cast<uint64_t>(ust * (Cfg::kBBytes >> 4));
-          const uint32_t d = tmem_base + buf * 128u;
-          umma_f8f6f4_pair(d, ad, bd, idesc, 0u);
-          umma_f8f6f4_pair(d, ad + 2u, bd + kBStep, idesc, 1u);
-          umma_f8f6f4_pair(d, ad + 4u, bd + 2u * kBStep, idesc, 1u);
-          umma_f8f6f4_pair(d, ad + 6u, bd + 3u * kBStep, idesc, 1u);
-          tc_commit_pair(&empty_bar[stage], 0x3);
-          tc_commit_pair(&acc_full[buf], 0x3);
-        }
-        __syncwarp();
-        if (++stage == S) {
-          stage = 0;
-          phase ^= 1u;
+      for (int u = cluster_id; u < p.total_units && ok; u += num_clusters) {
+        for (int kb = 0; kb < p.num_kb; ++kb, ++kbi) {
+          const uint32_t buf = kbi % NB;
+          const uint32_t use = kbi / NB;   // how many times this buffer was used before
+          if (!mbar_wait_cluster_relaxed(&acc_empty[buf], (use & 1u) ^ 1u, abort_flag, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (issuer) {
+            const uint32_t ust = static_cast<uint32_t>(stage);
+            const uint64_t ad = adesc0 + static_cast<uint64_t>(ust * (Cfg::kABytes >> 4));
+            const uint64_t bd = bdesc0 + static_cast<uint64_t>(ust * (Cfg::kBBytes >> 4));
+            const uint32_t d = tmem_base + buf * BN;
+            umma_f8f6f4_pair(d, ad, bd, idesc, 0u);
+            umma_f8f6f4_pair(d, ad + 2u, bd + kBStep, idesc, 1u);
+            umma_f8f6f4_pair(d, ad + 4u, bd + 2u * kBStep, idesc, 1u);
+            umma_f8f6f4_pair(d, ad + 6u, bd + 3u * kBStep, idesc, 1u);
+            tc_commit_pair(&empty_bar[stage], 0x3);
+            tc_commit_pair(&acc_full[buf], 0x3);
+          }
+          __syncwarp();
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
+      if (issuer) tc_commit_pair(drain_bar, 0x1);
+      int dummy = 0;
+      mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
     }
-    if (issuer) tc_commit_pair(drain_bar, 0x1);
-    int dummy = 0;
-    mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
-  } else if (warp >= 4) {
-    // ------------------------------------------------------------------ promotion + store (both CTAs)
+  } else {
+    setmaxnreg_inc<Cfg::kHighRegs>();
+    // ---------------------------------------------------------------- promotion + store (both CTAs)
     const int q = warp & 3;
-    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const int half = (warp - 4) >> 2;
+    const uint32_t t_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(half) * 128u;
     const uint32_t ae_leader = mapa_shared(smem_u32(acc_empty), 0);
+    uint8_t* out_buf = smem + Cfg::kOffOut + static_cast<uint32_t>(warp - 4) * 2u * Cfg::kOutBytes;
     uint32_t kbi = 0;
     bool ok = true;
     for (int u = cluster_id; u < p.total_units && ok; u += num_clusters) {
@@ -258,39 +301,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
       const int rbase = mt * 256 + static_cast<int>(rank) * 128;
       const int row = rbase + q * 32 + static_cast<int>(lane);
       const bool row_ok = row < p.m;
-      // a lane quarter whose 32 rows all lie beyond M skips the promotion
-      // work but still releases the buffers
-      const bool quarter_live = rbase + q * 32 < p.m;
-      const int n0 = nt * 128;
+      const int n0 = nt * 256 + half * 128;   // this warp's 128 columns: one B-scale block
+      // a warp whose 32 rows or 128 columns all lie beyond M or N skips the
+      // promotion work (and the scale loads) but still releases the buffers
+      const bool live = rbase + q * 32 < p.m && n0 < p.n;
       const float* sfa_row = p.sfa + b * p.sfa_batch + static_cast<long long>(row_ok ? row : 0) * p.sfa_m;
-      const float* sfb_blk = p.sfb + b * p.sfb_batch + static_cast<long long>(nt) * p.sfb_n;
+      const float* sfb_blk = p.sfb + b * p.sfb_batch + static_cast<long long>(live ? n0 / 128 : 0) * p.sfb_n;
       uint64_t accp[64];
 #pragma unroll
       for (int i = 0; i < 64; ++i) accp[i] = 0ull;
-      float sa_c = row_ok ? __ldg(sfa_row) : 0.0f;
-      float sb_c = __ldg(sfb_blk);
-      float sa_n = 0.0f, sb_n = 0.0f;
-      if (p.num_kb > 1) {
-        sa_n = row_ok ? __ldg(sfa_row + p.sfa_k) : 0.0f;
-        sb_n = __ldg(sfb_blk + p.sfb_k);
+      // scales of K blocks kb .. kb + 3 in a shift chain (static register
+      // indices): each load has three K blocks to arrive -- the row scales
+      // of the row-major layout miss L1, and one K block of distance left the
+      // promotion stalled on them
+      float sa[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      if (live) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (i < p.num_kb) {
+            sa[i] = row_ok ? __ldg(sfa_row + i * p.sfa_k) : 0.0f;
+            sb[i] = __ldg(sfb_blk + i * p.sfb_k);
+          }
       }
       for (int kb = 0; kb < p.num_kb; ++kb, ++kbi) {
-        const uint64_t scale2 = pack_f32x2(sa_c * sb_c);
+        const uint64_t scale2 = pack_f32x2(sa[0] * sb[0]);
         const uint32_t buf = kbi % NB;
         const uint32_t use = kbi / NB;
-        if (!mbar_wait(&acc_full[buf], use & 1u, abort_flag, p.timeout_ns)) {
+        if (!mbar_wait_spin(&acc_full[buf], use & 1u, abort_flag, p.timeout_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (quarter_live) {
+        if (live) {
           // two rounds of four 16-column loads in flight behind one wait
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             uint32_t r[4][16];
 #pragma unroll
             for (int j = 0; j < 4; ++j)
-              tmem_ld16_async(tmem_base + lane_base + buf * 128u + static_cast<uint32_t>(c * 64 + j * 16), r[j]);
+              tmem_ld16_async(t_base + buf * BN + static_cast<uint32_t>(c * 64 + j * 16), r[j]);
             tmem_wait_ld16(r[0]);
 #pragma unroll
             for (int j = 1; j < 4; ++j) tmem_reg_fence16(r[j]);
@@ -303,22 +352,58 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster_relaxed(ae_leader + buf * 8u);
-        sa_c = sa_n;
-        sb_c = sb_n;
-        if (kb + 2 < p.num_kb) {
-          sa_n = row_ok ? __ldg(sfa_row + (kb + 2) * p.sfa_k) : 0.0f;
-          sb_n = __ldg(sfb_blk + (kb + 2) * p.sfb_k);
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+          sa[i] = sa[i + 1];
+          sb[i] = sb[i + 1];
+        }
+        if (live && kb + 4 < p.num_kb) {
+          sa[3] = row_ok ? __ldg(sfa_row + (kb + 4) * p.sfa_k) : 0.0f;
+          sb[3] = __ldg(sfb_blk + (kb + 4) * p.sfb_k);
         }
       }
-      if (!ok || !row_ok) continue;
-      float acc[128];
+      if (!ok || !live) continue;
+      if constexpr (kOutF32) {
+        if (!row_ok) continue;
+        float acc[128];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) unpack_f32x2(accp[i], acc[2 * i], acc[2 * i + 1]);
-      if constexpr (kOutF32)
+        for (int i = 0; i < 64; ++i) unpack_f32x2(accp[i], acc[2 * i], acc[2 * i + 1]);
         store_row128<true>(acc, reinterpret_cast<float*>(p.c) + b * p.c_batch_stride + row * p.ldc, n0, p.n);
-      else
-        store_row128<false>(acc, reinterpret_cast<uint16_t*>(p.c) + b * p.c_batch_stride + row * p.ldc, n0, p.n);
+      } else {
+        // bf16 through TMA stores: per 32-column box each lane writes its row
+        // (64 bytes, 64-byte swizzle, so the 32 lanes' 16-byte writes spread
+        // over all banks) into one of this warp's two staging buffers; TMA
+        // clips the box at the M and N edges
+        const uint32_t swz = (lane >> 1) & 3u;
+        const int row0 = rbase + q * 32;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (n0 + c * 32 >= p.n) break;
+          uint8_t* sbuf = out_buf + static_cast<uint32_t>(c & 1) * Cfg::kOutBytes;
+          if (lane == 0) bulk_wait_group_read1();   // the box before the last has left sbuf
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t w[4];
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              float lo0, hi0;
+              unpack_f32x2(accp[c * 16 + j * 4 + v], lo0, hi0);
+              w[v] = pack_bf16x2(lo0, hi0);
+            }
+            st_shared_v4(sbuf + lane * 64u + ((static_cast<uint32_t>(j) ^ swz) * 16u), w[0], w[1], w[2], w[3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tmC, sbuf, n0 + c * 32, row0, b);
+            bulk_commit_group();
+          }
+        }
+      }
     }
+    if constexpr (!kOutF32)
+      if (lane == 0) bulk_wait_group0();   // every store of this warp has completed
   }
 
   __syncwarp();

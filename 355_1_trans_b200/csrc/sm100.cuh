@@ -120,6 +120,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return false;
 }
 
+// Bounded wait that polls with test_wait instead of suspending in try_wait:
+// the waiting warp sees the phase complete within a few cycles (a suspended
+// try_wait resumed about 600 cycles after the phase completed, measured on a
+// TMEM buffer hand-off), at the cost of issue slots while it polls.  Gives up
+// as mbar_wait does.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                               uint64_t timeout_ns) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1; it < 0x7fffffffu; ++it) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((it & 1023u) == 0u) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > timeout_ns) break;
+    }
+  }
+  *abort_flag = 1;
+  atomicCAS(&g_bsg_device_error, 0, kDevErrTimeout);
+  return false;
+}
+
 // ---------------------------------------------------------------------------
 // clusters of two CTAs (CTA pairs for cta_group::2)
 // ---------------------------------------------------------------------------
@@ -406,6 +427,10 @@ __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bul
 __device__ __forceinline__ void bulk_wait_group_read0() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+// wait until at most one committed bulk group of this thread still reads its source
+__device__ __forceinline__ void bulk_wait_group_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 // wait until every committed bulk group of this thread has completed
 __device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
@@ -471,6 +496,20 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    smem_u32(bar))
                : "memory");
+}
+
+// Warpgroup register reallocation.  Every warp of a warpgroup executes the
+// same one; an increase waits until decreases elsewhere in the CTA have freed
+// the registers, so the shares of all warpgroups must add up to at most the
+// CTA's registers at launch (threads x registers per thread).  The host checks
+// the launch register count of every kernel that uses these.
+template <uint32_t R>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(R));
+}
+template <uint32_t R>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(R));
 }
 
 // CTA-pair TMEM allocation: issued by the same warp in both CTAs of the pair.

@@ -112,7 +112,7 @@ def candidates(family: str, m: int, k: int, n: int | None = None, sms: int = 148
     kernels = ["1cta"]
     if m <= 64:
         kernels.append("swap")
-    if family != "fp8_block" and m >= 256:
+    if m >= 256 or (family == "fp8_block" and m > 128):
         kernels.append("pair")
     for kern in kernels:
         tiles = None

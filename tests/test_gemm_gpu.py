@@ -400,7 +400,7 @@ def test_fp8_block_swap_short_units(bs, orc, cuda, m, k, split_k):
     run_fp8_block(bs, orc, cuda, m, 640, k, seed=70 + k + split_k, kernel="swap", split_k=split_k)
 
 
-# ---- CTA-pair fp32 block-scale kernel (256 x 128 tiles) --------------------------------
+# ---- CTA-pair fp32 block-scale kernel (256 x 256 tiles) --------------------------------
 
 @pytest.mark.parametrize("m,n,k,layout,out_dtype,transposed", [
     (256, 256, 512, "kpanel", torch.bfloat16, False),
@@ -413,15 +413,16 @@ def test_fp8_block_swap_short_units(bs, orc, cuda, m, k, split_k):
 def test_fp8_block_pair(bs, orc, cuda, m, n, k, layout, out_dtype, transposed):
     """The pair kernel on every weight layout and both outputs.  M = 300 and 129
     leave the peer CTA's rows of the last pair tile wholly or partly past M; N =
-    200 and 1000 end inside a tile, and 200 leaves the peer's B half past N."""
+    200 and 1000 end inside a tile's second column half (and the peer's B rows),
+    N = 384 leaves that half wholly past N."""
     run_fp8_block(bs, orc, cuda, m, n, k, seed=90 + m, kpanel=layout == "kpanel", shuffle16=layout == "shuffle16",
                   transposed=transposed, out_dtype=out_dtype, kernel="pair")
 
 
 @pytest.mark.parametrize("grid_blocks", [2, 6, 0])
 def test_fp8_block_pair_persistent(bs, orc, cuda, grid_blocks):
-    """More pair tiles (5 x 20) than clusters: 1, 3 and all co-resident pairs walk the tiles."""
-    run_fp8_block(bs, orc, cuda, 1280, 2560, 384, seed=97, kernel="pair", grid_blocks=grid_blocks)
+    """More pair tiles (10 x 10) than clusters: 1, 3 and all co-resident pairs walk the tiles."""
+    run_fp8_block(bs, orc, cuda, 2560, 2560, 384, seed=97, kernel="pair", grid_blocks=grid_blocks)
 
 
 def test_fp8_block_pair_matches_1cta(bs, orc, cuda):
