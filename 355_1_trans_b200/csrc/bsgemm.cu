@@ -1061,22 +1061,62 @@ int fp8b2_launch(int fmt, bool f32, const CUtensorMap& ta, const CUtensorMap& tb
   }
 }
 
-// CTA-pair kernel (256 x 256 tiles, no split-K): on request, or for an
-// automatic call that the 1-CTA kernel (128 x 128 tiles) would cover in more
-// time, counted in waves: a pair unit's K block costs about 1.6 of a 1-CTA
-// tile's (B200, 8192 x 7168 x 8192: 1100 against 680 cycles), and a wave is
-// sms / 2 pair units or sms tiles.  Small tile counts, where the 1-CTA kernel
-// fills the GPU and may split K, stay with it.
+// Clusters of a pair launch: one per two SMs, or per two CTAs of a grid cap.
+int fp8b_pair_clusters(const bsgemm_args& a, int sms) {
+  int c = std::max(1, sms / 2);
+  if (a.grid_blocks > 0) c = std::min(c, std::max(1, a.grid_blocks / 2));
+  return c;
+}
+
+// Tail split of a pair launch: the units past the last full wave of
+// `clusters` (all units, when there are fewer than a wave) run as K slices,
+// as many per unit as the clusters allow, each at least 2 K blocks.  Returns
+// the bytes of fp32 partials it needs, 0 for no split.
+size_t fp8b_pair_tail(long long units, int clusters, int num_kb, int* tail_units, int* tail_split) {
+  const long long t = units >= clusters ? units % clusters : units;
+  const int s = t > 0 ? static_cast<int>(std::min<long long>(clusters / t, num_kb / 2)) : 1;
+  if (t == 0 || s < 2) {
+    *tail_units = 0;
+    *tail_split = 1;
+    return 0;
+  }
+  *tail_units = static_cast<int>(t);
+  *tail_split = s;
+  return static_cast<size_t>(t) * static_cast<size_t>(s) * 256u * 256u * 4u;
+}
+
+// CTA-pair kernel (256 x 256 tiles): on request, or for an automatic call
+// that the 1-CTA kernel (128 x 128 tiles) would cover in more time, counted
+// in waves: a pair unit's K block costs about 1.6 of a 1-CTA tile's (B200,
+// 8192 x 7168 x 8192: 1100 against 680 cycles), and a wave is sms / 2 pair
+// units or sms tiles.  With split_k 0 the pair's partial last wave runs as K
+// slices (fp8b_pair_tail), counted as 1/s of a wave plus kPairTailCost for
+// the partials and their reduction.
 constexpr double kPairKbCost = 1.6;
+constexpr double kPairTailCost = 0.1;
 bool fp8b_use_pair(const bsgemm_args& a, int sms) {
   if (a.kernel == BSG_KERNEL_PAIR) return true;
   if (a.kernel != BSG_KERNEL_AUTO || a.m <= 64 || a.split_k > 1) return false;
   const long long units = static_cast<long long>((a.m + 255) / 256) * ((a.n + 255) / 256) * a.batch;
   const long long tiles = static_cast<long long>((a.m + 127) / 128) * ((a.n + 127) / 128) * a.batch;
-  const long long clusters = std::max(1, sms / 2);
-  const double pair_waves = static_cast<double>((units + clusters - 1) / clusters) * kPairKbCost;
+  const int clusters = std::max(1, sms / 2);
+  int tu = 0, ts = 1;
+  fp8b_pair_tail(units, clusters, a.k / 128, &tu, &ts);
+  double pair_waves = static_cast<double>(units / clusters);
+  if (tu > 0)
+    pair_waves += 1.0 / ts + kPairTailCost;
+  else if (units % clusters)
+    pair_waves += 1.0;
   const double one_waves = static_cast<double>((tiles + sms - 1) / sms);
-  return pair_waves < one_waves;
+  return pair_waves * kPairKbCost < one_waves;
+}
+
+int fp8b2_tail_reduce(const Fp8BlockParams& p, bool f32, int sms, cudaStream_t st) {
+  const long long groups = static_cast<long long>(p.tail_units) * 256 * 64;
+  const int grid = static_cast<int>(std::min<long long>((groups + 255) / 256, 8LL * sms));
+  const int rc = f32 ? launch_pdl(bsg::fp8b_pair_tail_reduce_kernel<true>, grid, 256, 0, st, p)
+                     : launch_pdl(bsg::fp8b_pair_tail_reduce_kernel<false>, grid, 256, 0, st, p);
+  return rc != BSG_OK ? rc : launch_status();
 }
 
 bool fp8b_use_swap(const bsgemm_args& a) {
@@ -1336,9 +1376,25 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
                          CU_TENSOR_MAP_SWIZZLE_64B))
         return BSG_ERR_CUDA;
     }
-    int clusters = std::min(p.total_units, dev.sms / 2);
-    if (a.grid_blocks > 0) clusters = std::min(clusters, std::max(1, a.grid_blocks / 2));
-    return fp8b2_launch(bfmt, f32, ta, tb, tc, p, 2 * clusters, st);
+    // the partial last wave as K slices, when the caller's workspace holds
+    // their fp32 partials (split_k 1 keeps every unit whole)
+    const int cl = fp8b_pair_clusters(a, dev.sms);
+    int tu = 0, ts = 1;
+    size_t tail_bytes = a.split_k == 0 ? fp8b_pair_tail(p.total_units, cl, pl.num_kb, &tu, &ts) : 0;
+    if (tail_bytes && (!a.workspace || a.workspace_bytes < tail_bytes || !aligned16(a.workspace) ||
+                       overlaps(a.ptr_c, c_bytes, a.workspace, tail_bytes))) {
+      tu = 0;
+      ts = 1;
+      tail_bytes = 0;
+    }
+    p.tail_units = tu;
+    p.tail_split = ts;
+    p.total_items = p.total_units - tu + tu * ts;
+    p.ws = tail_bytes ? static_cast<float*>(a.workspace) : nullptr;
+    const int clusters = std::min(p.total_items, cl);
+    rc = fp8b2_launch(bfmt, f32, ta, tb, tc, p, 2 * clusters, st);
+    if (rc != BSG_OK || tu == 0) return rc;
+    return fp8b2_tail_reduce(p, f32, dev.sms, st);
   }
   if (fp8b_use_swap(a)) {
     switch (swap_mn(a.m)) {
@@ -1939,7 +1995,12 @@ size_t bsgemm_workspace_size(int family, const bsgemm_args* args) {
     return pl.ws_sfa + pl.ws_sfb + pl.ws_partials;
   }
   if (family == BSG_FAMILY_FP8_BLOCK) {
-    if (fp8b_use_pair(*args, dev.sms)) return 0;   // the pair kernel does not split K
+    if (fp8b_use_pair(*args, dev.sms)) {   // partials of the pair kernel's tail slices
+      if (args->split_k != 0) return 0;
+      int tu = 0, ts = 1;
+      const long long units = static_cast<long long>((args->m + 255) / 256) * ((args->n + 255) / 256) * args->batch;
+      return fp8b_pair_tail(units, fp8b_pair_clusters(*args, dev.sms), args->k / 128, &tu, &ts);
+    }
     Plan pl;
     fp8b_plan(*args, dev, pl, true);
     return pl.ws_partials;

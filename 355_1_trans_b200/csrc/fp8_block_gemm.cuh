@@ -46,6 +46,10 @@ struct Fp8BlockParams {
   // concatenated A, its scales and C; total_rows bounds those arrays
   const int* group_offsets;
   int total_rows;
+  // pair kernel only: the last tail_units units run as tail_split K slices
+  // each (fp32 partials in ws, summed by fp8b_pair_tail_reduce_kernel);
+  // total_items = total_units - tail_units + tail_units * tail_split
+  int tail_units, tail_split, total_items;
 };
 
 // First row and row count of group b in a grouped call.  The offsets come

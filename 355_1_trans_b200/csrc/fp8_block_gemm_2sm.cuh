@@ -114,7 +114,39 @@ __device__ __forceinline__ void store_row128(const float (&acc)[128], void* dst_
   }
 }
 
-// p.tiles_m counts 256-row pair tiles, p.tiles_n 256-column tiles; split_k 1.
+// Work item w of a pair launch: the whole units first (unit w, every K
+// block), then the K slices of the last p.tail_units units, p.tail_split per
+// unit (slice j covers K blocks [j*nkb/s, (j+1)*nkb/s)).  A persistent grid
+// of C clusters thus runs its full waves of whole units and then spreads the
+// tail over every cluster instead of leaving most of them idle for a whole
+// unit's time.  slot: -1 for a whole unit, else the slice's fp32 partial slot.
+struct PairItem {
+  int unit, kb0, kb1, slot;
+};
+__device__ __forceinline__ PairItem pair_item(const Fp8BlockParams& p, int w) {
+  const int whole = p.total_units - p.tail_units;
+  PairItem it;
+  if (w < whole) {
+    it.unit = w;
+    it.kb0 = 0;
+    it.kb1 = p.num_kb;
+    it.slot = -1;
+    return it;
+  }
+  const int t = w - whole;
+  const int j = t % p.tail_split;
+  it.unit = whole + t / p.tail_split;
+  it.kb0 = j * p.num_kb / p.tail_split;
+  it.kb1 = (j + 1) * p.num_kb / p.tail_split;
+  it.slot = t;
+  return it;
+}
+
+// A tail slice's partial: one 256 x 256 fp32 tile, row-major.
+constexpr long long kPairSlotFloats = 256LL * 256LL;
+
+// p.tiles_m counts 256-row pair tiles, p.tiles_n 256-column tiles; split_k 1
+// (the tail slices above are the only K split).
 template <int kBFmt, bool kOutF32>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThreads, 1)
     fp8_block_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -186,24 +218,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
       const uint64_t pol = l2_policy_evict_normal();
       int stage = 0;
       uint32_t phase = 0;
-      for (int u = cluster_id; u < p.total_units; u += num_clusters) {
+      for (int w = cluster_id; w < p.total_items; w += num_clusters) {
+        const PairItem it = pair_item(p, w);
         int b, mt, nt, s;
-        decode_unit(u, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
+        decode_unit(it.unit, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
         const int row_a = mt * 256 + static_cast<int>(rank) * 128;
         const int row_b = nt * 256 + static_cast<int>(rank) * 128;
         // every cluster reaches its next unit at about the same time, and the
         // new unit's A or B panel is often not in L2 yet: this CTA's operands of
         // that unit's first K blocks go to L2 a while before they are needed
-        const int un = u + num_clusters;
-        const int kb_pf = max(0, p.num_kb - Cfg::kPrefetchLead);
+        const int wn = w + num_clusters;
+        const int kb_pf = max(it.kb0, it.kb1 - Cfg::kPrefetchLead);
         bool ok = true;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (kb == kb_pf && un < p.total_units && issuer) {
+        for (int kb = it.kb0; kb < it.kb1; ++kb) {
+          if (kb == kb_pf && wn < p.total_items && issuer) {
+            const PairItem nx = pair_item(p, wn);
             int b2, mt2, nt2, s2;
-            decode_unit(un, p.tiles_m, p.tiles_n, 1, p.group_m, b2, mt2, nt2, s2);
+            decode_unit(nx.unit, p.tiles_m, p.tiles_n, 1, p.group_m, b2, mt2, nt2, s2);
             const int ra = mt2 * 256 + static_cast<int>(rank) * 128;
             const int rb = nt2 * 256 + static_cast<int>(rank) * 128;
-            for (int k2 = 0; k2 < min(Cfg::kPrefetchKb, p.num_kb); ++k2) {
+            for (int k2 = nx.kb0; k2 < min(nx.kb0 + Cfg::kPrefetchKb, nx.kb1); ++k2) {
               if (ra < p.m) tma_prefetch_3d(&tmA, k2 * 128, ra, b2);
               if (rb >= p.n) continue;
               if constexpr (kBFmt == kFmtKPanel)
@@ -249,8 +283,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
       uint32_t phase = 0;
       uint32_t kbi = 0;   // K blocks issued by this pair, selects the TMEM buffer
       bool ok = true;
-      for (int u = cluster_id; u < p.total_units && ok; u += num_clusters) {
-        for (int kb = 0; kb < p.num_kb; ++kb, ++kbi) {
+      for (int w = cluster_id; w < p.total_items && ok; w += num_clusters) {
+        const PairItem it = pair_item(p, w);
+        for (int kb = it.kb0; kb < it.kb1; ++kb, ++kbi) {
           const uint32_t buf = kbi % NB;
           const uint32_t use = kbi / NB;   // how many times this buffer was used before
           if (!mbar_wait_cluster_relaxed(&acc_empty[buf], (use & 1u) ^ 1u, abort_flag, p.timeout_ns)) {
@@ -295,9 +330,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
     uint8_t* out_buf = smem + Cfg::kOffOut + static_cast<uint32_t>(warp - 4) * 2u * Cfg::kOutBytes;
     uint32_t kbi = 0;
     bool ok = true;
-    for (int u = cluster_id; u < p.total_units && ok; u += num_clusters) {
+    for (int w = cluster_id; w < p.total_items && ok; w += num_clusters) {
+      const PairItem it = pair_item(p, w);
       int b, mt, nt, s;
-      decode_unit(u, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
+      decode_unit(it.unit, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
       const int rbase = mt * 256 + static_cast<int>(rank) * 128;
       const int row = rbase + q * 32 + static_cast<int>(lane);
       const bool row_ok = row < p.m;
@@ -318,12 +354,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
       if (live) {
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-          if (i < p.num_kb) {
-            sa[i] = row_ok ? __ldg(sfa_row + i * p.sfa_k) : 0.0f;
-            sb[i] = __ldg(sfb_blk + i * p.sfb_k);
+          if (it.kb0 + i < it.kb1) {
+            sa[i] = row_ok ? __ldg(sfa_row + (it.kb0 + i) * p.sfa_k) : 0.0f;
+            sb[i] = __ldg(sfb_blk + (it.kb0 + i) * p.sfb_k);
           }
       }
-      for (int kb = 0; kb < p.num_kb; ++kb, ++kbi) {
+      for (int kb = it.kb0; kb < it.kb1; ++kb, ++kbi) {
         const uint64_t scale2 = pack_f32x2(sa[0] * sb[0]);
         const uint32_t buf = kbi % NB;
         const uint32_t use = kbi / NB;
@@ -357,12 +393,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
           sa[i] = sa[i + 1];
           sb[i] = sb[i + 1];
         }
-        if (live && kb + 4 < p.num_kb) {
+        if (live && kb + 4 < it.kb1) {
           sa[3] = row_ok ? __ldg(sfa_row + (kb + 4) * p.sfa_k) : 0.0f;
           sb[3] = __ldg(sfb_blk + (kb + 4) * p.sfb_k);
         }
       }
       if (!ok || !live) continue;
+      if (it.slot >= 0) {
+        // a tail slice: this warp's 32 rows x 128 columns of the fp32 partial
+        // go to the slice's slot (rows past M too; the reduce clips)
+        float* dst = p.ws + it.slot * kPairSlotFloats +
+                     static_cast<long long>(static_cast<int>(rank) * 128 + q * 32 + static_cast<int>(lane)) * 256 +
+                     half * 128;
+#pragma unroll
+        for (int v = 0; v < 32; ++v)
+          st_global_v4(dst + 4 * v, static_cast<uint32_t>(accp[2 * v]), static_cast<uint32_t>(accp[2 * v] >> 32),
+                       static_cast<uint32_t>(accp[2 * v + 1]), static_cast<uint32_t>(accp[2 * v + 1] >> 32));
+        continue;
+      }
       if constexpr (kOutF32) {
         if (!row_ok) continue;
         float acc[128];
@@ -411,6 +459,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
   cluster_sync_all();   // both CTAs done with TMEM, barriers and remote arrives
   tc_fence_after();
   if (warp == 2) tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+}
+
+// Sums the tail slices of a pair launch into C, in slice order (so the
+// result does not depend on which slice finished first): p.tail_units tiles
+// of 256 x 256, clipped at M and N.  Launched after the GEMM with
+// programmatic stream serialization; waits for it before reading.
+template <bool kOutF32>
+__global__ void __launch_bounds__(256) fp8b_pair_tail_reduce_kernel(const Fp8BlockParams p) {
+  griddep_wait();
+  const int whole = p.total_units - p.tail_units;
+  const long long groups = static_cast<long long>(p.tail_units) * 256 * 64;   // 4-float groups
+  for (long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g < groups;
+       g += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int tu = static_cast<int>(g / (256 * 64));
+    const int rem = static_cast<int>(g % (256 * 64));
+    const int r = rem >> 6;
+    const int c4 = (rem & 63) * 4;
+    int b, mt, nt, s;
+    decode_unit(whole + tu, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
+    const int row = mt * 256 + r;
+    const int col = nt * 256 + c4;   // N is a multiple of 8, so col < N covers col + 3
+    if (row >= p.m || col >= p.n) continue;
+    const float* src = p.ws + static_cast<long long>(tu) * p.tail_split * kPairSlotFloats + r * 256 + c4;
+    float4 acc = __ldg(reinterpret_cast<const float4*>(src));
+    for (int j = 1; j < p.tail_split; ++j) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(src + j * kPairSlotFloats));
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    if constexpr (kOutF32) {
+      float* dst = reinterpret_cast<float*>(p.c) + b * p.c_batch_stride + static_cast<long long>(row) * p.ldc + col;
+      st_global_v4(dst, __float_as_uint(acc.x), __float_as_uint(acc.y), __float_as_uint(acc.z), __float_as_uint(acc.w));
+    } else {
+      uint16_t* dst =
+          reinterpret_cast<uint16_t*>(p.c) + b * p.c_batch_stride + static_cast<long long>(row) * p.ldc + col;
+      *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
+    }
+  }
 }
 
 }  // namespace bsg

@@ -118,6 +118,8 @@ def candidates(family: str, m: int, k: int, n: int | None = None, sms: int = 148
         tiles = None
         if n is not None:
             tiles = -(-n // 128) * (1 if kern == "swap" else -(-m // 128))
+        if kern == "pair" and family == "fp8_block":
+            out.append((kern, 0))   # the pair kernel's partial last wave as K slices
         for s in splits:
             if kern == "pair" and s > 1:
                 continue

@@ -442,6 +442,79 @@ def test_fp8_block_pair_matches_1cta(bs, orc, cuda):
     assert torch.equal(outs[0], outs[1])
 
 
+@pytest.mark.parametrize("m,n,k,grid_blocks,out_dtype", [
+    (1024, 5120, 1024, 0, torch.bfloat16),   # 80 units on 74 clusters: 6 tail units x 4 slices
+    (512, 2048, 2048, 0, torch.float32),     # 16 units, fewer than a wave: every unit in 4 slices
+    (1024, 5120, 1024, 26, torch.bfloat16),  # 13 clusters: 80 = 6 x 13 + 2 tail units x 4 slices
+])
+def test_fp8_block_pair_tail_slices(bs, orc, cuda, m, n, k, grid_blocks, out_dtype):
+    """The pair kernel's partial last wave as K slices (fp32 partials in the workspace, summed in
+    slice order by the tail reduce): correct against the oracle, bit-identical from run to run,
+    and within rounding of the unsplit run (split_k=1)."""
+    qa, sa = orc.quant_fp8_block(orc.normal((m, k), seed=500 + m), 1)
+    qb, sb = orc.quant_fp8_block(orc.normal((n, k), seed=501 + n), 128)
+    ref, mag = orc.gemm_fp8_block(qa, qb, sa, sb)
+    A = dev_u8(qa, cuda).view(torch.float8_e4m3fn)
+    B = dev_u8(orc.shuffle_kpanel(qb), cuda).view(torch.float8_e4m3fn)
+    SA, SB = torch.from_numpy(sa).to(cuda), torch.from_numpy(sb).to(cuda)
+    outs = [bs.gemm_a8w8_bpreshuffle(A, B, SA, SB, out_dtype, kernel="pair", grid_blocks=grid_blocks, split_k=sk)
+            for sk in (0, 0, 1)]
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    got = outs[0].float().cpu().numpy()
+    assert_close(orc, ref, got, mag, f"fp8 block pair tail {m}x{n}x{k}")
+    assert torch.equal(outs[0], outs[1])
+    assert_close(orc, outs[2].float().cpu().numpy(), got, mag, "tail slices against unsplit")
+
+
+@pytest.mark.parametrize("kernel", ["pair", "auto", "1cta"])
+def test_fp8_block_batched_c_abi(bs, orc, cuda, kernel):
+    """Batched fp32 block-scale through the C ABI (the Python wrapper is batch 1): batch strides
+    of A, K-panel B, both scales and C, with padding between A's and C's batch slices, checked
+    per batch against the oracle.  At this size "auto" takes the pair kernel (2 waves of 120 pair
+    units, counted 1.6 each, against 4 waves of 480 tiles)."""
+    import ctypes
+    batch, m, n, k = 2, 1536, 2560, 512
+    kb = k // 128
+    pads_a, pads_c = 64, 96   # extra rows between batch slices
+    A = torch.zeros(batch, m + pads_a, k, dtype=torch.uint8, device=cuda)
+    B = torch.empty(batch, kb, n, 128, dtype=torch.uint8, device=cuda)
+    SA = torch.empty(batch, m, kb, dtype=torch.float32, device=cuda)
+    SB = torch.empty(batch, n // 128, kb, dtype=torch.float32, device=cuda)
+    C = torch.full((batch, m + pads_c, n), float("nan"), dtype=torch.bfloat16, device=cuda)
+    refs = []
+    for e in range(batch):
+        qa, sa = orc.quant_fp8_block(orc.normal((m, k), seed=300 + e), 1)
+        qb, sb = orc.quant_fp8_block(orc.normal((n, k), seed=310 + e), 128)
+        refs.append(orc.gemm_fp8_block(qa, qb, sa, sb))
+        A[e, :m] = dev_u8(qa, cuda)
+        B[e] = dev_u8(orc.shuffle_kpanel(qb), cuda).view(kb, n, 128)
+        SA[e] = torch.from_numpy(sa).to(cuda)
+        SB[e] = torch.from_numpy(sb).to(cuda)
+    args = bs.Args()
+    bs.lib().bsgemm_args_init(ctypes.byref(args))
+    args.ptr_a, args.ptr_b, args.ptr_c = A.data_ptr(), B.data_ptr(), C.data_ptr()
+    args.m, args.n, args.k, args.batch = m, n, k, batch
+    args.stride_a, args.stride_b, args.stride_c = k, 128, n
+    args.stride_a_batch, args.stride_b_batch, args.stride_c_batch = (m + pads_a) * k, n * k, (m + pads_c) * n
+    args.ptr_sfa, args.ptr_sfb = SA.data_ptr(), SB.data_ptr()
+    args.stride_sfa, args.stride_sfb = kb, kb
+    args.stride_sfa_batch, args.stride_sfb_batch = m * kb, (n // 128) * kb
+    args.layout, args.b_format = bs.LAYOUTS["tn"], bs.B_KPANEL128
+    args.sfa_format, args.sfb_format, args.out_dtype = bs.SF_ROWMAJOR, bs.SF_ROWMAJOR, bs.OUT_BF16
+    args.kernel = bs.KERNELS[kernel]
+    ws = bs._workspace(bs.FAMILY_FP8_BLOCK, args, None, cuda)
+    status = bs.lib().bsgemm_a8w8_blockscale_bpreshuffle(ctypes.byref(args), bs._stream(cuda))
+    torch.cuda.synchronize()
+    del ws
+    assert status == bs.OK, bs.strerror(status)
+    assert bs.check_device_error() == 0
+    for e in range(batch):
+        ref, mag = refs[e]
+        assert_close(orc, ref, C[e, :m].float().cpu().numpy(), mag, f"fp8 block batch {e} {kernel}")
+        assert torch.isnan(C[e, m:].float()).all(), "padding rows after a batch slice were written"
+
+
 # ---- grouped (MoE) fp32 block-scale GEMM ----------------------------------------------
 
 def run_fp8_block_grouped(bs, orc, cuda, sizes, n, k, *, seed, b_layout="kpanel", tail=0, max_rows=None,
