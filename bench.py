@@ -100,6 +100,8 @@ def parse():
     ap.add_argument("--layout", default="tn", choices=["tn", "nn", "tt", "nt"])
     ap.add_argument("--kernel", default="auto", choices=["auto", "1cta", "pair"],
                     help="MX kernel: auto, single-CTA tiles or CTA pairs (cta_group::2)")
+    ap.add_argument("--split-k", type=int, default=0,
+                    help="fp8block: split_k of the timed call (0 = the library's choice; 1 keeps every unit whole)")
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=8192, help="per-rank N")
     ap.add_argument("--k", type=int, default=8192)
@@ -451,7 +453,8 @@ def run_ours(args):
             dist.broadcast(qa.view(torch.uint8), 0)
             dist.broadcast(sa, 0)
         out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
-        call = lambda: bs.gemm_a8w8_bpreshuffle(qa, qb, sa, sb, torch.bfloat16, preshuffled=True, out=out)
+        call = lambda: bs.gemm_a8w8_bpreshuffle(qa, qb, sa, sb, torch.bfloat16, preshuffled=True, out=out,
+                                                kernel=args.kernel, split_k=args.split_k)
         a_bytes, b_bytes = m * k, n * k
         sf_bytes = 4 * m * (k // 128) + 4 * (n // 128) * (k // 128)
     flops = 2.0 * m * n * k
@@ -468,6 +471,12 @@ def run_ours(args):
         flush_sink = torch.empty((), dtype=torch.float32, device=dev)
     torch.cuda.synchronize()
 
+    # The clock sampler starts (and takes its first readings) before the
+    # warm-up, so the timed steps follow the warm-up without an idle gap in
+    # which the SM clock could fall back.
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
     for _ in range(args.warmup):
         call()
     torch.cuda.synchronize()
@@ -505,12 +514,9 @@ def run_ours(args):
         assert bs.check_device_error() == 0
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    clocks = ClockSampler(local)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks.start()
-    time.sleep(0.3)   # let the sampler take its first readings
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
@@ -745,12 +751,12 @@ def sustained_record(call, kern_ms, stream, local, flops, peaks, peak_kind, seco
     with the measured sustained GEMM peak."""
     import torch
     steps = max(1, int(seconds * 1e3 / max(kern_ms, 1e-3)))
-    for _ in range(20):
-        call()
-    torch.cuda.synchronize()
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
+    for _ in range(20):
+        call()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(steps):
