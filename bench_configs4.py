@@ -116,9 +116,13 @@ class _Gemm:
             self.bs.gemm_a4w4_mxfp4(self.qa[r0:r1], self.qb, sa, self.sb, out=out[r0:r1], scale_format="native",
                                     b_format="shuffle16", kernel="auto", grid_blocks=g)
         else:
+            # split_k 1: every tile whole, so a row's result does not depend on
+            # the rows called with it (the serial and the strip-wise GEMMs agree
+            # bit for bit); K slices of the partial last wave would move < 1 %
+            # of the work at this size
             self.bs.gemm_a8w8_bpreshuffle(self.qa[r0:r1].view(torch.float8_e4m3fn), self.qb, self.sa[r0:r1],
                                           self.sb, torch.bfloat16, preshuffled=True, out=out[r0:r1],
-                                          grid_blocks=g)
+                                          grid_blocks=g, split_k=1)
 
 
 def _time(fn, steps, warmup, stream):
