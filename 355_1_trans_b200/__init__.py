@@ -373,7 +373,7 @@ def gemm_a8w8_bpreshuffle(A, B, x_scale, w_scale, out_dtype=torch.bfloat16, *,
 
 def gemm_a8w8_blockscale_grouped(A, B, x_scale, w_scale, group_offsets, max_rows: int,
                                  out_dtype=torch.bfloat16, *, out=None, b_layout: str = "kpanel",
-                                 grid_blocks: int = 0):
+                                 grid_blocks: int = 0, kernel: str = "auto"):
     """Grouped (MoE) a8w8 GEMM with fp32 1x128 / 128x128 block scales.
 
     The tokens of all groups (experts) are concatenated: A [T, K] E4M3 and
@@ -382,7 +382,11 @@ def gemm_a8w8_blockscale_grouped(A, B, x_scale, w_scale, group_offsets, max_rows
     multiplied by its own weights B[e] (layout b_layout, as in
     gemm_a8w8_bpreshuffle: B [E, K/128, N, 128] or [E, N, K]) with w_scale[e]
     [N/128, K/128].  max_rows bounds the rows of any group.  Returns C [T, N];
-    rows outside every group are left unwritten."""
+    rows outside every group are left unwritten.  kernel: "auto" / "1cta"
+    (128-row tiles) or "pair" (CTA pairs, 256-row tiles: for groups of a few
+    hundred rows or more)."""
+    if kernel not in ("auto", "1cta", "pair"):
+        raise ValueError("kernel must be 'auto', '1cta' or 'pair'")
     if b_layout not in ("kpanel", "shuffle16", "raw"):
         raise ValueError("b_layout must be 'kpanel', 'shuffle16' or 'raw'")
     tensors = (A, B, x_scale, w_scale, group_offsets)
@@ -427,6 +431,7 @@ def gemm_a8w8_blockscale_grouped(A, B, x_scale, w_scale, group_offsets, max_rows
     args.layout = LAYOUTS["tn"]
     args.out_dtype = OUT_BF16 if out_dtype == torch.bfloat16 else OUT_FP32
     args.grid_blocks = grid_blocks
+    args.kernel = KERNELS[kernel]
     with torch.cuda.device(A.device):
         status = lib().bsgemm_a8w8_blockscale_grouped(ctypes.byref(args), ctypes.c_void_p(group_offsets.data_ptr()),
                                                       t_rows, _stream(A.device))

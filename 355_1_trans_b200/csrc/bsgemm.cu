@@ -1028,11 +1028,11 @@ int fp8b_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockPa
   return rc != BSG_OK ? rc : launch_status();
 }
 
-template <int kBFmt, bool kOutF32>
+template <int kBFmt, bool kOutF32, bool kGrouped>
 int fp8b2_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Fp8BlockParams& p,
                    int grid, cudaStream_t st) {
   using Cfg = bsg::Fp8Block2Cfg;
-  auto* kern = bsg::fp8_block_gemm_2sm_kernel<kBFmt, kOutF32>;
+  auto* kern = bsg::fp8_block_gemm_2sm_kernel<kBFmt, kOutF32, kGrouped>;
   // The kernel's warpgroups re-split their registers with setmaxnreg; the
   // split is sized for exactly Cfg::kLaunchRegs registers per thread at launch
   // (with fewer, the promotion warps' increase could never be granted).
@@ -1046,18 +1046,19 @@ int fp8b2_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
   return rc != BSG_OK ? rc : launch_status();
 }
 
+template <bool kGrouped>
 int fp8b2_launch(int fmt, bool f32, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                  const Fp8BlockParams& p, int grid, cudaStream_t st) {
   switch (fmt) {
     case bsg::kFmtKPanel:
-      return f32 ? fp8b2_launch_t<bsg::kFmtKPanel, true>(ta, tb, tc, p, grid, st)
-                 : fp8b2_launch_t<bsg::kFmtKPanel, false>(ta, tb, tc, p, grid, st);
+      return f32 ? fp8b2_launch_t<bsg::kFmtKPanel, true, kGrouped>(ta, tb, tc, p, grid, st)
+                 : fp8b2_launch_t<bsg::kFmtKPanel, false, kGrouped>(ta, tb, tc, p, grid, st);
     case bsg::kFmtShuffle16:
-      return f32 ? fp8b2_launch_t<bsg::kFmtShuffle16, true>(ta, tb, tc, p, grid, st)
-                 : fp8b2_launch_t<bsg::kFmtShuffle16, false>(ta, tb, tc, p, grid, st);
+      return f32 ? fp8b2_launch_t<bsg::kFmtShuffle16, true, kGrouped>(ta, tb, tc, p, grid, st)
+                 : fp8b2_launch_t<bsg::kFmtShuffle16, false, kGrouped>(ta, tb, tc, p, grid, st);
     default:
-      return f32 ? fp8b2_launch_t<bsg::kFmtRaw, true>(ta, tb, tc, p, grid, st)
-                 : fp8b2_launch_t<bsg::kFmtRaw, false>(ta, tb, tc, p, grid, st);
+      return f32 ? fp8b2_launch_t<bsg::kFmtRaw, true, kGrouped>(ta, tb, tc, p, grid, st)
+                 : fp8b2_launch_t<bsg::kFmtRaw, false, kGrouped>(ta, tb, tc, p, grid, st);
   }
 }
 
@@ -1392,7 +1393,7 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
     p.total_items = p.total_units - tu + tu * ts;
     p.ws = tail_bytes ? static_cast<float*>(a.workspace) : nullptr;
     const int clusters = std::min(p.total_items, cl);
-    rc = fp8b2_launch(bfmt, f32, ta, tb, tc, p, 2 * clusters, st);
+    rc = fp8b2_launch<false>(bfmt, f32, ta, tb, tc, p, 2 * clusters, st);
     if (rc != BSG_OK || tu == 0) return rc;
     return fp8b2_tail_reduce(p, f32, dev.sms, st);
   }
@@ -1438,7 +1439,8 @@ int fp8b_grouped_run(const bsgemm_args* args, const int* group_offsets, int tota
     return BSG_ERR_INVALID_VALUE;
   if (a.out_dtype != BSG_OUT_BF16 && a.out_dtype != BSG_OUT_FP32) return BSG_ERR_INVALID_VALUE;
   if (a.split_k > 1) return BSG_ERR_UNSUPPORTED;
-  if (a.kernel != BSG_KERNEL_AUTO && a.kernel != BSG_KERNEL_1CTA) return BSG_ERR_UNSUPPORTED;
+  if (a.kernel != BSG_KERNEL_AUTO && a.kernel != BSG_KERNEL_1CTA && a.kernel != BSG_KERNEL_PAIR)
+    return BSG_ERR_UNSUPPORTED;
   if (a.layout != BSG_LAYOUT_TN) return BSG_ERR_UNSUPPORTED;
   if (a.sfa_format != BSG_SF_ROWMAJOR || a.sfb_format != BSG_SF_ROWMAJOR) return BSG_ERR_UNSUPPORTED;
   if (a.b_format != BSG_B_RAW && a.b_format != BSG_B_KPANEL128 && a.b_format != BSG_B_SHUFFLE16)
@@ -1512,8 +1514,23 @@ int fp8b_grouped_run(const bsgemm_args* args, const int* group_offsets, int tota
   p.timeout_ns = kTimeoutNs;
   p.group_offsets = group_offsets;
   p.total_rows = total_rows;
-  const int grid = grid_for(p.total_units, dev, a.grid_blocks);
   const bool f32 = a.out_dtype == BSG_OUT_FP32;
+  if (a.kernel == BSG_KERNEL_PAIR) {
+    // CTA pairs, 256-row tiles per group (on request: with groups of a few
+    // hundred rows or more; the host does not see the group sizes); C is
+    // stored with row masks, so no C tensor map
+    p.tiles_m = (a.m + 255) / 256;
+    p.tiles_n = (a.n + 255) / 256;
+    p.total_units = p.tiles_m * p.tiles_n * a.batch;
+    p.tail_units = 0;
+    p.tail_split = 1;
+    p.total_items = p.total_units;
+    CUtensorMap tc;
+    std::memset(&tc, 0, sizeof(tc));
+    const int clusters = std::min(p.total_units, fp8b_pair_clusters(a, dev.sms));
+    return fp8b2_launch<true>(bfmt, f32, ta, tb, tc, p, 2 * clusters, st);
+  }
+  const int grid = grid_for(p.total_units, dev, a.grid_blocks);
   switch (bfmt) {
     case bsg::kFmtKPanel:
       return f32 ? fp8b_grouped_launch_t<bsg::kFmtKPanel, true>(ta, tb, p, grid, st)

@@ -64,6 +64,10 @@ struct Fp8Block2Cfg {
   static constexpr uint32_t kOutBytes = 32u * 64u;
   static constexpr uint32_t kOffOut = kOffB + kBBytes * kStages;
   static constexpr uint32_t kOffBar = kOffOut + 8u * 2u * kOutBytes;
+  // grouped calls: the groups' pair-tile prefix lives in the staging area
+  // (grouped calls store C with row masks, not through it)
+  static constexpr int kMaxPrefixGroups = 1024;
+  static_assert(4u * (kMaxPrefixGroups + 1) <= 8u * 2u * kOutBytes, "prefix does not fit the staging area");
   // next unit's first K blocks prefetched into L2, this many K blocks before the unit ends
   static constexpr int kPrefetchKb = 8;
   static constexpr int kPrefetchLead = 16;
@@ -145,9 +149,58 @@ __device__ __forceinline__ PairItem pair_item(const Fp8BlockParams& p, int w) {
 // A tail slice's partial: one 256 x 256 fp32 tile, row-major.
 constexpr long long kPairSlotFloats = 256LL * 256LL;
 
+// The work of item w, the same for every role: batch (group) b, pair M tile
+// mt, N tile nt, K blocks [kb0, kb1), tail slot (-1: none) and the rows it
+// covers, [row0, row0 + rows) of A, sfa and C (row0 = 0, rows = M unless
+// grouped).  Grouped calls (no tail slices) enumerate, with the groups'
+// 256-row tile prefix `pre` in shared memory (live_tiles of them), only the
+// tiles that hold rows: tile gm belongs to the last group e with pre[e] <= gm.
+// Without the prefix they decode the full grid; false marks a tile past its
+// group's rows, which every role skips.
+struct PairWork {
+  int b, mt, nt, kb0, kb1, slot, row0, rows;
+};
+template <bool kGrouped>
+__device__ __forceinline__ bool pair_work(const Fp8BlockParams& p, const int* pre, int live_tiles, int w,
+                                          PairWork& x) {
+  int s;
+  if constexpr (kGrouped) {
+    x.kb0 = 0;
+    x.kb1 = p.num_kb;
+    x.slot = -1;
+    if (pre != nullptr) {
+      int gb, gm;
+      decode_unit(w, live_tiles, p.tiles_n, 1, p.group_m, gb, gm, x.nt, s);
+      int lo = 0, hi = p.batch - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (pre[mid] <= gm) lo = mid;
+        else hi = mid - 1;
+      }
+      x.b = lo;
+      x.mt = gm - pre[lo];
+    } else {
+      decode_unit(w, p.tiles_m, p.tiles_n, 1, p.group_m, x.b, x.mt, x.nt, s);
+    }
+    group_rows(p, x.b, x.row0, x.rows);
+    return x.mt >= 0 && x.mt * 256 < x.rows;
+  } else {
+    const PairItem it = pair_item(p, w);
+    decode_unit(it.unit, p.tiles_m, p.tiles_n, 1, p.group_m, x.b, x.mt, x.nt, s);
+    x.kb0 = it.kb0;
+    x.kb1 = it.kb1;
+    x.slot = it.slot;
+    x.row0 = 0;
+    x.rows = p.m;
+    return true;
+  }
+}
+
 // p.tiles_m counts 256-row pair tiles, p.tiles_n 256-column tiles; split_k 1
-// (the tail slices above are the only K split).
-template <int kBFmt, bool kOutF32>
+// (the tail slices above are the only K split).  kGrouped: the batch index is
+// a group (expert) whose rows of A, sfa and C start at group_offsets[b] (A's
+// tensor map spans all total_rows); B and sfb keep their per-group strides.
+template <int kBFmt, bool kOutF32, bool kGrouped = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThreads, 1)
     fp8_block_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                               const __grid_constant__ CUtensorMap tmC, const Fp8BlockParams p) {
@@ -195,7 +248,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
-    if constexpr (!kOutF32) prefetch_tmap(&tmC);
+    if constexpr (!kOutF32 && !kGrouped) prefetch_tmap(&tmC);
   }
   tc_fence_before();
   cluster_sync_all();   // barriers of both CTAs initialised, TMEM allocated
@@ -209,6 +262,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
   const int cluster_id = static_cast<int>(blockIdx.x >> 1);
   const int num_clusters = static_cast<int>(gridDim.x >> 1);
 
+  // Grouped calls: warp 0 writes the exclusive prefix of the groups' 256-row
+  // tiles (clamped as group_rows clamps); both CTAs of a pair compute the same.
+  const int* pre = nullptr;
+  int live_tiles = 0;
+  int n_items = p.total_items;
+  if constexpr (kGrouped) {
+    n_items = p.total_units;
+    if (p.batch <= Cfg::kMaxPrefixGroups) {
+      int* pre_s = reinterpret_cast<int*>(smem + Cfg::kOffOut);
+      if (warp == 0) {
+        int carry = 0;
+        for (int base = 0; base < p.batch; base += 32) {
+          const int g = base + static_cast<int>(lane);
+          int t = 0;
+          if (g < p.batch) {
+            int row0, rows;
+            group_rows(p, g, row0, rows);
+            t = (rows + 255) / 256;
+          }
+          int v = t;   // inclusive warp scan
+#pragma unroll
+          for (int d = 1; d < 32; d <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, v, d);
+            if (static_cast<int>(lane) >= d) v += y;
+          }
+          if (g < p.batch) pre_s[g] = carry + v - t;
+          carry += __shfl_sync(0xffffffffu, v, 31);
+        }
+        if (lane == 0) pre_s[p.batch] = carry;
+      }
+      __syncthreads();
+      pre = pre_s;
+      live_tiles = min(pre_s[p.batch], p.tiles_m * p.batch);
+      n_items = live_tiles * p.tiles_n;
+    }
+  }
+
   if (warp < 4) {
     setmaxnreg_dec<Cfg::kLowRegs>();
     if (warp == 0) {
@@ -218,12 +308,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
       const uint64_t pol = l2_policy_evict_normal();
       int stage = 0;
       uint32_t phase = 0;
-      for (int w = cluster_id; w < p.total_items; w += num_clusters) {
-        const PairItem it = pair_item(p, w);
-        int b, mt, nt, s;
-        decode_unit(it.unit, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
-        const int row_a = mt * 256 + static_cast<int>(rank) * 128;
-        const int row_b = nt * 256 + static_cast<int>(rank) * 128;
+      for (int w = cluster_id; w < n_items; w += num_clusters) {
+        PairWork x;
+        if (!pair_work<kGrouped>(p, pre, live_tiles, w, x)) continue;
+        const PairWork& it = x;
+        const int b = x.b;
+        const int a_batch = kGrouped ? 0 : x.b;
+        const int row_a = x.row0 + x.mt * 256 + static_cast<int>(rank) * 128;
+        const int row_b = x.nt * 256 + static_cast<int>(rank) * 128;
         // every cluster reaches its next unit at about the same time, and the
         // new unit's A or B panel is often not in L2 yet: this CTA's operands of
         // that unit's first K blocks go to L2 a while before they are needed
@@ -231,14 +323,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
         const int kb_pf = max(it.kb0, it.kb1 - Cfg::kPrefetchLead);
         bool ok = true;
         for (int kb = it.kb0; kb < it.kb1; ++kb) {
-          if (kb == kb_pf && wn < p.total_items && issuer) {
-            const PairItem nx = pair_item(p, wn);
-            int b2, mt2, nt2, s2;
-            decode_unit(nx.unit, p.tiles_m, p.tiles_n, 1, p.group_m, b2, mt2, nt2, s2);
-            const int ra = mt2 * 256 + static_cast<int>(rank) * 128;
-            const int rb = nt2 * 256 + static_cast<int>(rank) * 128;
+          PairWork nx;
+          if (kb == kb_pf && wn < n_items && issuer && pair_work<kGrouped>(p, pre, live_tiles, wn, nx)) {
+            const int b2 = nx.b;
+            const int ra = nx.row0 + nx.mt * 256 + static_cast<int>(rank) * 128;
+            const int rb = nx.nt * 256 + static_cast<int>(rank) * 128;
             for (int k2 = nx.kb0; k2 < min(nx.kb0 + Cfg::kPrefetchKb, nx.kb1); ++k2) {
-              if (ra < p.m) tma_prefetch_3d(&tmA, k2 * 128, ra, b2);
+              if (ra < (kGrouped ? p.total_rows : p.m)) tma_prefetch_3d(&tmA, k2 * 128, ra, kGrouped ? 0 : b2);
               if (rb >= p.n) continue;
               if constexpr (kBFmt == kFmtKPanel)
                 tma_prefetch_4d(&tmB, 0, rb, k2, b2);
@@ -255,7 +346,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
           const uint32_t fb_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
           if (issuer) {
             if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2u * Cfg::kStageBytes);
-            tma_load_3d_pair(sA + stage * Cfg::kABytes, &tmA, fb_leader, kb * 128, row_a, b, pol);
+            tma_load_3d_pair(sA + stage * Cfg::kABytes, &tmA, fb_leader, kb * 128, row_a, a_batch, pol);
             if constexpr (kBFmt == kFmtKPanel)
               tma_load_4d_pair(sB + stage * Cfg::kBBytes, &tmB, fb_leader, 0, row_b, kb, b, pol);
             else if constexpr (kBFmt == kFmtShuffle16)
@@ -283,8 +374,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
       uint32_t phase = 0;
       uint32_t kbi = 0;   // K blocks issued by this pair, selects the TMEM buffer
       bool ok = true;
-      for (int w = cluster_id; w < p.total_items && ok; w += num_clusters) {
-        const PairItem it = pair_item(p, w);
+      for (int w = cluster_id; w < n_items && ok; w += num_clusters) {
+        PairWork it;
+        if (!pair_work<kGrouped>(p, pre, live_tiles, w, it)) continue;
         for (int kb = it.kb0; kb < it.kb1; ++kb, ++kbi) {
           const uint32_t buf = kbi % NB;
           const uint32_t use = kbi / NB;   // how many times this buffer was used before
@@ -330,18 +422,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
     uint8_t* out_buf = smem + Cfg::kOffOut + static_cast<uint32_t>(warp - 4) * 2u * Cfg::kOutBytes;
     uint32_t kbi = 0;
     bool ok = true;
-    for (int w = cluster_id; w < p.total_items && ok; w += num_clusters) {
-      const PairItem it = pair_item(p, w);
-      int b, mt, nt, s;
-      decode_unit(it.unit, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
-      const int rbase = mt * 256 + static_cast<int>(rank) * 128;
+    for (int w = cluster_id; w < n_items && ok; w += num_clusters) {
+      PairWork it;
+      if (!pair_work<kGrouped>(p, pre, live_tiles, w, it)) continue;
+      const int b = it.b;
+      const int rbase = it.mt * 256 + static_cast<int>(rank) * 128;   // within the group (or matrix)
       const int row = rbase + q * 32 + static_cast<int>(lane);
-      const bool row_ok = row < p.m;
-      const int n0 = nt * 256 + half * 128;   // this warp's 128 columns: one B-scale block
+      const bool row_ok = row < it.rows;
+      const long long grow = static_cast<long long>(it.row0) + row;    // row of A, sfa and C
+      const int n0 = it.nt * 256 + half * 128;   // this warp's 128 columns: one B-scale block
       // a warp whose 32 rows or 128 columns all lie beyond M or N skips the
       // promotion work (and the scale loads) but still releases the buffers
-      const bool live = rbase + q * 32 < p.m && n0 < p.n;
-      const float* sfa_row = p.sfa + b * p.sfa_batch + static_cast<long long>(row_ok ? row : 0) * p.sfa_m;
+      const bool live = rbase + q * 32 < it.rows && n0 < p.n;
+      const float* sfa_row =
+          (kGrouped ? p.sfa : p.sfa + b * p.sfa_batch) + (row_ok ? grow : 0LL) * p.sfa_m;
       const float* sfb_blk = p.sfb + b * p.sfb_batch + static_cast<long long>(live ? n0 / 128 : 0) * p.sfb_n;
       uint64_t accp[64];
 #pragma unroll
@@ -399,7 +493,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
         }
       }
       if (!ok || !live) continue;
-      if (it.slot >= 0) {
+      if (!kGrouped && it.slot >= 0) {
         // a tail slice: this warp's 32 rows x 128 columns of the fp32 partial
         // go to the slice's slot (rows past M too; the reduce clips)
         float* dst = p.ws + it.slot * kPairSlotFloats +
@@ -411,12 +505,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
                        static_cast<uint32_t>(accp[2 * v + 1]), static_cast<uint32_t>(accp[2 * v + 1] >> 32));
         continue;
       }
-      if constexpr (kOutF32) {
+      if constexpr (kOutF32 || kGrouped) {
+        // fp32 C, and grouped calls (a TMA box would cross into the next
+        // group's rows): each lane stores its own row
         if (!row_ok) continue;
         float acc[128];
 #pragma unroll
         for (int i = 0; i < 64; ++i) unpack_f32x2(accp[i], acc[2 * i], acc[2 * i + 1]);
-        store_row128<true>(acc, reinterpret_cast<float*>(p.c) + b * p.c_batch_stride + row * p.ldc, n0, p.n);
+        const long long cb = kGrouped ? 0LL : b * p.c_batch_stride;
+        if constexpr (kOutF32)
+          store_row128<true>(acc, reinterpret_cast<float*>(p.c) + cb + grow * p.ldc, n0, p.n);
+        else
+          store_row128<false>(acc, reinterpret_cast<uint16_t*>(p.c) + cb + grow * p.ldc, n0, p.n);
       } else {
         // bf16 through TMA stores: per 32-column box each lane writes its row
         // (64 bytes, 64-byte swizzle, so the 32 lanes' 16-byte writes spread
@@ -450,7 +550,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
         }
       }
     }
-    if constexpr (!kOutF32)
+    if constexpr (!kOutF32 && !kGrouped)
       if (lane == 0) bulk_wait_group0();   // every store of this warp has completed
   }
 

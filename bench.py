@@ -1089,7 +1089,10 @@ def run_grouped(args):
                 B = qb1.view(torch.uint8).reshape(1, -1).repeat(e, 1).view(torch.float8_e4m3fn)
                 B = B.reshape(e, k // 128, n, 128)
                 SB = sb1.unsqueeze(0).repeat(e, 1, 1).contiguous()
-                call = lambda: bs.gemm_a8w8_blockscale_grouped(qa, B, sa, SB, offs, max(sizes), out=out)
+                calls = [("auto", lambda: bs.gemm_a8w8_blockscale_grouped(qa, B, sa, SB, offs, max(sizes), out=out))]
+                if "prefill" in label:   # CTA pairs, on request for grouped calls
+                    calls.append(("pair", lambda: bs.gemm_a8w8_blockscale_grouped(qa, B, sa, SB, offs, max(sizes),
+                                                                                  out=out, kernel="pair")))
                 sf_bytes = 4 * t * (k // 128) + 4 * e * (n // 128) * (k // 128)
             else:
                 hi = 256 if fp4 else 0x70   # any packed E2M1 byte; E4M3 bytes below the NaN codes
@@ -1105,23 +1108,24 @@ def run_grouped(args):
                 ws = torch.empty(1 << 26, dtype=torch.uint8, device=dev)
                 fn = bs.gemm_a4w4_mxfp4_grouped if fp4 else bs.gemm_a8w8_mxfp8_grouped
                 bfmt = "shuffle16" if fp4 else "raw"
-                call = lambda: fn(qa, B, sa, SB, offs, max(sizes), out=out, b_format=bfmt,
-                                  b_scale_format="native", workspace=ws)
+                calls = [("auto", lambda: fn(qa, B, sa, SB, offs, max(sizes), out=out, b_format=bfmt,
+                                             b_scale_format="native", workspace=ws))]
                 sf_bytes = t * (k // 32) + e * n * (k // 32)
-            for _ in range(3):
-                call()
-            torch.cuda.synchronize()
-
-            def both():
-                for _ in range(reps):
-                    torch.sum(flush, dim=0, out=sink)
+            for kern, call in calls:
+                for _ in range(3):
                     call()
+                torch.cuda.synchronize()
 
-            ms = max(graph_time(both) - t_flush, 1e-6) / reps
-            byts = e * n * kb + t * kb + sf_bytes + 2 * t * n
-            rows.append({"family": family, "mix": label, "experts": e, "tokens": t, "n": n, "k": k,
-                         "us": ms * 1e3, "tflops": 2.0 * t * n * k / ms / 1e9, "gbs": byts / ms / 1e6,
-                         "hbm_frac": byts / ms / 1e6 / peaks["hbm_gbs"]})
+                def both(call=call):
+                    for _ in range(reps):
+                        torch.sum(flush, dim=0, out=sink)
+                        call()
+
+                ms = max(graph_time(both) - t_flush, 1e-6) / reps
+                byts = e * n * kb + t * kb + sf_bytes + 2 * t * n
+                rows.append({"family": family, "mix": label, "kernel": kern, "experts": e, "tokens": t, "n": n,
+                             "k": k, "us": ms * 1e3, "tflops": 2.0 * t * n * k / ms / 1e9, "gbs": byts / ms / 1e6,
+                             "hbm_frac": byts / ms / 1e6 / peaks["hbm_gbs"]})
             del B, SB, qa, sa, out
     assert bs.check_device_error() == 0
     print(json.dumps({"grouped": "MoE GEMMs, experts x tokens, each expert its own weights",

@@ -518,7 +518,7 @@ def test_fp8_block_batched_c_abi(bs, orc, cuda, kernel):
 # ---- grouped (MoE) fp32 block-scale GEMM ----------------------------------------------
 
 def run_fp8_block_grouped(bs, orc, cuda, sizes, n, k, *, seed, b_layout="kpanel", tail=0, max_rows=None,
-                          out_dtype=torch.bfloat16):
+                          out_dtype=torch.bfloat16, kernel="auto"):
     """Groups of `sizes` rows concatenated (then `tail` rows in no group); each
     group against its own weights through the oracle.  Returns the output."""
     offs = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int32)
@@ -538,7 +538,7 @@ def run_fp8_block_grouped(bs, orc, cuda, sizes, n, k, *, seed, b_layout="kpanel"
     G = torch.from_numpy(offs).to(cuda)
     max_rows = max_rows or max(max(sizes), 1)
     out = poisoned((t_rows, n), out_dtype, cuda)
-    bs.gemm_a8w8_blockscale_grouped(A, B, SA, SB, G, max_rows, out_dtype, out=out, b_layout=b_layout)
+    bs.gemm_a8w8_blockscale_grouped(A, B, SA, SB, G, max_rows, out_dtype, out=out, b_layout=b_layout, kernel=kernel)
     torch.cuda.synchronize()
     assert bs.check_device_error() == 0
     got = out.float().cpu().numpy()
@@ -564,6 +564,35 @@ def test_fp8_block_grouped(bs, orc, cuda, sizes, n, k, b_layout, out_dtype):
     its own weights, with rows after the last group left untouched."""
     run_fp8_block_grouped(bs, orc, cuda, sizes, n, k, seed=400 + n + k, b_layout=b_layout, tail=9,
                           out_dtype=out_dtype)
+
+
+@pytest.mark.parametrize("sizes,n,k,b_layout,out_dtype", [
+    ((0, 5, 300, 17, 512, 1), 384, 512, "kpanel", torch.bfloat16),
+    ((256, 257, 3), 512, 1024, "raw", torch.float32),
+    ((600, 0, 40), 768, 384, "shuffle16", torch.bfloat16),
+])
+def test_fp8_block_grouped_pair(bs, orc, cuda, sizes, n, k, b_layout, out_dtype):
+    """Grouped calls on CTA pairs (256-row tiles): groups that end inside a pair tile (the peer
+    CTA's rows wholly or partly in the next group), empty and single-row groups, N ending
+    inside a column half; rows after the last group left untouched."""
+    run_fp8_block_grouped(bs, orc, cuda, sizes, n, k, seed=450 + n + k, b_layout=b_layout, tail=9,
+                          out_dtype=out_dtype, kernel="pair")
+
+
+def test_fp8_block_grouped_pair_many_experts(bs, orc, cuda):
+    """More groups than the pair kernel's tile prefix holds (1024): the full tile grid is
+    decoded and tiles past each group's rows are skipped by every role."""
+    sizes = [0] * 1100
+    for e, sz in ((3, 5), (500, 300), (1023, 1), (1024, 64), (1099, 200)):
+        sizes[e] = sz
+    run_fp8_block_grouped(bs, orc, cuda, tuple(sizes), 128, 256, seed=78, b_layout="raw", tail=3, kernel="pair")
+
+
+def test_fp8_block_grouped_pair_matches_1cta(bs, orc, cuda):
+    """Grouped pair and grouped 1-CTA results agree bit for bit (same per-row arithmetic)."""
+    a = run_fp8_block_grouped(bs, orc, cuda, (512, 300, 129), 512, 768, seed=79, kernel="pair")
+    b = run_fp8_block_grouped(bs, orc, cuda, (512, 300, 129), 512, 768, seed=79, kernel="1cta")
+    assert np.array_equal(a, b, equal_nan=True)
 
 
 def test_fp8_block_grouped_many_experts(bs, orc, cuda):
