@@ -40,8 +40,13 @@
 //       576 and 1182 TFLOPS against 1612 relaxed.  The MMA waits for the
 //       slowest of the sixteen warps, so each warp polls for its buffer
 //       (mbar_wait_spin) and has its scales loaded four K blocks ahead.
-// Split-K and grouped calls stay on the 1-CTA kernel.  Every wait is bounded
-// (sm100.cuh mbar_wait).
+//       After a unit's last K block: bf16 C through per-warp staging boxes
+//       and TMA stores (fp32 C, and grouped calls, store each lane's row).
+// The producer prefetches the next unit's first K blocks into L2 before the
+// current unit ends.  The partial last wave of units can run as K slices
+// (pair_item); their fp32 partials are summed by
+// fp8b_pair_tail_reduce_kernel.  Grouped (MoE) calls enumerate live 256-row
+// tiles per group (pair_work).  Every wait is bounded (sm100.cuh mbar_wait).
 #pragma once
 
 #include "fp8_block_gemm.cuh"

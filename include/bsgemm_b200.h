@@ -121,7 +121,7 @@ typedef struct bsgemm_args {
     int grid_blocks;        /* 0 = one CTA per SM; >0 caps the persistent grid
                                (the reference's PERSIST_GRID / m10 grid_blocks) */
     int kernel;             /* BSG_KERNEL_*: 0 = auto, 1 = single-CTA tiles,
-                               2 = CTA-pair (cta_group::2) 256x256 tiles (MX),
+                               2 = CTA-pair (cta_group::2) 256x256 tiles,
                                3 = transposed decode kernel (M <= 64; MX: layout tn) */
 } bsgemm_args;
 
@@ -168,7 +168,13 @@ BSG_API int bsgemm_a4w4_mxfp4(const bsgemm_args *args, bsg_stream_t stream);
  * BSG_B_RAW [N,K] or BSG_B_KPANEL128 B'[K/128][N][128] (stride_b = 128, as the
  * reference kargs); SFA fp32 BSG_SF_ROWMAJOR [M,K/128] (aiter x_scale) or
  * BSG_SF_KMAJOR_T [K/128,M] (reference kernel); SFB fp32 [N/128,K/128]
- * row-major.  Requires K % 128 == 0, N % 8 == 0.
+ * row-major.  Requires K % 128 == 0, N % 8 == 0.  kernel: AUTO (M <= 64 ->
+ * transposed decode kernel; CTA pairs when they cover the problem in fewer
+ * waves than single-CTA tiles; else single-CTA tiles with automatic split-K),
+ * 1CTA, PAIR or SWAP.  With split_k 0 the pair kernel runs its partial last
+ * wave as K slices whose fp32 partials use the workspace (without one, the
+ * tail runs unsplit); split_k 1 keeps every tile whole, and then 1CTA and PAIR
+ * give the same bits and a row's result does not depend on the other rows.
  * Replaces gemm_a8w8_blockscale_bpreshuffle_kernel's launch in
  * block_scale_gemm_bpreshuffle/gemm_a8w8_blockscale_bpreshuffle_host.cc:
  * 275-281 and aiter's gemm_a8w8_bpreshuffle_opus.
@@ -187,7 +193,8 @@ BSG_API int bsgemm_a8w8_blockscale_bpreshuffle(const bsgemm_args *args, bsg_stre
  * the tile grid; tiles past a group's rows are skipped).  Offsets are clamped
  * to [0, total_rows] and a group to args->m rows, so an inconsistent array
  * gives wrong rows, never an out-of-bounds access.  split_k must be 0 or 1;
- * kernel AUTO or 1CTA.
+ * kernel AUTO / 1CTA (128-row tiles) or PAIR (CTA pairs, 256-row tiles per
+ * group; the same bits).
  * No launcher in the reference; its notes point at a batched mxscale GEMM
  * (opus_gemm_splitk_and_interface_refactor.md:10, aiter PR #4320).
  */
@@ -242,8 +249,9 @@ BSG_API int bsgemm_mx_host_gemm(int family, const bsgemm_args *args, void *dev_w
                                 size_t dev_workspace_bytes, int chunks, bsg_stream_t stream);
 
 /*
- * Bytes of split-K workspace the call would need (0 when it runs without
- * split-K).  family = BSG_FAMILY_*.
+ * Bytes of workspace the call would need (0 when it needs none): split-K
+ * partials, the FP8 block-scale pair kernel's tail-slice partials, row-major
+ * MX scales repacked into native atoms.  family = BSG_FAMILY_*.
  */
 BSG_API size_t bsgemm_workspace_size(int family, const bsgemm_args *args);
 
