@@ -298,37 +298,53 @@ struct Plan {
   int clusters = 0;             // co-resident clusters used (grid = clusters * split)
 };
 
-// Split-K choice for a persistent grid of `sms` CTAs: the wall time is set by
-// the busiest CTA, i.e. ceil(tiles * split / sms) rounds of ceil(num_kb /
-// split) K stages, plus the fp32 partials every split writes and the reduce
-// reads back (expressed in K-stage units: `partial_cost` per extra slice).
-// Take the smallest split within 3 % of the best cost, at least 4 K stages
-// per slice.
-int balanced_split(long long tiles, int num_kb, int sms, int max_split, double partial_cost) {
+// Split-K choice for a persistent grid of `sms` CTAs, by a time model of the
+// call fitted to B200 measurements of the decode-shaped kernels (µs, L2
+// flushed): a round of units streams ceil(num_kb / s) K stages, each taking
+// the longer of one SM's streaming time (sm_bytes_per_kb at about 90 GB/s per
+// SM) and the round's share of HBM (hbm_bytes_per_kb of every active CTA at
+// about 6 TB/s); every further round adds about 1 µs; a split adds the reduce
+// kernel (about 3 µs) and the fp32 partials, an M x N write and read per
+// slice.  Slices keep at least 4 K stages.  (A count of rounds x K stages
+// alone chose 5 to 18 slices where 1 or 2 were fastest: M=16, N=7168,
+// K=18432 ran 28.3 µs at 5 slices against 26.3 at 2.)
+constexpr double kSmStreamBytesPerUs = 90.0e3;
+constexpr double kHbmBytesPerUs = 6.0e6;
+constexpr double kRoundUs = 1.0;
+constexpr double kReduceUs = 3.0;
+int timed_split(long long tiles, int num_kb, int sms, int max_split, double sm_bytes_per_kb,
+                double hbm_bytes_per_kb, double partial_bytes_per_slice) {
   if (tiles >= sms || num_kb < 8) return 1;
-  double best = -1.0;
-  double cost[65];
   const int smax = std::max(1, std::min(std::min(max_split, 64), num_kb / 4));
+  int best_s = 1;
+  double best = 0.0;
   for (int s = 1; s <= smax; ++s) {
-    const long long rounds = (tiles * s + sms - 1) / sms;
-    cost[s] = static_cast<double>(rounds * ((num_kb + s - 1) / s)) + (s > 1 ? partial_cost * s : 0.0);
-    if (best < 0.0 || cost[s] < best) best = cost[s];
+    const long long units = tiles * s;
+    const long long rounds = (units + sms - 1) / sms;
+    const double active = static_cast<double>(std::min<long long>(units, sms));
+    const double t_kb = std::max(sm_bytes_per_kb / kSmStreamBytesPerUs, active * hbm_bytes_per_kb / kHbmBytesPerUs);
+    double t = static_cast<double>(rounds) * ((num_kb + s - 1) / s) * t_kb + static_cast<double>(rounds - 1) * kRoundUs;
+    if (s > 1) t += kReduceUs + s * partial_bytes_per_slice / kHbmBytesPerUs;
+    if (s == 1 || t < best) {
+      best = t;
+      best_s = s;
+    }
   }
-  for (int s = 1; s <= smax; ++s)
-    if (cost[s] <= best * 1.03) return s;
-  return 1;
+  return best_s;
 }
 
-// bytes_per_kb: bytes one CTA streams per K stage (the cost unit).
-void plan_split(Plan& pl, const bsgemm_args& a, int sms, bool allow_auto, double bytes_per_kb) {
+// sm_bytes_per_kb: bytes one CTA streams per K stage (A and B tiles);
+// hbm_bytes_per_kb: the part of them that comes from HBM at decode shapes
+// (the weight tile; the activations are shared through L2).
+void plan_split(Plan& pl, const bsgemm_args& a, int sms, bool allow_auto, double sm_bytes_per_kb,
+                double hbm_bytes_per_kb) {
   const long long tiles = static_cast<long long>(pl.tiles_m) * pl.tiles_n * a.batch;
   int split = 1;
   if (a.split_k > 1) {
     split = a.split_k;
   } else if (a.split_k == 0 && allow_auto) {
-    // each slice adds an fp32 M x N write and read, spread over all SMs
-    const double partial = 8.0 * a.m * a.n * a.batch / (static_cast<double>(sms) * bytes_per_kb);
-    split = balanced_split(tiles, pl.num_kb, sms, 64, partial);
+    const double partial = 8.0 * a.m * a.n * a.batch;   // fp32 write + read of one slice
+    split = timed_split(tiles, pl.num_kb, sms, 64, sm_bytes_per_kb, hbm_bytes_per_kb, partial);
   }
   split = std::min(split, pl.num_kb);
   pl.kb_per = (pl.num_kb + split - 1) / split;
@@ -375,14 +391,14 @@ int mx_plan(const bsgemm_args& a, bool fp4, const DevInfo& dev, MxPlan& pl, bool
     pl.bn = swap_mn(a.m);   // activation rows per tile
     pl.tiles_m = 1;
     pl.tiles_n = (a.n + 127) / 128;
-    plan_split(pl, a, dev.sms, allow_auto, 128.0 * (128 + pl.bn));
+    plan_split(pl, a, dev.sms, allow_auto, 128.0 * (128 + pl.bn), 128.0 * 128);
   } else {
     pl.tiles_m = (a.m + 127) / 128;
     pl.bn = 256;
     if (static_cast<long long>(pl.tiles_m) * ((a.n + 255) / 256) * a.batch < dev.sms / 2 || a.n <= 128)
       pl.bn = 128;
     pl.tiles_n = (a.n + pl.bn - 1) / pl.bn;
-    plan_split(pl, a, dev.sms, allow_auto, 128.0 * (128 + pl.bn));
+    plan_split(pl, a, dev.sms, allow_auto, 128.0 * (128 + pl.bn), 128.0 * pl.bn);
   }
   pl.ws_sfa = a.sfa_format == BSG_SF_ROWMAJOR ? align256(native_sf_bytes(a.m, kg) * a.batch) : 0;
   pl.ws_sfb = a.sfb_format == BSG_SF_ROWMAJOR ? align256(native_sf_bytes(a.n, kg) * a.batch) : 0;
@@ -1071,12 +1087,17 @@ int fp8b_pair_clusters(const bsgemm_args& a, int sms) {
 
 // Tail split of a pair launch: the units past the last full wave of
 // `clusters` (all units, when there are fewer than a wave) run as K slices,
-// as many per unit as the clusters allow, each at least 2 K blocks.  Returns
-// the bytes of fp32 partials it needs, 0 for no split.
+// as many per unit as the clusters allow, each at least 8 K blocks (shorter
+// slices cost more in pipeline fill and partials than they save: 1024 x 24576
+// x 1536, 12 K blocks, ran slower in slices of 2 and of 4).  Returns the bytes
+// of fp32 partials it needs, 0 for no split.
 size_t fp8b_pair_tail(long long units, int clusters, int num_kb, int* tail_units, int* tail_split) {
   const long long t = units >= clusters ? units % clusters : units;
-  const int s = t > 0 ? static_cast<int>(std::min<long long>(clusters / t, num_kb / 2)) : 1;
-  if (t == 0 || s < 2) {
+  const int s = t > 0 ? static_cast<int>(std::min<long long>(clusters / t, num_kb / 8)) : 1;
+  // the slices' reduce costs about 6 µs: split only when the tail unit saves
+  // at least 16 K blocks (~10 µs; 8192 x 7168 x 2048, 16 K blocks in two
+  // slices, ran 3 % slower than whole)
+  if (t == 0 || s < 2 || num_kb - (num_kb + s - 1) / s < 16) {
     *tail_units = 0;
     *tail_split = 1;
     return 0;
@@ -1097,7 +1118,8 @@ constexpr double kPairKbCost = 1.6;
 constexpr double kPairTailCost = 0.1;
 bool fp8b_use_pair(const bsgemm_args& a, int sms) {
   if (a.kernel == BSG_KERNEL_PAIR) return true;
-  if (a.kernel != BSG_KERNEL_AUTO || a.m <= 64 || a.split_k > 1) return false;
+  // at M <= 128 the peer CTA of every pair would hold no rows
+  if (a.kernel != BSG_KERNEL_AUTO || a.m <= 128 || a.split_k > 1) return false;
   const long long units = static_cast<long long>((a.m + 255) / 256) * ((a.n + 255) / 256) * a.batch;
   const long long tiles = static_cast<long long>((a.m + 127) / 128) * ((a.n + 127) / 128) * a.batch;
   const int clusters = std::max(1, sms / 2);
@@ -1120,8 +1142,12 @@ int fp8b2_tail_reduce(const Fp8BlockParams& p, bool f32, int sms, cudaStream_t s
   return rc != BSG_OK ? rc : launch_status();
 }
 
+// Transposed decode kernel: on request (M <= 64), and automatically for
+// M <= 32.  From 33 to 64 rows the single-CTA kernel measured as fast or
+// faster (M=64: 9.9 against 13.2 µs at N=7168 K=2048, 33.4 against 43.2 at
+// K=18432; M=32 within 0.1 µs).
 bool fp8b_use_swap(const bsgemm_args& a) {
-  return a.kernel == BSG_KERNEL_SWAP || (a.kernel == BSG_KERNEL_AUTO && a.m <= 64);
+  return a.kernel == BSG_KERNEL_SWAP || (a.kernel == BSG_KERNEL_AUTO && a.m <= 32);
 }
 
 // Split-K of the transposed decode kernels for a call without the workspace
@@ -1156,11 +1182,11 @@ void fp8b_plan(const bsgemm_args& a, const DevInfo& dev, Plan& pl, bool allow_au
     const int mn = swap_mn(a.m);
     pl.bn = mn;
     pl.tiles_m = (a.m + mn - 1) / mn;
-    plan_split(pl, a, dev.sms, allow_auto, 16384.0 + 128.0 * mn);
+    plan_split(pl, a, dev.sms, allow_auto, 16384.0 + 128.0 * mn, 16384.0);
   } else {
     pl.bn = 128;
     pl.tiles_m = (a.m + 127) / 128;
-    plan_split(pl, a, dev.sms, allow_auto, 32768.0);
+    plan_split(pl, a, dev.sms, allow_auto, 32768.0, 16384.0);
   }
 }
 

@@ -443,9 +443,9 @@ def test_fp8_block_pair_matches_1cta(bs, orc, cuda):
 
 
 @pytest.mark.parametrize("m,n,k,grid_blocks,out_dtype", [
-    (1024, 5120, 1024, 0, torch.bfloat16),   # 80 units on 74 clusters: 6 tail units x 4 slices
-    (512, 2048, 2048, 0, torch.float32),     # 16 units, fewer than a wave: every unit in 4 slices
-    (1024, 5120, 1024, 26, torch.bfloat16),  # 13 clusters: 80 = 6 x 13 + 2 tail units x 4 slices
+    (1024, 5120, 4096, 0, torch.bfloat16),   # 80 units on 74 clusters: 6 tail units x 4 slices
+    (512, 2048, 4096, 0, torch.float32),     # 16 units, fewer than a wave: every unit in 4 slices
+    (1024, 5120, 4096, 26, torch.bfloat16),  # 13 clusters: 80 = 6 x 13 + 2 tail units x 4 slices
 ])
 def test_fp8_block_pair_tail_slices(bs, orc, cuda, m, n, k, grid_blocks, out_dtype):
     """The pair kernel's partial last wave as K slices (fp32 partials in the workspace, summed in
