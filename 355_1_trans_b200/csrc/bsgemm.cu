@@ -301,19 +301,21 @@ struct Plan {
 // Split-K choice for a persistent grid of `sms` CTAs, by a time model of the
 // call fitted to B200 measurements of the decode-shaped kernels (µs, L2
 // flushed): a round of units streams ceil(num_kb / s) K stages, each taking
-// the longer of one SM's streaming time (sm_bytes_per_kb at about 90 GB/s per
-// SM) and the round's share of HBM (hbm_bytes_per_kb of every active CTA at
-// about 6 TB/s); every further round adds about 1 µs; a split adds the reduce
+// the longer of one SM's streaming time (sm_bytes_per_kb at the kernel's
+// per-SM rate: about 90 GB/s for the fp32 block-scale and transposed decode
+// kernels, 130 GB/s for the single-CTA MX kernel) and the round's share of
+// HBM (hbm_bytes_per_kb of every active CTA at about 6 TB/s); every further round adds about 1 µs; a split adds the reduce
 // kernel (about 3 µs) and the fp32 partials, an M x N write and read per
 // slice.  Slices keep at least 4 K stages.  (A count of rounds x K stages
 // alone chose 5 to 18 slices where 1 or 2 were fastest: M=16, N=7168,
 // K=18432 ran 28.3 µs at 5 slices against 26.3 at 2.)
 constexpr double kSmStreamBytesPerUs = 90.0e3;
+constexpr double kSmStreamMxBytesPerUs = 130.0e3;
 constexpr double kHbmBytesPerUs = 6.0e6;
 constexpr double kRoundUs = 1.0;
 constexpr double kReduceUs = 3.0;
 int timed_split(long long tiles, int num_kb, int sms, int max_split, double sm_bytes_per_kb,
-                double hbm_bytes_per_kb, double partial_bytes_per_slice) {
+                double hbm_bytes_per_kb, double partial_bytes_per_slice, double sm_bytes_per_us) {
   if (tiles >= sms || num_kb < 8) return 1;
   const int smax = std::max(1, std::min(std::min(max_split, 64), num_kb / 4));
   int best_s = 1;
@@ -322,7 +324,7 @@ int timed_split(long long tiles, int num_kb, int sms, int max_split, double sm_b
     const long long units = tiles * s;
     const long long rounds = (units + sms - 1) / sms;
     const double active = static_cast<double>(std::min<long long>(units, sms));
-    const double t_kb = std::max(sm_bytes_per_kb / kSmStreamBytesPerUs, active * hbm_bytes_per_kb / kHbmBytesPerUs);
+    const double t_kb = std::max(sm_bytes_per_kb / sm_bytes_per_us, active * hbm_bytes_per_kb / kHbmBytesPerUs);
     double t = static_cast<double>(rounds) * ((num_kb + s - 1) / s) * t_kb + static_cast<double>(rounds - 1) * kRoundUs;
     if (s > 1) t += kReduceUs + s * partial_bytes_per_slice / kHbmBytesPerUs;
     if (s == 1 || t < best) {
@@ -337,14 +339,14 @@ int timed_split(long long tiles, int num_kb, int sms, int max_split, double sm_b
 // hbm_bytes_per_kb: the part of them that comes from HBM at decode shapes
 // (the weight tile; the activations are shared through L2).
 void plan_split(Plan& pl, const bsgemm_args& a, int sms, bool allow_auto, double sm_bytes_per_kb,
-                double hbm_bytes_per_kb) {
+                double hbm_bytes_per_kb, double sm_bytes_per_us = kSmStreamBytesPerUs) {
   const long long tiles = static_cast<long long>(pl.tiles_m) * pl.tiles_n * a.batch;
   int split = 1;
   if (a.split_k > 1) {
     split = a.split_k;
   } else if (a.split_k == 0 && allow_auto) {
     const double partial = 8.0 * a.m * a.n * a.batch;   // fp32 write + read of one slice
-    split = timed_split(tiles, pl.num_kb, sms, 64, sm_bytes_per_kb, hbm_bytes_per_kb, partial);
+    split = timed_split(tiles, pl.num_kb, sms, 64, sm_bytes_per_kb, hbm_bytes_per_kb, partial, sm_bytes_per_us);
   }
   split = std::min(split, pl.num_kb);
   pl.kb_per = (pl.num_kb + split - 1) / split;
@@ -398,7 +400,7 @@ int mx_plan(const bsgemm_args& a, bool fp4, const DevInfo& dev, MxPlan& pl, bool
     if (static_cast<long long>(pl.tiles_m) * ((a.n + 255) / 256) * a.batch < dev.sms / 2 || a.n <= 128)
       pl.bn = 128;
     pl.tiles_n = (a.n + pl.bn - 1) / pl.bn;
-    plan_split(pl, a, dev.sms, allow_auto, 128.0 * (128 + pl.bn), 128.0 * pl.bn);
+    plan_split(pl, a, dev.sms, allow_auto, 128.0 * (128 + pl.bn), 128.0 * pl.bn, kSmStreamMxBytesPerUs);
   }
   pl.ws_sfa = a.sfa_format == BSG_SF_ROWMAJOR ? align256(native_sf_bytes(a.m, kg) * a.batch) : 0;
   pl.ws_sfb = a.sfb_format == BSG_SF_ROWMAJOR ? align256(native_sf_bytes(a.n, kg) * a.batch) : 0;
