@@ -168,13 +168,14 @@ BSG_API int bsgemm_a4w4_mxfp4(const bsgemm_args *args, bsg_stream_t stream);
  * BSG_B_RAW [N,K] or BSG_B_KPANEL128 B'[K/128][N][128] (stride_b = 128, as the
  * reference kargs); SFA fp32 BSG_SF_ROWMAJOR [M,K/128] (aiter x_scale) or
  * BSG_SF_KMAJOR_T [K/128,M] (reference kernel); SFB fp32 [N/128,K/128]
- * row-major.  Requires K % 128 == 0, N % 8 == 0.  kernel: AUTO (M <= 64 ->
- * transposed decode kernel; CTA pairs when they cover the problem in fewer
- * waves than single-CTA tiles; else single-CTA tiles with automatic split-K),
- * 1CTA, PAIR or SWAP.  With split_k 0 the pair kernel runs its partial last
- * wave as K slices whose fp32 partials use the workspace (without one, the
- * tail runs unsplit); split_k 1 keeps every tile whole, and then 1CTA and PAIR
- * give the same bits and a row's result does not depend on the other rows.
+ * row-major.  Requires K % 128 == 0, N % 8 == 0.  kernel: AUTO (M <= 32 ->
+ * transposed decode kernel; M > 128 -> CTA pairs when they cover the problem
+ * in fewer waves than single-CTA tiles; else single-CTA tiles with automatic
+ * split-K), 1CTA, PAIR or SWAP (M <= 64).  With split_k 0 the pair kernel
+ * runs its partial last wave as K slices whose fp32 partials use the workspace
+ * (without one, the tail runs unsplit); split_k 1 keeps every tile whole, and
+ * then 1CTA and PAIR give the same bits and a row's result does not depend on
+ * the other rows.
  * Replaces gemm_a8w8_blockscale_bpreshuffle_kernel's launch in
  * block_scale_gemm_bpreshuffle/gemm_a8w8_blockscale_bpreshuffle_host.cc:
  * 275-281 and aiter's gemm_a8w8_bpreshuffle_opus.
