@@ -304,8 +304,12 @@ def gemm_a8w8_bpreshuffle(A, B, x_scale, w_scale, out_dtype=torch.bfloat16, *,
     preshuffled=False: B is plain [N, K].  b_layout overrides both:
     "kpanel", "shuffle16" (aiter shuffle_weight(16,16) bytes of [N, K], read in
     place) or "raw".  x_scale_transposed=True takes the reference kernel's
-    [K/128, M] SFA layout.  kernel: "auto", "1cta" (128x128 output tiles) or
-    "swap" (transposed decode kernel, M <= 64).
+    [K/128, M] SFA layout.  kernel: "auto", "1cta" (128x128 output tiles),
+    "pair" (CTA pairs, 256x256 tiles) or "swap" (transposed decode kernel,
+    M <= 64).  "auto" takes the decode kernel for M <= 32 and CTA pairs for
+    M > 128 when they need fewer waves.  split_k 0 lets the library split K
+    (and run the pair kernel's partial last wave as K slices); split_k 1 keeps
+    every tile whole, so a row's result does not depend on the other rows.
     """
     if b_layout is None:
         b_layout = "kpanel" if preshuffled else "raw"
