@@ -101,7 +101,8 @@ def parse():
     ap.add_argument("--kernel", default="auto", choices=["auto", "1cta", "pair"],
                     help="MX kernel: auto, single-CTA tiles or CTA pairs (cta_group::2)")
     ap.add_argument("--split-k", type=int, default=0,
-                    help="fp8block: split_k of the timed call (0 = the library's choice; 1 keeps every unit whole)")
+                    help="split_k of the timed call for the mxfp8, mxfp4 and fp8block workloads "
+                         "(0 = the library's choice; 1 keeps every unit whole)")
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=8192, help="per-rank N")
     ap.add_argument("--k", type=int, default=8192)
@@ -431,11 +432,12 @@ def run_ours(args):
         out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
         if fp4:
             call = lambda: bs.gemm_a4w4_mxfp4(qa, qb, sa_n, sb_n, out=out, scale_format="native",
-                                              kernel=args.kernel, b_format=b_format)
+                                              kernel=args.kernel, b_format=b_format, split_k=args.split_k)
             a_bytes, b_bytes = m * k // 2, n * k // 2
         else:
             call = lambda: bs.gemm_a8w8_mxfp8(qa, qb, sa_n, sb_n, layout=args.layout, out=out,
-                                              scale_format="native", kernel=args.kernel, b_format=b_format)
+                                              scale_format="native", kernel=args.kernel, b_format=b_format,
+                                              split_k=args.split_k)
             a_bytes, b_bytes = m * k, n * k
         sf_bytes = (m + n) * k // 32
     elif wl == "e8m0block":
