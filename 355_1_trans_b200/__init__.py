@@ -30,7 +30,7 @@ LAYOUTS = {"nt": 0, "tt": 1, "nn": 2, "tn": 3}
 B_RAW, B_KPANEL128, B_SHUFFLE16 = 0, 1, 2
 SF_NATIVE, SF_ROWMAJOR, SF_KMAJOR_T, SF_E8M0_SHUFFLE = 0, 1, 2, 3
 OUT_BF16, OUT_FP32 = 0, 1
-KERNELS = {"auto": 0, "1cta": 1, "pair": 2, "swap": 3}
+KERNELS = {"auto": 0, "1cta": 1, "pair": 2, "swap": 3, "wide": 4}
 FAMILY_MXFP8, FAMILY_MXFP4, FAMILY_FP8_BLOCK = 0, 1, 2
 
 
@@ -305,8 +305,9 @@ def gemm_a8w8_bpreshuffle(A, B, x_scale, w_scale, out_dtype=torch.bfloat16, *,
     "kpanel", "shuffle16" (aiter shuffle_weight(16,16) bytes of [N, K], read in
     place) or "raw".  x_scale_transposed=True takes the reference kernel's
     [K/128, M] SFA layout.  kernel: "auto", "1cta" (128x128 output tiles),
-    "pair" (CTA pairs, 256x256 tiles) or "swap" (transposed decode kernel,
-    M <= 64).  "auto" takes the decode kernel for M <= 32 and CTA pairs for
+    "pair" (CTA pairs, 256x256 tiles), "swap" (transposed decode kernel,
+    M <= 64) or "wide" (one CTA per 128x256 tile, every tile in the same
+    number of K slices).  "auto" takes the decode kernel for M <= 32 and CTA pairs for
     M > 128 when they need fewer waves.  split_k 0 lets the library split K
     (and run the pair kernel's partial last wave as K slices); split_k 1 keeps
     every tile whole, so a row's result does not depend on the other rows.

@@ -414,6 +414,7 @@ int validate_common(const bsgemm_args* a) {
   if (a->out_dtype != BSG_OUT_BF16 && a->out_dtype != BSG_OUT_FP32) return BSG_ERR_INVALID_VALUE;
   if (a->split_k < 0 || a->grid_blocks < 0) return BSG_ERR_INVALID_VALUE;
   if (a->layout < 0 || a->layout > 3) return BSG_ERR_INVALID_VALUE;
+  if (a->kernel < BSG_KERNEL_AUTO || a->kernel > BSG_KERNEL_WIDE) return BSG_ERR_INVALID_VALUE;
   const int vec = a->out_dtype == BSG_OUT_BF16 ? 8 : 4;
   if (a->n % vec || a->stride_c < a->n || a->stride_c % vec) return BSG_ERR_ALIGNMENT;
   if (!aligned16(a->ptr_c)) return BSG_ERR_ALIGNMENT;
@@ -852,6 +853,7 @@ int mx_run(const bsgemm_args* args, bool fp4, cudaStream_t st) {
   int rc = validate_common(args);
   if (rc != BSG_OK) return rc;
   const bsgemm_args& a = *args;
+  if (a.kernel == BSG_KERNEL_WIDE) return BSG_ERR_UNSUPPORTED;   // fp32 block scales only
   DevInfo dev;
   if ((rc = device_info(&dev)) != BSG_OK) return rc;
   if (!dev.sm100) return BSG_ERR_ARCH;
@@ -1049,7 +1051,7 @@ int fp8b_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8BlockPa
 template <int kBFmt, bool kOutF32, bool kGrouped>
 int fp8b2_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Fp8BlockParams& p,
                    int grid, cudaStream_t st) {
-  using Cfg = bsg::Fp8Block2Cfg;
+  using Cfg = bsg::Fp8Block2Cfg<true>;
   auto* kern = bsg::fp8_block_gemm_2sm_kernel<kBFmt, kOutF32, kGrouped>;
   // The kernel's warpgroups re-split their registers with setmaxnreg; the
   // split is sized for exactly Cfg::kLaunchRegs registers per thread at launch
@@ -1077,6 +1079,37 @@ int fp8b2_launch(int fmt, bool f32, const CUtensorMap& ta, const CUtensorMap& tb
     default:
       return f32 ? fp8b2_launch_t<bsg::kFmtRaw, true, kGrouped>(ta, tb, tc, p, grid, st)
                  : fp8b2_launch_t<bsg::kFmtRaw, false, kGrouped>(ta, tb, tc, p, grid, st);
+  }
+}
+
+// The wide single-CTA kernel (128 x 256 units); same register rule as the pair.
+template <int kBFmt, bool kOutF32>
+int fp8bw_launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Fp8BlockParams& p,
+                   int grid, cudaStream_t st) {
+  using Cfg = bsg::Fp8Block2Cfg<false>;
+  auto* kern = bsg::fp8_block_gemm_wide_kernel<kBFmt, kOutF32>;
+  static const int regs = [kern] {
+    cudaFuncAttributes fa{};
+    return cudaFuncGetAttributes(&fa, kern) == cudaSuccess ? fa.numRegs : -1;
+  }();
+  if (regs != Cfg::kLaunchRegs) return BSG_ERR_UNSUPPORTED;
+  if (set_smem(kern, Cfg::kSmemBytes) != BSG_OK) return BSG_ERR_CUDA;
+  const int rc = launch_pdl(kern, grid, Cfg::kThreads, Cfg::kSmemBytes, st, ta, tb, tc, p);
+  return rc != BSG_OK ? rc : launch_status();
+}
+
+int fp8bw_launch(int fmt, bool f32, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                 const Fp8BlockParams& p, int grid, cudaStream_t st) {
+  switch (fmt) {
+    case bsg::kFmtKPanel:
+      return f32 ? fp8bw_launch_t<bsg::kFmtKPanel, true>(ta, tb, tc, p, grid, st)
+                 : fp8bw_launch_t<bsg::kFmtKPanel, false>(ta, tb, tc, p, grid, st);
+    case bsg::kFmtShuffle16:
+      return f32 ? fp8bw_launch_t<bsg::kFmtShuffle16, true>(ta, tb, tc, p, grid, st)
+                 : fp8bw_launch_t<bsg::kFmtShuffle16, false>(ta, tb, tc, p, grid, st);
+    default:
+      return f32 ? fp8bw_launch_t<bsg::kFmtRaw, true>(ta, tb, tc, p, grid, st)
+                 : fp8bw_launch_t<bsg::kFmtRaw, false>(ta, tb, tc, p, grid, st);
   }
 }
 
@@ -1136,12 +1169,37 @@ bool fp8b_use_pair(const bsgemm_args& a, int sms) {
   return pair_waves * kPairKbCost < one_waves;
 }
 
-int fp8b2_tail_reduce(const Fp8BlockParams& p, bool f32, int sms, cudaStream_t st) {
-  const long long groups = static_cast<long long>(p.tail_units) * 256 * 64;
+// Sums the K slices of a pair launch (256-row units) or of a wide launch
+// (128-row units, `wide`).
+int fp8b2_tail_reduce(const Fp8BlockParams& p, bool f32, int sms, cudaStream_t st, bool wide = false) {
+  const long long groups = static_cast<long long>(p.tail_units) * (wide ? 128 : 256) * 64;
   const int grid = static_cast<int>(std::min<long long>((groups + 255) / 256, 8LL * sms));
-  const int rc = f32 ? launch_pdl(bsg::fp8b_pair_tail_reduce_kernel<true>, grid, 256, 0, st, p)
-                     : launch_pdl(bsg::fp8b_pair_tail_reduce_kernel<false>, grid, 256, 0, st, p);
+  int rc;
+  if (wide)
+    rc = f32 ? launch_pdl(bsg::fp8b_pair_tail_reduce_kernel<true, 128>, grid, 256, 0, st, p)
+             : launch_pdl(bsg::fp8b_pair_tail_reduce_kernel<false, 128>, grid, 256, 0, st, p);
+  else
+    rc = f32 ? launch_pdl(bsg::fp8b_pair_tail_reduce_kernel<true>, grid, 256, 0, st, p)
+             : launch_pdl(bsg::fp8b_pair_tail_reduce_kernel<false>, grid, 256, 0, st, p);
   return rc != BSG_OK ? rc : launch_status();
+}
+
+// Wide single-CTA kernel (128 x 256 units): on request.  K splits like the
+// other kernels (split_k > 1 forced, 0 by the time model of a unit's 48 KB
+// stage, 32 KB of it weights); every unit is then cut into that many K
+// slices, summed by the reduce above.  Returns the split and, in *ws_bytes,
+// the fp32 partials it needs.
+bool fp8b_use_wide(const bsgemm_args& a) { return a.kernel == BSG_KERNEL_WIDE; }
+int fp8b_wide_split(const bsgemm_args& a, int sms, size_t* ws_bytes) {
+  const long long units = static_cast<long long>((a.m + 127) / 128) * ((a.n + 255) / 256) * a.batch;
+  const int num_kb = a.k / 128;
+  int s = 1;
+  if (a.split_k > 1)
+    s = std::min(a.split_k, num_kb);
+  else if (a.split_k == 0)
+    s = timed_split(units, num_kb, sms, 64, 49152.0, 32768.0, 8.0 * a.m * a.n * a.batch, kSmStreamBytesPerUs);
+  *ws_bytes = s > 1 ? static_cast<size_t>(units) * static_cast<size_t>(s) * 128u * 256u * 4u : 0;
+  return s;
 }
 
 // Transposed decode kernel: on request (M <= 64), and automatically for
@@ -1326,12 +1384,14 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
   Plan pl;
   fp8b_plan(a, dev, pl, true);
   const bool pair = fp8b_use_pair(a, dev.sms);
-  if (pair) {
-    pl.tiles_m = (a.m + 255) / 256;
+  const bool wide = fp8b_use_wide(a);
+  if (pair || wide) {   // these plan their K slices themselves (the tail / wide split)
+    pl.tiles_m = pair ? (a.m + 255) / 256 : (a.m + 127) / 128;
     pl.tiles_n = (a.n + 255) / 256;
     pl.split = 1;
     pl.kb_per = pl.num_kb;
     pl.ws_partials = 0;
+    pl.cluster = false;
   }
   if (pl.ws_partials > a.workspace_bytes || (pl.ws_partials && !a.workspace)) {
     if (fp8b_use_swap(a) && swap_split_in_cluster(pl, a, swap_cluster_capacity)) {
@@ -1388,7 +1448,7 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
   const int grid = pl.cluster ? pl.clusters * pl.split : grid_for(p.total_units, dev, a.grid_blocks);
   const int cluster = pl.cluster ? pl.split : 1;
   const bool f32 = a.out_dtype == BSG_OUT_FP32;
-  if (pair) {
+  if (pair || wide) {
     // C (bf16) for the TMA-store epilogue: boxes of 32 columns x 32 rows,
     // 64-byte swizzle (fp32 C is stored directly)
     CUtensorMap tc;
@@ -1404,6 +1464,25 @@ int fp8b_run(const bsgemm_args* args, cudaStream_t st) {
       if (!make_tmap_swz(&tc, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.ptr_c, 3, dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_64B))
         return BSG_ERR_CUDA;
+    }
+    if (wide) {
+      // every unit in s K slices (s 1: whole units, stored directly)
+      size_t ws_bytes = 0;
+      int s = fp8b_wide_split(a, dev.sms, &ws_bytes);
+      if (ws_bytes && (!a.workspace || a.workspace_bytes < ws_bytes)) {
+        if (a.split_k > 1) return BSG_ERR_WORKSPACE;
+        s = 1;
+        ws_bytes = 0;
+      }
+      if (ws_bytes && !aligned16(a.workspace)) return BSG_ERR_ALIGNMENT;
+      if (ws_bytes && overlaps(a.ptr_c, c_bytes, a.workspace, ws_bytes)) return BSG_ERR_INVALID_VALUE;
+      p.tail_units = s > 1 ? p.total_units : 0;
+      p.tail_split = s;
+      p.total_items = p.total_units - p.tail_units + p.tail_units * s;
+      p.ws = ws_bytes ? static_cast<float*>(a.workspace) : nullptr;
+      rc = fp8bw_launch(bfmt, f32, ta, tb, tc, p, grid_for(p.total_items, dev, a.grid_blocks), st);
+      if (rc != BSG_OK || p.tail_units == 0) return rc;
+      return fp8b2_tail_reduce(p, f32, dev.sms, st, true);
     }
     // the partial last wave as K slices, when the caller's workspace holds
     // their fp32 partials (split_k 1 keeps every unit whole)
@@ -2040,6 +2119,11 @@ size_t bsgemm_workspace_size(int family, const bsgemm_args* args) {
     return pl.ws_sfa + pl.ws_sfb + pl.ws_partials;
   }
   if (family == BSG_FAMILY_FP8_BLOCK) {
+    if (fp8b_use_wide(*args)) {   // partials of the wide kernel's K slices
+      size_t bytes = 0;
+      fp8b_wide_split(*args, dev.sms, &bytes);
+      return bytes;
+    }
     if (fp8b_use_pair(*args, dev.sms)) {   // partials of the pair kernel's tail slices
       if (args->split_k != 0) return 0;
       int tu = 0, ts = 1;

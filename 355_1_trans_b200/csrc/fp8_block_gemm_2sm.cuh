@@ -47,12 +47,27 @@
 // (pair_item); their fp32 partials are summed by
 // fp8b_pair_tail_reduce_kernel.  Grouped (MoE) calls enumerate live 256-row
 // tiles per group (pair_work).  Every wait is bounded (sm100.cuh mbar_wait).
+//
+// The same body, with kPair false, is the wide single-CTA kernel
+// (fp8_block_gemm_wide_kernel, on request): one CTA per 128 x 256 unit, the
+// unit's 256 B rows loaded as two 128-row boxes per stage, single-CTA MMAs
+// (M = 128, N = 256) and commits, and K split by cutting every unit into the
+// same number of slices (the tail-slice mechanism with all units as tail).
+// Whole units give the 1-CTA kernel's bits.  Per K block it costs what its
+// area predicts (about 1.1 µs at 112 CTAs on 18432-deep K against 0.52 for a
+// 128 x 128 tile), so it pays only where it needs fewer rounds of units
+// (M=128 N=24576 K=1536: 14.1 against 17.5 µs).
 #pragma once
 
 #include "fp8_block_gemm.cuh"
 
 namespace bsg {
 
+// kPair: the CTA-pair kernel (256 x 256 units over two SMs).  Otherwise the
+// wide single-CTA kernel: one CTA computes a 128 x 256 unit with the same
+// warp roles, promotion and epilogue; per 128-K stage it loads 128 rows of A
+// and all 256 B rows (48 KB, 4 stages).
+template <bool kPair = true>
 struct Fp8Block2Cfg {
   static constexpr int kThreads = 384;
   static constexpr int kLaunchRegs = 168;      // 384 x 168 = 128 x 56 + 256 x 224
@@ -61,9 +76,13 @@ struct Fp8Block2Cfg {
   static_assert(128u * kLowRegs + 256u * kHighRegs <= static_cast<uint32_t>(kThreads * kLaunchRegs),
                 "register split exceeds the launch");
   static constexpr uint32_t kABytes = 128u * 128u;   // this CTA's 128 rows of A, one 128-K block
-  static constexpr uint32_t kBBytes = 128u * 128u;   // this CTA's 128 of the tile's 256 B rows
+  // the pair: this CTA's 128 of the tile's 256 B rows; wide: all 256
+  static constexpr uint32_t kBBytes = (kPair ? 128u : 256u) * 128u;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = 6;
+  static constexpr int kStages = kPair ? 6 : 4;
+  static constexpr int kTileRows = kPair ? 256 : 128;   // output rows of one unit
+  // a K slice's partial: one unit of fp32, row-major with 256 columns
+  static constexpr long long kSlotFloats = static_cast<long long>(kTileRows) * 256LL;
   static constexpr uint32_t kOffB = kABytes * kStages;
   // bf16 epilogue staging: two 32-row x 32-column boxes (64-byte rows) per promotion warp
   static constexpr uint32_t kOutBytes = 32u * 64u;
@@ -151,9 +170,6 @@ __device__ __forceinline__ PairItem pair_item(const Fp8BlockParams& p, int w) {
   return it;
 }
 
-// A tail slice's partial: one 256 x 256 fp32 tile, row-major.
-constexpr long long kPairSlotFloats = 256LL * 256LL;
-
 // The work of item w, the same for every role: batch (group) b, pair M tile
 // mt, N tile nt, K blocks [kb0, kb1), tail slot (-1: none) and the rows it
 // covers, [row0, row0 + rows) of A, sfa and C (row0 = 0, rows = M unless
@@ -205,11 +221,18 @@ __device__ __forceinline__ bool pair_work(const Fp8BlockParams& p, const int* pr
 // (the tail slices above are the only K split).  kGrouped: the batch index is
 // a group (expert) whose rows of A, sfa and C start at group_offsets[b] (A's
 // tensor map spans all total_rows); B and sfb keep their per-group strides.
-template <int kBFmt, bool kOutF32, bool kGrouped = false>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThreads, 1)
-    fp8_block_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                              const __grid_constant__ CUtensorMap tmC, const Fp8BlockParams p) {
-  using Cfg = Fp8Block2Cfg;
+//
+// kPair false (the wide kernel, fp8_block_gemm_wide_kernel): p.tiles_m counts
+// 128-row tiles; each CTA is its own "cluster" of one, so the pair-only steps
+// (pair TMA loads and MMAs, multicast commits, the pair TMEM allocation and
+// cluster barriers) become their single-CTA forms, and every CTA issues its
+// own MMAs.  Not used for grouped calls.
+template <int kBFmt, bool kOutF32, bool kGrouped, bool kPair>
+__device__ __forceinline__ void fp8b2_body(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC,
+                                           const Fp8BlockParams& p) {
+  static_assert(kPair || !kGrouped, "the wide kernel has no grouped mode");
+  using Cfg = Fp8Block2Cfg<kPair>;
+  constexpr int TR = Cfg::kTileRows;
   constexpr int S = Cfg::kStages;
   constexpr int NB = Cfg::kAccBufs;
   constexpr uint32_t BN = Cfg::kBN;
@@ -230,7 +253,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
 
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31u;
-  const uint32_t rank = cluster_ctarank();
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
   const bool leader = rank == 0;
 
   if (threadIdx.x == 32) {
@@ -240,15 +263,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
     }
     for (int i = 0; i < NB; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 16);   // eight promotion warps in each CTA
+      mbar_init(&acc_empty[i], kPair ? 16 : 8);   // eight promotion warps in each CTA
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 2) {
-    tmem_alloc_pair(tmem_holder, Cfg::kTmemCols);
-    tmem_relinquish_pair();
+    if constexpr (kPair) {
+      tmem_alloc_pair(tmem_holder, Cfg::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, Cfg::kTmemCols);
+      tmem_relinquish();
+    }
   }
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmA);
@@ -256,7 +284,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
     if constexpr (!kOutF32 && !kGrouped) prefetch_tmap(&tmC);
   }
   tc_fence_before();
-  cluster_sync_all();   // barriers of both CTAs initialised, TMEM allocated
+  if constexpr (kPair)
+    cluster_sync_all();   // barriers of both CTAs initialised, TMEM allocated
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   if (threadIdx.x == 0) griddep_launch_dependents();   // the next kernel's prologue may start
@@ -264,8 +295,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
   // the previous kernel on the stream; nothing of global memory is touched
   // before that kernel has completed.
   griddep_wait();
-  const int cluster_id = static_cast<int>(blockIdx.x >> 1);
-  const int num_clusters = static_cast<int>(gridDim.x >> 1);
+  const int cluster_id = static_cast<int>(kPair ? blockIdx.x >> 1 : blockIdx.x);
+  const int num_clusters = static_cast<int>(kPair ? gridDim.x >> 1 : gridDim.x);
 
   // Grouped calls: warp 0 writes the exclusive prefix of the groups' 256-row
   // tiles (clamped as group_rows clamps); both CTAs of a pair compute the same.
@@ -319,8 +350,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
         const PairWork& it = x;
         const int b = x.b;
         const int a_batch = kGrouped ? 0 : x.b;
-        const int row_a = x.row0 + x.mt * 256 + static_cast<int>(rank) * 128;
-        const int row_b = x.nt * 256 + static_cast<int>(rank) * 128;
+        const int row_a = x.row0 + x.mt * TR + static_cast<int>(rank) * 128;
+        const int row_b = x.nt * 256 + static_cast<int>(rank) * 128;   // wide: the first of two 128-row boxes
         // every cluster reaches its next unit at about the same time, and the
         // new unit's A or B panel is often not in L2 yet: this CTA's operands of
         // that unit's first K blocks go to L2 a while before they are needed
@@ -331,33 +362,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
           PairWork nx;
           if (kb == kb_pf && wn < n_items && issuer && pair_work<kGrouped>(p, pre, live_tiles, wn, nx)) {
             const int b2 = nx.b;
-            const int ra = nx.row0 + nx.mt * 256 + static_cast<int>(rank) * 128;
-            const int rb = nx.nt * 256 + static_cast<int>(rank) * 128;
+            const int ra = nx.row0 + nx.mt * TR + static_cast<int>(rank) * 128;
             for (int k2 = nx.kb0; k2 < min(nx.kb0 + Cfg::kPrefetchKb, nx.kb1); ++k2) {
               if (ra < (kGrouped ? p.total_rows : p.m)) tma_prefetch_3d(&tmA, k2 * 128, ra, kGrouped ? 0 : b2);
-              if (rb >= p.n) continue;
-              if constexpr (kBFmt == kFmtKPanel)
-                tma_prefetch_4d(&tmB, 0, rb, k2, b2);
-              else if constexpr (kBFmt == kFmtShuffle16)
-                tma_prefetch_5d(&tmB, 0, k2 * 8, 0, rb / 16, b2);
-              else
-                tma_prefetch_3d(&tmB, k2 * 128, rb, b2);
+#pragma unroll
+              for (int h = 0; h < (kPair ? 1 : 2); ++h) {
+                const int rb = nx.nt * 256 + static_cast<int>(rank) * 128 + h * 128;
+                if (rb >= p.n) continue;
+                if constexpr (kBFmt == kFmtKPanel)
+                  tma_prefetch_4d(&tmB, 0, rb, k2, b2);
+                else if constexpr (kBFmt == kFmtShuffle16)
+                  tma_prefetch_5d(&tmB, 0, k2 * 8, 0, rb / 16, b2);
+                else
+                  tma_prefetch_3d(&tmB, k2 * 128, rb, b2);
+              }
             }
           }
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, p.timeout_ns)) {
             ok = false;
             break;
           }
-          const uint32_t fb_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
-          if (issuer) {
-            if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2u * Cfg::kStageBytes);
-            tma_load_3d_pair(sA + stage * Cfg::kABytes, &tmA, fb_leader, kb * 128, row_a, a_batch, pol);
-            if constexpr (kBFmt == kFmtKPanel)
-              tma_load_4d_pair(sB + stage * Cfg::kBBytes, &tmB, fb_leader, 0, row_b, kb, b, pol);
-            else if constexpr (kBFmt == kFmtShuffle16)
-              tma_load_5d_pair(sB + stage * Cfg::kBBytes, &tmB, fb_leader, 0, kb * 8, 0, row_b / 16, b, pol);
-            else
-              tma_load_3d_pair(sB + stage * Cfg::kBBytes, &tmB, fb_leader, kb * 128, row_b, b, pol);
+          if constexpr (kPair) {
+            const uint32_t fb_leader = mapa_shared(smem_u32(&full_bar[stage]), 0);
+            if (issuer) {
+              if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2u * Cfg::kStageBytes);
+              tma_load_3d_pair(sA + stage * Cfg::kABytes, &tmA, fb_leader, kb * 128, row_a, a_batch, pol);
+              if constexpr (kBFmt == kFmtKPanel)
+                tma_load_4d_pair(sB + stage * Cfg::kBBytes, &tmB, fb_leader, 0, row_b, kb, b, pol);
+              else if constexpr (kBFmt == kFmtShuffle16)
+                tma_load_5d_pair(sB + stage * Cfg::kBBytes, &tmB, fb_leader, 0, kb * 8, 0, row_b / 16, b, pol);
+              else
+                tma_load_3d_pair(sB + stage * Cfg::kBBytes, &tmB, fb_leader, kb * 128, row_b, b, pol);
+            }
+          } else if (issuer) {
+            // the unit's 256 B rows as two 128-row boxes, one after the other
+            // in shared memory (the 8-row groups keep their 1024-byte stride)
+            mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
+            tma_load_3d_hint(sA + stage * Cfg::kABytes, &tmA, &full_bar[stage], kb * 128, row_a, a_batch, pol);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint8_t* dst = sB + stage * Cfg::kBBytes + static_cast<uint32_t>(h) * 16384u;
+              const int rb = row_b + h * 128;
+              if constexpr (kBFmt == kFmtKPanel)
+                tma_load_4d_hint(dst, &tmB, &full_bar[stage], 0, rb, kb, b, pol);
+              else if constexpr (kBFmt == kFmtShuffle16)
+                tma_load_5d_hint(dst, &tmB, &full_bar[stage], 0, kb * 8, 0, rb / 16, b, pol);
+              else
+                tma_load_3d_hint(dst, &tmB, &full_bar[stage], kb * 128, rb, b, pol);
+            }
           }
           __syncwarp();
           if (++stage == S) {
@@ -371,7 +423,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
       // MMA warp: all lanes run the loop, the elected lane issues
       const bool issuer = elect_one();
       // ---------------------------------------------------------------- MMA issuer (leader)
-      constexpr uint32_t idesc = idesc_f8f6f4(false, false, 256, BN);
+      constexpr uint32_t idesc = idesc_f8f6f4(false, false, kPair ? 256 : 128, BN);
       const uint64_t adesc0 = make_sdesc(smem_u32(sA), 16u, 1024u, kLayoutSW128);
       const uint64_t bdesc0 = weight_sdesc<kBFmt>(smem_u32(sB), 0);
       constexpr uint64_t kBStep = (kBFmt == kFmtShuffle16 ? 256u : 32u) >> 4;   // one K step, 16-byte units
@@ -399,12 +451,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
             const uint64_t ad = adesc0 + static_cast<uint64_t>(ust * (Cfg::kABytes >> 4));
             const uint64_t bd = bdesc0 + static_cast<uint64_t>(ust * (Cfg::kBBytes >> 4));
             const uint32_t d = tmem_base + buf * BN;
-            umma_f8f6f4_pair(d, ad, bd, idesc, 0u);
-            umma_f8f6f4_pair(d, ad + 2u, bd + kBStep, idesc, 1u);
-            umma_f8f6f4_pair(d, ad + 4u, bd + 2u * kBStep, idesc, 1u);
-            umma_f8f6f4_pair(d, ad + 6u, bd + 3u * kBStep, idesc, 1u);
-            tc_commit_pair(&empty_bar[stage], 0x3);
-            tc_commit_pair(&acc_full[buf], 0x3);
+            if constexpr (kPair) {
+              umma_f8f6f4_pair(d, ad, bd, idesc, 0u);
+              umma_f8f6f4_pair(d, ad + 2u, bd + kBStep, idesc, 1u);
+              umma_f8f6f4_pair(d, ad + 4u, bd + 2u * kBStep, idesc, 1u);
+              umma_f8f6f4_pair(d, ad + 6u, bd + 3u * kBStep, idesc, 1u);
+              tc_commit_pair(&empty_bar[stage], 0x3);
+              tc_commit_pair(&acc_full[buf], 0x3);
+            } else {
+              umma_f8f6f4(d, ad, bd, idesc, 0u);
+              umma_f8f6f4(d, ad + 2u, bd + kBStep, idesc, 1u);
+              umma_f8f6f4(d, ad + 4u, bd + 2u * kBStep, idesc, 1u);
+              umma_f8f6f4(d, ad + 6u, bd + 3u * kBStep, idesc, 1u);
+              tc_commit(&empty_bar[stage]);
+              tc_commit(&acc_full[buf]);
+            }
           }
           __syncwarp();
           if (++stage == S) {
@@ -413,7 +474,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
           }
         }
       }
-      if (issuer) tc_commit_pair(drain_bar, 0x1);
+      if (issuer) {
+        if constexpr (kPair)
+          tc_commit_pair(drain_bar, 0x1);
+        else
+          tc_commit(drain_bar);
+      }
       int dummy = 0;
       mbar_wait(drain_bar, 0, &dummy, p.timeout_ns);
     }
@@ -423,7 +489,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
     const int q = warp & 3;
     const int half = (warp - 4) >> 2;
     const uint32_t t_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(half) * 128u;
-    const uint32_t ae_leader = mapa_shared(smem_u32(acc_empty), 0);
+    // the leader's acc_empty (wide: this CTA's own, its shared::cta address
+    // being a valid shared::cluster address of itself)
+    const uint32_t ae_leader = kPair ? mapa_shared(smem_u32(acc_empty), 0) : smem_u32(acc_empty);
     uint8_t* out_buf = smem + Cfg::kOffOut + static_cast<uint32_t>(warp - 4) * 2u * Cfg::kOutBytes;
     uint32_t kbi = 0;
     bool ok = true;
@@ -431,7 +499,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
       PairWork it;
       if (!pair_work<kGrouped>(p, pre, live_tiles, w, it)) continue;
       const int b = it.b;
-      const int rbase = it.mt * 256 + static_cast<int>(rank) * 128;   // within the group (or matrix)
+      const int rbase = it.mt * TR + static_cast<int>(rank) * 128;   // within the group (or matrix)
       const int row = rbase + q * 32 + static_cast<int>(lane);
       const bool row_ok = row < it.rows;
       const long long grow = static_cast<long long>(it.row0) + row;    // row of A, sfa and C
@@ -501,7 +569,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
       if (!kGrouped && it.slot >= 0) {
         // a tail slice: this warp's 32 rows x 128 columns of the fp32 partial
         // go to the slice's slot (rows past M too; the reduce clips)
-        float* dst = p.ws + it.slot * kPairSlotFloats +
+        float* dst = p.ws + it.slot * Cfg::kSlotFloats +
                      static_cast<long long>(static_cast<int>(rank) * 128 + q * 32 + static_cast<int>(lane)) * 256 +
                      half * 128;
 #pragma unroll
@@ -561,35 +629,60 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg::kThrea
 
   __syncwarp();
   tc_fence_before();
-  cluster_sync_all();   // both CTAs done with TMEM, barriers and remote arrives
+  if constexpr (kPair)
+    cluster_sync_all();   // both CTAs done with TMEM, barriers and remote arrives
+  else
+    __syncthreads();
   tc_fence_after();
-  if (warp == 2) tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+  if (warp == 2) {
+    if constexpr (kPair)
+      tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    else
+      tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
 }
 
-// Sums the tail slices of a pair launch into C, in slice order (so the
-// result does not depend on which slice finished first): p.tail_units tiles
-// of 256 x 256, clipped at M and N.  Launched after the GEMM with
-// programmatic stream serialization; waits for it before reading.
-template <bool kOutF32>
+template <int kBFmt, bool kOutF32, bool kGrouped = false>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8Block2Cfg<true>::kThreads, 1)
+    fp8_block_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                              const __grid_constant__ CUtensorMap tmC, const Fp8BlockParams p) {
+  fp8b2_body<kBFmt, kOutF32, kGrouped, true>(tmA, tmB, tmC, p);
+}
+
+// The wide single-CTA kernel: 128 x 256 units, K slices through p.tail_*.
+template <int kBFmt, bool kOutF32>
+__global__ void __launch_bounds__(Fp8Block2Cfg<false>::kThreads, 1)
+    fp8_block_gemm_wide_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                               const __grid_constant__ CUtensorMap tmC, const Fp8BlockParams p) {
+  fp8b2_body<kBFmt, kOutF32, false, false>(tmA, tmB, tmC, p);
+}
+
+// Sums the K slices of a pair or wide launch into C, in slice order (so the
+// result does not depend on which slice finished first): p.tail_units units
+// of kRows x 256 (256 for pairs, 128 for the wide kernel), clipped at M and N.
+// Launched after the GEMM with programmatic stream serialization; waits for it
+// before reading.
+template <bool kOutF32, int kRows = 256>
 __global__ void __launch_bounds__(256) fp8b_pair_tail_reduce_kernel(const Fp8BlockParams p) {
+  constexpr long long kSlot = static_cast<long long>(kRows) * 256;
   griddep_wait();
   const int whole = p.total_units - p.tail_units;
-  const long long groups = static_cast<long long>(p.tail_units) * 256 * 64;   // 4-float groups
+  const long long groups = static_cast<long long>(p.tail_units) * kRows * 64;   // 4-float groups
   for (long long g = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; g < groups;
        g += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int tu = static_cast<int>(g / (256 * 64));
-    const int rem = static_cast<int>(g % (256 * 64));
+    const int tu = static_cast<int>(g / (kRows * 64));
+    const int rem = static_cast<int>(g % (kRows * 64));
     const int r = rem >> 6;
     const int c4 = (rem & 63) * 4;
     int b, mt, nt, s;
     decode_unit(whole + tu, p.tiles_m, p.tiles_n, 1, p.group_m, b, mt, nt, s);
-    const int row = mt * 256 + r;
+    const int row = mt * kRows + r;
     const int col = nt * 256 + c4;   // N is a multiple of 8, so col < N covers col + 3
     if (row >= p.m || col >= p.n) continue;
-    const float* src = p.ws + static_cast<long long>(tu) * p.tail_split * kPairSlotFloats + r * 256 + c4;
+    const float* src = p.ws + static_cast<long long>(tu) * p.tail_split * kSlot + r * 256 + c4;
     float4 acc = __ldg(reinterpret_cast<const float4*>(src));
     for (int j = 1; j < p.tail_split; ++j) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(src + j * kPairSlotFloats));
+      const float4 v = __ldg(reinterpret_cast<const float4*>(src + j * kSlot));
       acc.x += v.x;
       acc.y += v.y;
       acc.z += v.z;

@@ -7,7 +7,8 @@ TUNED_HEADER).  This module keeps that schema:
     gfx,cu_num,M,N,K,bias,dtype,outdtype,scaleAB,bpreshuffle,libtype,solidx,splitK,us,kernelName,err_ratio,tflops,bw
 
 with gfx = "sm_100a", libtype = "bsgemm", solidx = the bsgemm_args.kernel value
-(0 auto, 1 single-CTA tiles, 2 CTA pairs, 3 transposed decode kernel), and
+(0 auto, 1 single-CTA tiles, 2 CTA pairs, 3 transposed decode kernel, 4 wide
+single-CTA 128x256 tiles), and
 dtype naming the family ("fp8_block", "mxfp8", "mxfp4").
 
 `tune()` times every candidate (kernel, split-K) of each shape on the current
@@ -36,7 +37,7 @@ from pathlib import Path
 
 TUNED_HEADER = ["gfx", "cu_num", "M", "N", "K", "bias", "dtype", "outdtype", "scaleAB", "bpreshuffle",
                 "libtype", "solidx", "splitK", "us", "kernelName", "err_ratio", "tflops", "bw"]
-KERNEL_NAMES = {0: "auto", 1: "1cta", 2: "pair", 3: "swap"}
+KERNEL_NAMES = {0: "auto", 1: "1cta", 2: "pair", 3: "swap", 4: "wide"}
 DEFAULT_TABLE = Path(__file__).resolve().parent / "tuned" / "b200_sm100a.csv"
 
 
@@ -114,10 +115,12 @@ def candidates(family: str, m: int, k: int, n: int | None = None, sms: int = 148
         kernels.append("swap")
     if m >= 256 or (family == "fp8_block" and m > 128):
         kernels.append("pair")
+    if family == "fp8_block" and m > 64:
+        kernels.append("wide")
     for kern in kernels:
         tiles = None
         if n is not None:
-            tiles = -(-n // 128) * (1 if kern == "swap" else -(-m // 128))
+            tiles = -(-n // (256 if kern == "wide" else 128)) * (1 if kern == "swap" else -(-m // 128))
         if kern == "pair" and family == "fp8_block":
             out.append((kern, 0))   # the pair kernel's partial last wave as K slices
         for s in splits:

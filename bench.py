@@ -98,8 +98,9 @@ def parse():
     ap.add_argument("--b-format", default=None, choices=["raw", "shuffle16"],
                     help="B layout for the MX workloads (default: shuffle16 for mxfp4, raw for mxfp8)")
     ap.add_argument("--layout", default="tn", choices=["tn", "nn", "tt", "nt"])
-    ap.add_argument("--kernel", default="auto", choices=["auto", "1cta", "pair"],
-                    help="MX kernel: auto, single-CTA tiles or CTA pairs (cta_group::2)")
+    ap.add_argument("--kernel", default="auto", choices=["auto", "1cta", "pair", "swap", "wide"],
+                    help="kernel: auto, single-CTA tiles, CTA pairs (cta_group::2), the transposed decode "
+                         "kernel (M <= 64), or the wide single-CTA 128x256 kernel (fp8block only)")
     ap.add_argument("--split-k", type=int, default=0,
                     help="split_k of the timed call for the mxfp8, mxfp4 and fp8block workloads "
                          "(0 = the library's choice; 1 keeps every unit whole)")

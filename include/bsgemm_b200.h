@@ -122,10 +122,11 @@ typedef struct bsgemm_args {
                                (the reference's PERSIST_GRID / m10 grid_blocks) */
     int kernel;             /* BSG_KERNEL_*: 0 = auto, 1 = single-CTA tiles,
                                2 = CTA-pair (cta_group::2) 256x256 tiles,
-                               3 = transposed decode kernel (M <= 64; MX: layout tn) */
+                               3 = transposed decode kernel (M <= 64; MX: layout tn),
+                               4 = wide single-CTA 128x256 tiles (fp32 block scales only) */
 } bsgemm_args;
 
-enum { BSG_KERNEL_AUTO = 0, BSG_KERNEL_1CTA = 1, BSG_KERNEL_PAIR = 2, BSG_KERNEL_SWAP = 3 };
+enum { BSG_KERNEL_AUTO = 0, BSG_KERNEL_1CTA = 1, BSG_KERNEL_PAIR = 2, BSG_KERNEL_SWAP = 3, BSG_KERNEL_WIDE = 4 };
 
 /* Fill the 96-byte prefix's defaults and zero the extensions. */
 BSG_API void bsgemm_args_init(bsgemm_args *args);

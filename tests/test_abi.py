@@ -61,6 +61,13 @@ def test_invalid_arguments_rejected_without_gpu(bs):
     a.n = 260          # bf16 out needs N % 8
     a.stride_c = 260
     assert lib.bsgemm_a8w8_mxfp8(ctypes.byref(a), None) == bs.ERR_ALIGNMENT
+    a.n = a.stride_c = 256
+    for kernel in (-1, 5):   # kernel values outside BSG_KERNEL_*
+        a.kernel = kernel
+        assert lib.bsgemm_a8w8_mxfp8(ctypes.byref(a), None) == bs.ERR_INVALID_VALUE
+    a.kernel = bs.KERNELS["wide"]   # the wide kernel is for fp32 block scales only
+    assert lib.bsgemm_a8w8_mxfp8(ctypes.byref(a), None) == bs.ERR_UNSUPPORTED
+    a.kernel = 0
     assert lib.bsgemm_pack_b(None, None, 16, 16, 2, 0, None) == bs.ERR_INVALID_VALUE
     assert lib.bsgemm_pack_scales(None, 0, None, 1, 1, 1, 0, None) == bs.ERR_INVALID_VALUE
     assert lib.bsgemm_native_scales_size(200, 12) == 2 * 3 * 512

@@ -442,6 +442,55 @@ def test_fp8_block_pair_matches_1cta(bs, orc, cuda):
     assert torch.equal(outs[0], outs[1])
 
 
+# ---- wide single-CTA kernel (128 x 256 tiles, K slices of every tile) -------------------
+@pytest.mark.parametrize("m,n,k,split_k,layout,out_dtype,transposed", [
+    (128, 768, 1024, 0, "kpanel", torch.bfloat16, False),
+    (100, 520, 2048, 3, "raw", torch.float32, True),      # partial M and N tiles, slices of 5-6 K blocks
+    (64, 512, 1536, 1, "shuffle16", torch.bfloat16, False),
+    (200, 1032, 768, 2, "kpanel", torch.bfloat16, False),  # two M tiles, a last N tile of 8 columns
+    (1, 256, 384, 3, "kpanel", torch.bfloat16, False),     # slices of one K block
+    (300, 784, 3072, 0, "shuffle16", torch.float32, False),
+])
+def test_fp8_block_wide(bs, orc, cuda, m, n, k, split_k, layout, out_dtype, transposed):
+    ref, got = run_fp8_block(bs, orc, cuda, m, n, k, seed=600 + m + n, kpanel=layout == "kpanel",
+                             shuffle16=layout == "shuffle16", transposed=transposed, split_k=split_k,
+                             out_dtype=out_dtype, kernel="wide")
+    if out_dtype == torch.float32:
+        np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("layout", ["kpanel", "raw", "shuffle16"])
+def test_fp8_block_wide_matches_1cta(bs, orc, cuda, layout):
+    """Whole tiles (split_k=1): the wide kernel promotes each element in the 1-CTA kernel's
+    order with the same fma.rn, so the two agree bit for bit; with K slices the result is the
+    same from run to run."""
+    m, n, k = 200, 1040, 1536
+    qa, sa = orc.quant_fp8_block(orc.normal((m, k), seed=620), 1)
+    qb, sb = orc.quant_fp8_block(orc.normal((n, k), seed=621), 128)
+    A = dev_u8(qa, cuda).view(torch.float8_e4m3fn)
+    Bh = orc.shuffle_kpanel(qb) if layout == "kpanel" else orc.shuffle_weight16(qb) if layout == "shuffle16" else qb
+    B = dev_u8(Bh, cuda).view(torch.float8_e4m3fn)
+    SA, SB = torch.from_numpy(sa).to(cuda), torch.from_numpy(sb).to(cuda)
+    run = lambda kern, sk: bs.gemm_a8w8_bpreshuffle(A, B, SA, SB, torch.float32, b_layout=layout, kernel=kern,
+                                                    split_k=sk)
+    one, wide, s1, s2 = run("1cta", 1), run("wide", 1), run("wide", 4), run("wide", 4)
+    torch.cuda.synchronize()
+    assert bs.check_device_error() == 0
+    assert torch.equal(one, wide)
+    assert torch.equal(s1, s2)
+    ref, mag = orc.gemm_fp8_block(qa, qb, sa, sb)
+    assert_close(orc, ref, s1.cpu().numpy(), mag, f"fp8 block wide split 4 {layout}")
+
+
+def test_fp8_block_wide_mx_rejects(bs, orc, cuda):
+    """The wide kernel is for fp32 block scales only: the MX families refuse it."""
+    qa, sa = orc.quant_mxfp8(orc.normal((128, 256), seed=650))
+    qb, sb = orc.quant_mxfp8(orc.normal((256, 256), seed=651))
+    with pytest.raises(bs.BsgemmError):
+        bs.gemm_a8w8_mxfp8(dev_u8(qa, cuda).view(torch.float8_e4m3fn), dev_u8(qb, cuda).view(torch.float8_e4m3fn),
+                           dev_u8(sa, cuda), dev_u8(sb, cuda), kernel="wide")
+
+
 @pytest.mark.parametrize("m,n,k,grid_blocks,out_dtype", [
     (1024, 5120, 4096, 0, torch.bfloat16),   # 80 units on 74 clusters: 6 tail units x 4 slices
     (512, 2048, 4096, 0, torch.float32),     # 16 units, fewer than a wave: every unit in 4 slices
@@ -467,8 +516,8 @@ def test_fp8_block_pair_tail_slices(bs, orc, cuda, m, n, k, grid_blocks, out_dty
     assert_close(orc, outs[2].float().cpu().numpy(), got, mag, "tail slices against unsplit")
 
 
-@pytest.mark.parametrize("kernel", ["pair", "auto", "1cta"])
-def test_fp8_block_batched_c_abi(bs, orc, cuda, kernel):
+@pytest.mark.parametrize("kernel,split_k", [("pair", 0), ("auto", 0), ("1cta", 0), ("wide", 0), ("wide", 3)])
+def test_fp8_block_batched_c_abi(bs, orc, cuda, kernel, split_k):
     """Batched fp32 block-scale through the C ABI (the Python wrapper is batch 1): batch strides
     of A, K-panel B, both scales and C, with padding between A's and C's batch slices, checked
     per batch against the oracle.  At this size "auto" takes the pair kernel (2 waves of 120 pair
@@ -503,6 +552,7 @@ def test_fp8_block_batched_c_abi(bs, orc, cuda, kernel):
     args.layout, args.b_format = bs.LAYOUTS["tn"], bs.B_KPANEL128
     args.sfa_format, args.sfb_format, args.out_dtype = bs.SF_ROWMAJOR, bs.SF_ROWMAJOR, bs.OUT_BF16
     args.kernel = bs.KERNELS[kernel]
+    args.split_k = split_k
     ws = bs._workspace(bs.FAMILY_FP8_BLOCK, args, None, cuda)
     status = bs.lib().bsgemm_a8w8_blockscale_bpreshuffle(ctypes.byref(args), bs._stream(cuda))
     torch.cuda.synchronize()
@@ -511,7 +561,7 @@ def test_fp8_block_batched_c_abi(bs, orc, cuda, kernel):
     assert bs.check_device_error() == 0
     for e in range(batch):
         ref, mag = refs[e]
-        assert_close(orc, ref, C[e, :m].float().cpu().numpy(), mag, f"fp8 block batch {e} {kernel}")
+        assert_close(orc, ref, C[e, :m].float().cpu().numpy(), mag, f"fp8 block batch {e} {kernel} split {split_k}")
         assert torch.isnan(C[e, m:].float()).all(), "padding rows after a batch slice were written"
 
 
