@@ -482,6 +482,14 @@ def test_fp8_block_wide_matches_1cta(bs, orc, cuda, layout):
     assert_close(orc, ref, s1.cpu().numpy(), mag, f"fp8 block wide split 4 {layout}")
 
 
+@pytest.mark.parametrize("grid_blocks,split_k", [(7, 3), (1, 1), (5, 0)])
+def test_fp8_block_wide_persistent_grid(bs, orc, cuda, grid_blocks, split_k):
+    """A capped grid walks several units (and their K slices) per CTA: the TMEM buffers and the
+    stage ring carry over between units."""
+    run_fp8_block(bs, orc, cuda, 300, 1280, 1536, seed=660 + grid_blocks, split_k=split_k, kernel="wide",
+                  grid_blocks=grid_blocks)
+
+
 def test_fp8_block_wide_mx_rejects(bs, orc, cuda):
     """The wide kernel is for fp32 block scales only: the MX families refuse it."""
     qa, sa = orc.quant_mxfp8(orc.normal((128, 256), seed=650))
