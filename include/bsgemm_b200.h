@@ -172,11 +172,12 @@ BSG_API int bsgemm_a4w4_mxfp4(const bsgemm_args *args, bsg_stream_t stream);
  * row-major.  Requires K % 128 == 0, N % 8 == 0.  kernel: AUTO (M <= 32 ->
  * transposed decode kernel; M > 128 -> CTA pairs when they cover the problem
  * in fewer waves than single-CTA tiles; else single-CTA tiles with automatic
- * split-K), 1CTA, PAIR or SWAP (M <= 64).  With split_k 0 the pair kernel
- * runs its partial last wave as K slices whose fp32 partials use the workspace
- * (without one, the tail runs unsplit); split_k 1 keeps every tile whole, and
- * then 1CTA and PAIR give the same bits and a row's result does not depend on
- * the other rows.
+ * split-K), 1CTA, PAIR, SWAP (M <= 64) or WIDE (one CTA per 128x256 tile,
+ * every tile in split_k K slices; split_k 0 = the library's choice).  With
+ * split_k 0 the pair kernel runs its partial last wave as K slices whose fp32
+ * partials use the workspace (without one, the tail runs unsplit); split_k 1
+ * keeps every tile whole, and then 1CTA, PAIR and WIDE give the same bits and
+ * a row's result does not depend on the other rows.
  * Replaces gemm_a8w8_blockscale_bpreshuffle_kernel's launch in
  * block_scale_gemm_bpreshuffle/gemm_a8w8_blockscale_bpreshuffle_host.cc:
  * 275-281 and aiter's gemm_a8w8_bpreshuffle_opus.
@@ -252,8 +253,9 @@ BSG_API int bsgemm_mx_host_gemm(int family, const bsgemm_args *args, void *dev_w
 
 /*
  * Bytes of workspace the call would need (0 when it needs none): split-K
- * partials, the FP8 block-scale pair kernel's tail-slice partials, row-major
- * MX scales repacked into native atoms.  family = BSG_FAMILY_*.
+ * partials, the FP8 block-scale pair kernel's tail-slice partials and the
+ * wide kernel's K-slice partials, row-major MX scales repacked into native
+ * atoms.  family = BSG_FAMILY_*.
  */
 BSG_API size_t bsgemm_workspace_size(int family, const bsgemm_args *args);
 
