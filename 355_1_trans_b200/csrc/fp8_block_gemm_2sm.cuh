@@ -56,7 +56,9 @@
 // Whole units give the 1-CTA kernel's bits.  Per K block it costs what its
 // area predicts (about 1.1 µs at 112 CTAs on 18432-deep K against 0.52 for a
 // 128 x 128 tile), so it pays only where it needs fewer rounds of units
-// (M=128 N=24576 K=1536: 14.1 against 17.5 µs).
+// (M=128 N=24576 K=1536: 14.1 against 17.5 µs).  Tiles of 72 rows or fewer
+// run much slower for a reason not found (M=72 N=65536 K=1536: 44.9 against
+// 28.6 µs), so neither the automatic choice nor the tuner uses it.
 #pragma once
 
 #include "fp8_block_gemm.cuh"

@@ -115,12 +115,10 @@ def candidates(family: str, m: int, k: int, n: int | None = None, sms: int = 148
         kernels.append("swap")
     if m >= 256 or (family == "fp8_block" and m > 128):
         kernels.append("pair")
-    if family == "fp8_block" and m > 64:
-        kernels.append("wide")
     for kern in kernels:
         tiles = None
         if n is not None:
-            tiles = -(-n // (256 if kern == "wide" else 128)) * (1 if kern == "swap" else -(-m // 128))
+            tiles = -(-n // 128) * (1 if kern == "swap" else -(-m // 128))
         if kern == "pair" and family == "fp8_block":
             out.append((kern, 0))   # the pair kernel's partial last wave as K slices
         for s in splits:
