@@ -197,6 +197,23 @@ def test_tuned_table_lookup(tmp_path):
     assert t.lookup("mxfp8", 16, 7168, 2048) is None
 
 
+def test_tuner_candidates():
+    """The tuner times the kernels "auto" may use, never the wide kernel (slow on tiles of 72
+    rows or fewer, which a tuned row's M bucket would route to it); split-K only while the
+    output tiles leave SMs idle."""
+    import importlib
+    tuning = importlib.import_module("355_1_trans_b200.tuning")
+    c = tuning.candidates("fp8_block", 128, 1536, 24576)
+    assert ("auto", 0) in c and ("1cta", 1) in c
+    assert not any(k == "wide" for k, _ in c)
+    assert not any(s > 1 for _, s in c)            # 192 tiles fill the 148 SMs
+    c = tuning.candidates("fp8_block", 16, 7168, 7168)
+    assert ("swap", 4) in c and ("1cta", 2) in c
+    c = tuning.candidates("fp8_block", 512, 7168, 7168)
+    assert ("pair", 0) in c and ("pair", 1) in c and not any(k == "pair" and s > 1 for k, s in c)
+    assert tuning.KERNEL_NAMES[4] == "wide"        # a table row may still name it explicitly
+
+
 def test_shipped_tuned_table_loads():
     import importlib
     tuning = importlib.import_module("355_1_trans_b200.tuning")
